@@ -1,0 +1,123 @@
+/* maivs_b200.h - C ABI of the B200 MAIVS query engine.
+ *
+ * One opaque handle is one FlatCellIndex. Every entry point below replaces one method of the
+ * reference's Python/Rust API (src/index.rs #[pymethods], src/prof.rs), keeping its argument
+ * meaning, defaults (in the comments) and error behaviour; each cites the reference line it
+ * replaces. The index is built on the host cores; search runs on the GPU, and fails with
+ * MAIVS_NO_DEVICE when no CUDA device is visible (there is no CPU fallback).
+ *
+ * All functions return a maivs_status. On failure maivs_last_error(handle) describes the cause.
+ * Buffers are caller-owned, C-contiguous, and only read during the call.
+ */
+#ifndef MAIVS_B200_H
+#define MAIVS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct maivs_index maivs_index;
+
+typedef enum {
+    MAIVS_OK = 0,
+    MAIVS_BAD_SHAPE = 1,   /* dimension mismatch (PyValueError, index.rs:3329-3336) */
+    MAIVS_BAD_ARG = 2,     /* invalid argument (e.g. scan_mode, index.rs:2683-2685) */
+    MAIVS_BAD_STATE = 3,   /* e.g. add_batch before centroids (index.rs:2993-2996) */
+    MAIVS_OOM = 4,         /* host or device allocation failed */
+    MAIVS_CUDA_ERROR = 5,  /* a CUDA call failed */
+    MAIVS_OVERFLOW = 6,    /* candidate buffers overflowed after enlarging them */
+    MAIVS_UNSUPPORTED = 7, /* an option the GPU engine does not implement */
+    MAIVS_NOT_FOUND = 8,   /* unknown id or array name */
+    MAIVS_NO_DEVICE = 9    /* no CUDA device */
+} maivs_status;
+
+/* FlatCellIndex(dim, scan_mode="f32", rerank_factor=4, seed=0x5EED, code_bits=0)
+ * (index.rs:2672-2755). Only scan_mode "binary" is served by the GPU search. */
+int maivs_index_new(size_t dim, const char* scan_mode, size_t rerank_factor, uint64_t seed, size_t code_bits,
+                    maivs_index** out);
+void maivs_index_free(maivs_index* ix);
+const char* maivs_last_error(const maivs_index* ix);
+const char* maivs_status_string(int status);
+
+/* train_centroids(vectors, n_cells, sample=262144, seed=0x5EED) (index.rs:2761-2804) */
+int maivs_train_centroids(maivs_index* ix, const float* vectors, size_t n, size_t n_cells, size_t sample,
+                          uint64_t seed);
+/* set_centroids(centroids) (index.rs:2806-2821) */
+int maivs_set_centroids(maivs_index* ix, const float* centroids, size_t m);
+/* add_batch(ids, vectors) (index.rs:2987-3212) */
+int maivs_add_batch(maivs_index* ix, const uint64_t* ids, const float* vectors, size_t n);
+/* remove(id) -> bool (index.rs:3223-3276); *removed = 0 when the id is unknown */
+int maivs_remove(maivs_index* ix, uint64_t id, int* removed);
+/* compact() (index.rs:3565-3569) */
+int maivs_compact(maivs_index* ix);
+
+/* query-time and build-time switches (index.rs:2828-2984, :3520-3558) */
+int maivs_set_rerank_factor(maivs_index* ix, size_t rf);                                      /* :2949 */
+int maivs_set_two_stage(maivs_index* ix, int on, size_t mult);                                /* :2882 */
+int maivs_set_tree_route(maivs_index* ix, int on, size_t min_cells, size_t fanout, float beam_frac); /* :2839 */
+int maivs_set_graph_route(maivs_index* ix, int on, size_t min_cells);                         /* :2858 */
+int maivs_set_adaptive(maivs_index* ix, int on, float margin);                                /* :2899 */
+int maivs_set_fastscan(maivs_index* ix, int on);                                              /* :2962 */
+int maivs_set_orthogonal_polysemy(maivs_index* ix, size_t homes, float lam);                  /* :2979 */
+int maivs_set_replication(maivs_index* ix, size_t max_assign, float spill_margin);            /* :2970 */
+int maivs_set_per_dim_sq(maivs_index* ix, int on);                                            /* :2908 */
+int maivs_set_i8_rerank(maivs_index* ix, int on);                                             /* :2828 */
+int maivs_set_centroid_sq8(maivs_index* ix, int on);                                          /* :2872 */
+int maivs_set_tags(maivs_index* ix, const uint64_t* ids, const uint32_t* tags, size_t n);     /* :3535 */
+/* set_filter(lo=None, hi=None): has_filter = 0 clears it (index.rs:3550-3558) */
+int maivs_set_filter(maivs_index* ix, int has_filter, uint32_t lo, uint32_t hi);
+/* Smallest batch that takes the cell-major join (the reference uses 2 x its thread pool,
+ * index.rs:3348); default 32. */
+int maivs_set_cell_major_min_batch(maivs_index* ix, size_t n);
+
+/* __len__ (index.rs:3474) */
+int maivs_len(const maivs_index* ix, size_t* n);
+/* One value of stats() (index.rs:3393-3472) by name, e.g. "n_cells", "tree_depth". */
+int maivs_stat(maivs_index* ix, const char* name, double* value);
+
+/* Build (or rebuild) the device image on CUDA device `device`. search* calls do this on their
+ * first use (device 0, or the last one given) and after any mutation. */
+int maivs_to_device(maivs_index* ix, int device);
+
+/* search(query, k, nprobe=16, target_confidence=0.95, beta=8.0) (index.rs:3283-3305).
+ * Writes up to k results, best first; *n_out = how many (no padding). */
+int maivs_search(maivs_index* ix, const float* query, size_t k, size_t nprobe, float target_confidence, float beta,
+                 uint64_t* ids, float* scores, size_t* n_out);
+
+/* search_batch(queries, k, nprobe=16, target_confidence=0.95, beta=8.0, cell_major=True)
+ * (index.rs:3316-3391). ids/scores are nq*k, row-major, padded with UINT64_MAX / -inf. */
+int maivs_search_batch(maivs_index* ix, const float* queries, size_t nq, size_t k, size_t nprobe,
+                       float target_confidence, float beta, int cell_major, uint64_t* ids, float* scores);
+
+/* search_batch with device-resident queries and outputs, enqueued on `stream` (a cudaStream_t;
+ * NULL = the handle's stream). Returns once the work is enqueued; after synchronising the stream,
+ * maivs_device_flags() reports whether any query's candidate buffer overflowed (then the results
+ * of that call must be discarded and the call repeated; the handle has already enlarged its
+ * buffers). Same semantics as maivs_search_batch otherwise. */
+int maivs_search_batch_device(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
+                              float target_confidence, float beta, int cell_major, uint64_t* d_ids, float* d_scores,
+                              void* stream);
+int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags);
+
+/* Host copy of one internal array, for persistence, inspection and parity tests: the pointer
+ * stays valid until the next mutation of the index. Names: "vecs_f32", "scan_i8", "bits",
+ * "ext_ids", "slot_cell", "slot_cells", "cell_members", "cell_member_off", "centroids",
+ * "r_bound", "prim_len", "rep_off", "fs_codes", "fs_off", "cent_bits", "cent_sq8", "csq_min",
+ * "csq_step", "sq_min", "sq_step", "signs", "tags", "tree_level_n", "tree_codes",
+ * "tree_code_off", "tree_child_start", "tree_child_len", "tree_child_off", "tree_leaf_codes",
+ * "tree_leaf_ids", "config". */
+int maivs_array(maivs_index* ix, const char* name, const void** data, size_t* count, size_t* elem_bytes);
+
+/* profile(on) / profile_read(reset=True) (src/prof.rs:76-98): device time per query phase. The
+ * reader fills up to `cap` (name, milliseconds) pairs; names are static strings. */
+int maivs_profile(int on);
+int maivs_profile_read(int reset, const char** names, double* values, size_t cap, size_t* n_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAIVS_B200_H */

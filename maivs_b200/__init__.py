@@ -1,0 +1,279 @@
+"""B200-native MAIVS query engine: a drop-in for the reference's `maivs` Python module.
+
+`FlatCellIndex` keeps the reference's constructor, method names, defaults, return types and
+errors (src/index.rs #[pymethods], src/lib.rs:32-39). The index is built on the host cores;
+`search` / `search_batch` run on the GPU through hand-written sm_100a kernels behind the C ABI of
+include/maivs_b200.h. There is no CPU search path: without a CUDA device, search raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+
+__all__ = ["FlatCellIndex", "profile", "profile_read", "MaivsError"]
+
+
+class MaivsError(RuntimeError):
+    """A failure reported by the engine (CUDA error, overflow, unsupported option)."""
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def _as_f32_matrix(x, name: str, dim: int) -> np.ndarray:
+    if not isinstance(x, np.ndarray) or x.dtype != np.float32:
+        raise TypeError(f"{name} must be a float32 numpy array")
+    if x.ndim != 2:
+        raise ValueError(f"{name} must be 2-D")
+    if x.shape[1] != dim:
+        raise ValueError("query dim mismatch" if name == "queries" else "dim mismatch")
+    if not x.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"{name} must be C-contiguous (use np.ascontiguousarray)")
+    return x
+
+
+class FlatCellIndex:
+    """Partitioned vector index with fixed-size cells, 1-bit FastScan codes, orthogonal polysemy,
+    cell-major batch search and exact rerank; queries run on the GPU.
+
+    Only scan_mode="binary" is served (the reference's "f32"/"i8" modes are ablations that no
+    preset uses); a compacted FastScan index is required before searching."""
+
+    def __init__(self, dim: int, scan_mode: str = "f32", rerank_factor: int = 4, seed: int = 0x5EED,
+                 code_bits: int = 0):
+        L = _lib.lib()
+        h = C.c_void_p()
+        rc = L.maivs_index_new(int(dim), scan_mode.encode(), int(rerank_factor), int(seed) & (2**64 - 1),
+                               int(code_bits), C.byref(h))
+        self._h = h
+        self._dim = int(dim)
+        if rc != _lib.OK:
+            msg = L.maivs_last_error(h).decode() if h else "allocation failed"
+            if h:
+                L.maivs_index_free(h)
+            self._h = None
+            raise ValueError(msg)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            _lib.lib().maivs_index_free(h)
+            self._h = None
+
+    # ---- plumbing ----
+    def _check(self, rc: int) -> None:
+        if rc == _lib.OK:
+            return
+        L = _lib.lib()
+        msg = L.maivs_last_error(self._h).decode()
+        if rc in (_lib.BAD_SHAPE, _lib.BAD_ARG, _lib.BAD_STATE):
+            raise ValueError(msg)
+        raise MaivsError(f"{L.maivs_status_string(rc).decode()}: {msg}")
+
+    @property
+    def dim(self) -> int:
+        return self._dim
+
+    # ---- build (host cores) ----
+    def train_centroids(self, vectors: np.ndarray, n_cells: int, sample: int = 262_144, seed: int = 0x5EED) -> None:
+        v = _as_f32_matrix(vectors, "vectors", self._dim)
+        self._check(_lib.lib().maivs_train_centroids(self._h, _ptr(v), v.shape[0], int(n_cells), int(sample),
+                                                     int(seed) & (2**64 - 1)))
+
+    def set_centroids(self, centroids: np.ndarray) -> None:
+        c = np.asarray(centroids)
+        if c.ndim != 2 or c.shape[1] != self._dim:
+            raise ValueError("centroid dim mismatch")
+        c = np.ascontiguousarray(c, dtype=np.float32)
+        self._check(_lib.lib().maivs_set_centroids(self._h, _ptr(c), c.shape[0]))
+
+    def add_batch(self, ids, vectors: np.ndarray) -> None:
+        ids_a = np.ascontiguousarray(np.asarray(list(ids) if not isinstance(ids, np.ndarray) else ids,
+                                                dtype=np.uint64))
+        v = np.asarray(vectors)
+        if v.ndim != 2 or v.shape[0] != ids_a.shape[0] or v.shape[1] != self._dim:
+            raise ValueError("shape mismatch")
+        if v.dtype != np.float32:
+            raise TypeError("vectors must be a float32 numpy array")
+        if not v.flags["C_CONTIGUOUS"]:
+            raise ValueError("vectors must be C-contiguous (use np.ascontiguousarray)")
+        self._check(_lib.lib().maivs_add_batch(self._h, _ptr(ids_a), _ptr(v), ids_a.shape[0]))
+
+    def remove(self, id: int) -> bool:
+        r = C.c_int(0)
+        self._check(_lib.lib().maivs_remove(self._h, int(id), C.byref(r)))
+        return bool(r.value)
+
+    def compact(self) -> None:
+        self._check(_lib.lib().maivs_compact(self._h))
+
+    # ---- configuration (index.rs:2823-2984, :3520-3558) ----
+    def set_rerank_factor(self, rf: int) -> None:
+        self._check(_lib.lib().maivs_set_rerank_factor(self._h, int(rf)))
+
+    def set_two_stage(self, on: bool, mult: int) -> None:
+        self._check(_lib.lib().maivs_set_two_stage(self._h, int(bool(on)), int(mult)))
+
+    def set_tree_route(self, on: bool, min_cells: int = 0, fanout: int = 0, beam_frac: float = 0.0) -> None:
+        self._check(_lib.lib().maivs_set_tree_route(self._h, int(bool(on)), int(min_cells), int(fanout),
+                                                    float(beam_frac)))
+
+    def set_graph_route(self, on: bool, min_cells: int = 0) -> None:
+        self._check(_lib.lib().maivs_set_graph_route(self._h, int(bool(on)), int(min_cells)))
+
+    def set_adaptive(self, on: bool, margin: float) -> None:
+        self._check(_lib.lib().maivs_set_adaptive(self._h, int(bool(on)), float(margin)))
+
+    def set_fastscan(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_set_fastscan(self._h, int(bool(on))))
+
+    def set_orthogonal_polysemy(self, homes: int = 2, lam: float = 1.0) -> None:
+        self._check(_lib.lib().maivs_set_orthogonal_polysemy(self._h, int(homes), float(lam)))
+
+    def set_replication(self, max_assign: int, spill_margin: float) -> None:
+        self._check(_lib.lib().maivs_set_replication(self._h, int(max_assign), float(spill_margin)))
+
+    def set_per_dim_sq(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_set_per_dim_sq(self._h, int(bool(on))))
+
+    def set_i8_rerank(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_set_i8_rerank(self._h, int(bool(on))))
+
+    def set_centroid_sq8(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_set_centroid_sq8(self._h, int(bool(on))))
+
+    def set_tags(self, ids, tags) -> None:
+        ids_a = np.ascontiguousarray(np.asarray(ids, dtype=np.uint64))
+        tg = np.ascontiguousarray(np.asarray(tags, dtype=np.uint32))
+        if ids_a.shape != tg.shape:
+            raise ValueError("ids/tags length mismatch")
+        self._check(_lib.lib().maivs_set_tags(self._h, _ptr(ids_a), _ptr(tg), ids_a.shape[0]))
+
+    def set_filter(self, lo: Optional[int] = None, hi: Optional[int] = None) -> None:
+        if lo is None and hi is None:
+            self._check(_lib.lib().maivs_set_filter(self._h, 0, 0, 0))
+        else:
+            self._check(_lib.lib().maivs_set_filter(self._h, 1, 0 if lo is None else int(lo),
+                                                    0xFFFFFFFF if hi is None else int(hi)))
+
+    def set_cell_major_min_batch(self, n: int) -> None:
+        """Smallest batch that takes the cell-major join (reference: 2 x its thread count)."""
+        self._check(_lib.lib().maivs_set_cell_major_min_batch(self._h, int(n)))
+
+    def to_device(self, device: int = 0) -> None:
+        """Build the device image now on CUDA device `device` (search does it on first use)."""
+        self._check(_lib.lib().maivs_to_device(self._h, int(device)))
+
+    # ---- search (GPU) ----
+    def search(self, query: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+               beta: float = 8.0):
+        q = np.ascontiguousarray(np.asarray(query, dtype=np.float32).reshape(-1))
+        if q.shape[0] != self._dim:
+            raise ValueError("query dim mismatch")
+        ids = np.empty(max(int(k), 1), dtype=np.uint64)
+        sc = np.empty(max(int(k), 1), dtype=np.float32)
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_search(self._h, _ptr(q), int(k), int(nprobe), float(target_confidence),
+                                            float(beta), _ptr(ids), _ptr(sc), C.byref(n)))
+        m = n.value
+        return [int(x) for x in ids[:m]], [float(x) for x in sc[:m]]
+
+    def search_batch_arrays(self, queries: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+                            beta: float = 8.0, cell_major: bool = True):
+        """search_batch returning numpy arrays (ids uint64 [nq*k], scores float32 [nq*k])."""
+        Q = _as_f32_matrix(queries, "queries", self._dim)
+        nq = Q.shape[0]
+        ids = np.empty(nq * int(k), dtype=np.uint64)
+        sc = np.empty(nq * int(k), dtype=np.float32)
+        self._check(_lib.lib().maivs_search_batch(self._h, _ptr(Q), nq, int(k), int(nprobe),
+                                                  float(target_confidence), float(beta), int(bool(cell_major)),
+                                                  _ptr(ids), _ptr(sc)))
+        return ids, sc
+
+    def search_batch(self, queries: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+                     beta: float = 8.0, cell_major: bool = True):
+        ids, sc = self.search_batch_arrays(queries, k, nprobe, target_confidence, beta, cell_major)
+        return ids.tolist(), sc.tolist()
+
+    def search_batch_device(self, d_queries: int, nq: int, k: int, d_ids: int, d_scores: int, nprobe: int = 16,
+                            target_confidence: float = 0.95, beta: float = 8.0, cell_major: bool = True,
+                            stream: int = 0) -> None:
+        """Enqueue a search on device pointers (e.g. torch tensors' data_ptr()) on `stream`."""
+        self._check(_lib.lib().maivs_search_batch_device(
+            self._h, C.c_void_p(d_queries), int(nq), int(k), int(nprobe), float(target_confidence), float(beta),
+            int(bool(cell_major)), C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(stream or None)))
+
+    def device_flags(self, stream: int = 0) -> int:
+        f = C.c_uint32(0)
+        self._check(_lib.lib().maivs_device_flags(self._h, C.c_void_p(stream or None), C.byref(f)))
+        return int(f.value)
+
+    # ---- introspection ----
+    def __len__(self) -> int:
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_len(self._h, C.byref(n)))
+        return n.value
+
+    _STATS = ("n_live", "n_cells", "free_slots", "quant_scale", "scan_bytes_per_vec", "cell_size_mean",
+              "cell_size_max", "cell_size_min", "max_assign", "centroid_graph_nodes", "tree_depth",
+              "tree_top_width", "tree_fanout", "tree_beam_frac", "replication_factor", "member_entries",
+              "total_bytes", "live_cells", "device_bytes")
+
+    def stats(self) -> dict:
+        out = {}
+        v = C.c_double(0.0)
+        for name in self._STATS:
+            self._check(_lib.lib().maivs_stat(self._h, name.encode(), C.byref(v)))
+            out[name] = float(v.value)
+        return out
+
+    _DTYPES = {1: np.uint8, 4: None, 8: None}
+
+    def array(self, name: str) -> np.ndarray:
+        """Copy of an internal host array (see maivs_array in include/maivs_b200.h)."""
+        p = C.c_void_p()
+        n = C.c_size_t(0)
+        eb = C.c_size_t(0)
+        self._check(_lib.lib().maivs_array(self._h, name.encode(), C.byref(p), C.byref(n), C.byref(eb)))
+        dt = _ARRAY_DTYPES.get(name)
+        if n.value == 0 or not p.value:
+            return np.zeros(0, dtype=dt)
+        buf = (C.c_uint8 * (n.value * eb.value)).from_address(p.value)
+        return np.frombuffer(bytes(buf), dtype=dt).copy()
+
+
+_ARRAY_DTYPES = {
+    "vecs_f32": np.float32, "scan_i8": np.int8, "bits": np.uint64, "ext_ids": np.uint64, "slot_cell": np.uint32,
+    "slot_cells": np.uint32, "cell_members": np.uint32, "cell_member_off": np.uint32, "centroids": np.float32,
+    "r_bound": np.float32, "prim_len": np.uint32, "rep_off": np.uint32, "fs_codes": np.uint8, "fs_off": np.uint32,
+    "cent_bits": np.uint64, "cent_sq8": np.uint8, "csq_min": np.float32, "csq_step": np.float32,
+    "sq_min": np.float32, "sq_step": np.float32, "signs": np.float32, "tags": np.uint32, "tree_level_n": np.uint64,
+    "tree_codes": np.uint64, "tree_code_off": np.uint64, "tree_child_start": np.uint64,
+    "tree_child_len": np.uint64, "tree_child_off": np.uint64, "tree_leaf_codes": np.uint64,
+    "tree_leaf_ids": np.uint32, "config": np.float64,
+}
+
+CONFIG_FIELDS = ("dim", "dim_pad", "nw", "rerank_factor", "two_stage", "shortlist_mult", "centroid_sq8", "has_tree",
+                 "max_assign", "fastscan", "per_dim_sq", "i8_rerank", "keep_f32", "adaptive", "at_margin",
+                 "quant_scale", "compacted", "n_live", "cm_min_batch", "has_filter", "filter_lo", "filter_hi",
+                 "tree_beam_frac", "tree_n_leaf", "graph_route", "graph_min_cells")
+
+
+def profile(on: bool) -> None:
+    """Turn phase profiling on or off (process-wide), as the reference's maivs.profile."""
+    _lib.lib().maivs_profile(int(bool(on)))
+
+
+def profile_read(reset: bool = True):
+    """Accumulated phase times in milliseconds (q.count is a count), as maivs.profile_read."""
+    n = 32
+    names = (C.c_char_p * n)()
+    vals = (C.c_double * n)()
+    got = C.c_size_t(0)
+    _lib.lib().maivs_profile_read(int(bool(reset)), names, vals, n, C.byref(got))
+    return [(names[i].decode(), float(vals[i])) for i in range(got.value)]

@@ -1,0 +1,496 @@
+// Device image upload and the two search pipelines (cell-major join, per-query scan).
+#include <omp.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "../host/hostmath.h"
+#include "engine.h"
+
+namespace maivs {
+
+namespace {
+
+constexpr int kPerQueryChunk = 64;  // queries per per-query pipeline pass (bounds its scratch)
+
+struct Bump {
+    char* base;
+    size_t off = 0, cap;
+    template <typename T>
+    T* take(size_t n) {
+        size_t a = (off + 255) & ~size_t(255);
+        off = a + n * sizeof(T);
+        return base ? reinterpret_cast<T*>(base + a) : nullptr;
+    }
+};
+
+#define CUDA_TRY(expr)                                             \
+    do {                                                           \
+        cudaError_t e_ = (expr);                                   \
+        if (e_ != cudaSuccess) {                                   \
+            err = std::string(#expr) + ": " + cudaGetErrorString(e_); \
+            return e_ == cudaErrorMemoryAllocation ? kOom : kCudaError; \
+        }                                                          \
+    } while (0)
+
+}  // namespace
+
+DeviceIndex::~DeviceIndex() {
+    if (device_ >= 0) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void* p : allocs_) cudaFree(p);
+    if (ws_) cudaFree(ws_);
+    if (pin_) cudaFreeHost(pin_);
+    for (auto& e : ev_)
+        if (e) cudaEventDestroy(e);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void* DeviceIndex::alloc(size_t bytes) {
+    void* p = nullptr;
+    if (bytes == 0) bytes = 16;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    allocs_.push_back(p);
+    bytes_ += bytes;
+    return p;
+}
+
+template <typename T>
+T* DeviceIndex::upload_vec(const std::vector<T>& v) {
+    T* p = static_cast<T*>(alloc(v.size() * sizeof(T)));
+    if (p && !v.empty()) cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice);
+    return p;
+}
+
+std::string DeviceIndex::upload(const HostIndex& h, int device) {
+    if (!h.compacted || !h.fastscan || h.fs_off.empty())
+        return "the GPU search needs a compacted FastScan index: call set_fastscan(True) and compact() first";
+    if (h.nw > 16) return "codes longer than 1024 bits are not supported";
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return "no CUDA device is visible";
+    if (device < 0 || device >= ndev) return "device ordinal out of range";
+    device_ = device;
+    cudaSetDevice(device_);
+    if (!stream_) cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking);
+    for (auto& e : ev_)
+        if (!e) cudaEventCreate(&e);
+    for (void* p : allocs_) cudaFree(p);
+    allocs_.clear();
+    bytes_ = 0;
+
+    const size_t M = h.cells.size(), dim = h.dim, nw = h.nw, npos = nw * 16, ma = h.max_assign;
+    dev::IndexView v{};
+    v.dim = (int)dim;
+    v.dim_pad = (int)h.dim_pad;
+    v.nw = (int)nw;
+    v.npos = (int)npos;
+    v.M = (int)M;
+    v.ma = (int)ma;
+    v.maxk = 255u * (uint32_t)npos;
+
+    // ---- scan layout: per cell, its members' codes as position-major 8-member nibble words ----
+    std::vector<uint32_t> moff(M + 1, 0), woff(M + 1, 0);
+    max_members_ = 0;
+    for (size_t c = 0; c < M; ++c) {
+        size_t n = h.cells[c].members.size();
+        max_members_ = std::max(max_members_, n);
+        moff[c + 1] = moff[c] + (uint32_t)n;
+        woff[c + 1] = woff[c] + (uint32_t)(npos * ((n + 7) / 8));
+    }
+    std::vector<uint32_t> slots(moff[M]), codes(woff[M], 0);
+#pragma omp parallel for schedule(dynamic, 16)
+    for (long long c = 0; c < (long long)M; ++c) {
+        const auto& mem = h.cells[c].members;
+        size_t n = mem.size(), ng = (n + 7) / 8;
+        std::copy(mem.begin(), mem.end(), slots.begin() + moff[c]);
+        uint32_t* cw = codes.data() + woff[c];
+        for (size_t g = 0; g < ng; ++g)
+            for (size_t b = 0; b < 8 && 8 * g + b < n; ++b) {
+                const uint64_t* code = &h.bits[(size_t)mem[8 * g + b] * nw];
+                for (size_t j = 0; j < npos; ++j) cw[j * ng + g] |= (uint32_t)nib(code, j) << (4 * b);
+            }
+    }
+    v.cell_moff = upload_vec(moff);
+    v.cell_woff = upload_vec(woff);
+    v.cell_slots = upload_vec(slots);
+    v.cell_codes = upload_vec(codes);
+    v.slot_cells = upload_vec(h.slot_cells);
+    v.ext_ids = upload_vec(h.ext_ids);
+    v.tags = h.tags.empty() ? nullptr : upload_vec(h.tags);
+
+    // ---- rerank store (index.rs:1309-1371) ----
+    if (h.per_dim_sq) {
+        v.rerank_mode = 1;
+    } else if (h.i8_rerank) {
+        v.rerank_mode = 2;
+    } else {
+        v.rerank_mode = 0;
+    }
+    if (v.rerank_mode == 0) {
+        v.vecs_f32 = upload_vec(h.vecs_f32);
+    } else {
+        std::vector<uint8_t> u(h.scan_i8.size());
+        std::memcpy(u.data(), h.scan_i8.data(), u.size());
+        v.rr_u8 = upload_vec(u);
+    }
+    if (h.per_dim_sq) {
+        v.sq_min = upload_vec(h.sq_min);
+        v.sq_step = upload_vec(h.sq_step);
+    }
+
+    // ---- routing tables ----
+    std::vector<uint8_t> live(M);
+    std::vector<float> rb(M), cf(M * dim);
+    n_live_ = 0;
+    for (size_t c = 0; c < M; ++c) {
+        live[c] = h.cells[c].members.empty() ? 0 : 1;
+        n_live_ += live[c];
+        rb[c] = h.cells[c].r_bound;
+        std::copy(h.cells[c].centroid.begin(), h.cells[c].centroid.end(), cf.begin() + c * dim);
+    }
+    v.live = upload_vec(live);
+    v.r_bound = upload_vec(rb);
+    v.cent_f32 = upload_vec(cf);
+    v.signs = upload_vec(h.signs);
+    std::vector<uint64_t> cb = h.cent_bits;
+    if (cb.size() != M * nw) {
+        // route_batch needs the codes even when only the tree was built (index.rs:1873-1876 reads
+        // cent_bits only with two_stage; the codes are cheap, so they always exist here).
+        cb.assign(M * nw, 0);
+        std::vector<float> rot(h.dim_pad);
+        for (size_t c = 0; c < M; ++c) {
+            rotate(h.cells[c].centroid.data(), dim, h.signs.data(), h.dim_pad, rot.data());
+            pack_signs_trunc(rot.data(), h.dim_pad, &cb[c * nw], nw);
+        }
+    }
+    v.cent_bits = upload_vec(cb);
+    use_sq8_ = h.centroid_sq8 && !h.cent_sq8.empty();
+    if (use_sq8_) {
+        v.cent_sq8 = upload_vec(h.cent_sq8);
+        v.csq_min = upload_vec(h.csq_min);
+        v.csq_step = upload_vec(h.csq_step);
+    }
+    // ---- centroid tree ----
+    v.tree_depth = 0;
+    n_leaf_ = 0;
+    tree_cap_ = 0;
+    if (h.tree) {
+        const CentroidTree& t = *h.tree;
+        if (t.levels.size() > (size_t)dev::kMaxTreeLevels) return "centroid tree deeper than 8 levels";
+        v.tree_depth = (int)t.levels.size();
+        for (size_t i = 0; i < t.levels.size(); ++i) {
+            v.tree_codes[i] = upload_vec(t.levels[i].codes);
+            v.tree_child_start[i] = upload_vec(t.levels[i].child_start);
+            v.tree_child_len[i] = upload_vec(t.levels[i].child_len);
+            v.tree_n[i] = (int)t.levels[i].n;
+            tree_cap_ = std::max(tree_cap_, t.levels[i].n);
+        }
+        v.leaf_codes = upload_vec(t.leaf_codes);
+        v.leaf_ids = upload_vec(t.leaf_ids);
+        v.n_leaf = (int)t.n_leaf;
+        n_leaf_ = t.n_leaf;
+        tree_cap_ = std::max(tree_cap_, t.n_leaf);
+    }
+    d_flags_ = static_cast<uint32_t*>(alloc(4 * sizeof(uint32_t)));
+    for (void* p : allocs_)
+        if (!p) return "device allocation failed";
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return std::string("upload: ") + cudaGetErrorString(e);
+    if (!d_flags_) return "device allocation failed";
+    cudaMemset(d_flags_, 0, 4 * sizeof(uint32_t));
+    view_ = v;
+    version_ = h.version;
+    return "";
+}
+
+int DeviceIndex::ensure_ws(size_t bytes, std::string& err) {
+    if (bytes <= ws_bytes_) return kOk;
+    if (ws_) {
+        cudaStreamSynchronize(stream_);
+        cudaDeviceSynchronize();
+        cudaFree(ws_);
+        ws_ = nullptr;
+        ws_bytes_ = 0;
+    }
+    size_t want = bytes + bytes / 4;
+    CUDA_TRY(cudaMalloc(&ws_, want));
+    ws_bytes_ = want;
+    return kOk;
+}
+
+uint32_t DeviceIndex::read_flags(cudaStream_t st) {
+    uint32_t f[4] = {0, 0, 0, 0};
+    cudaMemcpyAsync(f, d_flags_, sizeof(f), cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    return f[0] + f[1];
+}
+
+bool DeviceIndex::use_cell_major(const HostIndex& h, const SearchArgs& a) const {
+    // cm_ok (index.rs:3343-3348)
+    return a.cell_major && h.compacted && (h.max_assign == 1 || !h.rep_off.empty()) && !h.has_filter &&
+           (size_t)a.nq >= h.cm_min_batch;
+}
+
+int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc,
+                       float beta, bool batch_router, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch,
+                       uint32_t* chosen, float* cscore, uint32_t* nch, cudaStream_t st, std::string& err) {
+    const int M = view_.M;
+    const size_t mult2 = std::max<size_t>(h.shortlist_mult, 2);
+    bool have_codes = h.two_stage && !h.cent_bits.empty();
+    if (batch_router && have_codes) {
+        // route_batch (index.rs:1873-1980): exact flat Hamming shortlist for every query
+        int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_live_);
+        dev::launch_route_flat(view_, e, nq, want_c, sl, sl_n, M, st);
+    } else if (h.tree) {
+        // route_query tree branch (index.rs:1188-1211)
+        int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_leaf_);
+        std::vector<size_t> b = h.tree->beams((size_t)want_c);
+        int beams[dev::kMaxTreeLevels] = {0};
+        for (size_t i = 0; i < b.size(); ++i) beams[i] = (int)b[i];
+        dev::launch_route_tree(view_, e, nq, beams, want_c, tree_scratch, (int)tree_cap_, sl, sl_n, M, st);
+    } else if (h.graph_route && n_live_ >= h.graph_min_cells) {
+        err = "centroid-graph routing is not supported by the GPU search; call set_graph_route(False)";
+        return kUnsupported;
+    } else if (have_codes) {
+        // route_query two-stage branch (index.rs:1241-1259): note the multiplier is not floored at 2
+        int want_c = (int)std::min<size_t>((size_t)nprobe * h.shortlist_mult, n_live_);
+        dev::launch_route_flat(view_, e, nq, want_c, sl, sl_n, M, st);
+    } else {
+        dev::launch_route_all(view_, nq, sl, sl_n, M, st);
+    }
+    dev::launch_rescore_select(view_, e, dQ, nq, sl, sl_n, M, nprobe, tc, beta, use_sq8_, chosen, cscore, nch,
+                               d_flags_ + 1, st);
+    return kOk;
+}
+
+int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids,
+                               float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err) {
+    const int nq = a.nq, M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
+    const int nprobe = std::max(1, std::min(a.nprobe, M));
+    const int target = (int)std::max<size_t>((size_t)a.k * h.rerank_factor, 1);
+    const int mwords = (M + 63) / 64;
+    const int seed_cap = (int)std::max<size_t>(dev::kSeedCells * max_members_, 1);
+    const int rest_cap = std::max(32 * target, 16384) * grow_factor;
+    const int cand_cap = seed_cap + rest_cap;
+    const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
+
+    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint32_t*& tsc, uint32_t*& chosen,
+                     float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
+        e.qbits = bp.take<uint64_t>((size_t)nq * nw);
+        e.lut = bp.take<uint8_t>((size_t)nq * npos * 16);
+        e.fs_delta = bp.take<float>(nq);
+        e.fs_bias = bp.take<float>(nq);
+        e.cqs = bp.take<float>((size_t)nq * dim);
+        e.cqbase = bp.take<float>(nq);
+        e.rqs = bp.take<float>((size_t)nq * dim);
+        e.rbase = bp.take<float>(nq);
+        sl = bp.take<uint32_t>((size_t)nq * M);
+        sl_n = bp.take<uint32_t>(nq);
+        tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        chosen = bp.take<uint32_t>((size_t)nq * nprobe);
+        cscore = bp.take<float>((size_t)nq * nprobe);
+        nch = bp.take<uint32_t>(nq);
+        b.mwords = mwords;
+        b.probed = h.max_assign > 1 ? bp.take<uint64_t>((size_t)nq * mwords) : nullptr;
+        b.seed_cap = seed_cap;
+        b.seed_buf = bp.take<uint64_t>((size_t)nq * seed_cap);
+        b.seed_n = bp.take<uint32_t>(nq);
+        b.tau = bp.take<uint32_t>(nq);
+        b.rest_hi = bp.take<uint32_t>(nq);
+        b.cell_cnt = bp.take<uint32_t>((size_t)M + 1);
+        b.cell_fill = bp.take<uint32_t>(M);
+        b.qof = bp.take<uint32_t>((size_t)nq * nprobe);
+        b.rest_cap = rest_cap;
+        b.rest_buf = bp.take<uint64_t>((size_t)nq * rest_cap);
+        b.rest_n = bp.take<uint32_t>(nq);
+        b.cand_cap = cand_cap;
+        b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
+        b.cand_n = bp.take<uint32_t>(nq);
+        b.overflow = d_flags_;
+    };
+    dev::QueryEnc e{};
+    uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
+    float* cscore;
+    dev::CellMajorBufs b{};
+    Bump sizing{nullptr, 0, 0};
+    carve(sizing, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    int rc = ensure_ws(sizing.off + 256, err);
+    if (rc != kOk) return rc;
+    Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
+    carve(bp, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+
+    if (timing_) cudaEventRecord(ev_[0], st);
+    dev::launch_encode(view_, dQ, nq, e, use_sq8_, view_.rerank_mode == 1, st);
+    if (timing_) cudaEventRecord(ev_[1], st);
+    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+    if (rc != kOk) return rc;
+    if (timing_) cudaEventRecord(ev_[2], st);
+    dev::launch_cellmajor(view_, e, nq, chosen, cscore, nch, nprobe, target, h.adaptive, h.at_margin, b, st);
+    if (timing_) cudaEventRecord(ev_[3], st);
+    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, st);
+    if (timing_) cudaEventRecord(ev_[4], st);
+    CUDA_TRY(cudaGetLastError());
+    return kOk;
+}
+
+int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids,
+                              float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err) {
+    const int M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
+    const int nprobe = std::max(1, std::min(a.nprobe, M));
+    const int want0 = (int)((size_t)a.k * h.rerank_factor);
+    const int cand_cap = std::max(want0, 1);
+    const int ent_cap = (int)std::min<size_t>((size_t)nprobe * max_members_ + 1, (size_t)1 << 30);
+    const bool filtering = h.has_filter && !h.tags.empty();
+    const bool tree_router = h.tree != nullptr;
+    const int chunk = std::min(a.nq, kPerQueryChunk);
+
+    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint32_t*& tsc, uint32_t*& chosen,
+                     float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
+        int nq = chunk;
+        e.qbits = bp.take<uint64_t>((size_t)nq * nw);
+        e.lut = bp.take<uint8_t>((size_t)nq * npos * 16);
+        e.fs_delta = bp.take<float>(nq);
+        e.fs_bias = bp.take<float>(nq);
+        e.cqs = bp.take<float>((size_t)nq * dim);
+        e.cqbase = bp.take<float>(nq);
+        e.rqs = bp.take<float>((size_t)nq * dim);
+        e.rbase = bp.take<float>(nq);
+        sl = bp.take<uint32_t>((size_t)nq * M);
+        sl_n = bp.take<uint32_t>(nq);
+        tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        chosen = bp.take<uint32_t>((size_t)nq * nprobe);
+        cscore = bp.take<float>((size_t)nq * nprobe);
+        nch = bp.take<uint32_t>(nq);
+        b.crank = bp.take<uint32_t>((size_t)nq * M);
+        b.seg_off = bp.take<uint32_t>((size_t)nq * (nprobe + 1));
+        b.ent_cap = ent_cap;
+        b.ent = bp.take<uint64_t>((size_t)nq * ent_cap);
+        b.cand_cap = cand_cap;
+        b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
+        b.cand_n = bp.take<uint32_t>(nq);
+        b.overflow = d_flags_;
+    };
+    dev::QueryEnc e{};
+    uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
+    float* cscore;
+    dev::PerQueryBufs b{};
+    Bump sizing{nullptr, 0, 0};
+    carve(sizing, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    int rc = ensure_ws(sizing.off + 256, err);
+    if (rc != kOk) return rc;
+    Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
+    carve(bp, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+
+    if (timing_) cudaEventRecord(ev_[0], st);
+    for (int q0 = 0; q0 < a.nq; q0 += chunk) {
+        int nq = std::min(chunk, a.nq - q0);
+        const float* Qc = dQ + (size_t)q0 * dim;
+        dev::launch_encode(view_, Qc, nq, e, use_sq8_, view_.rerank_mode == 1, st);
+        if (timing_ && q0 == 0) cudaEventRecord(ev_[1], st);
+        rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+        if (rc != kOk) return rc;
+        if (timing_ && q0 == 0) cudaEventRecord(ev_[2], st);
+        dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
+                             h.filter_lo, h.filter_hi, b, st);
+        if (timing_ && q0 == 0) cudaEventRecord(ev_[3], st);
+        dev::launch_rerank(view_, Qc, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids + (size_t)q0 * a.k,
+                           d_scores + (size_t)q0 * a.k, d_nout + q0, st);
+    }
+    if (timing_) cudaEventRecord(ev_[4], st);
+    CUDA_TRY(cudaGetLastError());
+    return kOk;
+}
+
+int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids,
+                               float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err) {
+    if (h.version != version_) {
+        err = "the index changed since it was uploaded";
+        return kBadState;
+    }
+    if (a.k <= 0) {
+        err = "k must be positive";
+        return kBadArg;
+    }
+    if (a.k > 4096) {
+        err = "k above 4096 is not supported";
+        return kUnsupported;
+    }
+    if (a.nq <= 0) return kOk;
+    cudaSetDevice(device_);
+    if (!st) st = stream_;
+    cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
+    if (use_cell_major(h, a)) return run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+    return run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+}
+
+int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
+                             uint32_t* nout, std::string& err) {
+    if (a.nq <= 0) return kOk;
+    cudaSetDevice(device_);
+    const size_t nq = a.nq, k = a.k, dim = view_.dim;
+    const size_t qb = nq * dim * sizeof(float), ib = nq * k * sizeof(uint64_t), sb = nq * k * sizeof(float),
+                 nb = nq * sizeof(uint32_t);
+    size_t need = qb + ib + sb + nb + 4 * 256;
+    if (need > pin_bytes_) {
+        if (pin_) cudaFreeHost(pin_);
+        pin_ = nullptr;
+        pin_bytes_ = 0;
+        CUDA_TRY(cudaMallocHost(&pin_, need));
+        pin_bytes_ = need;
+    }
+    // device I/O buffers come from the stream-ordered pool
+    char* dio = nullptr;
+    CUDA_TRY(cudaMallocAsync((void**)&dio, need, stream_));
+    char* hp = static_cast<char*>(pin_);
+    std::memcpy(hp, Q, qb);
+    float* dQ = reinterpret_cast<float*>(dio);
+    uint64_t* dI = reinterpret_cast<uint64_t*>(dio + ((qb + 255) & ~size_t(255)));
+    float* dS = reinterpret_cast<float*>(reinterpret_cast<char*>(dI) + ((ib + 255) & ~size_t(255)));
+    uint32_t* dN = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(dS) + ((sb + 255) & ~size_t(255)));
+    int rc = kOk;
+    for (int attempt = 0; attempt < 4; ++attempt) {
+        CUDA_TRY(cudaMemcpyAsync(dQ, hp, qb, cudaMemcpyHostToDevice, stream_));
+        rc = search_device(h, dQ, a, dI, dS, dN, stream_, err);
+        if (rc != kOk) break;
+        uint32_t f[4] = {0, 0, 0, 0};
+        cudaMemcpyAsync(f, d_flags_, sizeof(f), cudaMemcpyDeviceToHost, stream_);
+        CUDA_TRY(cudaStreamSynchronize(stream_));
+        if (f[1] != 0) {
+            err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
+            rc = kUnsupported;
+            break;
+        }
+        if (f[0] == 0) break;
+        if (attempt == 3) {
+            err = "candidate buffers overflowed after enlarging them";
+            rc = kOverflow;
+            break;
+        }
+        grow_factor *= 4;
+    }
+    if (rc == kOk) {
+        CUDA_TRY(cudaMemcpyAsync(hp + qb, dI, ib, cudaMemcpyDeviceToHost, stream_));
+        CUDA_TRY(cudaMemcpyAsync(hp + qb + ib, dS, sb, cudaMemcpyDeviceToHost, stream_));
+        CUDA_TRY(cudaMemcpyAsync(hp + qb + ib + sb, dN, nb, cudaMemcpyDeviceToHost, stream_));
+    }
+    cudaFreeAsync(dio, stream_);
+    CUDA_TRY(cudaStreamSynchronize(stream_));
+    if (rc != kOk) return rc;
+    std::memcpy(ids, hp + qb, ib);
+    std::memcpy(scores, hp + qb + ib, sb);
+    if (nout) std::memcpy(nout, hp + qb + ib + sb, nb);
+    return kOk;
+}
+
+PhaseTimes DeviceIndex::collect_phases() {
+    PhaseTimes p;
+    if (!timing_ || !ev_[4]) return p;
+    if (cudaEventSynchronize(ev_[4]) != cudaSuccess) return p;
+    cudaEventElapsedTime(&p.encode, ev_[0], ev_[1]);
+    cudaEventElapsedTime(&p.route, ev_[1], ev_[2]);
+    cudaEventElapsedTime(&p.scan, ev_[2], ev_[3]);
+    cudaEventElapsedTime(&p.rerank, ev_[3], ev_[4]);
+    return p;
+}
+
+}  // namespace maivs

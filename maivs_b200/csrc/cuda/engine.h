@@ -1,0 +1,106 @@
+// Device image of a host index plus the search pipelines that run on it.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../host/index_host.h"
+#include "kernels.cuh"
+
+namespace maivs {
+
+// Status codes of the C ABI (mirrored in include/maivs_b200.h).
+enum Status : int {
+    kOk = 0,
+    kBadShape = 1,
+    kBadArg = 2,
+    kBadState = 3,
+    kOom = 4,
+    kCudaError = 5,
+    kOverflow = 6,
+    kUnsupported = 7,
+    kNotFound = 8,
+    kNoDevice = 9,
+};
+
+struct SearchArgs {
+    int nq = 0;
+    int k = 0;
+    int nprobe = 16;
+    float tc = 0.95f;
+    float beta = 8.0f;
+    bool cell_major = true;
+};
+
+// Per-phase device times of the last search, in milliseconds (the reference's profile phases
+// q.route / q.scan / q.rerank, src/prof.rs:35-42).
+struct PhaseTimes {
+    float encode = 0, route = 0, scan = 0, rerank = 0;
+};
+
+class DeviceIndex {
+   public:
+    ~DeviceIndex();
+    // Builds the device image from a compacted FastScan host index; returns an error message.
+    std::string upload(const HostIndex& h, int device);
+    uint64_t version() const { return version_; }
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    // Search with device-resident queries and outputs, enqueued on `st`. Chooses the cell-major
+    // join or the per-query path like the reference's search_batch (index.rs:3343-3348).
+    // Returns a Status; `err` receives a message on failure.
+    int search_device(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
+                      uint32_t* d_nout, cudaStream_t st, std::string& err);
+    // Host buffers: copies in, searches, copies out, synchronises, and retries with larger
+    // candidate buffers if any query overflowed them.
+    int search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
+                    uint32_t* nout, std::string& err);
+
+    // Overflow/error counters of the last device search (read after synchronising its stream).
+    uint32_t read_flags(cudaStream_t st);
+    bool use_cell_major(const HostIndex& h, const SearchArgs& a) const;
+    void set_timing(bool on) { timing_ = on; }
+    // Synchronises on the last timed search and returns its phase times.
+    PhaseTimes collect_phases();
+    size_t device_bytes() const { return bytes_; }
+
+    int grow_factor = 1;  // multiplies the candidate-buffer capacities after an overflow
+
+   private:
+    void* alloc(size_t bytes);
+    template <typename T>
+    T* upload_vec(const std::vector<T>& v);
+    int ensure_ws(size_t bytes, std::string& err);
+    int run_cellmajor(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
+                      uint32_t* d_nout, cudaStream_t st, std::string& err);
+    int run_perquery(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
+                     uint32_t* d_nout, cudaStream_t st, std::string& err);
+    int route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc, float beta,
+              bool batch_router, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch, uint32_t* chosen,
+              float* cscore, uint32_t* nch, cudaStream_t st, std::string& err);
+
+    int device_ = -1;
+    cudaStream_t stream_ = nullptr;
+    uint64_t version_ = 0;
+    std::vector<void*> allocs_;
+    size_t bytes_ = 0;
+    dev::IndexView view_{};
+    size_t n_live_ = 0, n_leaf_ = 0, max_members_ = 0, tree_cap_ = 0;
+    bool use_sq8_ = false;
+    uint32_t* d_flags_ = nullptr;  // [0] overflow, [1] routing errors
+    void* ws_ = nullptr;
+    size_t ws_bytes_ = 0;
+    // pinned staging for the host-buffer API
+    void* pin_ = nullptr;
+    size_t pin_bytes_ = 0;
+    bool timing_ = false;
+    PhaseTimes phases_;
+    cudaEvent_t ev_[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+};
+
+}  // namespace maivs

@@ -1,0 +1,1114 @@
+// MAIVS query kernels for sm_100a: query encoding, routing, seed + adaptive prune, cell-major
+// inversion and scan, per-query scan with the sequential stop rule, exact cut and rerank.
+//
+// Integer work (codes, table sums, distances, cut-offs) is exact by construction. Floating-point
+// work follows the reference's evaluation order (see common.cuh), so scores are bit-identical to
+// the reference's CPU path on the same inputs.
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace maivs {
+namespace dev {
+
+namespace {
+
+constexpr int kBS = 256;
+
+// ---- block utilities ----------------------------------------------------------------------------
+
+// Sum of each lane's 8 FastScan table sums of group g over npos positions. Word (j, g) of the
+// cell holds nibble j of members 8g..8g+7; `lut` is npos x 16 bytes (layout of
+// src/quantize.rs:303-311: entry e of position j at byte 16j + e). acc[b>>1] holds member b's
+// 16-bit sum in half (b & 1). Sums never exceed 255 * npos <= 65280.
+__device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, int ng, int g, bool active,
+                                           const uint8_t* lut, int npos, uint32_t acc[4]) {
+    acc[0] = acc[1] = acc[2] = acc[3] = 0;
+    const uint4* T = reinterpret_cast<const uint4*>(lut);
+#pragma unroll 4
+    for (int j = 0; j < npos; ++j) {
+        uint4 t = T[j];
+        uint32_t w = active ? __ldg(codes + (size_t)j * ng + g) : 0u;
+        uint32_t r0 = lut16x4(t, w);
+        uint32_t r1 = lut16x4(t, w >> 16);
+        acc[0] += __byte_perm(r0, 0, 0x4140);
+        acc[1] += __byte_perm(r0, 0, 0x4342);
+        acc[2] += __byte_perm(r1, 0, 0x4140);
+        acc[3] += __byte_perm(r1, 0, 0x4342);
+    }
+}
+
+__device__ __forceinline__ uint32_t member_sum(const uint32_t acc[4], int b) {
+    return (acc[b >> 1] >> (16 * (b & 1))) & 0xFFFFu;
+}
+
+// Exactly-once rule of the cell-major join: a multi-home vector is scored only at its lowest-id
+// probed home (index.rs:2036-2045).
+__device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot, uint32_t c, const uint64_t* probed) {
+    const uint32_t* h = ix.slot_cells + (size_t)slot * ix.ma;
+    for (int j = 0; j < ix.ma; ++j) {
+        uint32_t hc = h[j];
+        if (hc != kNoCell && hc < c && ((probed[hc >> 6] >> (hc & 63)) & 1ull)) return false;
+    }
+    return true;
+}
+
+// The kth smallest (1-based) of up to two key segments, by radix selection on bytes [lo_byte,
+// hi_byte] of the 64-bit keys (higher bytes must be zero). Returns the selected key with the
+// unselected low bytes zero. All threads of the block must call it; `hist` is 256 shared words.
+__device__ uint64_t block_select_kth(const uint64_t* a, int na, const uint64_t* b, int nb, int kth, int hi_byte,
+                                     int lo_byte, uint32_t* hist) {
+    __shared__ uint64_t s_prefix;
+    __shared__ int s_rem;
+    if (threadIdx.x == 0) {
+        s_prefix = 0;
+        s_rem = kth;
+    }
+    __syncthreads();
+    uint64_t mask = 0;
+    for (int by = hi_byte; by >= lo_byte; --by) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        uint64_t prefix = s_prefix;
+        int shift = by * 8;
+        for (int i = threadIdx.x; i < na + nb; i += blockDim.x) {
+            uint64_t k = i < na ? a[i] : b[i - na];
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int rem = s_rem, digit = 255;
+            for (int d = 0; d < 256; ++d) {
+                if ((int)hist[d] >= rem) {
+                    digit = d;
+                    break;
+                }
+                rem -= (int)hist[d];
+            }
+            s_rem = rem;
+            s_prefix = prefix | ((uint64_t)digit << shift);
+        }
+        mask |= 0xFFull << shift;
+        __syncthreads();
+    }
+    uint64_t r = s_prefix;
+    __syncthreads();
+    return r;
+}
+
+// Bitonic sort, ascending, of P (power of two) 64-bit keys in shared memory.
+__device__ void block_bitonic_u64(uint64_t* keys, int P) {
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                int ixj = i ^ j;
+                if (ixj > i) {
+                    uint64_t a = keys[i], b = keys[ixj];
+                    bool up = (i & k) == 0;
+                    if ((a > b) == up) {
+                        keys[i] = b;
+                        keys[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__host__ __device__ inline int next_pow2(int n) {
+    int p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+// ---- K1: query encoding ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kBS) k_encode(IndexView ix, const float* __restrict__ Q, QueryEnc e, int want_cqs,
+                                                int want_rqs) {
+    extern __shared__ float sm[];
+    float* rot = sm;
+    float* mins = rot + ix.dim_pad;
+    const int q = blockIdx.x, dp = ix.dim_pad, dim = ix.dim, npos = ix.npos;
+    const float* x = Q + (size_t)q * dim;
+    for (int i = threadIdx.x; i < dp; i += kBS) rot[i] = i < dim ? x[i] : 0.0f;
+    __syncthreads();
+    // rotate(): ROUNDS x (sign flip, normalised FWHT) (quantize.rs:152-163, :71-126)
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dp));
+    for (int r = 0; r < 2; ++r) {
+        const float* s = ix.signs + (size_t)r * dp;
+        for (int i = threadIdx.x; i < dp; i += kBS) rot[i] = __fmul_rn(rot[i], s[i]);
+        __syncthreads();
+        for (int h = 1; h < dp; h <<= 1) {
+            for (int bt = threadIdx.x; bt < dp / 2; bt += kBS) {
+                int i = (bt / h) * (2 * h) + (bt % h);
+                float u = rot[i], v = rot[i + h];
+                rot[i] = __fadd_rn(u, v);
+                rot[i + h] = __fsub_rn(u, v);
+            }
+            __syncthreads();
+        }
+        for (int i = threadIdx.x; i < dp; i += kBS) rot[i] = __fmul_rn(rot[i], scale);
+        __syncthreads();
+    }
+    // pack_signs_trunc (quantize.rs:57-67)
+    for (int w = threadIdx.x; w < ix.nw; w += kBS) {
+        uint64_t bits = 0;
+        for (int t = 0; t < 64; ++t) {
+            int i = w * 64 + t;
+            if (i < dp && rot[i] < 0.0f) bits |= 1ull << t;
+        }
+        e.qbits[(size_t)q * ix.nw + w] = bits;
+    }
+    // FsQuery::new (quantize.rs:279-313); npos <= kBS, one position per thread
+    float raw[16];
+    float lo = INFINITY, hi = -INFINITY;
+    const int j = threadIdx.x;
+    if (j < npos) {
+#pragma unroll
+        for (int ev = 0; ev < 16; ++ev) {
+            float v = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                float xv = rot[4 * j + t];
+                v = ((ev >> t) & 1) ? __fsub_rn(v, xv) : __fadd_rn(v, xv);
+            }
+            raw[ev] = v;
+            lo = fminf(lo, v);
+            hi = fmaxf(hi, v);
+        }
+        mins[j] = lo;
+    }
+    float rj = j < npos ? __fsub_rn(hi, lo) : 0.0f;
+    using BR = cub::BlockReduce<float, kBS>;
+    __shared__ typename BR::TempStorage red;
+    float range = BR(red).Reduce(rj, [](float a, float b) { return fmaxf(a, b); });
+    __shared__ float s_range;
+    if (threadIdx.x == 0) s_range = fmaxf(0.0f, range);
+    __syncthreads();
+    const float delta = fmaxf(__fdiv_rn(s_range, 255.0f), 1e-12f);
+    if (j < npos) {
+        uint32_t wv[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int ev = 0; ev < 16; ++ev) {
+            float qv = roundf(__fdiv_rn(__fsub_rn(raw[ev], lo), delta));
+            qv = clampf(qv, 0.0f, 255.0f);
+            wv[ev >> 2] |= ((uint32_t)qv) << (8 * (ev & 3));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(e.lut + ((size_t)q * npos + j) * 16);
+        *dst = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    // Sequential sums, each in its own warp: bias (quantize.rs:312), the centroid SQ8 pre-scale
+    // base (index.rs:1184-1186) and the rerank SQ8 base (index.rs:1324-1327).
+    if (threadIdx.x == 0) {
+        float b = 0.0f;
+        for (int t = 0; t < npos; ++t) b = __fadd_rn(b, mins[t]);
+        e.fs_delta[q] = delta;
+        e.fs_bias[q] = b;
+    }
+    if (want_cqs && threadIdx.x == 32) {
+        float b = 0.0f;
+        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(x[t], ix.csq_min[t]));
+        e.cqbase[q] = b;
+    }
+    if (want_rqs && threadIdx.x == 64) {
+        float b = 0.0f;
+        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(x[t], ix.sq_min[t]));
+        e.rbase[q] = b;
+    }
+    if (want_cqs)
+        for (int t = threadIdx.x; t < dim; t += kBS) e.cqs[(size_t)q * dim + t] = __fmul_rn(x[t], ix.csq_step[t]);
+    if (want_rqs)
+        for (int t = threadIdx.x; t < dim; t += kBS) e.rqs[(size_t)q * dim + t] = __fmul_rn(x[t], ix.sq_step[t]);
+}
+
+// ---- K2: flat Hamming shortlist ------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t ham_row(const uint64_t* qb, const uint64_t* __restrict__ code, int nw) {
+    uint32_t h = 0;
+    for (int w = 0; w < nw; ++w) h += __popcll(qb[w] ^ __ldg(code + w));
+    return h;
+}
+
+// Smallest t with prefix(t) >= want over hist[0..bits] (the counting cut-off of index.rs:86-104);
+// bits when never reached. Warp 0 computes it.
+__device__ int warp_hist_cut(const uint32_t* hist, int bits, long long want) {
+    int lane = threadIdx.x & 31;
+    int nb = bits + 1;
+    int per = (nb + 31) / 32;
+    int b0 = lane * per, b1 = min(b0 + per, nb);
+    long long s = 0;
+    for (int i = b0; i < b1; ++i) s += hist[i];
+    long long inc = s;
+    for (int o = 1; o < 32; o <<= 1) {
+        long long v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    long long excl = inc - s;
+    int found = (excl < want && inc >= want) ? 1 : 0;
+    unsigned bal = __ballot_sync(0xFFFFFFFFu, found);
+    int res = bits;
+    if (bal) {
+        int src = __ffs(bal) - 1;
+        int t = bits;
+        if (lane == src) {
+            long long c = excl;
+            for (int i = b0; i < b1; ++i) {
+                c += hist[i];
+                if (c >= want) {
+                    t = i;
+                    break;
+                }
+            }
+        }
+        res = __shfl_sync(0xFFFFFFFFu, t, src);
+    }
+    return res;
+}
+
+__global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int want_c, int all, uint32_t* sl,
+                                                    uint32_t* sl_n, int sl_cap) {
+    extern __shared__ uint32_t hist[];
+    __shared__ uint64_t qb[16];
+    __shared__ int s_cut;
+    __shared__ uint32_t s_count;
+    const int q = blockIdx.x, nw = ix.nw, bits = nw * 64, M = ix.M;
+    // `all` lists every live cell and needs no query code (e carries no buffers then)
+    if (!all && threadIdx.x < nw) qb[threadIdx.x] = e.qbits[(size_t)q * nw + threadIdx.x];
+    for (int i = threadIdx.x; i <= bits; i += kBS) hist[i] = 0;
+    if (threadIdx.x == 0) s_count = 0;
+    __syncthreads();
+    int cut = bits;
+    if (!all) {
+        for (int c = threadIdx.x; c < M; c += kBS)
+            if (ix.live[c]) atomicAdd(&hist[ham_row(qb, ix.cent_bits + (size_t)c * nw, nw)], 1u);
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            int t = want_c == 0 ? 0 : warp_hist_cut(hist, bits, want_c);
+            if (threadIdx.x == 0) s_cut = t;
+        }
+        __syncthreads();
+        cut = s_cut;
+    }
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    for (int base = 0; base < M; base += kBS) {
+        int c = base + threadIdx.x;
+        uint32_t f = 0;
+        if (c < M && ix.live[c]) f = all ? 1u : (ham_row(qb, ix.cent_bits + (size_t)c * nw, nw) <= (uint32_t)cut ? 1u : 0u);
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        uint32_t off = s_count;
+        if (f && off + pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + off + pos] = (uint32_t)c;
+        __syncthreads();
+        if (threadIdx.x == 0) s_count = off + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) sl_n[q] = s_count;
+}
+
+// ---- tree descent ---------------------------------------------------------------------------------
+
+// keep_smallest (tree.rs:120-159) on n (h, id) pairs: the `keep` smallest h, ties at the cut-off
+// in encounter order; stable compaction from (h_in, id_in) to id_out. Returns the kept count.
+__device__ int block_keep_smallest(const uint32_t* h_in, const uint32_t* id_in, int n, int keep, int bits,
+                                   uint32_t* id_out, uint32_t* hist) {
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    __shared__ int s_t;
+    __shared__ long long s_need;
+    __shared__ uint32_t s_off, s_eq;
+    if (keep >= n) {
+        for (int i = threadIdx.x; i < n; i += kBS) id_out[i] = id_in[i];
+        __syncthreads();
+        return n;
+    }
+    for (int i = threadIdx.x; i <= bits; i += kBS) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kBS) atomicAdd(&hist[h_in[i]], 1u);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int t = warp_hist_cut(hist, bits, keep);
+        if (threadIdx.x == 0) {
+            long long below = 0;
+            for (int i = 0; i < t; ++i) below += hist[i];
+            s_t = t;
+            s_need = keep - below;
+            s_off = 0;
+            s_eq = 0;
+        }
+    }
+    __syncthreads();
+    const uint32_t t = (uint32_t)s_t;
+    const long long need = s_need;
+    for (int base = 0; base < n; base += kBS) {
+        int i = base + threadIdx.x;
+        uint32_t h = i < n ? h_in[i] : 0xFFFFFFFFu;
+        uint32_t eq = (i < n && h == t) ? 1u : 0u;
+        uint32_t eq_rank, eq_agg;
+        BS(scan).ExclusiveSum(eq, eq_rank, eq_agg);
+        __syncthreads();
+        uint32_t eq0 = s_eq;
+        uint32_t kf = (i < n && (h < t || (eq && (long long)(eq0 + eq_rank) < need))) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(kf, pos, agg);
+        uint32_t off = s_off;
+        if (kf) id_out[off + pos] = id_in[i];
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            s_off = off + agg;
+            s_eq = eq0 + eq_agg;
+        }
+        __syncthreads();
+    }
+    return (int)s_off;
+}
+
+struct Beams {
+    int b[kMaxTreeLevels];
+};
+
+__global__ void __launch_bounds__(kBS) k_route_tree(IndexView ix, QueryEnc e, Beams bm, int want, uint32_t* scratch,
+                                                    int cap, uint32_t* sl, uint32_t* sl_n, int sl_cap) {
+    extern __shared__ uint32_t hist[];
+    __shared__ uint64_t qb[16];
+    __shared__ uint32_t s_n;
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    const int q = blockIdx.x, nw = ix.nw, bits = nw * 64;
+    uint32_t* fa = scratch + (size_t)q * 3 * cap;  // frontier
+    uint32_t* fb = fa + cap;                      // survivors
+    uint32_t* hh = fb + cap;                      // Hamming of the frontier
+    if (threadIdx.x < nw) qb[threadIdx.x] = e.qbits[(size_t)q * nw + threadIdx.x];
+    int nf = ix.tree_n[0];
+    for (int i = threadIdx.x; i < nf; i += kBS) fa[i] = (uint32_t)i;
+    __syncthreads();
+    for (int li = 0; li < ix.tree_depth; ++li) {
+        const uint64_t* codes = ix.tree_codes[li];
+        for (int i = threadIdx.x; i < nf; i += kBS) hh[i] = ham_row(qb, codes + (size_t)fa[i] * nw, nw);
+        __syncthreads();
+        int keep = min(bm.b[li], nf);
+        if (keep == 0) {
+            nf = 0;
+            break;
+        }
+        int ns = block_keep_smallest(hh, fa, nf, keep, bits, fb, hist);
+        // expand kept nodes' children, in kept order (child_idx is the identity after compact_layout)
+        const uint32_t* cst = ix.tree_child_start[li];
+        const uint32_t* cln = ix.tree_child_len[li];
+        if (threadIdx.x == 0) s_n = 0;
+        __syncthreads();
+        for (int base = 0; base < ns; base += kBS) {
+            int i = base + threadIdx.x;
+            uint32_t len = i < ns ? cln[fb[i]] : 0u;
+            uint32_t pos, agg;
+            BS(scan).ExclusiveSum(len, pos, agg);
+            uint32_t off = s_n;
+            if (i < ns) {
+                uint32_t st = cst[fb[i]];
+                for (uint32_t r = 0; r < len; ++r) fa[off + pos + r] = st + r;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) s_n = off + agg;
+            __syncthreads();
+        }
+        nf = (int)s_n;
+        __syncthreads();
+    }
+    // final scan over candidate leaves
+    for (int i = threadIdx.x; i < nf; i += kBS) hh[i] = ham_row(qb, ix.leaf_codes + (size_t)fa[i] * nw, nw);
+    __syncthreads();
+    int keep = min(want, nf);
+    int ns = keep > 0 ? block_keep_smallest(hh, fa, nf, keep, bits, fb, hist) : 0;
+    // leaf ids, live cells only (index.rs:1199-1209)
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    for (int base = 0; base < ns; base += kBS) {
+        int i = base + threadIdx.x;
+        uint32_t c = i < ns ? ix.leaf_ids[fb[i]] : 0u;
+        uint32_t f = (i < ns && ix.live[c]) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        uint32_t off = s_n;
+        if (f && off + pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + off + pos] = c;
+        __syncthreads();
+        if (threadIdx.x == 0) s_n = off + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) sl_n[q] = s_n;
+}
+
+// ---- K3: exact re-order of the shortlist + nucleus -----------------------------------------------
+
+__global__ void __launch_bounds__(kBS) k_rescore_select(IndexView ix, QueryEnc e, const float* __restrict__ Q,
+                                                        const uint32_t* __restrict__ sl, const uint32_t* __restrict__ sl_n,
+                                                        int sl_cap, int nprobe, float tc, float beta, int use_sq8,
+                                                        uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err) {
+    extern __shared__ uint64_t keys[];
+    const int q = blockIdx.x, dim = ix.dim;
+    const int n = (int)sl_n[q];
+    if (n > kSortCap || n > sl_cap) {
+        if (threadIdx.x == 0) {
+            nch[q] = 0;
+            atomicAdd(err, 1u);
+        }
+        return;
+    }
+    const int P = next_pow2(max(n, 1));
+    float* qv = reinterpret_cast<float*>(keys + P);
+    const float* src = use_sq8 ? e.cqs + (size_t)q * dim : Q + (size_t)q * dim;
+    for (int t = threadIdx.x; t < dim; t += kBS) qv[t] = src[t];
+    for (int i = n + threadIdx.x; i < P; i += kBS) keys[i] = ~0ull;
+    __syncthreads();
+    const float base = use_sq8 ? e.cqbase[q] : 0.0f;
+    const int l8 = threadIdx.x & 7;
+    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+    for (int i = threadIdx.x >> 3; i < n; i += kBS / 8) {
+        uint32_t c = sl[(size_t)q * sl_cap + i];
+        float s;
+        if (use_sq8)
+            s = __fadd_rn(dot_f32_u8_g8(qv, ix.cent_sq8 + (size_t)c * dim, dim, l8, gmask), base);
+        else
+            s = dot_f32_g8(qv, ix.cent_f32 + (size_t)c * dim, dim, l8, gmask);
+        if (l8 == 0) keys[i] = ((uint64_t)(~float_key(s)) << 32) | c;
+    }
+    __syncthreads();
+    block_bitonic_u64(keys, P);
+    const int cap = min(nprobe, n);
+    for (int i = threadIdx.x; i < cap; i += kBS) {
+        uint64_t k = keys[i];
+        chosen[(size_t)q * nprobe + i] = (uint32_t)k;
+        cscore[(size_t)q * nprobe + i] = key_float(~(uint32_t)(k >> 32));
+    }
+    if (threadIdx.x == 0) {
+        int m = cap;
+        if (cap > 0 && tc < 1.0f) {
+            // nucleus over the capped, sorted candidates (index.rs:1289-1300)
+            float max_s = key_float(~(uint32_t)(keys[0] >> 32));
+            float z = 0.0f;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(keys[i] >> 32));
+                z = __fadd_rn(z, (float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)));
+            }
+            float cum = 0.0f;
+            m = 0;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(keys[i] >> 32));
+                ++m;
+                float p = __fdiv_rn((float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)), __fadd_rn(z, 1e-9f));
+                cum = __fadd_rn(cum, p);
+                if (cum >= tc) break;
+            }
+        }
+        nch[q] = (uint32_t)m;
+    }
+}
+
+// ---- cell-major: seed + adaptive prune (index.rs:2126-2191) --------------------------------------
+
+__global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                              const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
+                                              int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b) {
+    extern __shared__ uint8_t lut_s[];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_n;
+    __shared__ int s_last;
+    const int q = blockIdx.x, npos = ix.npos;
+    const int n_ch = (int)nch[q];
+    const int ns = min(kSeedCells, n_ch);
+    const uint32_t* ch = chosen + (size_t)q * nprobe;
+    uint64_t* probed = b.probed + (size_t)q * b.mwords;
+    if (ix.ma > 1) {
+        for (int w = threadIdx.x; w < b.mwords; w += kBS) probed[w] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n_ch; i += kBS) atomicOr((unsigned long long*)&probed[ch[i] >> 6], 1ull << (ch[i] & 63));
+    }
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(e.lut + (size_t)q * npos * 16);
+        uint4* dst = reinterpret_cast<uint4*>(lut_s);
+        for (int i = threadIdx.x; i < npos; i += kBS) dst[i] = src[i];
+    }
+    if (threadIdx.x == 0) {
+        s_n = 0;
+        s_last = -1;
+    }
+    __syncthreads();
+    uint64_t* sbuf = b.seed_buf + (size_t)q * b.seed_cap;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
+    const uint32_t maxk = ix.maxk;
+    for (int r = 0; r < ns; ++r) {
+        const uint32_t c = ch[r];
+        const uint32_t moff = ix.cell_moff[c];
+        const int nc = (int)(ix.cell_moff[c + 1] - moff);
+        const int ng = (nc + 7) >> 3;
+        const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
+        for (int chk = warp; chk * 32 < ng; chk += nwarps) {
+            int g = chk * 32 + lane;
+            bool act = g < ng;
+            uint32_t acc[4];
+            group_sums(codes, ng, g, act, lut_s, npos, acc);
+            if (act) {
+                for (int bb = 0; bb < 8; ++bb) {
+                    int pos = 8 * g + bb;
+                    if (pos >= nc) break;
+                    uint32_t d = maxk - member_sum(acc, bb);
+                    uint32_t slot = ix.cell_slots[moff + pos];
+                    if (ix.ma > 1 && !canonical_cm(ix, slot, c, probed)) continue;
+                    uint32_t p = atomicAdd(&s_n, 1u);
+                    if (p < (uint32_t)b.seed_cap) sbuf[p] = ((uint64_t)d << 32) | slot;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    int n = (int)s_n;
+    if (n > b.seed_cap) {
+        if (threadIdx.x == 0) atomicAdd(b.overflow, 1u);
+        n = b.seed_cap;
+    }
+    uint32_t tau = maxk;
+    if (n >= target) {
+        uint64_t kk = block_select_kth(sbuf, n, nullptr, 0, target, 5, 4, hist);
+        tau = (uint32_t)(kk >> 32);
+        // retain d <= tau (ties kept)
+        using BS = cub::BlockScan<uint32_t, kBS>;
+        __shared__ typename BS::TempStorage scan;
+        __shared__ uint32_t s_off;
+        if (threadIdx.x == 0) s_off = 0;
+        __syncthreads();
+        for (int base = 0; base < n; base += kBS) {
+            int i = base + threadIdx.x;
+            uint64_t key = i < n ? sbuf[i] : 0;
+            uint32_t f = (i < n && (uint32_t)(key >> 32) <= tau) ? 1u : 0u;
+            uint32_t pos, agg;
+            BS(scan).ExclusiveSum(f, pos, agg);
+            __syncthreads();
+            uint32_t off = s_off;
+            if (f) sbuf[off + pos] = key;
+            __syncthreads();
+            if (threadIdx.x == 0) s_off = off + agg;
+            __syncthreads();
+        }
+        n = (int)s_off;
+    }
+    int rest_end = n_ch;
+    if (adaptive && n >= target && ns < n_ch) {
+        const float norm = fs_norm(ix.dim_pad);
+        float thr = clampf(__fdiv_rn(fs_estimate(e.fs_delta[q], e.fs_bias[q], maxk - tau), norm), -1.0f, 1.0f);
+        float X = __fsub_rn(thr, at_margin);
+        for (int i = ns + threadIdx.x; i < n_ch; i += kBS) {
+            float bnd = cell_bound(cscore[(size_t)q * nprobe + i], ix.r_bound[ch[i]]);
+            if (bnd >= X) atomicMax(&s_last, i);
+        }
+        __syncthreads();
+        rest_end = s_last >= 0 ? s_last + 1 : ns;
+    }
+    if (threadIdx.x == 0) {
+        b.tau[q] = tau;
+        b.seed_n[q] = (uint32_t)n;
+        b.rest_hi[q] = (uint32_t)rest_end;
+        b.rest_n[q] = 0;
+    }
+}
+
+// ---- cell-major: inversion (index.rs:2193-2213) ---------------------------------------------------
+
+__global__ void k_inv_count(const uint32_t* __restrict__ chosen, const uint32_t* __restrict__ nch,
+                            const uint32_t* __restrict__ rest_hi, int nq, int nprobe, uint32_t* cnt) {
+    int q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (q >= nq) return;
+    int lo = min(kSeedCells, (int)nch[q]), hi = (int)rest_hi[q];
+    for (int i = lo + (threadIdx.x & 31); i < hi; i += 32) atomicAdd(&cnt[chosen[(size_t)q * nprobe + i]], 1u);
+}
+
+// Exclusive scan of cnt[0..M) in place, cnt[M] = total.
+__global__ void __launch_bounds__(1024) k_inv_scan(uint32_t* cnt, int M) {
+    using BS = cub::BlockScan<uint32_t, 1024>;
+    __shared__ typename BS::TempStorage scan;
+    __shared__ uint32_t s_run;
+    if (threadIdx.x == 0) s_run = 0;
+    __syncthreads();
+    for (int base = 0; base < M; base += 1024) {
+        int i = base + threadIdx.x;
+        uint32_t v = i < M ? cnt[i] : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(v, pos, agg);
+        uint32_t run = s_run;
+        if (i < M) cnt[i] = run + pos;
+        __syncthreads();
+        if (threadIdx.x == 0) s_run = run + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) cnt[M] = s_run;
+}
+
+__global__ void k_inv_scatter(const uint32_t* __restrict__ chosen, const uint32_t* __restrict__ nch,
+                              const uint32_t* __restrict__ rest_hi, int nq, int nprobe, const uint32_t* start,
+                              uint32_t* fill, uint32_t* qof) {
+    int q = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (q >= nq) return;
+    int lo = min(kSeedCells, (int)nch[q]), hi = (int)rest_hi[q];
+    for (int i = lo + (threadIdx.x & 31); i < hi; i += 32) {
+        uint32_t c = chosen[(size_t)q * nprobe + i];
+        uint32_t p = start[c] + atomicAdd(&fill[c], 1u);
+        qof[p] = (uint32_t)q;
+    }
+}
+
+// ---- cell-major: the scan (index.rs:2231-2275) ------------------------------------------------------
+// One CTA per cell; each warp scores one interested query against 32 member groups (256 members)
+// at a time. A member survives when its distance is within the query's seed cut-off tau, which is
+// a valid bound on the final cut (index.rs:2266-2269), and it is canonical.
+
+__global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const uint32_t* __restrict__ start,
+                                                 const uint32_t* __restrict__ qof, CellMajorBufs b) {
+    const uint32_t c = blockIdx.x;
+    const uint32_t s0 = start[c], s1 = start[c + 1];
+    if (s0 == s1) return;
+    const uint32_t moff = ix.cell_moff[c];
+    const int nc = (int)(ix.cell_moff[c + 1] - moff);
+    if (nc == 0) return;
+    const int ng = (nc + 7) >> 3;
+    const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
+    const int npos = ix.npos;
+    const uint32_t maxk = ix.maxk;
+    for (int chk = 0; chk * 32 < ng; ++chk) {
+        const int g = chk * 32 + lane;
+        const bool act = g < ng;
+        for (uint32_t qi = s0 + warp; qi < s1; qi += nwarps) {
+            const uint32_t q = qof[qi];
+            const uint32_t t = b.tau[q];
+            uint32_t acc[4];
+            group_sums(codes, ng, g, act, e.lut + (size_t)q * npos * 16, npos, acc);
+            if (!act) continue;
+            for (int bb = 0; bb < 8; ++bb) {
+                int pos = 8 * g + bb;
+                if (pos >= nc) break;
+                uint32_t d = maxk - member_sum(acc, bb);
+                if (d > t) continue;
+                uint32_t slot = ix.cell_slots[moff + pos];
+                if (ix.ma > 1 && !canonical_cm(ix, slot, c, b.probed + (size_t)q * b.mwords)) continue;
+                uint32_t p = atomicAdd(&b.rest_n[q], 1u);
+                if (p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)q * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
+            }
+        }
+    }
+}
+
+// ---- cell-major: merge + exact global cut, ties kept (index.rs:2277-2306) ---------------------------
+
+__global__ void __launch_bounds__(kBS) k_final_cm(CellMajorBufs b, int target) {
+    __shared__ uint32_t hist[256];
+    const int q = blockIdx.x;
+    const uint64_t* sb = b.seed_buf + (size_t)q * b.seed_cap;
+    const uint64_t* rb = b.rest_buf + (size_t)q * b.rest_cap;
+    int ns = (int)b.seed_n[q];
+    int nr = (int)b.rest_n[q];
+    if (nr > b.rest_cap) {
+        if (threadIdx.x == 0) atomicAdd(b.overflow, 1u);
+        nr = b.rest_cap;
+    }
+    const int total = ns + nr;
+    uint32_t D = 0xFFFFFFFFu;
+    if (total > target) D = (uint32_t)(block_select_kth(sb, ns, rb, nr, target, 5, 4, hist) >> 32);
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    __shared__ uint32_t s_off;
+    if (threadIdx.x == 0) s_off = 0;
+    __syncthreads();
+    uint32_t* out = b.cand + (size_t)q * b.cand_cap;
+    for (int base = 0; base < total; base += kBS) {
+        int i = base + threadIdx.x;
+        uint64_t key = i < ns ? sb[i] : (i < total ? rb[i - ns] : ~0ull);
+        uint32_t f = (i < total && (uint32_t)(key >> 32) <= D) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        uint32_t off = s_off;
+        if (f && off + pos < (uint32_t)b.cand_cap) out[off + pos] = (uint32_t)key;
+        __syncthreads();
+        if (threadIdx.x == 0) s_off = off + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) b.cand_n[q] = min(s_off, (uint32_t)b.cand_cap);
+}
+
+// ---- per-query path (index.rs:1381-1864, FastScan branch) -------------------------------------------
+
+// Probe ranks and the entry segment of every chosen cell.
+__global__ void __launch_bounds__(kBS) k_pq_prep(IndexView ix, const uint32_t* __restrict__ chosen,
+                                                 const uint32_t* __restrict__ nch, int nprobe, PerQueryBufs b) {
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    __shared__ uint32_t s_run;
+    const int q = blockIdx.x, M = ix.M;
+    const int n = (int)nch[q];
+    uint32_t* crank = b.crank + (size_t)q * M;
+    for (int c = threadIdx.x; c < M; c += kBS) crank[c] = kNoCell;
+    if (threadIdx.x == 0) s_run = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kBS) crank[chosen[(size_t)q * nprobe + i]] = (uint32_t)i;
+    uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    for (int base = 0; base < n; base += kBS) {
+        int i = base + threadIdx.x;
+        uint32_t len = 0;
+        if (i < n) {
+            uint32_t c = chosen[(size_t)q * nprobe + i];
+            len = ix.cell_moff[c + 1] - ix.cell_moff[c];
+        }
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(len, pos, agg);
+        uint32_t run = s_run;
+        if (i < n) so[i] = run + pos;
+        __syncthreads();
+        if (threadIdx.x == 0) s_run = run + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) so[n] = s_run;
+}
+
+// Every member of every chosen cell: (d << 32 | slot) when canonical under the first-ranked-home
+// rule (index.rs:1443-1460) and inside the tag filter (index.rs:1430-1439), else kInvalidEntry.
+__global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                 const uint32_t* __restrict__ nch, int nprobe, int filtering,
+                                                 uint32_t flo, uint32_t fhi, PerQueryBufs b) {
+    const int r = blockIdx.x, q = blockIdx.y;
+    if (r >= (int)nch[q]) return;
+    const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    if (so[r + 1] > (uint32_t)b.ent_cap) return;  // reported by the fold
+    const uint32_t c = chosen[(size_t)q * nprobe + r];
+    const uint32_t moff = ix.cell_moff[c];
+    const int nc = (int)(ix.cell_moff[c + 1] - moff);
+    const int ng = (nc + 7) >> 3;
+    const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
+    const uint32_t* crank = b.crank + (size_t)q * ix.M;
+    uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
+    const uint8_t* lut = e.lut + (size_t)q * ix.npos * 16;
+    for (int chk = warp; chk * 32 < ng; chk += nwarps) {
+        int g = chk * 32 + lane;
+        bool act = g < ng;
+        uint32_t acc[4];
+        group_sums(codes, ng, g, act, lut, ix.npos, acc);
+        if (!act) continue;
+        for (int bb = 0; bb < 8; ++bb) {
+            int pos = 8 * g + bb;
+            if (pos >= nc) break;
+            uint32_t d = ix.maxk - member_sum(acc, bb);
+            uint32_t slot = ix.cell_slots[moff + pos];
+            bool ok = true;
+            if (filtering) {
+                uint32_t tg = ix.tags[slot];
+                ok = tg >= flo && tg <= fhi;
+            }
+            if (ok && ix.ma > 1) {
+                const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
+                for (int j = 0; j < ix.ma; ++j) {
+                    uint32_t h = hs[j];
+                    if (h != kNoCell && h != c) {
+                        uint32_t rh = crank[h];
+                        if (rh != kNoCell && rh < (uint32_t)r) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+            }
+            out[pos] = ok ? (((uint64_t)d << 32) | slot) : kInvalidEntry;
+        }
+    }
+}
+
+// The sequential part of the per-query scan: cells in probe order feed a bucket queue on d >> 6
+// with a falling cut-off tau, and the scan stops once no later cell can reach the current
+// want0-th best (index.rs:1630-1679). tau after any prefix of cells is the target-th smallest
+// bucket among that prefix's surviving entries, so whole cells are folded at once.
+__global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                 const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
+                                                 int nprobe, int target, int adaptive, float at_margin,
+                                                 PerQueryBufs b) {
+    extern __shared__ uint32_t sh[];
+    const int nb = (int)(ix.maxk >> 6) + 1;
+    uint32_t* hist = sh;              // nb buckets
+    float* suffix = reinterpret_cast<float*>(sh + nb);  // nprobe + 1
+    __shared__ uint32_t s_add, s_tau, s_stop, s_cnt;
+    __shared__ unsigned long long s_kept;
+    __shared__ uint32_t hist256[256];
+    const int q = blockIdx.x;
+    const int n = (int)nch[q];
+    const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    const uint64_t* ent = b.ent + (size_t)q * b.ent_cap;
+    if (so[n] > (uint32_t)b.ent_cap) {
+        if (threadIdx.x == 0) {
+            atomicAdd(b.overflow, 1u);
+            b.cand_n[q] = 0;
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < nb; i += kBS) hist[i] = 0;
+    if (adaptive) {
+        // suffix[i] = max bound over cells i..n-1 (index.rs:1467-1490)
+        for (int i = threadIdx.x; i < n; i += kBS)
+            suffix[i] = cell_bound(cscore[(size_t)q * nprobe + i], ix.r_bound[chosen[(size_t)q * nprobe + i]]);
+        if (threadIdx.x == 0) suffix[n] = -INFINITY;
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int i = n - 1; i >= 0; --i) suffix[i] = fmaxf(suffix[i], suffix[i + 1]);
+    }
+    if (threadIdx.x == 0) {
+        s_tau = ix.maxk >> 6;
+        s_kept = 0;
+        s_add = 0;
+        s_stop = (uint32_t)n;
+    }
+    __syncthreads();
+    const float norm = fs_norm(ix.dim_pad);
+    const float delta = e.fs_delta[q], bias = e.fs_bias[q];
+    for (int r = 0; r < n; ++r) {
+        const uint32_t tau = s_tau;
+        for (uint32_t i = so[r] + threadIdx.x; i < so[r + 1]; i += kBS) {
+            uint64_t k = ent[i];
+            if (k == kInvalidEntry) continue;
+            uint32_t hc = (uint32_t)(k >> 32) >> 6;
+            if (hc <= tau) {
+                atomicAdd(&hist[hc], 1u);
+                atomicAdd(&s_add, 1u);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long kept = s_kept + s_add;
+            s_add = 0;
+            uint32_t t = s_tau;
+            while (t > 0 && kept - hist[t] >= (unsigned long long)target) {
+                kept -= hist[t];
+                --t;
+            }
+            s_kept = kept;
+            s_tau = t;
+            if (adaptive && kept >= (unsigned long long)target) {
+                uint32_t wsub = ((t + 1) << 6) - 1;
+                uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
+                float thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+                if (suffix[r + 1] < __fsub_rn(thr, at_margin)) s_stop = (uint32_t)(r + 1);
+            }
+        }
+        __syncthreads();
+        if (s_stop != (uint32_t)n) break;
+    }
+    // candidates: entries of the scanned cells with bucket <= tau (index.rs:1680-1685)
+    const uint32_t tau = s_tau, end = so[s_stop];
+    uint64_t* keys = b.ent + (size_t)q * b.ent_cap;  // compacted in place (order-free)
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (uint32_t base = 0; base < end; base += kBS) {
+        uint32_t i = base + threadIdx.x;
+        uint64_t k = i < end ? ent[i] : kInvalidEntry;
+        uint32_t f = (k != kInvalidEntry && ((uint32_t)(k >> 32) >> 6) <= tau) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        __syncthreads();
+        uint32_t off = s_cnt;
+        if (f) keys[off + pos] = k;
+        __syncthreads();
+        if (threadIdx.x == 0) s_cnt = off + agg;
+        __syncthreads();
+    }
+    const int cnt = (int)s_cnt;
+    // top want0 (= target) by d; ties at the cut broken by ascending slot (index.rs:1689-1691)
+    uint64_t K = ~0ull;
+    if (cnt > target) K = block_select_kth(keys, cnt, nullptr, 0, target, 5, 0, hist256);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    uint32_t* out = b.cand + (size_t)q * b.cand_cap;
+    for (int base = 0; base < cnt; base += kBS) {
+        int i = base + threadIdx.x;
+        uint64_t k = i < cnt ? keys[i] : ~0ull;
+        uint32_t f = (i < cnt && k <= K) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        uint32_t off = s_cnt;
+        if (f && off + pos < (uint32_t)b.cand_cap) out[off + pos] = (uint32_t)k;
+        __syncthreads();
+        if (threadIdx.x == 0) s_cnt = off + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) b.cand_n[q] = min(s_cnt, (uint32_t)b.cand_cap);
+}
+
+// ---- exact rerank + top-k (index.rs:1309-1378) --------------------------------------------------------
+
+constexpr int kRerankChunk = 1024;
+
+__device__ __forceinline__ bool better(float sa, uint64_t ia, float sb, uint64_t ib) {
+    return sa > sb || (sa == sb && ia < ib);
+}
+
+__global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __restrict__ Q, QueryEnc e,
+                                                const uint32_t* __restrict__ cand, const uint32_t* __restrict__ cand_n,
+                                                int cand_cap, int k, int P, uint64_t* ids, float* scores,
+                                                uint32_t* out_n) {
+    extern __shared__ uint64_t rsm[];
+    uint64_t* sid = rsm;                                   // P ids
+    float* ssc = reinterpret_cast<float*>(sid + P);        // P scores
+    float* qv = ssc + P;                                   // dim
+    const int q = blockIdx.x, dim = ix.dim;
+    const int n = (int)cand_n[q];
+    const float* qsrc = ix.rerank_mode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+    for (int t = threadIdx.x; t < dim; t += kBS) qv[t] = qsrc[t];
+    for (int i = threadIdx.x; i < P; i += kBS) {
+        sid[i] = ~0ull;
+        ssc[i] = -INFINITY;
+    }
+    __syncthreads();
+    const float base = ix.rerank_mode == 1 ? e.rbase[q] : 0.0f;
+    const int l8 = threadIdx.x & 7;
+    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+    const uint32_t* cq = cand + (size_t)q * cand_cap;
+    for (int c0 = 0; c0 < n; c0 += kRerankChunk) {
+        const int cn = min(kRerankChunk, n - c0);
+        for (int i = k + threadIdx.x; i < P; i += kBS) {
+            sid[i] = ~0ull;
+            ssc[i] = -INFINITY;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x >> 3; i < cn; i += kBS / 8) {
+            uint32_t slot = cq[c0 + i];
+            float s;
+            if (ix.rerank_mode == 0)
+                s = dot_f32_g8(qv, ix.vecs_f32 + (size_t)slot * dim, dim, l8, gmask);
+            else if (ix.rerank_mode == 1)
+                s = __fadd_rn(base, dot_f32_u8_g8(qv, ix.rr_u8 + (size_t)slot * dim, dim, l8, gmask));
+            else
+                s = dot_f32_i8_g8(qv, reinterpret_cast<const int8_t*>(ix.rr_u8) + (size_t)slot * dim, dim, l8, gmask);
+            if (l8 == 0) {
+                sid[k + i] = ix.ext_ids[slot];
+                ssc[k + i] = s;
+            }
+        }
+        __syncthreads();
+        // bitonic sort of the P (score, id) pairs, best first
+        for (int kk = 2; kk <= P; kk <<= 1) {
+            for (int j = kk >> 1; j > 0; j >>= 1) {
+                for (int i = threadIdx.x; i < P; i += kBS) {
+                    int ixj = i ^ j;
+                    if (ixj > i) {
+                        float sa = ssc[i], sb = ssc[ixj];
+                        uint64_t ia = sid[i], ib = sid[ixj];
+                        bool first = (i & kk) == 0;
+                        bool sw = first ? better(sb, ib, sa, ia) : better(sa, ia, sb, ib);
+                        if (sw) {
+                            ssc[i] = sb;
+                            ssc[ixj] = sa;
+                            sid[i] = ib;
+                            sid[ixj] = ia;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+    }
+    const int m = min(k, n);
+    for (int i = threadIdx.x; i < k; i += kBS) {
+        bool v = i < m;
+        ids[(size_t)q * k + i] = v ? sid[i] : ~0ull;
+        scores[(size_t)q * k + i] = v ? ssc[i] : -INFINITY;
+    }
+    if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
+}
+
+}  // namespace
+
+// ---- launchers ----------------------------------------------------------------------------------------
+
+static void set_smem(const void* f, size_t bytes) {
+    if (bytes > 48 * 1024) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& e, bool want_cqs, bool want_rqs,
+                   cudaStream_t st) {
+    if (nq <= 0) return;
+    size_t smem = (size_t)(ix.dim_pad + ix.npos) * sizeof(float);
+    k_encode<<<nq, kBS, smem, st>>>(ix, Q, e, want_cqs ? 1 : 0, want_rqs ? 1 : 0);
+}
+
+void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint32_t* sl, uint32_t* sl_n,
+                       int sl_cap, cudaStream_t st) {
+    if (nq <= 0) return;
+    size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
+    k_route_flat<<<nq, kBS, smem, st>>>(ix, e, want_c, 0, sl, sl_n, sl_cap);
+}
+
+void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
+    if (nq <= 0) return;
+    QueryEnc e{};
+    size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
+    k_route_flat<<<nq, kBS, smem, st>>>(ix, e, 0, 1, sl, sl_n, sl_cap);
+}
+
+void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,
+                       int scratch_cap, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
+    if (nq <= 0) return;
+    Beams bm{};
+    for (int i = 0; i < ix.tree_depth && i < kMaxTreeLevels; ++i) bm.b[i] = beams[i];
+    size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
+    k_route_tree<<<nq, kBS, smem, st>>>(ix, e, bm, want, scratch, scratch_cap, sl, sl_n, sl_cap);
+}
+
+void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
+                           const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
+                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, cudaStream_t st) {
+    if (nq <= 0) return;
+    int P = next_pow2(std::min(std::max(sl_cap, 1), kSortCap));
+    size_t smem = (size_t)P * sizeof(uint64_t) + (size_t)ix.dim * sizeof(float);
+    set_smem((const void*)k_rescore_select, smem);
+    k_rescore_select<<<nq, kBS, smem, st>>>(ix, e, Q, sl, sl_n, sl_cap, nprobe, tc, beta, use_sq8 ? 1 : 0, chosen,
+                                            cscore, nch, err);
+}
+
+void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                      const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
+                      const CellMajorBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    size_t lut_bytes = (size_t)ix.npos * 16;
+    k_seed<<<nq, kBS, lut_bytes, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b);
+    cudaMemsetAsync(b.cell_cnt, 0, sizeof(uint32_t) * (ix.M + 1), st);
+    cudaMemsetAsync(b.cell_fill, 0, sizeof(uint32_t) * ix.M, st);
+    int wb = (nq + 7) / 8;
+    k_inv_count<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt);
+    k_inv_scan<<<1, 1024, 0, st>>>(b.cell_cnt, ix.M);
+    k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof);
+    k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b);
+    k_final_cm<<<nq, kBS, 0, st>>>(b, target);
+}
+
+void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                     const uint32_t* nch, int nprobe, int want0, bool adaptive, float at_margin, bool filtering,
+                     uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    k_pq_prep<<<nq, kBS, 0, st>>>(ix, chosen, nch, nprobe, b);
+    k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b);
+    int nb = (int)(ix.maxk >> 6) + 1;
+    size_t smem = (size_t)nb * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
+    set_smem((const void*)k_pq_fold, smem);
+    int target = std::max(want0, 1);
+    k_pq_fold<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b);
+}
+
+void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
+                   const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
+                   cudaStream_t st) {
+    if (nq <= 0) return;
+    int P = next_pow2(k + kRerankChunk);
+    size_t smem = (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (size_t)ix.dim * sizeof(float);
+    set_smem((const void*)k_rerank, smem);
+    k_rerank<<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, ids, scores, out_n);
+}
+
+}  // namespace dev
+}  // namespace maivs

@@ -1,0 +1,128 @@
+// Kernel declarations and the device image of a MAIVS index.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace maivs {
+namespace dev {
+
+// Read-only view of the device image, passed to kernels by value.
+struct IndexView {
+    int dim, dim_pad, nw, npos, M, ma;
+    uint32_t maxk;  // 255 * npos, the largest FastScan table sum
+    // routing tables
+    const uint64_t* cent_bits;  // M x nw
+    const uint8_t* cent_sq8;    // M x dim (null when the SQ8 re-order is off)
+    const float* cent_f32;      // M x dim
+    const float* csq_min;       // dim
+    const float* csq_step;      // dim
+    const uint8_t* live;        // M: cell has members
+    const float* r_bound;       // M
+    const float* signs;         // 2 x dim_pad
+    // scan layout: cell c's members are cell_slots[cell_moff[c] ..], its codes are the words
+    // cell_codes[cell_woff[c] + j * ng + g] = nibble j of members 8g..8g+7 (nibble b = member 8g+b)
+    const uint32_t* cell_moff;  // M + 1
+    const uint32_t* cell_woff;  // M + 1
+    const uint32_t* cell_codes;
+    const uint32_t* cell_slots;
+    const uint32_t* slot_cells;  // n_slots x ma
+    const uint32_t* tags;        // n_slots or null
+    // rerank store
+    int rerank_mode;  // 0 f32, 1 per-dimension SQ8, 2 global int8
+    const float* vecs_f32;
+    const uint8_t* rr_u8;
+    const float* sq_min;
+    const float* sq_step;
+    const uint64_t* ext_ids;
+    // centroid tree (leaf level and up to kMaxTreeLevels levels, coarsest first)
+    int tree_depth;
+    const uint64_t* tree_codes[8];
+    const uint32_t* tree_child_start[8];
+    const uint32_t* tree_child_len[8];
+    int tree_n[8];
+    const uint64_t* leaf_codes;
+    const uint32_t* leaf_ids;
+    int n_leaf;
+};
+
+constexpr int kMaxTreeLevels = 8;
+constexpr int kSeedCells = 8;  // index.rs:2019 SEED_CELLS
+constexpr int kSortCap = 16384;  // largest shortlist sorted in shared memory
+constexpr uint64_t kInvalidEntry = ~0ull;
+
+// Per-query encodings (src/quantize.rs rotate/pack/FsQuery, index.rs:1177-1187, :1320-1327).
+struct QueryEnc {
+    uint64_t* qbits;  // nq x nw
+    uint8_t* lut;     // nq x npos*16
+    float* fs_delta;  // nq
+    float* fs_bias;   // nq
+    float* cqs;       // nq x dim  (centroid SQ8 pre-scale)
+    float* cqbase;    // nq
+    float* rqs;       // nq x dim  (rerank SQ8 pre-scale)
+    float* rbase;     // nq
+};
+
+void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& e, bool want_cqs, bool want_rqs,
+                   cudaStream_t st);
+// Flat two-stage shortlist: live cells with Hamming <= the want_c-th smallest, ties kept, in cell
+// order (index.rs:1903-1927 route_batch, :1241-1259 route_query).
+void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint32_t* sl, uint32_t* sl_n,
+                       int sl_cap, cudaStream_t st);
+// Every live cell, in cell order (index.rs:1274-1282).
+void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st);
+// Centroid-tree beam descent (tree.rs:574-628); `beams` per level, `want` leaves.
+void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,
+                       int scratch_cap, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st);
+// SQ8 (or f32) re-order of the shortlist, top-nprobe by score desc (ties: lower cell id first),
+// nucleus cut (index.rs:1931-1977, :1283-1301).
+void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
+                           const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
+                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, cudaStream_t st);
+
+// Cell-major batch (index.rs:1999-2311).
+struct CellMajorBufs {
+    uint64_t* probed;     // nq x mwords (polysemy only)
+    int mwords;
+    uint64_t* seed_buf;   // nq x seed_cap
+    int seed_cap;
+    uint32_t* seed_n;     // nq
+    uint32_t* tau;        // nq
+    uint32_t* rest_hi;    // nq (rest range is [min(8, nch), rest_hi))
+    uint32_t* cell_cnt;   // M + 1 (counts, then start offsets)
+    uint32_t* cell_fill;  // M
+    uint32_t* qof;        // nq x nprobe
+    uint64_t* rest_buf;   // nq x rest_cap
+    int rest_cap;
+    uint32_t* rest_n;     // nq
+    uint32_t* cand;       // nq x cand_cap slots
+    int cand_cap;
+    uint32_t* cand_n;     // nq
+    uint32_t* overflow;   // 1: queries whose buffers overflowed
+};
+void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                      const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
+                      const CellMajorBufs& b, cudaStream_t st);
+
+// Per-query path (index.rs:1381-1864, FastScan branch).
+struct PerQueryBufs {
+    uint32_t* crank;     // nq x M probe rank or kNoCell
+    uint32_t* seg_off;   // nq x (nprobe + 1)
+    uint64_t* ent;       // nq x ent_cap entries (d << 32 | slot) or kInvalidEntry
+    int ent_cap;
+    uint32_t* cand;      // nq x cand_cap
+    int cand_cap;
+    uint32_t* cand_n;    // nq
+    uint32_t* overflow;
+};
+void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                     const uint32_t* nch, int nprobe, int want0, bool adaptive, float at_margin, bool filtering,
+                     uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st);
+
+// Exact rerank + top-k (index.rs:1309-1378); writes k ids/scores per query, padded.
+void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
+                   const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
+                   cudaStream_t st);
+
+}  // namespace dev
+}  // namespace maivs

@@ -1,0 +1,252 @@
+"""TEST INFRASTRUCTURE ONLY: Python binding of the parity oracle (maivs_oracle.cpp).
+
+The oracle restates the reference's CPU query path (Rust, V47VANSH/MAIVS src/quantize.rs,
+src/tree.rs, src/index.rs) in C++ with the reference's AVX2 arithmetic. It reads an index's
+arrays through `FlatCellIndex.array()` and recomputes search results from them. Only tests/,
+__graft_entry__.smoke() and the CPU-baseline arm of bench.py import this package; the product
+(maivs_b200) never does.
+
+Parity pinning: the reference has no golden vectors for this path and cannot be built in this
+environment (no Rust toolchain), so value-level parity is unpinned by the reference itself; the
+oracle is checked against published splitmix64 outputs, the reference's property tests
+(quantize.rs:445-492) and its invariant suite (tests/test_index.py), see tests/test_oracle.py.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "libmaivs_oracle.so")
+SRC = os.path.join(HERE, "maivs_oracle.cpp")
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with the committed recipe (oracle/Makefile)."""
+    if force or not os.path.exists(LIB) or os.path.getmtime(SRC) > os.path.getmtime(LIB):
+        r = subprocess.run(["make", "-C", HERE, "-B" if force else "libmaivs_oracle.so"], capture_output=True,
+                           text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
+    return LIB
+
+
+class _Arrays(C.Structure):
+    _fields_ = [
+        ("dim", C.c_uint64), ("dim_pad", C.c_uint64), ("nw", C.c_uint64), ("M", C.c_uint64), ("ma", C.c_uint64),
+        ("n_slots", C.c_uint64),
+        ("signs", C.c_void_p), ("centroids", C.c_void_p), ("r_bound", C.c_void_p), ("cell_members", C.c_void_p),
+        ("cell_member_off", C.c_void_p), ("fs_codes", C.c_void_p), ("n_fs_codes", C.c_uint64),
+        ("fs_off", C.c_void_p), ("slot_cells", C.c_void_p), ("ext_ids", C.c_void_p), ("cent_bits", C.c_void_p),
+        ("n_cent_bits", C.c_uint64), ("cent_sq8", C.c_void_p), ("n_cent_sq8", C.c_uint64), ("csq_min", C.c_void_p),
+        ("csq_step", C.c_void_p), ("vecs_f32", C.c_void_p), ("n_vecs_f32", C.c_uint64), ("scan_i8", C.c_void_p),
+        ("n_scan_i8", C.c_uint64), ("sq_min", C.c_void_p), ("sq_step", C.c_void_p), ("tags", C.c_void_p),
+        ("n_tags", C.c_uint64),
+        ("tree_depth", C.c_uint64), ("tree_level_n", C.c_void_p), ("tree_codes", C.c_void_p),
+        ("tree_code_off", C.c_void_p), ("tree_child_start", C.c_void_p), ("tree_child_len", C.c_void_p),
+        ("tree_child_off", C.c_void_p), ("tree_leaf_codes", C.c_void_p), ("tree_leaf_ids", C.c_void_p),
+        ("config", C.c_void_p), ("n_config", C.c_uint64),
+    ]
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(LIB)
+        vp, u64, f32 = C.c_void_p, C.c_uint64, C.c_float
+        L.oracle_index_new.restype = vp
+        L.oracle_index_new.argtypes = [C.POINTER(_Arrays)]
+        L.oracle_index_free.argtypes = [vp]
+        L.oracle_set_threads.argtypes = [C.c_int]
+        L.oracle_search_batch.restype = C.c_int
+        L.oracle_search_batch.argtypes = [vp, vp, u64, u64, u64, f32, f32, C.c_int, vp, vp, vp, u64, vp, vp]
+        L.oracle_route.restype = C.c_int
+        L.oracle_route.argtypes = [vp, vp, u64, u64, f32, f32, C.c_int, vp, vp, vp]
+        L.oracle_make_signs.argtypes = [u64, u64, vp]
+        L.oracle_splitmix64.argtypes = [u64, u64, vp]
+        L.oracle_fht.argtypes = [vp, u64]
+        L.oracle_rotate.argtypes = [vp, u64, vp, u64, vp]
+        L.oracle_pack_signs_trunc.argtypes = [vp, u64, vp, u64]
+        L.oracle_encode.argtypes = [vp, u64, u64, vp, u64, u64, vp]
+        L.oracle_fsquery.argtypes = [vp, u64, u64, vp, vp, vp]
+        L.oracle_fs_block_sums.argtypes = [vp, vp, u64, C.c_int, vp]
+        L.oracle_fs_pack_block.argtypes = [vp, u64, u64, vp]
+        L.oracle_dot_f32.restype = f32
+        L.oracle_dot_f32.argtypes = [vp, vp, u64]
+        L.oracle_dot_f32_u8.restype = f32
+        L.oracle_dot_f32_u8.argtypes = [vp, vp, u64]
+        L.oracle_hamming_cutoff.restype = u64
+        L.oracle_hamming_cutoff.argtypes = [vp, u64, u64, u64]
+        L.oracle_keep_smallest.restype = u64
+        L.oracle_keep_smallest.argtypes = [vp, vp, u64, u64, u64, vp]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None or a.size == 0:
+        return None
+    return a.ctypes.data
+
+
+class OracleIndex:
+    """The reference's query path over a snapshot of a FlatCellIndex's arrays."""
+
+    NAMES = ("signs", "centroids", "r_bound", "cell_members", "cell_member_off", "fs_codes", "fs_off", "slot_cells",
+             "ext_ids", "cent_bits", "cent_sq8", "csq_min", "csq_step", "vecs_f32", "scan_i8", "sq_min", "sq_step",
+             "tags", "tree_level_n", "tree_codes", "tree_code_off", "tree_child_start", "tree_child_len",
+             "tree_child_off", "tree_leaf_codes", "tree_leaf_ids", "config")
+
+    def __init__(self, arrays: dict):
+        self.a = {k: np.ascontiguousarray(v) for k, v in arrays.items()}
+        a = self.a
+        cfg = a["config"]
+        self.dim, self.dim_pad, self.nw = int(cfg[0]), int(cfg[1]), int(cfg[2])
+        M = a["r_bound"].shape[0]
+        ext = a["ext_ids"]
+        ma = int(cfg[8])
+        s = _Arrays()
+        s.dim, s.dim_pad, s.nw, s.M, s.ma, s.n_slots = self.dim, self.dim_pad, self.nw, M, ma, ext.shape[0]
+        for name in ("signs", "centroids", "r_bound", "cell_members", "cell_member_off", "fs_codes", "fs_off",
+                     "slot_cells", "ext_ids", "cent_bits", "cent_sq8", "csq_min", "csq_step", "vecs_f32",
+                     "scan_i8", "sq_min", "sq_step", "tags", "tree_level_n", "tree_codes", "tree_code_off",
+                     "tree_child_start", "tree_child_len", "tree_child_off", "tree_leaf_codes", "tree_leaf_ids",
+                     "config"):
+            setattr(s, name, _p(a.get(name)))
+        s.n_fs_codes = a["fs_codes"].size
+        s.n_cent_bits = a["cent_bits"].size
+        s.n_cent_sq8 = a["cent_sq8"].size
+        s.n_vecs_f32 = a["vecs_f32"].size
+        s.n_scan_i8 = a["scan_i8"].size
+        s.n_tags = a["tags"].size
+        s.tree_depth = a["tree_level_n"].size
+        s.n_config = cfg.size
+        self._s = s
+        self.h = lib().oracle_index_new(C.byref(s))
+
+    @classmethod
+    def from_index(cls, ix) -> "OracleIndex":
+        return cls({n: ix.array(n) for n in cls.NAMES})
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().oracle_index_free(self.h)
+            self.h = None
+
+    def search_batch(self, Q: np.ndarray, k: int, nprobe: int = 16, tc: float = 0.95, beta: float = 8.0,
+                     cell_major: bool = True, cand_cap: int = 0, threads: int | None = None):
+        """Returns (ids[nq*k], scores[nq*k], cands[nq, cand_cap] or None, cand_n or None, used_cm)."""
+        Q = np.ascontiguousarray(Q, dtype=np.float32)
+        nq = Q.shape[0]
+        if threads is not None:
+            lib().oracle_set_threads(int(threads))
+        ids = np.empty(nq * k, np.uint64)
+        sc = np.empty(nq * k, np.float32)
+        cands = np.empty((nq, cand_cap), np.uint32) if cand_cap else None
+        cand_n = np.empty(nq, np.uint32) if cand_cap else None
+        used = C.c_int(0)
+        rc = lib().oracle_search_batch(self.h, Q.ctypes.data, nq, k, nprobe, tc, beta, int(cell_major), ids.ctypes.data,
+                                       sc.ctypes.data, _p(cands), cand_cap, _p(cand_n), C.byref(used))
+        if rc != 0:
+            raise RuntimeError(f"oracle_search_batch failed with {rc}")
+        return ids, sc, cands, cand_n, bool(used.value)
+
+    def route(self, Q: np.ndarray, nprobe: int, tc: float = 1.0, beta: float = 8.0, batch_router: bool = True):
+        Q = np.ascontiguousarray(Q, dtype=np.float32)
+        nq = Q.shape[0]
+        chosen = np.empty((nq, nprobe), np.uint32)
+        cscore = np.empty((nq, nprobe), np.float32)
+        nch = np.empty(nq, np.uint32)
+        rc = lib().oracle_route(self.h, Q.ctypes.data, nq, nprobe, tc, beta, int(batch_router), chosen.ctypes.data,
+                                cscore.ctypes.data, nch.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"oracle_route failed with {rc}")
+        return chosen, cscore, nch
+
+
+# ---- component helpers -------------------------------------------------------------------------
+
+def splitmix64(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.uint64)
+    lib().oracle_splitmix64(seed, n, out.ctypes.data)
+    return out
+
+
+def make_signs(dim_pad: int, seed: int) -> np.ndarray:
+    out = np.empty(2 * dim_pad, np.float32)
+    lib().oracle_make_signs(dim_pad, seed, out.ctypes.data)
+    return out
+
+
+def fht(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32).copy()
+    lib().oracle_fht(a.ctypes.data, a.size)
+    return a
+
+
+def rotate(v: np.ndarray, signs: np.ndarray, dim_pad: int) -> np.ndarray:
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    out = np.empty(dim_pad, np.float32)
+    lib().oracle_rotate(v.ctypes.data, v.size, np.ascontiguousarray(signs).ctypes.data, dim_pad, out.ctypes.data)
+    return out
+
+
+def encode(V: np.ndarray, signs: np.ndarray, dim_pad: int, nw: int) -> np.ndarray:
+    V = np.ascontiguousarray(V, dtype=np.float32)
+    out = np.empty((V.shape[0], nw), np.uint64)
+    lib().oracle_encode(V.ctypes.data, V.shape[0], V.shape[1], np.ascontiguousarray(signs).ctypes.data, dim_pad, nw,
+                        out.ctypes.data)
+    return out
+
+
+def fsquery(rot: np.ndarray, nw: int):
+    rot = np.ascontiguousarray(rot, dtype=np.float32)
+    lut = np.empty(nw * 16 * 16, np.uint8)
+    d, b = C.c_float(), C.c_float()
+    lib().oracle_fsquery(rot.ctypes.data, rot.size, nw, lut.ctypes.data, C.byref(d), C.byref(b))
+    return lut, d.value, b.value
+
+
+def fs_block_sums(block: np.ndarray, lut: np.ndarray, nw: int, avx2: bool = True) -> np.ndarray:
+    out = np.empty(32, np.uint16)
+    lib().oracle_fs_block_sums(np.ascontiguousarray(block).ctypes.data, np.ascontiguousarray(lut).ctypes.data, nw,
+                               int(avx2), out.ctypes.data)
+    return out
+
+
+def fs_pack_block(codes: np.ndarray, nw: int) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.uint64)
+    out = np.empty(nw * 64 * 32 // 8, np.uint8)
+    lib().oracle_fs_pack_block(codes.ctypes.data if codes.size else None, codes.shape[0], nw, out.ctypes.data)
+    return out
+
+
+def dot_f32(a, b) -> float:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return float(lib().oracle_dot_f32(a.ctypes.data, b.ctypes.data, a.size))
+
+
+def dot_f32_u8(a, b) -> float:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.uint8)
+    return float(lib().oracle_dot_f32_u8(a.ctypes.data, b.ctypes.data, a.size))
+
+
+def hamming_cutoff(hs: np.ndarray, want: int, bits: int) -> int:
+    hs = np.ascontiguousarray(hs, np.uint16)
+    return int(lib().oracle_hamming_cutoff(hs.ctypes.data, hs.size, want, bits))
+
+
+def keep_smallest(h: np.ndarray, ids: np.ndarray, keep: int, bits: int) -> np.ndarray:
+    h = np.ascontiguousarray(h, np.uint32)
+    ids = np.ascontiguousarray(ids, np.uint32)
+    out = np.empty(max(h.size, 1), np.uint32)
+    n = lib().oracle_keep_smallest(h.ctypes.data, ids.ctypes.data, h.size, keep, bits, out.ctypes.data)
+    return out[:n]

@@ -1,0 +1,152 @@
+"""GPU search == the reference's CPU path (the oracle), bit for bit, on seeded indexes.
+
+Each case builds an index with the product's host build, runs the same queries through the GPU
+engine (C ABI via the FlatCellIndex drop-in) and through the oracle's restatement of the
+reference query path, and requires identical ids and identical f32 scores. Ties in the reference's
+unstable sorts are broken the same way on both sides (cell id, slot, external id).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from datagen import build_index, exact_topk, mixture, recall, shifted
+
+pytestmark = pytest.mark.gpu
+
+K = 10
+
+
+@pytest.fixture(scope="module")
+def data():
+    rng = np.random.default_rng(7)
+    X, centers = mixture(rng, 50_000, 384, 400)
+    Q, _ = mixture(rng, 300, 384, 400, centers=centers)
+    Qs = shifted(rng, Q[:100])
+    return X, np.ascontiguousarray(np.vstack([Q, Qs]))
+
+
+def _oracle(ix):
+    import oracle
+
+    return oracle.OracleIndex.from_index(ix)
+
+
+def _compare(ix, Q, k, nprobe, tc=1.0, cell_major=True):
+    got_ids, got_sc = ix.search_batch_arrays(Q, k, nprobe, tc, 8.0, cell_major)
+    o = _oracle(ix)
+    ref_ids, ref_sc, _, _, used = o.search_batch(Q, k, nprobe, tc, 8.0, cell_major)
+    bad = np.nonzero((got_ids != ref_ids) | ~((got_sc == ref_sc) | (np.isinf(got_sc) & np.isinf(ref_sc))))[0]
+    assert bad.size == 0, (
+        f"{bad.size} mismatches (first query {bad[0] // k}): gpu {got_ids[bad[:5]]} {got_sc[bad[:5]]} "
+        f"oracle {ref_ids[bad[:5]]} {ref_sc[bad[:5]]}")
+    return got_ids, used
+
+
+@pytest.fixture(scope="module")
+def quality(data):
+    X, _ = data
+    return build_index(X, "quality", rf=8, tree_min_cells=64)
+
+
+@pytest.fixture(scope="module")
+def memory(data):
+    X, _ = data
+    return build_index(X, "memory", rf=16, tree_min_cells=64)
+
+
+@pytest.mark.parametrize("nprobe", [1, 8, 32, 128, 512])
+def test_cellmajor_quality_bit_exact(data, quality, nprobe):
+    X, Q = data
+    ids, used = _compare(quality, Q, K, nprobe, cell_major=True)
+    assert used
+
+
+@pytest.mark.parametrize("nprobe", [1, 8, 32, 128])
+def test_perquery_quality_bit_exact(data, quality, nprobe):
+    X, Q = data
+    _compare(quality, Q[:64], K, nprobe, cell_major=False)
+
+
+@pytest.mark.parametrize("nprobe", [4, 64, 256])
+def test_memory_preset_both_paths(data, memory, nprobe):
+    X, Q = data
+    _compare(memory, Q, K, nprobe, cell_major=True)
+    _compare(memory, Q[:48], K, nprobe, cell_major=False)
+
+
+def test_recall_matches_oracle_and_brute_force(data, quality):
+    X, Q = data
+    truth = exact_topk(X, Q[:300])
+    ids, _ = quality.search_batch_arrays(Q[:300], K, 256, 1.0, 8.0, True)
+    r = recall(ids, truth)
+    o = _oracle(quality)
+    ref_ids, *_ = o.search_batch(Q[:300], K, 256, 1.0, 8.0, True)
+    assert r == recall(ref_ids, truth)
+    assert r > 0.9
+
+
+@pytest.mark.parametrize("homes,adaptive,two_stage", [(1, False, True), (1, True, False), (3, True, True)])
+def test_variants(data, homes, adaptive, two_stage):
+    X, Q = data
+    ix = build_index(X[:20_000], "quality", rf=4, homes=homes, adaptive=adaptive, two_stage=two_stage,
+                     tree_min_cells=10**9)
+    for nprobe in (3, 40):
+        _compare(ix, Q, K, nprobe, cell_major=True)
+        _compare(ix, Q[:40], K, nprobe, cell_major=False)
+
+
+def test_truncated_codes_and_i8_rerank(data):
+    X, Q = data
+    import maivs_b200 as M
+
+    ix = M.FlatCellIndex(384, "binary", 8, 0x5EED, 256)
+    ix.set_i8_rerank(True)
+    ix.set_orthogonal_polysemy(2, 1.0)
+    ix.set_fastscan(True)
+    ix.set_two_stage(True, 2)
+    ix.set_adaptive(True, 0.02)
+    ix.train_centroids(X[:20_000], 100)
+    ix.add_batch(list(range(20_000)), X[:20_000])
+    ix.compact()
+    _compare(ix, Q, K, 24, cell_major=True)
+    _compare(ix, Q[:40], K, 24, cell_major=False)
+
+
+def test_d768_codes(data):
+    rng = np.random.default_rng(11)
+    X, c = mixture(rng, 12_000, 768, 100, sigma=0.3)
+    Q, _ = mixture(rng, 64, 768, 100, sigma=0.3, centers=c)
+    ix = build_index(X, "memory", rf=8)
+    _compare(ix, Q, K, 16, cell_major=True)
+    _compare(ix, Q[:16], K, 16, cell_major=False)
+
+
+def test_filter_per_query_path(data, quality):
+    X, Q = data
+    n = X.shape[0]
+    tags = (np.arange(n) * 2654435761 % 1000).astype(np.uint32)
+    quality.set_tags(np.arange(n, dtype=np.uint64), tags)
+    try:
+        quality.set_filter(0, 99)
+        ids, used = _compare(quality, Q[:64], K, 64, cell_major=True)
+        assert not used  # a filter disables the cell-major join (index.rs:3347)
+        live = ids[ids != np.iinfo(np.uint64).max].astype(np.int64)
+        assert np.all(tags[live] <= 99)
+    finally:
+        quality.set_filter()
+
+
+def test_nucleus_close_to_oracle(data, quality):
+    X, Q = data
+    got, _ = quality.search_batch_arrays(Q, K, 64, 0.9, 8.0, True)
+    ref, *_ = _oracle(quality).search_batch(Q, K, 64, 0.9, 8.0, True)
+    # exp() may round differently by one ulp on the two sides; the probe sets still agree
+    assert np.mean(got == ref) > 0.999
+
+
+def test_single_search_matches_batch(data, quality):
+    X, Q = data
+    ids, sc = quality.search(Q[0], K, 32, 1.0, 8.0)
+    bi, bs = quality.search_batch_arrays(Q[:1], K, 32, 1.0, 8.0, False)
+    assert ids == [int(x) for x in bi] and np.array_equal(np.asarray(sc, np.float32), bs)
