@@ -116,6 +116,17 @@ int maivs_array(maivs_index* ix, const char* name, const void** data, size_t* co
 int maivs_profile(int on);
 int maivs_profile_read(int reset, const char** names, double* values, size_t cap, size_t* n_out);
 
+/* Instrumentation (no counterpart in the reference; used by bench.py and the profiles):
+ * per-kernel device times while the clock is on, the number of kernels this library launched,
+ * and the work counters of the last search ("nq", "probes", "candidates", "rerank_bytes",
+ * "scan_code_bytes", "scan_pairs", ...; names '\n'-separated in `names`). */
+int maivs_kernel_clock(maivs_index* ix, int on);
+int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* ms, uint64_t* launches, size_t cap,
+                       size_t* n_out);
+uint64_t maivs_launch_count(void);
+int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, double* values, size_t cap,
+                            size_t* n_out);
+
 #ifdef __cplusplus
 }
 #endif

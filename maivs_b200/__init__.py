@@ -213,6 +213,31 @@ class FlatCellIndex:
         self._check(_lib.lib().maivs_device_flags(self._h, C.c_void_p(stream or None), C.byref(f)))
         return int(f.value)
 
+    # ---- instrumentation ----
+    def kernel_clock(self, on: bool) -> None:
+        """Time every kernel of subsequent searches with CUDA events on their launch stream."""
+        self._check(_lib.lib().maivs_kernel_clock(self._h, int(bool(on))))
+
+    def kernel_times(self, reset: bool = False) -> dict:
+        """{kernel name: (total ms, launches)} accumulated while the clock was on."""
+        n = 32
+        names = (C.c_char_p * n)()
+        ms = (C.c_double * n)()
+        la = (C.c_uint64 * n)()
+        got = C.c_size_t(0)
+        self._check(_lib.lib().maivs_kernel_times(self._h, int(bool(reset)), names, ms, la, n, C.byref(got)))
+        return {names[i].decode(): (float(ms[i]), int(la[i])) for i in range(got.value)}
+
+    def last_search_stats(self) -> dict:
+        """Work counters of the last search (probes, candidates, bytes scanned and reranked)."""
+        cap = 64
+        buf = C.create_string_buffer(4096)
+        vals = (C.c_double * cap)()
+        got = C.c_size_t(0)
+        self._check(_lib.lib().maivs_last_search_stats(self._h, buf, 4096, vals, cap, C.byref(got)))
+        names = buf.value.decode().split("\n")
+        return {names[i]: float(vals[i]) for i in range(got.value)}
+
     # ---- introspection ----
     def __len__(self) -> int:
         n = C.c_size_t(0)
@@ -240,11 +265,11 @@ class FlatCellIndex:
         n = C.c_size_t(0)
         eb = C.c_size_t(0)
         self._check(_lib.lib().maivs_array(self._h, name.encode(), C.byref(p), C.byref(n), C.byref(eb)))
-        dt = _ARRAY_DTYPES.get(name)
+        dt = np.dtype(_ARRAY_DTYPES.get(name))
         if n.value == 0 or not p.value:
             return np.zeros(0, dtype=dt)
-        buf = (C.c_uint8 * (n.value * eb.value)).from_address(p.value)
-        return np.frombuffer(bytes(buf), dtype=dt).copy()
+        raw = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(n.value * eb.value,))
+        return raw.view(dt).copy()
 
 
 _ARRAY_DTYPES = {
@@ -262,6 +287,11 @@ CONFIG_FIELDS = ("dim", "dim_pad", "nw", "rerank_factor", "two_stage", "shortlis
                  "max_assign", "fastscan", "per_dim_sq", "i8_rerank", "keep_f32", "adaptive", "at_margin",
                  "quant_scale", "compacted", "n_live", "cm_min_batch", "has_filter", "filter_lo", "filter_hi",
                  "tree_beam_frac", "tree_n_leaf", "graph_route", "graph_min_cells")
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process."""
+    return int(_lib.lib().maivs_launch_count())
 
 
 def profile(on: bool) -> None:

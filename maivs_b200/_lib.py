@@ -47,6 +47,12 @@ _SIGS = {
     "maivs_device_flags": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint32)]),
     "maivs_array": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t),
                               C.POINTER(C.c_size_t)]),
+    "maivs_kernel_clock": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_kernel_times": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
+                                     C.POINTER(C.c_uint64), C.c_size_t, C.POINTER(C.c_size_t)]),
+    "maivs_launch_count": (C.c_uint64, []),
+    "maivs_last_search_stats": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double), C.c_size_t,
+                                          C.POINTER(C.c_size_t)]),
     "maivs_profile": (C.c_int, [C.c_int]),
     "maivs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.c_size_t,
                                      C.POINTER(C.c_size_t)]),
@@ -59,7 +65,7 @@ def lib() -> C.CDLL:
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise ImportError(f"{LIB_PATH} is missing: build it with `python -m maivs_b200.build`")
-        L = C.CDLL(LIB_PATH)
+        L = C.CDLL(LIB_PATH, mode=os.RTLD_NOW | os.RTLD_LOCAL)
         for name, (res, args) in _SIGS.items():
             f = getattr(L, name)
             f.restype = res

@@ -84,9 +84,27 @@ void put(maivs_index* ix, const std::string& name, const T* p, size_t n) {
     if (n) std::memcpy(v.data(), p, n * sizeof(T));
 }
 
+// Query-time switches (rerank factor, adaptive margin, filter, ...) change no index version, so
+// the configuration array is rebuilt on every request.
+void put_config(maivs_index* ix) {
+    HostIndex& h = ix->h;
+    double cfg[] = {(double)h.dim,          (double)h.dim_pad,       (double)h.nw,
+                    (double)h.rerank_factor, (double)h.two_stage,     (double)h.shortlist_mult,
+                    (double)h.centroid_sq8,  (double)(h.tree != nullptr), (double)h.max_assign,
+                    (double)h.fastscan,      (double)h.per_dim_sq,    (double)h.i8_rerank,
+                    (double)h.keep_f32,      (double)h.adaptive,      (double)h.at_margin,
+                    (double)h.quant_scale,   (double)h.compacted,     (double)h.n_live,
+                    (double)h.cm_min_batch,  (double)h.has_filter,    (double)h.filter_lo,
+                    (double)h.filter_hi,     (double)(h.tree ? h.tree->beam_frac : 0.0f),
+                    (double)(h.tree ? h.tree->n_leaf : 0), (double)h.graph_route, (double)h.graph_min_cells};
+    put(ix, "config", cfg, sizeof(cfg) / sizeof(double));
+}
+
 void build_arrays(maivs_index* ix) {
+    put_config(ix);
     if (ix->arrays_version == ix->h.version) return;
     ix->arrays.clear();
+    put_config(ix);
     HostIndex& h = ix->h;
     put(ix, "vecs_f32", h.vecs_f32.data(), h.vecs_f32.size());
     put(ix, "scan_i8", h.scan_i8.data(), h.scan_i8.size());
@@ -140,17 +158,6 @@ void build_arrays(maivs_index* ix) {
     put(ix, "tree_child_off", tchoff.data(), tchoff.size());
     put(ix, "tree_leaf_codes", lcodes.data(), lcodes.size());
     put(ix, "tree_leaf_ids", lids.data(), lids.size());
-    // scalar configuration the query path reads, as doubles in a fixed order
-    double cfg[] = {(double)h.dim,          (double)h.dim_pad,       (double)h.nw,
-                    (double)h.rerank_factor, (double)h.two_stage,     (double)h.shortlist_mult,
-                    (double)h.centroid_sq8,  (double)(h.tree != nullptr), (double)h.max_assign,
-                    (double)h.fastscan,      (double)h.per_dim_sq,    (double)h.i8_rerank,
-                    (double)h.keep_f32,      (double)h.adaptive,      (double)h.at_margin,
-                    (double)h.quant_scale,   (double)h.compacted,     (double)h.n_live,
-                    (double)h.cm_min_batch,  (double)h.has_filter,    (double)h.filter_lo,
-                    (double)h.filter_hi,     (double)(h.tree ? h.tree->beam_frac : 0.0f),
-                    (double)(h.tree ? h.tree->n_leaf : 0), (double)h.graph_route, (double)h.graph_min_cells};
-    put(ix, "config", cfg, sizeof(cfg) / sizeof(double));
     ix->arrays_version = h.version;
 }
 
@@ -470,6 +477,57 @@ int maivs_array(maivs_index* ix, const char* name, const void** data, size_t* co
     *data = it->second.empty() ? nullptr : it->second.data();
     *count = it->second.size() / e;
     if (elem_bytes) *elem_bytes = e;
+    return MAIVS_OK;
+}
+
+int maivs_kernel_clock(maivs_index* ix, int on) {
+    LOCK(ix);
+    int rc = ensure_device(ix);
+    if (rc != MAIVS_OK) return rc;
+    ix->d->enable_kernel_clock(on != 0);
+    return MAIVS_OK;
+}
+
+int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* ms, uint64_t* launches, size_t cap,
+                       size_t* n_out) {
+    LOCK(ix);
+    size_t n = std::min<size_t>(cap, maivs::dev::kNumKernels);
+    if (n_out) *n_out = n;
+    maivs::dev::KernelClock* c = ix->d ? ix->d->kernel_clock() : nullptr;
+    if (c) c->collect();
+    for (size_t i = 0; i < n; ++i) {
+        if (names) names[i] = maivs::dev::kernel_name((int)i);
+        if (ms) ms[i] = c ? c->ms[i] : 0.0;
+        if (launches) launches[i] = c ? c->launches[i] : 0;
+    }
+    if (reset && c)
+        for (size_t i = 0; i < maivs::dev::kNumKernels; ++i) {
+            c->ms[i] = 0.0;
+            c->launches[i] = 0;
+        }
+    return MAIVS_OK;
+}
+
+uint64_t maivs_launch_count(void) { return maivs::dev::total_launches(); }
+
+int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, double* values, size_t cap,
+                            size_t* n_out) {
+    LOCK(ix);
+    if (!ix->d) return fail(ix, MAIVS_BAD_STATE, "no search has run");
+    auto st = ix->d->last_stats();
+    size_t n = std::min(cap, st.size());
+    std::string joined;
+    for (size_t i = 0; i < n; ++i) {
+        values[i] = st[i].second;
+        joined += st[i].first;
+        joined += '\n';
+    }
+    if (names && names_cap) {
+        size_t m = std::min(names_cap - 1, joined.size());
+        std::memcpy(names, joined.data(), m);
+        names[m] = 0;
+    }
+    if (n_out) *n_out = n;
     return MAIVS_OK;
 }
 

@@ -40,6 +40,7 @@ DeviceIndex::~DeviceIndex() {
     if (stream_) cudaStreamSynchronize(stream_);
     for (void* p : allocs_) cudaFree(p);
     if (ws_) cudaFree(ws_);
+    if (io_) cudaFree(io_);
     if (pin_) cudaFreeHost(pin_);
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
@@ -111,6 +112,7 @@ std::string DeviceIndex::upload(const HostIndex& h, int device) {
             }
     }
     v.cell_moff = upload_vec(moff);
+    moff_ = moff;
     v.cell_woff = upload_vec(woff);
     v.cell_slots = upload_vec(slots);
     v.cell_codes = upload_vec(codes);
@@ -232,7 +234,8 @@ bool DeviceIndex::use_cell_major(const HostIndex& h, const SearchArgs& a) const 
 }
 
 int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc,
-                       float beta, bool batch_router, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch,
+                       float beta, bool batch_router, uint16_t* hs, uint32_t* sl, uint32_t* sl_n,
+                       uint32_t* tree_scratch,
                        uint32_t* chosen, float* cscore, uint32_t* nch, cudaStream_t st, std::string& err) {
     const int M = view_.M;
     const size_t mult2 = std::max<size_t>(h.shortlist_mult, 2);
@@ -240,7 +243,7 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
     if (batch_router && have_codes) {
         // route_batch (index.rs:1873-1980): exact flat Hamming shortlist for every query
         int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_live_);
-        dev::launch_route_flat(view_, e, nq, want_c, sl, sl_n, M, st);
+        dev::launch_route_flat(view_, e, nq, want_c, hs, sl, sl_n, M, st);
     } else if (h.tree) {
         // route_query tree branch (index.rs:1188-1211)
         int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_leaf_);
@@ -254,7 +257,7 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
     } else if (have_codes) {
         // route_query two-stage branch (index.rs:1241-1259): note the multiplier is not floored at 2
         int want_c = (int)std::min<size_t>((size_t)nprobe * h.shortlist_mult, n_live_);
-        dev::launch_route_flat(view_, e, nq, want_c, sl, sl_n, M, st);
+        dev::launch_route_flat(view_, e, nq, want_c, hs, sl, sl_n, M, st);
     } else {
         dev::launch_route_all(view_, nq, sl, sl_n, M, st);
     }
@@ -274,8 +277,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     const int cand_cap = seed_cap + rest_cap;
     const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
 
-    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint32_t*& tsc, uint32_t*& chosen,
-                     float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
+    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
+                     uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
         e.qbits = bp.take<uint64_t>((size_t)nq * nw);
         e.lut = bp.take<uint8_t>((size_t)nq * npos * 16);
         e.fs_delta = bp.take<float>(nq);
@@ -286,6 +289,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         e.rbase = bp.take<float>(nq);
         sl = bp.take<uint32_t>((size_t)nq * M);
         sl_n = bp.take<uint32_t>(nq);
+        hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
         chosen = bp.take<uint32_t>((size_t)nq * nprobe);
         cscore = bp.take<float>((size_t)nq * nprobe);
@@ -310,19 +314,39 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
+    uint16_t* hs;
     float* cscore;
     dev::CellMajorBufs b{};
     Bump sizing{nullptr, 0, 0};
-    carve(sizing, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    carve(sizing, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
     Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
-    carve(bp, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    carve(bp, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
 
+    last_ = LastCall{};
+    last_.valid = true;
+    last_.cell_major = true;
+    last_.nq = nq;
+    last_.nprobe = nprobe;
+    last_.target = target;
+    last_.nch = nch;
+    last_.chosen = chosen;
+    last_.sl_n = sl_n;
+    last_.cell_cnt = b.cell_cnt;
+    last_.cand_n = b.cand_n;
+    last_.seed_n = b.seed_n;
+    last_.rest_n = b.rest_n;
+    last_.rest_hi = b.rest_hi;
+    last_.st = st;
+    dev::set_thread_clock(clock_.get());
+    struct Unset {
+        ~Unset() { dev::set_thread_clock(nullptr); }
+    } unset;
     if (timing_) cudaEventRecord(ev_[0], st);
     dev::launch_encode(view_, dQ, nq, e, use_sq8_, view_.rerank_mode == 1, st);
     if (timing_) cudaEventRecord(ev_[1], st);
-    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
     if (rc != kOk) return rc;
     if (timing_) cudaEventRecord(ev_[2], st);
     dev::launch_cellmajor(view_, e, nq, chosen, cscore, nch, nprobe, target, h.adaptive, h.at_margin, b, st);
@@ -344,8 +368,8 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     const bool tree_router = h.tree != nullptr;
     const int chunk = std::min(a.nq, kPerQueryChunk);
 
-    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint32_t*& tsc, uint32_t*& chosen,
-                     float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
+    auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
+                     uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
         int nq = chunk;
         e.qbits = bp.take<uint64_t>((size_t)nq * nw);
         e.lut = bp.take<uint8_t>((size_t)nq * npos * 16);
@@ -357,6 +381,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         e.rbase = bp.take<float>(nq);
         sl = bp.take<uint32_t>((size_t)nq * M);
         sl_n = bp.take<uint32_t>(nq);
+        hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
         chosen = bp.take<uint32_t>((size_t)nq * nprobe);
         cscore = bp.take<float>((size_t)nq * nprobe);
@@ -372,22 +397,37 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
+    uint16_t* hs;
     float* cscore;
     dev::PerQueryBufs b{};
     Bump sizing{nullptr, 0, 0};
-    carve(sizing, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    carve(sizing, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
     Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
-    carve(bp, e, sl, sl_n, tsc, chosen, cscore, nch, b);
+    carve(bp, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
 
+    last_ = LastCall{};
+    last_.valid = a.nq <= chunk;
+    last_.nq = a.nq;
+    last_.nprobe = nprobe;
+    last_.target = std::max(want0, 1);
+    last_.nch = nch;
+    last_.chosen = chosen;
+    last_.sl_n = sl_n;
+    last_.cand_n = b.cand_n;
+    last_.st = st;
+    dev::set_thread_clock(clock_.get());
+    struct Unset {
+        ~Unset() { dev::set_thread_clock(nullptr); }
+    } unset;
     if (timing_) cudaEventRecord(ev_[0], st);
     for (int q0 = 0; q0 < a.nq; q0 += chunk) {
         int nq = std::min(chunk, a.nq - q0);
         const float* Qc = dQ + (size_t)q0 * dim;
         dev::launch_encode(view_, Qc, nq, e, use_sq8_, view_.rerank_mode == 1, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[1], st);
-        rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+        rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
         if (rc != kOk) return rc;
         if (timing_ && q0 == 0) cudaEventRecord(ev_[2], st);
         dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
@@ -428,9 +468,12 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
     if (a.nq <= 0) return kOk;
     cudaSetDevice(device_);
     const size_t nq = a.nq, k = a.k, dim = view_.dim;
+    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
     const size_t qb = nq * dim * sizeof(float), ib = nq * k * sizeof(uint64_t), sb = nq * k * sizeof(float),
-                 nb = nq * sizeof(uint32_t);
-    size_t need = qb + ib + sb + nb + 4 * 256;
+                 nb = nq * sizeof(uint32_t), fb = 4 * sizeof(uint32_t);
+    const size_t need = al(qb) + al(ib) + al(sb) + al(nb) + al(fb);
+    // pinned staging and device I/O buffers persist across calls (grown on demand), so a call
+    // allocates nothing in the common case and synchronises once
     if (need > pin_bytes_) {
         if (pin_) cudaFreeHost(pin_);
         pin_ = nullptr;
@@ -438,48 +481,129 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
         CUDA_TRY(cudaMallocHost(&pin_, need));
         pin_bytes_ = need;
     }
-    // device I/O buffers come from the stream-ordered pool
-    char* dio = nullptr;
-    CUDA_TRY(cudaMallocAsync((void**)&dio, need, stream_));
+    if (need > io_bytes_) {
+        if (io_) {
+            cudaStreamSynchronize(stream_);
+            cudaFree(io_);
+        }
+        io_ = nullptr;
+        io_bytes_ = 0;
+        CUDA_TRY(cudaMalloc(&io_, need));
+        io_bytes_ = need;
+    }
     char* hp = static_cast<char*>(pin_);
-    std::memcpy(hp, Q, qb);
-    float* dQ = reinterpret_cast<float*>(dio);
-    uint64_t* dI = reinterpret_cast<uint64_t*>(dio + ((qb + 255) & ~size_t(255)));
-    float* dS = reinterpret_cast<float*>(reinterpret_cast<char*>(dI) + ((ib + 255) & ~size_t(255)));
-    uint32_t* dN = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(dS) + ((sb + 255) & ~size_t(255)));
+    char* dp = static_cast<char*>(io_);
+    float* hQ = reinterpret_cast<float*>(hp);
+    uint64_t* hI = reinterpret_cast<uint64_t*>(hp + al(qb));
+    float* hS = reinterpret_cast<float*>(hp + al(qb) + al(ib));
+    uint32_t* hN = reinterpret_cast<uint32_t*>(hp + al(qb) + al(ib) + al(sb));
+    uint32_t* hF = reinterpret_cast<uint32_t*>(hp + al(qb) + al(ib) + al(sb) + al(nb));
+    float* dQ = reinterpret_cast<float*>(dp);
+    uint64_t* dI = reinterpret_cast<uint64_t*>(dp + al(qb));
+    float* dS = reinterpret_cast<float*>(dp + al(qb) + al(ib));
+    uint32_t* dN = reinterpret_cast<uint32_t*>(dp + al(qb) + al(ib) + al(sb));
+    std::memcpy(hQ, Q, qb);
     int rc = kOk;
     for (int attempt = 0; attempt < 4; ++attempt) {
-        CUDA_TRY(cudaMemcpyAsync(dQ, hp, qb, cudaMemcpyHostToDevice, stream_));
+        CUDA_TRY(cudaMemcpyAsync(dQ, hQ, qb, cudaMemcpyHostToDevice, stream_));
         rc = search_device(h, dQ, a, dI, dS, dN, stream_, err);
-        if (rc != kOk) break;
-        uint32_t f[4] = {0, 0, 0, 0};
-        cudaMemcpyAsync(f, d_flags_, sizeof(f), cudaMemcpyDeviceToHost, stream_);
+        if (rc != kOk) return rc;
+        CUDA_TRY(cudaMemcpyAsync(hI, dI, ib, cudaMemcpyDeviceToHost, stream_));
+        CUDA_TRY(cudaMemcpyAsync(hS, dS, sb, cudaMemcpyDeviceToHost, stream_));
+        CUDA_TRY(cudaMemcpyAsync(hN, dN, nb, cudaMemcpyDeviceToHost, stream_));
+        CUDA_TRY(cudaMemcpyAsync(hF, d_flags_, fb, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaStreamSynchronize(stream_));
-        if (f[1] != 0) {
+        if (hF[1] != 0) {
             err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
-            rc = kUnsupported;
-            break;
+            return kUnsupported;
         }
-        if (f[0] == 0) break;
+        if (hF[0] == 0) break;
         if (attempt == 3) {
             err = "candidate buffers overflowed after enlarging them";
-            rc = kOverflow;
-            break;
+            return kOverflow;
         }
         grow_factor *= 4;
     }
-    if (rc == kOk) {
-        CUDA_TRY(cudaMemcpyAsync(hp + qb, dI, ib, cudaMemcpyDeviceToHost, stream_));
-        CUDA_TRY(cudaMemcpyAsync(hp + qb + ib, dS, sb, cudaMemcpyDeviceToHost, stream_));
-        CUDA_TRY(cudaMemcpyAsync(hp + qb + ib + sb, dN, nb, cudaMemcpyDeviceToHost, stream_));
-    }
-    cudaFreeAsync(dio, stream_);
-    CUDA_TRY(cudaStreamSynchronize(stream_));
-    if (rc != kOk) return rc;
-    std::memcpy(ids, hp + qb, ib);
-    std::memcpy(scores, hp + qb + ib, sb);
-    if (nout) std::memcpy(nout, hp + qb + ib + sb, nb);
+    std::memcpy(ids, hI, ib);
+    std::memcpy(scores, hS, sb);
+    if (nout) std::memcpy(nout, hN, nb);
     return kOk;
+}
+
+void DeviceIndex::enable_kernel_clock(bool on) {
+    if (on && !clock_) clock_ = std::make_unique<dev::KernelClock>();
+    if (!on) clock_.reset();
+}
+
+std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
+    std::vector<std::pair<std::string, double>> out;
+    if (!last_.valid) return out;
+    cudaSetDevice(device_);
+    cudaStreamSynchronize(last_.st);
+    const int nq = last_.nq, np = last_.nprobe, M = view_.M;
+    auto get = [&](const uint32_t* d, size_t n) {
+        std::vector<uint32_t> v(n, 0);
+        if (d && n) cudaMemcpy(v.data(), d, n * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+        return v;
+    };
+    std::vector<uint32_t> nch = get(last_.nch, nq), chosen = get(last_.chosen, (size_t)nq * np),
+                          sl_n = get(last_.sl_n, nq), cand_n = get(last_.cand_n, nq);
+    const double code_bytes = (double)view_.nw * 8.0;
+    double probes = 0, shortlist = 0, cands = 0;
+    for (int q = 0; q < nq; ++q) {
+        probes += nch[q];
+        shortlist += sl_n[q];
+        cands += cand_n[q];
+    }
+    out.push_back({"nq", (double)nq});
+    out.push_back({"probes", probes});
+    out.push_back({"shortlist", shortlist});
+    out.push_back({"candidates", cands});
+    double row_bytes = view_.rerank_mode == 0 ? 4.0 * view_.dim : (double)view_.dim;
+    out.push_back({"rerank_row_bytes", row_bytes});
+    out.push_back({"rerank_bytes", cands * row_bytes});
+    out.push_back({"route_code_bytes", (double)M * code_bytes});
+    if (last_.cell_major) {
+        std::vector<uint32_t> start = get(last_.cell_cnt, (size_t)M + 1), seed_n = get(last_.seed_n, nq),
+                              rest_n = get(last_.rest_n, nq), rest_hi = get(last_.rest_hi, nq);
+        double cells = 0, bytes = 0, pairs = 0, seed_pairs = 0, seed_kept = 0, rest_kept = 0, rest_probes = 0;
+        std::vector<uint8_t> seen(M, 0);
+        double seed_bytes = 0;
+        for (int c = 0; c < M; ++c) {
+            uint32_t nqc = start[c + 1] - start[c];
+            double nc = (double)(moff_[c + 1] - moff_[c]);
+            if (nqc) {
+                cells += 1;
+                bytes += nc * code_bytes;
+                pairs += nqc * nc;
+                seen[c] = 1;
+            }
+        }
+        for (int q = 0; q < nq; ++q) {
+            int ns = std::min<int>(dev::kSeedCells, (int)nch[q]);
+            for (int r = 0; r < ns; ++r) {
+                uint32_t c = chosen[(size_t)q * np + r];
+                double nc = (double)(moff_[c + 1] - moff_[c]);
+                seed_pairs += nc;
+                if (!seen[c]) {
+                    seen[c] = 2;
+                    seed_bytes += nc * code_bytes;
+                }
+            }
+            seed_kept += seed_n[q];
+            rest_kept += rest_n[q];
+            rest_probes += (double)rest_hi[q] - ns;
+        }
+        out.push_back({"scan_cells", cells});
+        out.push_back({"scan_code_bytes", bytes});
+        out.push_back({"scan_pairs", pairs});
+        out.push_back({"seed_pairs", seed_pairs});
+        out.push_back({"seed_extra_code_bytes", seed_bytes});
+        out.push_back({"seed_kept", seed_kept});
+        out.push_back({"rest_kept", rest_kept});
+        out.push_back({"rest_probes", rest_probes});
+    }
+    return out;
 }
 
 PhaseTimes DeviceIndex::collect_phases() {

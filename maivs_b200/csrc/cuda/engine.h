@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -71,6 +72,12 @@ class DeviceIndex {
 
     int grow_factor = 1;  // multiplies the candidate-buffer capacities after an overflow
 
+    // Per-kernel device times (only while enabled) and the work counters of the last search,
+    // read from its workspace after synchronising: name -> value.
+    void enable_kernel_clock(bool on);
+    dev::KernelClock* kernel_clock() { return clock_.get(); }
+    std::vector<std::pair<std::string, double>> last_stats();
+
    private:
     void* alloc(size_t bytes);
     template <typename T>
@@ -81,7 +88,7 @@ class DeviceIndex {
     int run_perquery(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                      uint32_t* d_nout, cudaStream_t st, std::string& err);
     int route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc, float beta,
-              bool batch_router, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch, uint32_t* chosen,
+              bool batch_router, uint16_t* hs, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch, uint32_t* chosen,
               float* cscore, uint32_t* nch, cudaStream_t st, std::string& err);
 
     int device_ = -1;
@@ -98,7 +105,18 @@ class DeviceIndex {
     // pinned staging for the host-buffer API
     void* pin_ = nullptr;
     size_t pin_bytes_ = 0;
+    void* io_ = nullptr;  // device queries and results of the host-buffer API
+    size_t io_bytes_ = 0;
     bool timing_ = false;
+    std::unique_ptr<dev::KernelClock> clock_;
+    std::vector<uint32_t> moff_;  // host copy of the member offsets
+    struct LastCall {
+        bool valid = false, cell_major = false;
+        int nq = 0, nprobe = 0, target = 0;
+        const uint32_t *nch = nullptr, *chosen = nullptr, *sl_n = nullptr, *cell_cnt = nullptr,
+                       *cand_n = nullptr, *seed_n = nullptr, *rest_n = nullptr, *rest_hi = nullptr;
+        cudaStream_t st = nullptr;
+    } last_;
     PhaseTimes phases_;
     cudaEvent_t ev_[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
 };

@@ -5,6 +5,7 @@
 // work follows the reference's evaluation order (see common.cuh), so scores are bit-identical to
 // the reference's CPU path on the same inputs.
 #include <cub/block/block_reduce.cuh>
+#include <atomic>
 #include <cub/block/block_scan.cuh>
 
 #include "common.cuh"
@@ -27,21 +28,40 @@ __device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, i
                                            const uint8_t* lut, int npos, uint32_t acc[4]) {
     acc[0] = acc[1] = acc[2] = acc[3] = 0;
     const uint4* T = reinterpret_cast<const uint4*>(lut);
-#pragma unroll 4
-    for (int j = 0; j < npos; ++j) {
-        uint4 t = T[j];
-        uint32_t w = active ? __ldg(codes + (size_t)j * ng + g) : 0u;
-        uint32_t r0 = lut16x4(t, w);
-        uint32_t r1 = lut16x4(t, w >> 16);
-        acc[0] += __byte_perm(r0, 0, 0x4140);
-        acc[1] += __byte_perm(r0, 0, 0x4342);
-        acc[2] += __byte_perm(r1, 0, 0x4140);
-        acc[3] += __byte_perm(r1, 0, 0x4342);
+    // npos is a multiple of 16; eight independent code-word loads are issued before their lookups
+    for (int j0 = 0; j0 < npos; j0 += 8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint4 t = T[j0 + u];
+            const uint32_t r0 = lut16x4(t, w[u]);
+            const uint32_t r1 = lut16x4(t, w[u] >> 16);
+            acc[0] += __byte_perm(r0, 0, 0x4140);
+            acc[1] += __byte_perm(r0, 0, 0x4342);
+            acc[2] += __byte_perm(r1, 0, 0x4140);
+            acc[3] += __byte_perm(r1, 0, 0x4342);
+        }
     }
 }
 
 __device__ __forceinline__ uint32_t member_sum(const uint32_t acc[4], int b) {
     return (acc[b >> 1] >> (16 * (b & 1))) & 0xFFFFu;
+}
+
+// Appends `key` for every lane whose `valid` is set with one atomic per warp: returns the slot
+// index for this lane (undefined when !valid). All 32 lanes must call it.
+__device__ __forceinline__ uint32_t warp_append(bool valid, uint32_t* counter) {
+    const unsigned mask = __ballot_sync(0xFFFFFFFFu, valid);
+    const int lane = threadIdx.x & 31;
+    uint32_t base = 0;
+    if (mask) {
+        const int leader = __ffs(mask) - 1;
+        if (lane == leader) base = atomicAdd(counter, (uint32_t)__popc(mask));
+        base = __shfl_sync(0xFFFFFFFFu, base, leader);
+    }
+    return base + (uint32_t)__popc(mask & ((1u << lane) - 1u));
 }
 
 // Exactly-once rule of the cell-major join: a multi-home vector is scored only at its lowest-id
@@ -78,17 +98,35 @@ __device__ uint64_t block_select_kth(const uint64_t* a, int na, const uint64_t* 
             if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1u);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int rem = s_rem, digit = 255;
-            for (int d = 0; d < 256; ++d) {
-                if ((int)hist[d] >= rem) {
-                    digit = d;
-                    break;
-                }
-                rem -= (int)hist[d];
+        if (threadIdx.x < 32) {
+            // warp scan over 256 bins, 8 per lane: the digit where the running count reaches rem
+            const int lane = threadIdx.x;
+            const int rem = s_rem;
+            int local = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) local += (int)hist[lane * 8 + t];
+            int inc = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                int v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+                if (lane >= o) inc += v;
             }
-            s_rem = rem;
-            s_prefix = prefix | ((uint64_t)digit << shift);
+            const int excl = inc - local;
+            const unsigned hit = __ballot_sync(0xFFFFFFFFu, excl < rem && inc >= rem);
+            const int src = hit ? __ffs(hit) - 1 : 31;
+            if (lane == src) {
+                int r = rem - excl, digit = lane * 8 + 7;
+                for (int t = 0; t < 8; ++t) {
+                    int hv = (int)hist[lane * 8 + t];
+                    if (hv >= r) {
+                        digit = lane * 8 + t;
+                        break;
+                    }
+                    r -= hv;
+                }
+                s_rem = r;
+                s_prefix = prefix | ((uint64_t)digit << shift);
+            }
         }
         mask |= 0xFFull << shift;
         __syncthreads();
@@ -210,12 +248,14 @@ __global__ void __launch_bounds__(kBS) k_encode(IndexView ix, const float* __res
     }
     if (want_cqs && threadIdx.x == 32) {
         float b = 0.0f;
-        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(x[t], ix.csq_min[t]));
+#pragma unroll 16
+        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(ix.csq_min + t)));
         e.cqbase[q] = b;
     }
     if (want_rqs && threadIdx.x == 64) {
         float b = 0.0f;
-        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(x[t], ix.sq_min[t]));
+#pragma unroll 16
+        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(ix.sq_min + t)));
         e.rbase[q] = b;
     }
     if (want_cqs)
@@ -268,45 +308,61 @@ __device__ int warp_hist_cut(const uint32_t* hist, int bits, long long want) {
     return res;
 }
 
-__global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int want_c, int all, uint32_t* sl,
-                                                    uint32_t* sl_n, int sl_cap) {
-    extern __shared__ uint32_t hist[];
-    __shared__ uint64_t qb[16];
-    __shared__ int s_cut;
-    __shared__ uint32_t s_count;
-    const int q = blockIdx.x, nw = ix.nw, bits = nw * 64, M = ix.M;
-    // `all` lists every live cell and needs no query code (e carries no buffers then)
-    if (!all && threadIdx.x < nw) qb[threadIdx.x] = e.qbits[(size_t)q * nw + threadIdx.x];
-    for (int i = threadIdx.x; i <= bits; i += kBS) hist[i] = 0;
-    if (threadIdx.x == 0) s_count = 0;
-    __syncthreads();
-    int cut = bits;
+constexpr int kRouteQB = 8;  // queries per CTA of the flat router (one warp each in pass 2)
+
+// Pass 1: every centroid code is loaded once per CTA and scored against kRouteQB queries; the
+// Hamming values go to `hs` (nq x M) and a per-query histogram. Pass 2: warp j finds query j's
+// counting cut-off and compacts its shortlist in cell order with ballots.
+__global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int nq, int want_c, int all,
+                                                    uint16_t* hs, uint32_t* sl, uint32_t* sl_n, int sl_cap) {
+    extern __shared__ uint32_t hist[];  // kRouteQB x (bits + 1)
+    __shared__ uint64_t qb[kRouteQB][16];
+    const int q0 = blockIdx.x * kRouteQB, nw = ix.nw, bits = nw * 64, M = ix.M;
+    const int nqb = min(kRouteQB, nq - q0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (!all) {
-        for (int c = threadIdx.x; c < M; c += kBS)
-            if (ix.live[c]) atomicAdd(&hist[ham_row(qb, ix.cent_bits + (size_t)c * nw, nw)], 1u);
+        for (int i = threadIdx.x; i < kRouteQB * 16; i += kBS) {
+            int j = i / 16, w = i % 16;
+            qb[j][w] = (j < nqb && w < nw) ? e.qbits[(size_t)(q0 + j) * nw + w] : 0ull;
+        }
+        for (int i = threadIdx.x; i < kRouteQB * (bits + 1); i += kBS) hist[i] = 0;
         __syncthreads();
-        if (threadIdx.x < 32) {
-            int t = want_c == 0 ? 0 : warp_hist_cut(hist, bits, want_c);
-            if (threadIdx.x == 0) s_cut = t;
+        for (int c = threadIdx.x; c < M; c += kBS) {
+            if (!ix.live[c]) continue;
+            const uint64_t* src = ix.cent_bits + (size_t)c * nw;
+            uint32_t h[kRouteQB];
+#pragma unroll
+            for (int j = 0; j < kRouteQB; ++j) h[j] = 0;
+            for (int w = 0; w < nw; ++w) {
+                const uint64_t cw = __ldg(src + w);
+#pragma unroll
+                for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw);
+            }
+#pragma unroll
+            for (int j = 0; j < kRouteQB; ++j) {
+                if (j < nqb) {
+                    hs[(size_t)(q0 + j) * M + c] = (uint16_t)h[j];
+                    atomicAdd(&hist[j * (bits + 1) + h[j]], 1u);
+                }
+            }
         }
         __syncthreads();
-        cut = s_cut;
     }
-    using BS = cub::BlockScan<uint32_t, kBS>;
-    __shared__ typename BS::TempStorage scan;
-    for (int base = 0; base < M; base += kBS) {
-        int c = base + threadIdx.x;
-        uint32_t f = 0;
-        if (c < M && ix.live[c]) f = all ? 1u : (ham_row(qb, ix.cent_bits + (size_t)c * nw, nw) <= (uint32_t)cut ? 1u : 0u);
-        uint32_t pos, agg;
-        BS(scan).ExclusiveSum(f, pos, agg);
-        uint32_t off = s_count;
-        if (f && off + pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + off + pos] = (uint32_t)c;
-        __syncthreads();
-        if (threadIdx.x == 0) s_count = off + agg;
-        __syncthreads();
+    if (warp >= nqb) return;
+    const int q = q0 + warp;
+    int cut = bits;
+    if (!all) cut = want_c == 0 ? 0 : warp_hist_cut(hist + warp * (bits + 1), bits, want_c);
+    const uint16_t* hq = hs + (size_t)q * M;
+    uint32_t count = 0;
+    for (int base = 0; base < M; base += 32) {
+        const int c = base + lane;
+        bool f = c < M && ix.live[c] && (all || hq[c] <= (uint16_t)cut);
+        unsigned m = __ballot_sync(0xFFFFFFFFu, f);
+        uint32_t pos = count + (uint32_t)__popc(m & ((1u << lane) - 1u));
+        if (f && pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + pos] = (uint32_t)c;
+        count += (uint32_t)__popc(m);
     }
-    if (threadIdx.x == 0) sl_n[q] = s_count;
+    if (lane == 0) sl_n[q] = count;
 }
 
 // ---- tree descent ---------------------------------------------------------------------------------
@@ -538,28 +594,43 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     uint64_t* sbuf = b.seed_buf + (size_t)q * b.seed_cap;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
     const uint32_t maxk = ix.maxk;
-    for (int r = 0; r < ns; ++r) {
+    // (cell, 32-group chunk) work items of the seed cells, spread over all warps
+    __shared__ int s_items[kSeedCells + 1];
+    if (threadIdx.x == 0) {
+        s_items[0] = 0;
+        for (int r = 0; r < ns; ++r) {
+            uint32_t c = ch[r];
+            int ng = (int)((ix.cell_moff[c + 1] - ix.cell_moff[c] + 7) >> 3);
+            s_items[r + 1] = s_items[r] + (ng + 31) / 32;
+        }
+    }
+    __syncthreads();
+    const int n_items = s_items[ns];
+    for (int it = warp; it < n_items; it += nwarps) {
+        int r = 0;
+        while (s_items[r + 1] <= it) ++r;
+        const int chk = it - s_items[r];
         const uint32_t c = ch[r];
         const uint32_t moff = ix.cell_moff[c];
         const int nc = (int)(ix.cell_moff[c + 1] - moff);
         const int ng = (nc + 7) >> 3;
         const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
-        for (int chk = warp; chk * 32 < ng; chk += nwarps) {
-            int g = chk * 32 + lane;
-            bool act = g < ng;
-            uint32_t acc[4];
-            group_sums(codes, ng, g, act, lut_s, npos, acc);
-            if (act) {
-                for (int bb = 0; bb < 8; ++bb) {
-                    int pos = 8 * g + bb;
-                    if (pos >= nc) break;
-                    uint32_t d = maxk - member_sum(acc, bb);
-                    uint32_t slot = ix.cell_slots[moff + pos];
-                    if (ix.ma > 1 && !canonical_cm(ix, slot, c, probed)) continue;
-                    uint32_t p = atomicAdd(&s_n, 1u);
-                    if (p < (uint32_t)b.seed_cap) sbuf[p] = ((uint64_t)d << 32) | slot;
-                }
+        const int g = chk * 32 + lane;
+        const bool act = g < ng;
+        uint32_t acc[4];
+        group_sums(codes, ng, g, act, lut_s, npos, acc);
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb) {
+            const int pos = 8 * g + bb;
+            bool valid = act && pos < nc;
+            uint32_t d = 0, slot = 0;
+            if (valid) {
+                d = maxk - member_sum(acc, bb);
+                slot = ix.cell_slots[moff + pos];
+                if (ix.ma > 1) valid = canonical_cm(ix, slot, c, probed);
             }
+            uint32_t p = warp_append(valid, &s_n);
+            if (valid && p < (uint32_t)b.seed_cap) sbuf[p] = ((uint64_t)d << 32) | slot;
         }
     }
     __syncthreads();
@@ -683,16 +754,21 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
             const uint32_t t = b.tau[q];
             uint32_t acc[4];
             group_sums(codes, ng, g, act, e.lut + (size_t)q * npos * 16, npos, acc);
-            if (!act) continue;
+#pragma unroll
             for (int bb = 0; bb < 8; ++bb) {
-                int pos = 8 * g + bb;
-                if (pos >= nc) break;
-                uint32_t d = maxk - member_sum(acc, bb);
-                if (d > t) continue;
-                uint32_t slot = ix.cell_slots[moff + pos];
-                if (ix.ma > 1 && !canonical_cm(ix, slot, c, b.probed + (size_t)q * b.mwords)) continue;
-                uint32_t p = atomicAdd(&b.rest_n[q], 1u);
-                if (p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)q * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
+                const int pos = 8 * g + bb;
+                bool valid = act && pos < nc;
+                uint32_t d = 0, slot = 0;
+                if (valid) {
+                    d = maxk - member_sum(acc, bb);
+                    valid = d <= t;
+                }
+                if (valid) {
+                    slot = ix.cell_slots[moff + pos];
+                    if (ix.ma > 1) valid = canonical_cm(ix, slot, c, b.probed + (size_t)q * b.mwords);
+                }
+                uint32_t p = warp_append(valid, &b.rest_n[q]);
+                if (valid && p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)q * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
             }
         }
     }
@@ -948,6 +1024,78 @@ __device__ __forceinline__ bool better(float sa, uint64_t ia, float sb, uint64_t
     return sa > sb || (sa == sb && ia < ib);
 }
 
+// The 8 SIMD-lane accumulators of the reference's AVX2 dots, kept by one thread, closed with the
+// hsum_ps tree (src/index.rs:58-65).
+__device__ __forceinline__ float close8(const float a[8]) {
+    float s0 = __fadd_rn(a[0], a[4]), s1 = __fadd_rn(a[1], a[5]), s2 = __fadd_rn(a[2], a[6]),
+          s3 = __fadd_rn(a[3], a[7]);
+    return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+
+// dot_f32 (index.rs:136-152) of the shared-memory query with one f32 row, 32 bytes per step.
+__device__ __forceinline__ float row_dot_f32(const float* qv, const float* __restrict__ row, int dim) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int full = dim & ~7;
+    if ((dim & 3) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        const float4* q4 = reinterpret_cast<const float4*>(qv);
+#pragma unroll 4
+        for (int g = 0; g < full / 8; ++g) {
+            float4 x0 = __ldg(r4 + 2 * g), x1 = __ldg(r4 + 2 * g + 1);
+            float4 y0 = q4[2 * g], y1 = q4[2 * g + 1];
+            a[0] = __fmaf_rn(y0.x, x0.x, a[0]);
+            a[1] = __fmaf_rn(y0.y, x0.y, a[1]);
+            a[2] = __fmaf_rn(y0.z, x0.z, a[2]);
+            a[3] = __fmaf_rn(y0.w, x0.w, a[3]);
+            a[4] = __fmaf_rn(y1.x, x1.x, a[4]);
+            a[5] = __fmaf_rn(y1.y, x1.y, a[5]);
+            a[6] = __fmaf_rn(y1.z, x1.z, a[6]);
+            a[7] = __fmaf_rn(y1.w, x1.w, a[7]);
+        }
+    } else {
+        for (int i = 0; i < full; ++i) a[i & 7] = __fmaf_rn(qv[i], __ldg(row + i), a[i & 7]);
+    }
+    float s = close8(a);
+    for (int i = full; i < dim; ++i) s = __fadd_rn(s, __fmul_rn(qv[i], __ldg(row + i)));
+    return s;
+}
+
+// dot_f32_u8 / dot_f32_i8 (index.rs:278-294, :161-177) of the shared-memory weights with one
+// byte row, 8 bytes per step.
+template <bool kSigned>
+__device__ __forceinline__ float row_dot_bytes(const float* qv, const uint8_t* __restrict__ row, int dim) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int full = dim & ~7;
+    auto cvt = [](uint32_t w, int b) -> float {
+        uint32_t v = (w >> (8 * b)) & 0xFFu;
+        return kSigned ? (float)(int8_t)v : (float)v;
+    };
+    if ((dim & 7) == 0) {
+        const uint2* r2 = reinterpret_cast<const uint2*>(row);
+        const float4* q4 = reinterpret_cast<const float4*>(qv);
+#pragma unroll 4
+        for (int g = 0; g < full / 8; ++g) {
+            uint2 w = __ldg(r2 + g);
+            float4 y0 = q4[2 * g], y1 = q4[2 * g + 1];
+            a[0] = __fmaf_rn(y0.x, cvt(w.x, 0), a[0]);
+            a[1] = __fmaf_rn(y0.y, cvt(w.x, 1), a[1]);
+            a[2] = __fmaf_rn(y0.z, cvt(w.x, 2), a[2]);
+            a[3] = __fmaf_rn(y0.w, cvt(w.x, 3), a[3]);
+            a[4] = __fmaf_rn(y1.x, cvt(w.y, 0), a[4]);
+            a[5] = __fmaf_rn(y1.y, cvt(w.y, 1), a[5]);
+            a[6] = __fmaf_rn(y1.z, cvt(w.y, 2), a[6]);
+            a[7] = __fmaf_rn(y1.w, cvt(w.y, 3), a[7]);
+        }
+    } else {
+        for (int i = 0; i < full; ++i) a[i & 7] = __fmaf_rn(qv[i], cvt(__ldg(row + i), 0), a[i & 7]);
+    }
+    float s = close8(a);
+    for (int i = full; i < dim; ++i) s = __fadd_rn(s, __fmul_rn(qv[i], cvt(__ldg(row + i), 0)));
+    return s;
+}
+
+// One CTA per query, one thread per candidate row; the best k by (score desc, external id asc)
+// are kept across chunks of 1024 candidates by a bitonic sort in shared memory.
 __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __restrict__ Q, QueryEnc e,
                                                 const uint32_t* __restrict__ cand, const uint32_t* __restrict__ cand_n,
                                                 int cand_cap, int k, int P, uint64_t* ids, float* scores,
@@ -955,46 +1103,42 @@ __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __res
     extern __shared__ uint64_t rsm[];
     uint64_t* sid = rsm;                                   // P ids
     float* ssc = reinterpret_cast<float*>(sid + P);        // P scores
-    float* qv = ssc + P;                                   // dim
+    float* qv = ssc + P;                                   // dim (16-byte aligned: P is a power of two >= 1024)
     const int q = blockIdx.x, dim = ix.dim;
     const int n = (int)cand_n[q];
     const float* qsrc = ix.rerank_mode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
     for (int t = threadIdx.x; t < dim; t += kBS) qv[t] = qsrc[t];
-    for (int i = threadIdx.x; i < P; i += kBS) {
+    for (int i = threadIdx.x; i < k; i += kBS) {
         sid[i] = ~0ull;
         ssc[i] = -INFINITY;
     }
-    __syncthreads();
     const float base = ix.rerank_mode == 1 ? e.rbase[q] : 0.0f;
-    const int l8 = threadIdx.x & 7;
-    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
     const uint32_t* cq = cand + (size_t)q * cand_cap;
     for (int c0 = 0; c0 < n; c0 += kRerankChunk) {
         const int cn = min(kRerankChunk, n - c0);
-        for (int i = k + threadIdx.x; i < P; i += kBS) {
+        const int Pe = next_pow2(k + cn);
+        for (int i = k + threadIdx.x; i < Pe; i += kBS) {
             sid[i] = ~0ull;
             ssc[i] = -INFINITY;
         }
         __syncthreads();
-        for (int i = threadIdx.x >> 3; i < cn; i += kBS / 8) {
-            uint32_t slot = cq[c0 + i];
+        for (int i = threadIdx.x; i < cn; i += kBS) {
+            const uint32_t slot = cq[c0 + i];
             float s;
             if (ix.rerank_mode == 0)
-                s = dot_f32_g8(qv, ix.vecs_f32 + (size_t)slot * dim, dim, l8, gmask);
+                s = row_dot_f32(qv, ix.vecs_f32 + (size_t)slot * dim, dim);
             else if (ix.rerank_mode == 1)
-                s = __fadd_rn(base, dot_f32_u8_g8(qv, ix.rr_u8 + (size_t)slot * dim, dim, l8, gmask));
+                s = __fadd_rn(base, row_dot_bytes<false>(qv, ix.rr_u8 + (size_t)slot * dim, dim));
             else
-                s = dot_f32_i8_g8(qv, reinterpret_cast<const int8_t*>(ix.rr_u8) + (size_t)slot * dim, dim, l8, gmask);
-            if (l8 == 0) {
-                sid[k + i] = ix.ext_ids[slot];
-                ssc[k + i] = s;
-            }
+                s = row_dot_bytes<true>(qv, ix.rr_u8 + (size_t)slot * dim, dim);
+            sid[k + i] = ix.ext_ids[slot];
+            ssc[k + i] = s;
         }
         __syncthreads();
-        // bitonic sort of the P (score, id) pairs, best first
-        for (int kk = 2; kk <= P; kk <<= 1) {
+        // bitonic sort of the Pe (score, id) pairs, best first
+        for (int kk = 2; kk <= Pe; kk <<= 1) {
             for (int j = kk >> 1; j > 0; j >>= 1) {
-                for (int i = threadIdx.x; i < P; i += kBS) {
+                for (int i = threadIdx.x; i < Pe; i += kBS) {
                     int ixj = i ^ j;
                     if (ixj > i) {
                         float sa = ssc[i], sb = ssc[ixj];
@@ -1013,6 +1157,7 @@ __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __res
             }
         }
     }
+    __syncthreads();
     const int m = min(k, n);
     for (int i = threadIdx.x; i < k; i += kBS) {
         bool v = i < m;
@@ -1026,6 +1171,75 @@ __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __res
 
 // ---- launchers ----------------------------------------------------------------------------------------
 
+namespace {
+thread_local KernelClock* t_clock = nullptr;
+std::atomic<unsigned long long> g_launches{0};
+
+// Brackets one kernel launch: counts it and, with a clock installed, records its events.
+struct Tick {
+    cudaStream_t st;
+    Tick(int id, cudaStream_t s) : st(s) {
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        if (t_clock) t_clock->begin(id, st);
+    }
+    ~Tick() {
+        if (t_clock) t_clock->end(st);
+    }
+};
+}  // namespace
+
+const char* kernel_name(int id) {
+    static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
+                                             "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
+                                             "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
+                                             "k_pq_fold", "k_rerank"};
+    return id >= 0 && id < kNumKernels ? names[id] : "?";
+}
+
+KernelClock::~KernelClock() {
+    for (auto& m : pending) {
+        cudaEventDestroy(m.a);
+        cudaEventDestroy(m.b);
+    }
+    for (auto e : pool) cudaEventDestroy(e);
+}
+
+cudaEvent_t KernelClock::take() {
+    if (!pool.empty()) {
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void KernelClock::begin(int id, cudaStream_t st) {
+    Mark m{id, take(), take()};
+    cudaEventRecord(m.a, st);
+    pending.push_back(m);
+    launches[id] += 1;
+}
+
+void KernelClock::end(cudaStream_t st) {
+    if (!pending.empty()) cudaEventRecord(pending.back().b, st);
+}
+
+void KernelClock::collect() {
+    for (auto& m : pending) {
+        float t = 0.0f;
+        if (cudaEventSynchronize(m.b) == cudaSuccess && cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess)
+            ms[m.id] += t;
+        pool.push_back(m.a);
+        pool.push_back(m.b);
+    }
+    pending.clear();
+}
+
+void set_thread_clock(KernelClock* c) { t_clock = c; }
+unsigned long long total_launches() { return g_launches.load(); }
+
 static void set_smem(const void* f, size_t bytes) {
     if (bytes > 48 * 1024) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
@@ -1034,21 +1248,24 @@ void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& 
                    cudaStream_t st) {
     if (nq <= 0) return;
     size_t smem = (size_t)(ix.dim_pad + ix.npos) * sizeof(float);
+    Tick tk(kKEncode, st);
     k_encode<<<nq, kBS, smem, st>>>(ix, Q, e, want_cqs ? 1 : 0, want_rqs ? 1 : 0);
 }
 
-void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint32_t* sl, uint32_t* sl_n,
-                       int sl_cap, cudaStream_t st) {
+void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint16_t* hs, uint32_t* sl,
+                       uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
-    size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
-    k_route_flat<<<nq, kBS, smem, st>>>(ix, e, want_c, 0, sl, sl_n, sl_cap);
+    size_t smem = (size_t)kRouteQB * (ix.nw * 64 + 1) * sizeof(uint32_t);
+    set_smem((const void*)k_route_flat, smem);
+    Tick tk(kKRouteFlat, st);
+    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, smem, st>>>(ix, e, nq, want_c, 0, hs, sl, sl_n, sl_cap);
 }
 
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
     QueryEnc e{};
-    size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
-    k_route_flat<<<nq, kBS, smem, st>>>(ix, e, 0, 1, sl, sl_n, sl_cap);
+    Tick tk(kKRouteFlat, st);
+    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, nullptr, sl, sl_n, sl_cap);
 }
 
 void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,
@@ -1057,6 +1274,7 @@ void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int
     Beams bm{};
     for (int i = 0; i < ix.tree_depth && i < kMaxTreeLevels; ++i) bm.b[i] = beams[i];
     size_t smem = (size_t)(ix.nw * 64 + 1) * sizeof(uint32_t);
+    Tick tk(kKRouteTree, st);
     k_route_tree<<<nq, kBS, smem, st>>>(ix, e, bm, want, scratch, scratch_cap, sl, sl_n, sl_cap);
 }
 
@@ -1067,6 +1285,7 @@ void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* 
     int P = next_pow2(std::min(std::max(sl_cap, 1), kSortCap));
     size_t smem = (size_t)P * sizeof(uint64_t) + (size_t)ix.dim * sizeof(float);
     set_smem((const void*)k_rescore_select, smem);
+    Tick tk(kKRescore, st);
     k_rescore_select<<<nq, kBS, smem, st>>>(ix, e, Q, sl, sl_n, sl_cap, nprobe, tc, beta, use_sq8 ? 1 : 0, chosen,
                                             cscore, nch, err);
 }
@@ -1076,28 +1295,37 @@ void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint
                       const CellMajorBufs& b, cudaStream_t st) {
     if (nq <= 0) return;
     size_t lut_bytes = (size_t)ix.npos * 16;
-    k_seed<<<nq, kBS, lut_bytes, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b);
+    { Tick tk(kKSeed, st);
+    k_seed<<<nq, kBS, lut_bytes, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b); }
     cudaMemsetAsync(b.cell_cnt, 0, sizeof(uint32_t) * (ix.M + 1), st);
     cudaMemsetAsync(b.cell_fill, 0, sizeof(uint32_t) * ix.M, st);
     int wb = (nq + 7) / 8;
-    k_inv_count<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt);
-    k_inv_scan<<<1, 1024, 0, st>>>(b.cell_cnt, ix.M);
-    k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof);
-    k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b);
-    k_final_cm<<<nq, kBS, 0, st>>>(b, target);
+    { Tick tk(kKInvCount, st);
+    k_inv_count<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt); }
+    { Tick tk(kKInvScan, st);
+    k_inv_scan<<<1, 1024, 0, st>>>(b.cell_cnt, ix.M); }
+    { Tick tk(kKInvScatter, st);
+    k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof); }
+    { Tick tk(kKScanCm, st);
+    k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b); }
+    { Tick tk(kKFinalCm, st);
+    k_final_cm<<<nq, kBS, 0, st>>>(b, target); }
 }
 
 void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
                      const uint32_t* nch, int nprobe, int want0, bool adaptive, float at_margin, bool filtering,
                      uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st) {
     if (nq <= 0) return;
-    k_pq_prep<<<nq, kBS, 0, st>>>(ix, chosen, nch, nprobe, b);
-    k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b);
+    { Tick tk(kKPqPrep, st);
+    k_pq_prep<<<nq, kBS, 0, st>>>(ix, chosen, nch, nprobe, b); }
+    { Tick tk(kKPqScan, st);
+    k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b); }
     int nb = (int)(ix.maxk >> 6) + 1;
     size_t smem = (size_t)nb * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
     set_smem((const void*)k_pq_fold, smem);
     int target = std::max(want0, 1);
-    k_pq_fold<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b);
+    { Tick tk(kKPqFold, st);
+    k_pq_fold<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b); }
 }
 
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
@@ -1107,6 +1335,7 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
     int P = next_pow2(k + kRerankChunk);
     size_t smem = (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (size_t)ix.dim * sizeof(float);
     set_smem((const void*)k_rerank, smem);
+    Tick tk(kKRerank, st);
     k_rerank<<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, ids, scores, out_n);
 }
 

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace maivs {
 namespace dev {
 
@@ -46,6 +48,33 @@ struct IndexView {
     int n_leaf;
 };
 
+// Per-kernel device clock. When a clock is installed on the calling thread, every launcher
+// brackets its kernels with CUDA events on the launch stream; the owner reads the elapsed times
+// after synchronising. Every launch is counted whether or not a clock is installed.
+enum KernelId : int {
+    kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
+    kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kNumKernels
+};
+const char* kernel_name(int id);
+struct KernelClock {
+    struct Mark {
+        int id;
+        cudaEvent_t a, b;
+    };
+    std::vector<Mark> pending;
+    std::vector<cudaEvent_t> pool;
+    double ms[kNumKernels] = {0};
+    unsigned long long launches[kNumKernels] = {0};
+    ~KernelClock();
+    cudaEvent_t take();
+    void begin(int id, cudaStream_t st);
+    void end(cudaStream_t st);
+    // Accumulates the elapsed times of every pending mark (their events must have completed).
+    void collect();
+};
+void set_thread_clock(KernelClock* c);
+unsigned long long total_launches();
+
 constexpr int kMaxTreeLevels = 8;
 constexpr int kSeedCells = 8;  // index.rs:2019 SEED_CELLS
 constexpr int kSortCap = 16384;  // largest shortlist sorted in shared memory
@@ -67,8 +96,9 @@ void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& 
                    cudaStream_t st);
 // Flat two-stage shortlist: live cells with Hamming <= the want_c-th smallest, ties kept, in cell
 // order (index.rs:1903-1927 route_batch, :1241-1259 route_query).
-void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint32_t* sl, uint32_t* sl_n,
-                       int sl_cap, cudaStream_t st);
+// `hs` is nq x M scratch for the Hamming distances.
+void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint16_t* hs, uint32_t* sl,
+                       uint32_t* sl_n, int sl_cap, cudaStream_t st);
 // Every live cell, in cell order (index.rs:1274-1282).
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st);
 // Centroid-tree beam descent (tree.rs:574-628); `beams` per level, `want` leaves.
