@@ -127,6 +127,22 @@ uint64_t maivs_launch_count(void);
 int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, double* values, size_t cap,
                             size_t* n_out);
 
+/* Diagnostics (no counterpart in the reference): run one search (host buffers) only up to
+ * `stage` and return its intermediate results - stage 0: query sign codes (nq x nw words),
+ * FastScan tables (nq x 16*npos bytes), their delta and bias; stage 1: probe lists (nq x nprobe,
+ * UINT32_MAX padded), re-order scores and counts; stage 2: the candidate slots sent to the exact
+ * rerank, ascending (nq x cand_cap, UINT32_MAX padded) and their counts. Any output may be NULL. */
+int maivs_debug_stage(maivs_index* ix, int stage, const float* queries, size_t nq, size_t k, size_t nprobe,
+                      float target_confidence, float beta, int cell_major, uint64_t* qbits, uint8_t* lut,
+                      float* delta, float* bias, uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* cand,
+                      size_t cand_cap, uint32_t* cand_n);
+
+/* Diagnostics: per-query internals of the cell-major join for one batch - seed survivors, seed
+ * cut-off tau, end of the unpruned probe range, survivors of the scan - and the CUDA status. */
+int maivs_debug_cellmajor(maivs_index* ix, const float* queries, size_t nq, size_t k, size_t nprobe,
+                          float target_confidence, float beta, uint32_t* seed_n, uint32_t* tau, uint32_t* rest_hi,
+                          uint32_t* rest_n, char* info, size_t info_cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -238,6 +238,48 @@ class FlatCellIndex:
         names = buf.value.decode().split("\n")
         return {names[i]: float(vals[i]) for i in range(got.value)}
 
+    def debug_stage(self, stage: int, queries: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+                    beta: float = 8.0, cell_major: bool = True, cand_cap: int = 4096) -> dict:
+        """Run one search only up to `stage` (0 codes/tables, 1 probe lists, 2 rerank candidates)."""
+        Q = _as_f32_matrix(queries, "queries", self._dim)
+        nq = Q.shape[0]
+        cfg = self.array("config")
+        nw = int(cfg[2])
+        out = {}
+        z = C.c_void_p(None)
+        if stage == 0:
+            out["qbits"] = np.zeros((nq, nw), np.uint64)
+            out["lut"] = np.zeros((nq, nw * 256), np.uint8)
+            out["delta"] = np.zeros(nq, np.float32)
+            out["bias"] = np.zeros(nq, np.float32)
+            args = [_ptr(out["qbits"]), _ptr(out["lut"]), _ptr(out["delta"]), _ptr(out["bias"]), z, z, z, z, 0, z]
+        elif stage == 1:
+            out["chosen"] = np.zeros((nq, nprobe), np.uint32)
+            out["cscore"] = np.zeros((nq, nprobe), np.float32)
+            out["nch"] = np.zeros(nq, np.uint32)
+            args = [z, z, z, z, _ptr(out["chosen"]), _ptr(out["cscore"]), _ptr(out["nch"]), z, 0, z]
+        else:
+            out["cand"] = np.zeros((nq, cand_cap), np.uint32)
+            out["cand_n"] = np.zeros(nq, np.uint32)
+            args = [z, z, z, z, z, z, z, _ptr(out["cand"]), cand_cap, _ptr(out["cand_n"])]
+        self._check(_lib.lib().maivs_debug_stage(self._h, int(stage), _ptr(Q), nq, int(k), int(nprobe),
+                                                 float(target_confidence), float(beta), int(bool(cell_major)), *args))
+        return out
+
+    def debug_cellmajor(self, queries: np.ndarray, k: int, nprobe: int, target_confidence: float = 1.0,
+                        beta: float = 8.0) -> dict:
+        """Per-query internals of the cell-major join (seed survivors, tau, probe range, scan survivors)."""
+        Q = _as_f32_matrix(queries, "queries", self._dim)
+        nq = Q.shape[0]
+        out = {n: np.zeros(nq, np.uint32) for n in ("seed_n", "tau", "rest_hi", "rest_n")}
+        info = C.create_string_buffer(256)
+        self._check(_lib.lib().maivs_debug_cellmajor(self._h, _ptr(Q), nq, int(k), int(nprobe),
+                                                     float(target_confidence), float(beta), _ptr(out["seed_n"]),
+                                                     _ptr(out["tau"]), _ptr(out["rest_hi"]), _ptr(out["rest_n"]),
+                                                     info, 256))
+        out["info"] = info.value.decode()
+        return out
+
     # ---- introspection ----
     def __len__(self) -> int:
         n = C.c_size_t(0)

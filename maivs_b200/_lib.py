@@ -53,6 +53,12 @@ _SIGS = {
     "maivs_launch_count": (C.c_uint64, []),
     "maivs_last_search_stats": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double), C.c_size_t,
                                           C.POINTER(C.c_size_t)]),
+    "maivs_debug_stage": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_float,
+                                    C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "maivs_debug_cellmajor": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_float,
+                                        C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
+                                        C.c_size_t]),
     "maivs_profile": (C.c_int, [C.c_int]),
     "maivs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.c_size_t,
                                      C.POINTER(C.c_size_t)]),

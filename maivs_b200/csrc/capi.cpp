@@ -531,6 +531,118 @@ int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, doub
     return MAIVS_OK;
 }
 
+int maivs_debug_stage(maivs_index* ix, int stage, const float* Q, size_t nq, size_t k, size_t nprobe, float tc,
+                      float beta, int cell_major, uint64_t* qbits, uint8_t* lut, float* delta, float* bias,
+                      uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* cand, size_t cand_cap,
+                      uint32_t* cand_n) {
+    LOCK(ix);
+    if (nq == 0 || k == 0) return fail(ix, MAIVS_BAD_ARG, "nq and k must be positive");
+    if (!cell_major && nq > 64) return fail(ix, MAIVS_BAD_ARG, "the per-query debug path takes at most 64 queries");
+    int rc = ensure_device(ix);
+    if (rc != MAIVS_OK) return rc;
+    maivs::SearchArgs a;
+    a.nq = (int)nq;
+    a.k = (int)k;
+    a.nprobe = (int)std::min<size_t>(nprobe, 1u << 30);
+    a.tc = tc;
+    a.beta = beta;
+    a.cell_major = cell_major != 0;
+    maivs::DebugOut out;
+    out.stage = stage;
+    float* dQ = nullptr;
+    uint64_t* dI = nullptr;
+    float* dS = nullptr;
+    cudaMalloc(&dQ, nq * ix->h.dim * sizeof(float));
+    cudaMalloc(&dI, nq * k * sizeof(uint64_t));
+    cudaMalloc(&dS, nq * k * sizeof(float) + nq * sizeof(uint32_t));
+    cudaMemcpy(dQ, Q, nq * ix->h.dim * sizeof(float), cudaMemcpyHostToDevice);
+    ix->d->dbg = &out;
+    std::string err;
+    rc = ix->d->search_device(ix->h, dQ, a, dI, dS, reinterpret_cast<uint32_t*>(dS + nq * k), ix->d->stream(), err);
+    ix->d->dbg = nullptr;
+    cudaStreamSynchronize(ix->d->stream());
+    cudaFree(dQ);
+    cudaFree(dI);
+    cudaFree(dS);
+    if (rc != MAIVS_OK) return fail(ix, rc, err);
+    const size_t nw = ix->h.nw, npos = nw * 16;
+    if (stage == 0) {
+        if (qbits) std::memcpy(qbits, out.qbits.data(), nq * nw * 8);
+        if (lut) std::memcpy(lut, out.lut.data(), nq * npos * 16);
+        if (delta) std::memcpy(delta, out.delta.data(), nq * 4);
+        if (bias) std::memcpy(bias, out.bias.data(), nq * 4);
+    } else if (stage == 1) {
+        const size_t np = (size_t)out.nprobe;
+        for (size_t q = 0; q < nq; ++q) {
+            if (nch) nch[q] = out.nch[q];
+            for (size_t i = 0; i < nprobe; ++i) {
+                bool v = i < np && i < out.nch[q];
+                if (chosen) chosen[q * nprobe + i] = v ? out.chosen[q * np + i] : UINT32_MAX;
+                if (cscore) cscore[q * nprobe + i] = v ? out.cscore[q * np + i] : -INFINITY;
+            }
+        }
+    } else if (stage == 2) {
+        const size_t cc = (size_t)out.cand_cap;
+        for (size_t q = 0; q < nq; ++q) {
+            uint32_t n = out.cand_n[q];
+            if (cand_n) cand_n[q] = n;
+            if (cand) {
+                std::vector<uint32_t> v(out.cand.begin() + q * cc, out.cand.begin() + q * cc + n);
+                std::sort(v.begin(), v.end());
+                for (size_t i = 0; i < cand_cap; ++i) cand[q * cand_cap + i] = i < v.size() ? v[i] : UINT32_MAX;
+            }
+        }
+    }
+    return MAIVS_OK;
+}
+
+int maivs_debug_cellmajor(maivs_index* ix, const float* Q, size_t nq, size_t k, size_t nprobe, float tc, float beta,
+                          uint32_t* seed_n, uint32_t* tau, uint32_t* rest_hi, uint32_t* rest_n, char* info,
+                          size_t info_cap) {
+    LOCK(ix);
+    if (nq == 0 || k == 0) return fail(ix, MAIVS_BAD_ARG, "nq and k must be positive");
+    int rc = ensure_device(ix);
+    if (rc != MAIVS_OK) return rc;
+    maivs::SearchArgs a;
+    a.nq = (int)nq;
+    a.k = (int)k;
+    a.nprobe = (int)nprobe;
+    a.tc = tc;
+    a.beta = beta;
+    a.cell_major = true;
+    if (!ix->d->use_cell_major(ix->h, a)) return fail(ix, MAIVS_BAD_STATE, "this batch does not take the cell-major join");
+    maivs::DebugOut out;
+    out.stage = 2;
+    float* dQ = nullptr;
+    void* dO = nullptr;
+    cudaMalloc(&dQ, nq * ix->h.dim * sizeof(float));
+    cudaMalloc(&dO, nq * k * 16 + nq * 4);
+    cudaMemcpy(dQ, Q, nq * ix->h.dim * sizeof(float), cudaMemcpyHostToDevice);
+    ix->d->dbg = &out;
+    std::string err;
+    cudaGetLastError();
+    rc = ix->d->search_device(ix->h, dQ, a, (uint64_t*)dO, (float*)((char*)dO + nq * k * 8),
+                              (uint32_t*)((char*)dO + nq * k * 12), ix->d->stream(), err);
+    ix->d->dbg = nullptr;
+    cudaError_t ce = cudaStreamSynchronize(ix->d->stream());
+    cudaError_t le = cudaGetLastError();
+    cudaFree(dQ);
+    cudaFree(dO);
+    if (rc != MAIVS_OK) return fail(ix, rc, err);
+    for (size_t q = 0; q < nq; ++q) {
+        if (seed_n) seed_n[q] = out.seed_n[q];
+        if (tau) tau[q] = out.tau[q];
+        if (rest_hi) rest_hi[q] = out.rest_hi[q];
+        if (rest_n) rest_n[q] = out.rest_n[q];
+    }
+    if (info && info_cap) {
+        std::string s = std::string("sync=") + cudaGetErrorString(ce) + " last=" + cudaGetErrorString(le);
+        std::strncpy(info, s.c_str(), info_cap - 1);
+        info[info_cap - 1] = 0;
+    }
+    return MAIVS_OK;
+}
+
 int maivs_profile(int on) {
     g_prof_on.store(on != 0);
     return MAIVS_OK;

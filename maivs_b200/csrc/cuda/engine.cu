@@ -266,6 +266,15 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
     return kOk;
 }
 
+namespace {
+template <typename T>
+std::vector<T> fetch(const T* d, size_t n, cudaStream_t st) {
+    std::vector<T> v(n);
+    if (n) cudaMemcpyAsync(v.data(), d, n * sizeof(T), cudaMemcpyDeviceToHost, st);
+    return v;
+}
+}  // namespace
+
 int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids,
                                float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err) {
     const int nq = a.nq, M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
@@ -345,13 +354,23 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     } unset;
     if (timing_) cudaEventRecord(ev_[0], st);
     dev::launch_encode(view_, dQ, nq, e, use_sq8_, view_.rerank_mode == 1, st);
+    if (dbg && dbg->stage == 0) return debug_encode(e, nq, st);
     if (timing_) cudaEventRecord(ev_[1], st);
     rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
     if (rc != kOk) return rc;
+    if (dbg && dbg->stage == 1) return debug_route(chosen, cscore, nch, nq, nprobe, st);
     if (timing_) cudaEventRecord(ev_[2], st);
     dev::launch_cellmajor(view_, e, nq, chosen, cscore, nch, nprobe, target, h.adaptive, h.at_margin, b, st);
+    if (dbg && dbg->stage == 2) {
+        dbg->seed_n = fetch(b.seed_n, nq, st);
+        dbg->tau = fetch(b.tau, nq, st);
+        dbg->rest_hi = fetch(b.rest_hi, nq, st);
+        dbg->rest_n = fetch(b.rest_n, nq, st);
+        return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
+    }
     if (timing_) cudaEventRecord(ev_[3], st);
-    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, st);
+    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, d_flags_ + 2,
+                       st);
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
     return kOk;
@@ -426,15 +445,18 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         int nq = std::min(chunk, a.nq - q0);
         const float* Qc = dQ + (size_t)q0 * dim;
         dev::launch_encode(view_, Qc, nq, e, use_sq8_, view_.rerank_mode == 1, st);
+        if (dbg && dbg->stage == 0) return debug_encode(e, nq, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[1], st);
         rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
         if (rc != kOk) return rc;
+        if (dbg && dbg->stage == 1) return debug_route(chosen, cscore, nch, nq, nprobe, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[2], st);
         dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
                              h.filter_lo, h.filter_hi, b, st);
+        if (dbg && dbg->stage == 2) return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[3], st);
         dev::launch_rerank(view_, Qc, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids + (size_t)q0 * a.k,
-                           d_scores + (size_t)q0 * a.k, d_nout + q0, st);
+                           d_scores + (size_t)q0 * a.k, d_nout + q0, d_flags_ + 2, st);
     }
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
@@ -458,9 +480,17 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
     if (a.nq <= 0) return kOk;
     cudaSetDevice(device_);
     if (!st) st = stream_;
+    dev::take_launch_error(nullptr);
     cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
-    if (use_cell_major(h, a)) return run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err);
-    return run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+    int rc = use_cell_major(h, a) ? run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err)
+                                  : run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+    int kid = -1;
+    cudaError_t le = dev::take_launch_error(&kid);
+    if (le != cudaSuccess) {
+        err = std::string("launch of ") + dev::kernel_name(kid) + " failed: " + cudaGetErrorString(le);
+        return le == cudaErrorMemoryAllocation ? kOom : kCudaError;
+    }
+    return rc;
 }
 
 int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
@@ -517,6 +547,10 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
             err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
             return kUnsupported;
         }
+        if (hF[2] != 0) {
+            err = "a rerank row copy did not complete within the wait limit";
+            return kCudaError;
+        }
         if (hF[0] == 0) break;
         if (attempt == 3) {
             err = "candidate buffers overflowed after enlarging them";
@@ -564,7 +598,9 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
     out.push_back({"rerank_bytes", cands * row_bytes});
     out.push_back({"route_code_bytes", (double)M * code_bytes});
     if (last_.cell_major) {
-        std::vector<uint32_t> start = get(last_.cell_cnt, (size_t)M + 1), seed_n = get(last_.seed_n, nq),
+        std::vector<uint32_t> start = np > dev::kSeedCells ? get(last_.cell_cnt, (size_t)M + 1)
+                                                           : std::vector<uint32_t>((size_t)M + 1, 0),
+                              seed_n = get(last_.seed_n, nq),
                               rest_n = get(last_.rest_n, nq), rest_hi = get(last_.rest_hi, nq);
         double cells = 0, bytes = 0, pairs = 0, seed_pairs = 0, seed_kept = 0, rest_kept = 0, rest_probes = 0;
         std::vector<uint8_t> seen(M, 0);
@@ -604,6 +640,33 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
         out.push_back({"rest_probes", rest_probes});
     }
     return out;
+}
+
+int DeviceIndex::debug_encode(const dev::QueryEnc& e, int nq, cudaStream_t st) {
+    dbg->qbits = fetch(e.qbits, (size_t)nq * view_.nw, st);
+    dbg->lut = fetch(e.lut, (size_t)nq * view_.npos * 16, st);
+    dbg->delta = fetch(e.fs_delta, nq, st);
+    dbg->bias = fetch(e.fs_bias, nq, st);
+    cudaStreamSynchronize(st);
+    return kOk;
+}
+
+int DeviceIndex::debug_route(const uint32_t* chosen, const float* cscore, const uint32_t* nch, int nq, int nprobe,
+                             cudaStream_t st) {
+    dbg->nprobe = nprobe;
+    dbg->chosen = fetch(chosen, (size_t)nq * nprobe, st);
+    dbg->cscore = fetch(cscore, (size_t)nq * nprobe, st);
+    dbg->nch = fetch(nch, nq, st);
+    cudaStreamSynchronize(st);
+    return kOk;
+}
+
+int DeviceIndex::debug_cands(const uint32_t* cand, const uint32_t* cand_n, int nq, int cap, cudaStream_t st) {
+    dbg->cand_cap = cap;
+    dbg->cand = fetch(cand, (size_t)nq * cap, st);
+    dbg->cand_n = fetch(cand_n, nq, st);
+    cudaStreamSynchronize(st);
+    return kOk;
 }
 
 PhaseTimes DeviceIndex::collect_phases() {

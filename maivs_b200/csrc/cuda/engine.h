@@ -43,8 +43,23 @@ struct PhaseTimes {
     float encode = 0, route = 0, scan = 0, rerank = 0;
 };
 
+// Intermediate buffers of a search stopped after one stage (parity tests and diagnostics):
+// stage 0 = query codes and FastScan tables, 1 = probe lists, 2 = candidate slots sent to rerank.
+struct DebugOut {
+    int stage = 0;
+    int nprobe = 0, cand_cap = 0;
+    std::vector<uint64_t> qbits;
+    std::vector<uint8_t> lut;
+    std::vector<float> delta, bias, cscore;
+    std::vector<uint32_t> chosen, nch, cand, cand_n;
+    std::vector<uint32_t> seed_n, tau, rest_hi, rest_n;  // cell-major only (stage 2)
+};
+
 class DeviceIndex {
    public:
+    // When set, the next search stops after dbg->stage and fills *dbg (synchronous).
+    DebugOut* dbg = nullptr;
+
     ~DeviceIndex();
     // Builds the device image from a compacted FastScan host index; returns an error message.
     std::string upload(const HostIndex& h, int device);
@@ -85,6 +100,10 @@ class DeviceIndex {
     int ensure_ws(size_t bytes, std::string& err);
     int run_cellmajor(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                       uint32_t* d_nout, cudaStream_t st, std::string& err);
+    int debug_encode(const dev::QueryEnc& e, int nq, cudaStream_t st);
+    int debug_route(const uint32_t* chosen, const float* cscore, const uint32_t* nch, int nq, int nprobe,
+                    cudaStream_t st);
+    int debug_cands(const uint32_t* cand, const uint32_t* cand_n, int nq, int cap, cudaStream_t st);
     int run_perquery(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                      uint32_t* d_nout, cudaStream_t st, std::string& err);
     int route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc, float beta,

@@ -264,6 +264,124 @@ __global__ void __launch_bounds__(kBS) k_encode(IndexView ix, const float* __res
         for (int t = threadIdx.x; t < dim; t += kBS) e.rqs[(size_t)q * dim + t] = __fmul_rn(x[t], ix.sq_step[t]);
 }
 
+// One warp per query, E = dim_pad / 32 rotated coordinates per lane (lane l holds l*E .. l*E+E-1).
+// Butterflies of the FWHT with h < E stay inside a lane; h >= E pair lane l with l ^ (h / E).
+// Every level applies the reference's butterflies (quantize.rs:71-126), so the bits are the same.
+template <int E>
+__global__ void __launch_bounds__(kBS) k_encode_warp(IndexView ix, const float* __restrict__ Q, QueryEnc e, int nq,
+                                                     int want_cqs, int want_rqs) {
+    __shared__ float s_mins[kBS / 32][256];
+    __shared__ uint32_t s_mask[kBS / 32][32];
+    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * (kBS / 32) + wq;
+    if (q >= nq) return;
+    const int dp = ix.dim_pad, dim = ix.dim, npos = ix.npos;
+    const float* x = Q + (size_t)q * dim;
+    float v[E];
+#pragma unroll
+    for (int t = 0; t < E; ++t) {
+        const int i = lane * E + t;
+        v[t] = i < dim ? __ldg(x + i) : 0.0f;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dp));
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const float* sg = ix.signs + (size_t)r * dp + lane * E;
+#pragma unroll
+        for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], __ldg(sg + t));
+#pragma unroll
+        for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+            for (int t = 0; t < E; ++t) {
+                if ((t & h) == 0) {
+                    const float a = v[t], b = v[t + h];
+                    v[t] = __fadd_rn(a, b);
+                    v[t + h] = __fsub_rn(a, b);
+                }
+            }
+        }
+        for (int hl = 1; hl < 32; hl <<= 1) {  // h = hl * E
+#pragma unroll
+            for (int t = 0; t < E; ++t) {
+                const float o = __shfl_xor_sync(0xFFFFFFFFu, v[t], hl);
+                v[t] = (lane & hl) ? __fsub_rn(o, v[t]) : __fadd_rn(v[t], o);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], scale);
+    }
+    // sign bits (quantize.rs:57-67): lane masks, then one 64-bit word per assembling lane
+    uint32_t m = 0;
+#pragma unroll
+    for (int t = 0; t < E; ++t)
+        if (v[t] < 0.0f) m |= 1u << t;
+    s_mask[wq][lane] = m;
+    __syncwarp();
+    if (lane < ix.nw) {
+        uint64_t w = 0;
+        const int per = 64 / E;  // lanes per word
+        for (int u = 0; u < per; ++u) w |= (uint64_t)s_mask[wq][lane * per + u] << (u * E);
+        e.qbits[(size_t)q * ix.nw + lane] = w;
+    }
+    // FsQuery::new (quantize.rs:279-313): this lane's E/4 nibble positions
+    constexpr int PP = E / 4;
+    float lo[PP], range = 0.0f;
+    float raw[PP][16];
+#pragma unroll
+    for (int pp = 0; pp < PP; ++pp) {
+        lo[pp] = INFINITY;
+        float hi = -INFINITY;
+#pragma unroll
+        for (int ev = 0; ev < 16; ++ev) {
+            float a = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) a = ((ev >> t) & 1) ? __fsub_rn(a, v[4 * pp + t]) : __fadd_rn(a, v[4 * pp + t]);
+            raw[pp][ev] = a;
+            lo[pp] = fminf(lo[pp], a);
+            hi = fmaxf(hi, a);
+        }
+        const int j = lane * PP + pp;
+        if (j < npos) {
+            range = fmaxf(range, __fsub_rn(hi, lo[pp]));
+            s_mins[wq][j] = lo[pp];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) range = fmaxf(range, __shfl_xor_sync(0xFFFFFFFFu, range, o));
+    const float delta = fmaxf(__fdiv_rn(range, 255.0f), 1e-12f);
+#pragma unroll
+    for (int pp = 0; pp < PP; ++pp) {
+        const int j = lane * PP + pp;
+        if (j >= npos) continue;
+        uint32_t wv[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int ev = 0; ev < 16; ++ev) {
+            float qv = clampf(roundf(__fdiv_rn(__fsub_rn(raw[pp][ev], lo[pp]), delta)), 0.0f, 255.0f);
+            wv[ev >> 2] |= ((uint32_t)qv) << (8 * (ev & 3));
+        }
+        *reinterpret_cast<uint4*>(e.lut + ((size_t)q * npos + j) * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    __syncwarp();
+    // sequential sums: bias (lane 2), centroid SQ8 base (lane 0), rerank SQ8 base (lane 1)
+    if (lane == 2) {
+        float b = 0.0f;
+        for (int t = 0; t < npos; ++t) b = __fadd_rn(b, s_mins[wq][t]);
+        e.fs_delta[q] = delta;
+        e.fs_bias[q] = b;
+    }
+    if ((lane == 0 && want_cqs) || (lane == 1 && want_rqs)) {
+        const float* mn = lane == 0 ? ix.csq_min : ix.sq_min;
+        float b = 0.0f;
+#pragma unroll 16
+        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(mn + t)));
+        (lane == 0 ? e.cqbase : e.rbase)[q] = b;
+    }
+    if (want_cqs)
+        for (int t = lane; t < dim; t += 32) e.cqs[(size_t)q * dim + t] = __fmul_rn(__ldg(x + t), __ldg(ix.csq_step + t));
+    if (want_rqs)
+        for (int t = lane; t < dim; t += 32) e.rqs[(size_t)q * dim + t] = __fmul_rn(__ldg(x + t), __ldg(ix.sq_step + t));
+}
+
 // ---- K2: flat Hamming shortlist ------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t ham_row(const uint64_t* qb, const uint64_t* __restrict__ code, int nw) {
@@ -308,18 +426,24 @@ __device__ int warp_hist_cut(const uint32_t* hist, int bits, long long want) {
     return res;
 }
 
-constexpr int kRouteQB = 8;  // queries per CTA of the flat router (one warp each in pass 2)
+constexpr int kRouteQB = 4;  // queries per CTA of the flat router (one warp each in pass 2)
+constexpr int kRouteSmemH = 160 * 1024;  // Hamming rows kept in shared memory up to this size
 
 // Pass 1: every centroid code is loaded once per CTA and scored against kRouteQB queries; the
-// Hamming values go to `hs` (nq x M) and a per-query histogram. Pass 2: warp j finds query j's
-// counting cut-off and compacts its shortlist in cell order with ballots.
+// Hamming values (0xFFFF for empty cells) go to shared memory, or to the `hs` scratch (nq x M)
+// when M is too large, plus a per-query histogram. Pass 2: warp j finds query j's counting
+// cut-off and compacts its shortlist in cell order with ballots.
 __global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int nq, int want_c, int all,
-                                                    uint16_t* hs, uint32_t* sl, uint32_t* sl_n, int sl_cap) {
-    extern __shared__ uint32_t hist[];  // kRouteQB x (bits + 1)
+                                                    int h_in_smem, uint16_t* hs, uint32_t* sl, uint32_t* sl_n,
+                                                    int sl_cap) {
+    extern __shared__ uint32_t rsh[];
     __shared__ uint64_t qb[kRouteQB][16];
     const int q0 = blockIdx.x * kRouteQB, nw = ix.nw, bits = nw * 64, M = ix.M;
     const int nqb = min(kRouteQB, nq - q0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* hist = rsh;                                                     // kRouteQB x (bits + 1)
+    uint16_t* hrow = h_in_smem ? reinterpret_cast<uint16_t*>(rsh + kRouteQB * (bits + 1))
+                               : hs + (size_t)q0 * M;                         // kRouteQB x M
     if (!all) {
         for (int i = threadIdx.x; i < kRouteQB * 16; i += kBS) {
             int j = i / 16, w = i % 16;
@@ -328,21 +452,23 @@ __global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, in
         for (int i = threadIdx.x; i < kRouteQB * (bits + 1); i += kBS) hist[i] = 0;
         __syncthreads();
         for (int c = threadIdx.x; c < M; c += kBS) {
-            if (!ix.live[c]) continue;
-            const uint64_t* src = ix.cent_bits + (size_t)c * nw;
             uint32_t h[kRouteQB];
+            const bool lv = ix.live[c] != 0;
+            if (lv) {
+                const uint64_t* src = ix.cent_bits + (size_t)c * nw;
 #pragma unroll
-            for (int j = 0; j < kRouteQB; ++j) h[j] = 0;
-            for (int w = 0; w < nw; ++w) {
-                const uint64_t cw = __ldg(src + w);
+                for (int j = 0; j < kRouteQB; ++j) h[j] = 0;
+                for (int w = 0; w < nw; ++w) {
+                    const uint64_t cw = __ldg(src + w);
 #pragma unroll
-                for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw);
+                    for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw);
+                }
             }
 #pragma unroll
             for (int j = 0; j < kRouteQB; ++j) {
                 if (j < nqb) {
-                    hs[(size_t)(q0 + j) * M + c] = (uint16_t)h[j];
-                    atomicAdd(&hist[j * (bits + 1) + h[j]], 1u);
+                    hrow[(size_t)j * M + c] = lv ? (uint16_t)h[j] : (uint16_t)0xFFFF;
+                    if (lv) atomicAdd(&hist[j * (bits + 1) + h[j]], 1u);
                 }
             }
         }
@@ -352,15 +478,23 @@ __global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, in
     const int q = q0 + warp;
     int cut = bits;
     if (!all) cut = want_c == 0 ? 0 : warp_hist_cut(hist + warp * (bits + 1), bits, want_c);
-    const uint16_t* hq = hs + (size_t)q * M;
+    const uint16_t* hq = hrow + (size_t)warp * M;
     uint32_t count = 0;
-    for (int base = 0; base < M; base += 32) {
-        const int c = base + lane;
-        bool f = c < M && ix.live[c] && (all || hq[c] <= (uint16_t)cut);
-        unsigned m = __ballot_sync(0xFFFFFFFFu, f);
-        uint32_t pos = count + (uint32_t)__popc(m & ((1u << lane) - 1u));
-        if (f && pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + pos] = (uint32_t)c;
-        count += (uint32_t)__popc(m);
+    for (int base = 0; base < M; base += 128) {
+        bool f[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = base + u * 32 + lane;
+            f[u] = c < M && (all ? ix.live[c] != 0 : hq[c] <= (uint16_t)cut);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = base + u * 32 + lane;
+            unsigned m = __ballot_sync(0xFFFFFFFFu, f[u]);
+            uint32_t pos = count + (uint32_t)__popc(m & ((1u << lane) - 1u));
+            if (f[u] && pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + pos] = (uint32_t)c;
+            count += (uint32_t)__popc(m);
+        }
     }
     if (lane == 0) sl_n[q] = count;
 }
@@ -566,8 +700,9 @@ __global__ void __launch_bounds__(kBS) k_rescore_select(IndexView ix, QueryEnc e
 
 __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                               const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
-                                              int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b) {
-    extern __shared__ uint8_t lut_s[];
+                                              int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
+                                              int keys_in_smem) {
+    extern __shared__ __align__(16) uint8_t lut_s[];  // npos x 16 LUT bytes, then (optionally) the keys
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_n;
     __shared__ int s_last;
@@ -592,6 +727,8 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     }
     __syncthreads();
     uint64_t* sbuf = b.seed_buf + (size_t)q * b.seed_cap;
+    // all canonical seed entries go to `keys`: shared memory when they fit, else the global buffer
+    uint64_t* keys = keys_in_smem ? reinterpret_cast<uint64_t*>(lut_s + (size_t)npos * 16) : sbuf;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
     const uint32_t maxk = ix.maxk;
     // (cell, 32-group chunk) work items of the seed cells, spread over all warps
@@ -630,7 +767,7 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
                 if (ix.ma > 1) valid = canonical_cm(ix, slot, c, probed);
             }
             uint32_t p = warp_append(valid, &s_n);
-            if (valid && p < (uint32_t)b.seed_cap) sbuf[p] = ((uint64_t)d << 32) | slot;
+            if (valid && p < (uint32_t)b.seed_cap) keys[p] = ((uint64_t)d << 32) | slot;
         }
     }
     __syncthreads();
@@ -641,13 +778,29 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     }
     uint32_t tau = maxk;
     if (n >= target) {
-        uint64_t kk = block_select_kth(sbuf, n, nullptr, 0, target, 5, 4, hist);
+        uint64_t kk = block_select_kth(keys, n, nullptr, 0, target, 5, 4, hist);
         tau = (uint32_t)(kk >> 32);
-        // retain d <= tau (ties kept)
+    }
+    // retain d <= tau (ties kept): warps append the survivors to the global seed buffer
+    __shared__ uint32_t s_out;
+    if (keys_in_smem) {
+        if (threadIdx.x == 0) s_out = 0;
+        __syncthreads();
+        const int per = (n + nwarps - 1) / nwarps;
+        const int i0 = warp * per, i1 = min(n, i0 + per);
+        for (int base = i0; base < i1; base += 32) {
+            const int i = base + lane;
+            const uint64_t key = i < i1 ? keys[i] : ~0ull;
+            const bool keep = i < i1 && (uint32_t)(key >> 32) <= tau;
+            const uint32_t p = warp_append(keep, &s_out);
+            if (keep) sbuf[p] = key;
+        }
+        __syncthreads();
+        n = (int)s_out;
+    } else if (n >= target) {
         using BS = cub::BlockScan<uint32_t, kBS>;
         __shared__ typename BS::TempStorage scan;
-        __shared__ uint32_t s_off;
-        if (threadIdx.x == 0) s_off = 0;
+        if (threadIdx.x == 0) s_out = 0;
         __syncthreads();
         for (int base = 0; base < n; base += kBS) {
             int i = base + threadIdx.x;
@@ -656,13 +809,13 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
             uint32_t pos, agg;
             BS(scan).ExclusiveSum(f, pos, agg);
             __syncthreads();
-            uint32_t off = s_off;
+            uint32_t off = s_out;
             if (f) sbuf[off + pos] = key;
             __syncthreads();
-            if (threadIdx.x == 0) s_off = off + agg;
+            if (threadIdx.x == 0) s_out = off + agg;
             __syncthreads();
         }
-        n = (int)s_off;
+        n = (int)s_out;
     }
     int rest_end = n_ch;
     if (adaptive && n >= target && ns < n_ch) {
@@ -1167,26 +1320,225 @@ __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __res
     if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
 }
 
+// ---- exact rerank, TMA-staged rows -------------------------------------------------------------
+// Candidate rows are copied HBM -> shared memory by the bulk-copy engine (cp.async.bulk, one
+// thread issues a batch, completion on an mbarrier) into a double-buffered ring, so the gather
+// costs no per-thread load instructions. Eight threads then score one row from shared memory,
+// each running one SIMD lane's FMA chain of the reference's dot (index.rs:136-152, :278-294),
+// closed with the hsum_ps tree. Waits are bounded: a copy that does not land within the limit
+// sets err[0] and the block returns after draining.
+
+constexpr int kTmaRows = 32;          // rows per batch (8 threads per row, 256 threads)
+constexpr int kTmaSortChunk = 512;    // candidates scored between two top-k merges
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int kMode>  // 0: f32 rows, 1: per-dimension SQ8 rows, 2: global int8 rows
+__global__ void __launch_bounds__(kBS) k_rerank_tma(IndexView ix, const float* __restrict__ Q, QueryEnc e,
+                                                    const uint32_t* __restrict__ cand,
+                                                    const uint32_t* __restrict__ cand_n, int cand_cap, int k, int P,
+                                                    int row_bytes, int stride, uint64_t* ids, float* scores,
+                                                    uint32_t* out_n, uint32_t* err) {
+    extern __shared__ __align__(16) uint8_t tsm[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(tsm);               // 2 mbarriers
+    uint64_t* sid = reinterpret_cast<uint64_t*>(tsm + 16);          // P ids
+    float* ssc = reinterpret_cast<float*>(sid + P);                 // P scores
+    float* qv = ssc + P;                                            // dim, padded to 16 B
+    const int dim = ix.dim;
+    uint8_t* ring = reinterpret_cast<uint8_t*>(qv) + ((dim * 4 + 15) & ~15);  // 2 x kTmaRows x stride
+    const int q = blockIdx.x;
+    const int n = (int)cand_n[q];
+    const uint32_t* cq = cand + (size_t)q * cand_cap;
+    const float* qsrc = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
+    for (int t = threadIdx.x; t < dim; t += kBS) qv[t] = qsrc[t];
+    for (int i = threadIdx.x; i < P; i += kBS) {
+        sid[i] = ~0ull;
+        ssc[i] = -INFINITY;
+    }
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int nbatch = (n + kTmaRows - 1) / kTmaRows;
+    auto issue = [&](int b) {  // thread 0 only
+        const int r0 = b * kTmaRows, nr = min(kTmaRows, n - r0);
+        uint8_t* dst = ring + (size_t)(b & 1) * kTmaRows * stride;
+        mbar_expect_tx(&bar[b & 1], (uint32_t)(nr * row_bytes));
+        for (int r = 0; r < nr; ++r)
+            bulk_g2s(dst + (size_t)r * stride, base + (size_t)cq[r0 + r] * row_bytes, (uint32_t)row_bytes, &bar[b & 1]);
+    };
+    if (threadIdx.x == 0) {
+        if (nbatch > 0) issue(0);
+        if (nbatch > 1) issue(1);
+    }
+    const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
+    const int row = threadIdx.x >> 3, l8 = threadIdx.x & 7;
+    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+    const int full = dim & ~7;
+    bool failed = false;
+    int filled = 0;  // candidates written at [k, k + filled) since the last merge
+    for (int b = 0; b < nbatch; ++b) {
+        const bool ok = mbar_wait(&bar[b & 1], (uint32_t)((b >> 1) & 1));
+        // every thread leaves together if any thread's wait ran out
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        const int r0 = b * kTmaRows, nr = min(kTmaRows, n - r0);
+        const uint8_t* buf = ring + (size_t)(b & 1) * kTmaRows * stride;
+        if (row < nr) {
+            const uint8_t* rp = buf + (size_t)row * stride;
+            float acc = 0.0f;
+            for (int i = l8; i < full; i += 8) {
+                float x;
+                if (kMode == 0)
+                    x = reinterpret_cast<const float*>(rp)[i];
+                else if (kMode == 1)
+                    x = (float)rp[i];
+                else
+                    x = (float)(int8_t)rp[i];
+                acc = __fmaf_rn(qv[i], x, acc);
+            }
+            float sc = hsum8_group(acc, gmask);
+            if (l8 == 0) {
+                for (int i = full; i < dim; ++i) {
+                    float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
+                                         : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
+                    sc = __fadd_rn(sc, __fmul_rn(qv[i], x));
+                }
+                if (kMode == 1) sc = __fadd_rn(rbase, sc);
+                sid[k + filled + row] = ix.ext_ids[cq[r0 + row]];
+                ssc[k + filled + row] = sc;
+            }
+        }
+        __syncthreads();  // every thread is done with this buffer
+        if (threadIdx.x == 0 && b + 2 < nbatch) issue(b + 2);
+        filled += nr;
+        if (filled + kTmaRows > kTmaSortChunk || b + 1 == nbatch) {
+            const int Pe = next_pow2(k + filled);
+            for (int kk = 2; kk <= Pe; kk <<= 1) {
+                for (int j = kk >> 1; j > 0; j >>= 1) {
+                    for (int i = threadIdx.x; i < Pe; i += kBS) {
+                        int ixj = i ^ j;
+                        if (ixj > i) {
+                            float sa = ssc[i], sb = ssc[ixj];
+                            uint64_t ia = sid[i], ib = sid[ixj];
+                            bool first = (i & kk) == 0;
+                            bool sw = first ? better(sb, ib, sa, ia) : better(sa, ia, sb, ib);
+                            if (sw) {
+                                ssc[i] = sb;
+                                ssc[ixj] = sa;
+                                sid[i] = ib;
+                                sid[ixj] = ia;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            for (int i = k + threadIdx.x; i < Pe; i += kBS) {
+                sid[i] = ~0ull;
+                ssc[i] = -INFINITY;
+            }
+            __syncthreads();
+            filled = 0;
+        }
+    }
+    if (failed) {
+        // drain: wait (bounded) for every batch still in flight before the block exits
+        if (threadIdx.x == 0) {
+            atomicAdd(err, 1u);
+            // both ring slots may still be receiving: wait (bounded) for their current phases
+            for (int b = 0; b < 2; ++b) mbar_wait(&bar[b], 0), mbar_wait(&bar[b], 1);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < k; i += kBS) {
+            ids[(size_t)q * k + i] = ~0ull;
+            scores[(size_t)q * k + i] = -INFINITY;
+        }
+        if (threadIdx.x == 0) out_n[q] = 0;
+        return;
+    }
+    const int m = min(k, n);
+    for (int i = threadIdx.x; i < k; i += kBS) {
+        bool v = i < m;
+        ids[(size_t)q * k + i] = v ? sid[i] : ~0ull;
+        scores[(size_t)q * k + i] = v ? ssc[i] : -INFINITY;
+    }
+    if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
+}
+
 }  // namespace
 
 // ---- launchers ----------------------------------------------------------------------------------------
 
 namespace {
 thread_local KernelClock* t_clock = nullptr;
+thread_local cudaError_t t_launch_err = cudaSuccess;
+thread_local int t_launch_err_kernel = -1;
 std::atomic<unsigned long long> g_launches{0};
 
-// Brackets one kernel launch: counts it and, with a clock installed, records its events.
+// Brackets one kernel launch: counts it, records the first launch error of the calling thread,
+// and, with a clock installed, records its events.
 struct Tick {
     cudaStream_t st;
-    Tick(int id, cudaStream_t s) : st(s) {
+    int id;
+    Tick(int i, cudaStream_t s) : st(s), id(i) {
         g_launches.fetch_add(1, std::memory_order_relaxed);
         if (t_clock) t_clock->begin(id, st);
     }
     ~Tick() {
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess && t_launch_err == cudaSuccess) {
+            t_launch_err = e;
+            t_launch_err_kernel = id;
+        }
         if (t_clock) t_clock->end(st);
     }
 };
 }  // namespace
+
+cudaError_t take_launch_error(int* kernel) {
+    cudaError_t e = t_launch_err;
+    if (kernel) *kernel = t_launch_err_kernel;
+    t_launch_err = cudaSuccess;
+    t_launch_err_kernel = -1;
+    return e;
+}
 
 const char* kernel_name(int id) {
     static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
@@ -1240,32 +1592,47 @@ void KernelClock::collect() {
 void set_thread_clock(KernelClock* c) { t_clock = c; }
 unsigned long long total_launches() { return g_launches.load(); }
 
+// The 48 KiB default covers static plus dynamic shared memory, so any dynamic request opts in to
+// its exact size; a refused opt-in surfaces as the launch error recorded by Tick.
 static void set_smem(const void* f, size_t bytes) {
-    if (bytes > 48 * 1024) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (bytes > 0) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& e, bool want_cqs, bool want_rqs,
                    cudaStream_t st) {
     if (nq <= 0) return;
-    size_t smem = (size_t)(ix.dim_pad + ix.npos) * sizeof(float);
     Tick tk(kKEncode, st);
-    k_encode<<<nq, kBS, smem, st>>>(ix, Q, e, want_cqs ? 1 : 0, want_rqs ? 1 : 0);
+    const int blocks = (nq + kBS / 32 - 1) / (kBS / 32);
+    const int wc = want_cqs ? 1 : 0, wr = want_rqs ? 1 : 0;
+    switch (ix.dim_pad) {
+        case 128: k_encode_warp<4><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
+        case 256: k_encode_warp<8><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
+        case 512: k_encode_warp<16><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
+        case 1024: k_encode_warp<32><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
+        default: break;
+    }
+    size_t smem = (size_t)(ix.dim_pad + ix.npos) * sizeof(float);
+    k_encode<<<nq, kBS, smem, st>>>(ix, Q, e, wc, wr);
 }
 
 void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint16_t* hs, uint32_t* sl,
                        uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
-    size_t smem = (size_t)kRouteQB * (ix.nw * 64 + 1) * sizeof(uint32_t);
+    const size_t hist_b = (size_t)kRouteQB * (ix.nw * 64 + 1) * sizeof(uint32_t);
+    const size_t h_b = (size_t)kRouteQB * ix.M * sizeof(uint16_t);
+    const int in_smem = h_b <= (size_t)kRouteSmemH ? 1 : 0;
+    const size_t smem = hist_b + (in_smem ? h_b : 0);
     set_smem((const void*)k_route_flat, smem);
     Tick tk(kKRouteFlat, st);
-    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, smem, st>>>(ix, e, nq, want_c, 0, hs, sl, sl_n, sl_cap);
+    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n,
+                                                                      sl_cap);
 }
 
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
     QueryEnc e{};
     Tick tk(kKRouteFlat, st);
-    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, nullptr, sl, sl_n, sl_cap);
+    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, 0, nullptr, sl, sl_n, sl_cap);
 }
 
 void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,
@@ -1295,8 +1662,15 @@ void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint
                       const CellMajorBufs& b, cudaStream_t st) {
     if (nq <= 0) return;
     size_t lut_bytes = (size_t)ix.npos * 16;
+    const size_t key_bytes = (size_t)b.seed_cap * sizeof(uint64_t);
+    const int keys_in_smem = key_bytes <= 96 * 1024 ? 1 : 0;
+    const size_t smem = lut_bytes + (keys_in_smem ? key_bytes : 0);
+    set_smem((const void*)k_seed, smem);
     { Tick tk(kKSeed, st);
-    k_seed<<<nq, kBS, lut_bytes, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b); }
+    k_seed<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b,
+                                  keys_in_smem); }
+    if (nprobe > kSeedCells) {
+    // every probe beyond the seed cells goes through the inverted cell -> queries scan
     cudaMemsetAsync(b.cell_cnt, 0, sizeof(uint32_t) * (ix.M + 1), st);
     cudaMemsetAsync(b.cell_fill, 0, sizeof(uint32_t) * ix.M, st);
     int wb = (nq + 7) / 8;
@@ -1308,6 +1682,7 @@ void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint
     k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof); }
     { Tick tk(kKScanCm, st);
     k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b); }
+    }
     { Tick tk(kKFinalCm, st);
     k_final_cm<<<nq, kBS, 0, st>>>(b, target); }
 }
@@ -1330,8 +1705,33 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   cudaStream_t st) {
+                   uint32_t* err, cudaStream_t st) {
     if (nq <= 0) return;
+    const int row_bytes = ix.rerank_mode == 0 ? ix.dim * 4 : ix.dim;
+    if (row_bytes % 16 == 0 && k <= 2048) {
+        // TMA-staged rows: padded stride keeps the 8-lane reads of 4 rows per warp on distinct banks
+        int words = row_bytes / 4;
+        int stride_words = words + ((8 - words % 32) + 32) % 32;
+        const int stride = stride_words * 4;
+        const int P = next_pow2(k + kTmaSortChunk);
+        size_t smem = 16 + (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (((size_t)ix.dim * 4 + 15) & ~size_t(15)) +
+                      2 * (size_t)kTmaRows * stride;
+        Tick tk(kKRerank, st);
+        if (ix.rerank_mode == 0) {
+            set_smem((const void*)k_rerank_tma<0>, smem);
+            k_rerank_tma<0><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
+                                                   scores, out_n, err);
+        } else if (ix.rerank_mode == 1) {
+            set_smem((const void*)k_rerank_tma<1>, smem);
+            k_rerank_tma<1><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
+                                                   scores, out_n, err);
+        } else {
+            set_smem((const void*)k_rerank_tma<2>, smem);
+            k_rerank_tma<2><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
+                                                   scores, out_n, err);
+        }
+        return;
+    }
     int P = next_pow2(k + kRerankChunk);
     size_t smem = (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (size_t)ix.dim * sizeof(float);
     set_smem((const void*)k_rerank, smem);

@@ -73,6 +73,8 @@ struct KernelClock {
     void collect();
 };
 void set_thread_clock(KernelClock* c);
+// First kernel-launch error on this thread since the last call (and the kernel it came from).
+cudaError_t take_launch_error(int* kernel);
 unsigned long long total_launches();
 
 constexpr int kMaxTreeLevels = 8;
@@ -150,9 +152,10 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
                      uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st);
 
 // Exact rerank + top-k (index.rs:1309-1378); writes k ids/scores per query, padded.
+// `err` counts blocks whose row copies did not complete within the wait limit.
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   cudaStream_t st);
+                   uint32_t* err, cudaStream_t st);
 
 }  // namespace dev
 }  // namespace maivs

@@ -150,3 +150,15 @@ def test_single_search_matches_batch(data, quality):
     ids, sc = quality.search(Q[0], K, 32, 1.0, 8.0)
     bi, bs = quality.search_batch_arrays(Q[:1], K, 32, 1.0, 8.0, False)
     assert ids == [int(x) for x in bi] and np.array_equal(np.asarray(sc, np.float32), bs)
+
+
+@pytest.mark.parametrize("dim,preset", [(60, "quality"), (100, "quality"), (100, "memory"), (200, "memory")])
+def test_odd_dims(dim, preset):
+    # dim_pad 64 uses the block encoder; 100-byte SQ8 rows take the per-thread rerank; f32 rows
+    # of 240 / 400 bytes take the staged rerank with a scalar tail (dim % 8 != 0)
+    rng = np.random.default_rng(dim)
+    X, c = mixture(rng, 6000, dim, 60)
+    Q, _ = mixture(rng, 48, dim, 60, centers=c)
+    ix = build_index(X, preset, rf=8)
+    _compare(ix, Q, K, 12, cell_major=True)
+    _compare(ix, Q[:12], K, 12, cell_major=False)
