@@ -286,6 +286,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     const int cand_cap = seed_cap + rest_cap;
     const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
 
+    float* rsc = nullptr;  // rerank scores (nq x cand_cap) of the pipelined gather
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
         e.qbits = bp.take<uint64_t>((size_t)nq * nw);
@@ -320,6 +321,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
+        rsc = bp.take<float>((size_t)nq * cand_cap);
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
@@ -370,7 +372,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     }
     if (timing_) cudaEventRecord(ev_[3], st);
     dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, d_flags_ + 2,
-                       st);
+                       rsc, st);
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
     return kOk;
@@ -387,6 +389,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     const bool tree_router = h.tree != nullptr;
     const int chunk = std::min(a.nq, kPerQueryChunk);
 
+    float* rsc = nullptr;  // rerank scores (chunk x cand_cap) of the pipelined gather
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
         int nq = chunk;
@@ -413,6 +416,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
+        rsc = bp.take<float>((size_t)nq * cand_cap);
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
@@ -456,7 +460,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         if (dbg && dbg->stage == 2) return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[3], st);
         dev::launch_rerank(view_, Qc, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids + (size_t)q0 * a.k,
-                           d_scores + (size_t)q0 * a.k, d_nout + q0, d_flags_ + 2, st);
+                           d_scores + (size_t)q0 * a.k, d_nout + q0, d_flags_ + 2, rsc, st);
     }
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());

@@ -67,12 +67,16 @@ __device__ __forceinline__ uint32_t warp_append(bool valid, uint32_t* counter) {
 // Exactly-once rule of the cell-major join: a multi-home vector is scored only at its lowest-id
 // probed home (index.rs:2036-2045).
 __device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot, uint32_t c, const uint64_t* probed) {
+    // branch-free over the homes so the loads of several members can be in flight together
     const uint32_t* h = ix.slot_cells + (size_t)slot * ix.ma;
+    bool ok = true;
     for (int j = 0; j < ix.ma; ++j) {
-        uint32_t hc = h[j];
-        if (hc != kNoCell && hc < c && ((probed[hc >> 6] >> (hc & 63)) & 1ull)) return false;
+        const uint32_t hc = __ldg(h + j);
+        const bool lower = hc != kNoCell && hc < c;
+        const uint64_t word = lower ? __ldg(probed + (hc >> 6)) : 0ull;
+        ok = ok && !(lower && ((word >> (hc & 63)) & 1ull));
     }
-    return true;
+    return ok;
 }
 
 // The kth smallest (1-based) of up to two key segments, by radix selection on bytes [lo_byte,
@@ -756,18 +760,25 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
         const bool act = g < ng;
         uint32_t acc[4];
         group_sums(codes, ng, g, act, lut_s, npos, acc);
+        // all eight members' slots first, then their home checks, so the loads overlap
+        uint32_t slot[8];
+        bool valid[8];
 #pragma unroll
         for (int bb = 0; bb < 8; ++bb) {
             const int pos = 8 * g + bb;
-            bool valid = act && pos < nc;
-            uint32_t d = 0, slot = 0;
-            if (valid) {
-                d = maxk - member_sum(acc, bb);
-                slot = ix.cell_slots[moff + pos];
-                if (ix.ma > 1) valid = canonical_cm(ix, slot, c, probed);
-            }
-            uint32_t p = warp_append(valid, &s_n);
-            if (valid && p < (uint32_t)b.seed_cap) keys[p] = ((uint64_t)d << 32) | slot;
+            valid[bb] = act && pos < nc;
+            slot[bb] = valid[bb] ? __ldg(ix.cell_slots + moff + pos) : 0u;
+        }
+        if (ix.ma > 1) {
+#pragma unroll
+            for (int bb = 0; bb < 8; ++bb)
+                if (valid[bb]) valid[bb] = canonical_cm(ix, slot[bb], c, probed);
+        }
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb) {
+            const uint32_t d = maxk - member_sum(acc, bb);
+            const uint32_t p = warp_append(valid[bb], &s_n);
+            if (valid[bb] && p < (uint32_t)b.seed_cap) keys[p] = ((uint64_t)d << 32) | slot[bb];
         }
     }
     __syncthreads();
@@ -1502,6 +1513,317 @@ __global__ void __launch_bounds__(kBS) k_rerank_tma(IndexView ix, const float* _
     if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
 }
 
+// ---- exact rerank: persistent TMA pipeline ------------------------------------------------------
+// One CTA per SM. Warp 8 (producer) streams each of its queries' candidate rows HBM -> shared
+// memory with cp.async.bulk into a kStages-deep ring (full/empty mbarriers); warps 0-7 (consumers)
+// score 32 rows per stage, eight threads per row, each thread one SIMD lane's FMA chain of the
+// reference's dot, closed with the hsum_ps tree. Scores go to `out` (nq x cand_cap); k_topk picks
+// the best k. All waits are bounded: on a timeout err[0] is raised and the block drains and exits.
+
+constexpr int kPipeStages = 3;
+constexpr int kPipeRows = 32;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(288) k_rerank_pipe(IndexView ix, const float* __restrict__ Q, QueryEnc e,
+                                                     const uint32_t* __restrict__ cand,
+                                                     const uint32_t* __restrict__ cand_n, int cand_cap, int nq,
+                                                     int row_bytes, int stride, float* out, uint32_t* err) {
+    extern __shared__ __align__(16) uint8_t psm[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(psm);           // kPipeStages
+    uint64_t* empty = full + kPipeStages;                         // kPipeStages
+    uint8_t* ring = psm + 128;                                    // kPipeStages x kPipeRows x stride
+    const int dim = ix.dim;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kPipeStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 8);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    if (warp == 8) {
+        // ---- producer: one elected lane issues every copy ----
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int q = blockIdx.x; q < nq && ok; q += gridDim.x) {
+                const int n = (int)cand_n[q];
+                const uint32_t* cq = cand + (size_t)q * cand_cap;
+                for (int r0 = 0; r0 < n && ok; r0 += kPipeRows, ++it) {
+                    const int stg = it % kPipeStages;
+                    if (it >= (uint32_t)kPipeStages && !mbar_wait(&empty[stg], ((it / kPipeStages) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const int nr = min(kPipeRows, n - r0);
+                    uint8_t* dst = ring + (size_t)stg * kPipeRows * stride;
+                    mbar_expect_tx(&full[stg], (uint32_t)(nr * row_bytes));
+                    for (int r = 0; r < nr; ++r)
+                        bulk_g2s(dst + (size_t)r * stride, base + (size_t)cq[r0 + r] * row_bytes, (uint32_t)row_bytes,
+                                 &full[stg]);
+                }
+            }
+            if (!ok) {
+                atomicAdd(err, 1u);
+                s_fail = 1;
+            }
+            // drain: every issued stage must have landed before the block may exit
+            for (int stg = 0; stg < kPipeStages && it > 0; ++stg) {
+                if ((uint32_t)stg >= it) break;
+                const uint32_t last = it - 1 - ((it - 1 - stg) % kPipeStages);  // last use of this stage
+                mbar_wait(&full[stg], (last / kPipeStages) & 1);
+            }
+        }
+        return;
+    }
+    // ---- consumers: 256 threads = 32 rows x 8 lanes ----
+    const int row = threadIdx.x >> 3, l8 = threadIdx.x & 7;
+    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
+    const int full8 = dim & ~7;
+    uint32_t it = 0;
+    for (int q = blockIdx.x; q < nq; q += gridDim.x) {
+        const int n = (int)cand_n[q];
+        const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+        const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
+        for (int r0 = 0; r0 < n; r0 += kPipeRows, ++it) {
+            const int stg = it % kPipeStages;
+            const bool ok = mbar_wait(&full[stg], (it / kPipeStages) & 1);
+            if (!ok || *(volatile int*)&s_fail) {
+                if (lane == 0 && !ok) atomicAdd(err, 1u);
+                return;
+            }
+            const int nr = min(kPipeRows, n - r0);
+            if (row < nr) {
+                const uint8_t* rp = ring + ((size_t)stg * kPipeRows + row) * stride;
+                float acc = 0.0f;
+                for (int i = l8; i < full8; i += 8) {
+                    float x;
+                    if (kMode == 0)
+                        x = reinterpret_cast<const float*>(rp)[i];
+                    else if (kMode == 1)
+                        x = (float)rp[i];
+                    else
+                        x = (float)(int8_t)rp[i];
+                    acc = __fmaf_rn(__ldg(qv + i), x, acc);
+                }
+                float sc = hsum8_group(acc, gmask);
+                if (l8 == 0) {
+                    for (int i = full8; i < dim; ++i) {
+                        float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
+                                             : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
+                        sc = __fadd_rn(sc, __fmul_rn(__ldg(qv + i), x));
+                    }
+                    if (kMode == 1) sc = __fadd_rn(rbase, sc);
+                    out[(size_t)q * cand_cap + r0 + row] = sc;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stg]);
+        }
+    }
+}
+
+// Best k of each query's scored candidates by (score desc, external id asc), chunks of 1024
+// merged by a bitonic sort in shared memory (same order rule as k_rerank).
+__global__ void __launch_bounds__(kBS) k_topk(IndexView ix, const uint32_t* __restrict__ cand,
+                                              const uint32_t* __restrict__ cand_n, const float* __restrict__ sc_in,
+                                              int cand_cap, int k, int P, uint64_t* ids, float* scores,
+                                              uint32_t* out_n) {
+    extern __shared__ uint64_t tsh[];
+    uint64_t* sid = tsh;
+    float* ssc = reinterpret_cast<float*>(sid + P);
+    const int q = blockIdx.x;
+    const int n = (int)cand_n[q];
+    for (int i = threadIdx.x; i < k; i += kBS) {
+        sid[i] = ~0ull;
+        ssc[i] = -INFINITY;
+    }
+    for (int c0 = 0; c0 < n; c0 += kRerankChunk) {
+        const int cn = min(kRerankChunk, n - c0);
+        const int Pe = next_pow2(k + cn);
+        for (int i = threadIdx.x; i < Pe - k; i += kBS) {
+            const bool v = i < cn;
+            sid[k + i] = v ? ix.ext_ids[cand[(size_t)q * cand_cap + c0 + i]] : ~0ull;
+            ssc[k + i] = v ? sc_in[(size_t)q * cand_cap + c0 + i] : -INFINITY;
+        }
+        __syncthreads();
+        for (int kk = 2; kk <= Pe; kk <<= 1) {
+            for (int j = kk >> 1; j > 0; j >>= 1) {
+                for (int i = threadIdx.x; i < Pe; i += kBS) {
+                    int ixj = i ^ j;
+                    if (ixj > i) {
+                        float sa = ssc[i], sb = ssc[ixj];
+                        uint64_t ia = sid[i], ib = sid[ixj];
+                        bool first = (i & kk) == 0;
+                        bool sw = first ? better(sb, ib, sa, ia) : better(sa, ia, sb, ib);
+                        if (sw) {
+                            ssc[i] = sb;
+                            ssc[ixj] = sa;
+                            sid[i] = ib;
+                            sid[ixj] = ia;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+    }
+    const int m = min(k, n);
+    for (int i = threadIdx.x; i < k; i += kBS) {
+        bool v = i < m;
+        ids[(size_t)q * k + i] = v ? sid[i] : ~0ull;
+        scores[(size_t)q * k + i] = v ? ssc[i] : -INFINITY;
+    }
+    if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
+}
+
+// ---- exact rerank: per-warp cp.async pipeline, fused top-k -----------------------------------------
+// One CTA per query, 8 warps. Warp w owns rows 32b + 4w .. 32b + 4w + 3 of batch b: it copies
+// them HBM -> its own double-buffered shared-memory slice with 16-byte cp.async (each warp
+// instruction moves 512 contiguous bytes of a row), then scores them, eight lanes per row, each
+// lane one SIMD lane's FMA chain of the reference's dot closed with the hsum_ps tree. Each warp
+// keeps its best k (k <= 32) in registers, lane j holding the j-th best; the 8 lists are merged
+// at the end. Order: score desc, external id asc.
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Insert (s, id) into the warp's sorted list (lane j < k holds the j-th best).
+__device__ __forceinline__ void warp_insert(float& ms, uint64_t& mid, float s, uint64_t id, int k) {
+    const int lane = threadIdx.x & 31;
+    const unsigned ahead = __ballot_sync(0xFFFFFFFFu, lane < k && better(ms, mid, s, id));
+    const int p = __popc(ahead);
+    const float us = __shfl_up_sync(0xFFFFFFFFu, ms, 1);
+    const uint64_t uid = __shfl_up_sync(0xFFFFFFFFu, mid, 1);
+    if (p < k) {
+        if (lane == p) {
+            ms = s;
+            mid = id;
+        } else if (lane > p && lane < k) {
+            ms = us;
+            mid = uid;
+        }
+    }
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kBS) k_rerank_async(IndexView ix, const float* __restrict__ Q, QueryEnc e,
+                                                      const uint32_t* __restrict__ cand,
+                                                      const uint32_t* __restrict__ cand_n, int cand_cap, int k,
+                                                      int row_bytes, int stride, uint64_t* ids, float* scores,
+                                                      uint32_t* out_n, float* score_out) {
+    extern __shared__ __align__(16) uint8_t asm_[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* mine = asm_ + (size_t)warp * 2 * 4 * stride;  // 2 stages x 4 rows
+    __shared__ float s_sc[8][32];
+    __shared__ uint64_t s_id[8][32];
+    const int q = blockIdx.x, dim = ix.dim;
+    const int n = (int)cand_n[q];
+    const uint32_t* cq = cand + (size_t)q * cand_cap;
+    const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+    const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
+    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
+    const int chunks = row_bytes / 16;
+    const int nbatch = n > 4 * warp ? (n - 4 * warp + 31) / 32 : 0;
+    auto issue = [&](int b) {
+        uint8_t* dst = mine + (size_t)(b & 1) * 4 * stride;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = 32 * b + 4 * warp + i;
+            if (r < n) {
+                const uint8_t* src = base + (size_t)__ldg(cq + r) * row_bytes;
+                for (int c = lane; c < chunks; c += 32) cp_async16(dst + (size_t)i * stride + 16 * c, src + 16 * c);
+            }
+        }
+        cp_async_commit();
+    };
+    const int i_row = lane >> 3, l8 = lane & 7;
+    const unsigned gmask = 0xFFu << (lane & ~7);
+    const int full8 = dim & ~7;
+    float ms = -INFINITY;
+    uint64_t mid = ~0ull;
+    const bool fused = score_out == nullptr;
+    if (nbatch > 0) issue(0);
+    for (int b = 0; b < nbatch; ++b) {
+        if (b + 1 < nbatch) {
+            issue(b + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncwarp();
+        const int r = 32 * b + 4 * warp + i_row;
+        float sc = -INFINITY;
+        uint64_t id = ~0ull;
+        if (r < n) {
+            const uint8_t* rp = mine + (size_t)(b & 1) * 4 * stride + (size_t)i_row * stride;
+            float acc = 0.0f;
+            for (int i = l8; i < full8; i += 8) {
+                float x;
+                if (kMode == 0)
+                    x = reinterpret_cast<const float*>(rp)[i];
+                else if (kMode == 1)
+                    x = (float)rp[i];
+                else
+                    x = (float)(int8_t)rp[i];
+                acc = __fmaf_rn(__ldg(qv + i), x, acc);
+            }
+            sc = hsum8_group(acc, gmask);
+            if (l8 == 0) {
+                for (int i = full8; i < dim; ++i) {
+                    float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
+                                         : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
+                    sc = __fadd_rn(sc, __fmul_rn(__ldg(qv + i), x));
+                }
+                if (kMode == 1) sc = __fadd_rn(rbase, sc);
+                id = ix.ext_ids[__ldg(cq + r)];
+                if (!fused) score_out[(size_t)q * cand_cap + r] = sc;
+            }
+        }
+        __syncwarp();  // the buffer of batch b is refilled by issue(b + 2)
+        if (fused) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float cs = __shfl_sync(0xFFFFFFFFu, sc, 8 * i);
+                const uint64_t ci = __shfl_sync(0xFFFFFFFFu, id, 8 * i);
+                if (32 * b + 4 * warp + i < n) warp_insert(ms, mid, cs, ci, k);
+            }
+        }
+    }
+    if (!fused) return;
+    s_sc[warp][lane] = ms;
+    s_id[warp][lane] = mid;
+    __syncthreads();
+    if (warp == 0) {
+        float fs = -INFINITY;
+        uint64_t fid = ~0ull;
+        for (int w = 0; w < 8; ++w)
+            for (int j = 0; j < k; ++j) warp_insert(fs, fid, s_sc[w][j], s_id[w][j], k);
+        const int m = min(k, n);
+        if (lane < k) {
+            const bool v = lane < m;
+            ids[(size_t)q * k + lane] = v ? fid : ~0ull;
+            scores[(size_t)q * k + lane] = v ? fs : -INFINITY;
+        }
+        if (lane == 0) out_n[q] = (uint32_t)m;
+    }
+}
+
 }  // namespace
 
 // ---- launchers ----------------------------------------------------------------------------------------
@@ -1544,7 +1866,7 @@ const char* kernel_name(int id) {
     static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
                                              "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
-                                             "k_pq_fold", "k_rerank"};
+                                             "k_pq_fold", "k_rerank",    "k_topk"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -1705,9 +2027,73 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   uint32_t* err, cudaStream_t st) {
+                   uint32_t* err, float* score_scratch, cudaStream_t st) {
     if (nq <= 0) return;
     const int row_bytes = ix.rerank_mode == 0 ? ix.dim * 4 : ix.dim;
+    if (row_bytes % 16 == 0) {
+        int words = row_bytes / 4;
+        int stride_words = words + ((8 - words % 32) + 32) % 32;
+        const int stride = stride_words * 4;
+        const size_t smem = (size_t)8 * 2 * 4 * stride;
+        const bool fused = k <= 32;
+        float* so = fused ? nullptr : score_scratch;
+        {
+            Tick tk(kKRerank, st);
+            if (ix.rerank_mode == 0) {
+                set_smem((const void*)k_rerank_async<0>, smem);
+                k_rerank_async<0><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
+                                                         scores, out_n, so);
+            } else if (ix.rerank_mode == 1) {
+                set_smem((const void*)k_rerank_async<1>, smem);
+                k_rerank_async<1><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
+                                                         scores, out_n, so);
+            } else {
+                set_smem((const void*)k_rerank_async<2>, smem);
+                k_rerank_async<2><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
+                                                         scores, out_n, so);
+            }
+        }
+        if (!fused) {
+            const int P = next_pow2(k + kRerankChunk);
+            const size_t tsm = (size_t)P * (sizeof(uint64_t) + sizeof(float));
+            set_smem((const void*)k_topk, tsm);
+            Tick tk(kKTopk, st);
+            k_topk<<<nq, kBS, tsm, st>>>(ix, cand, cand_n, score_scratch, cand_cap, k, P, ids, scores, out_n);
+        }
+        return;
+    }
+    if (row_bytes % 16 == 0 && score_scratch && k <= 4096) {
+        int words = row_bytes / 4;
+        int stride_words = words + ((8 - words % 32) + 32) % 32;
+        const int stride = stride_words * 4;
+        const size_t smem = 128 + (size_t)kPipeStages * kPipeRows * stride;
+        int sms = 148, cur = 0;
+        cudaGetDevice(&cur);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur);
+        const int grid = std::min(nq, sms);
+        {
+            Tick tk(kKRerank, st);
+            if (ix.rerank_mode == 0) {
+                set_smem((const void*)k_rerank_pipe<0>, smem);
+                k_rerank_pipe<0><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
+                                                          score_scratch, err);
+            } else if (ix.rerank_mode == 1) {
+                set_smem((const void*)k_rerank_pipe<1>, smem);
+                k_rerank_pipe<1><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
+                                                          score_scratch, err);
+            } else {
+                set_smem((const void*)k_rerank_pipe<2>, smem);
+                k_rerank_pipe<2><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
+                                                          score_scratch, err);
+            }
+        }
+        const int P = next_pow2(k + kRerankChunk);
+        const size_t tsm = (size_t)P * (sizeof(uint64_t) + sizeof(float));
+        set_smem((const void*)k_topk, tsm);
+        Tick tk(kKTopk, st);
+        k_topk<<<nq, kBS, tsm, st>>>(ix, cand, cand_n, score_scratch, cand_cap, k, P, ids, scores, out_n);
+        return;
+    }
     if (row_bytes % 16 == 0 && k <= 2048) {
         // TMA-staged rows: padded stride keeps the 8-lane reads of 4 rows per warp on distinct banks
         int words = row_bytes / 4;
