@@ -102,6 +102,25 @@ int maivs_search_batch_device(maivs_index* ix, const float* d_queries, size_t nq
                               void* stream);
 int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags);
 
+/* Allocation-free search (no counterpart in the reference). For callers that must not allocate
+ * device memory while serving: a process whose GPU memory is already held by another runtime's
+ * pool, or a latency-bound loop that cannot afford cudaMalloc's device-wide synchronisation.
+ * Runs the per-query path (search_batch with cell_major = 0) on at most 64 device-resident
+ * queries, enqueued on `stream`, with every intermediate buffer carved from one 32 MiB device
+ * array that the library reserves statically on each GPU it uses. It allocates nothing:
+ *  - the device image must be current (call maivs_to_device() after the last mutation), else
+ *    MAIVS_BAD_STATE;
+ *  - more than 64 queries, or a search whose buffers (about nq x nprobe x 1 KiB for 128-member
+ *    cells) exceed 32 MiB, is rejected with MAIVS_BAD_ARG and a message giving the size;
+ *  - the first call on a device looks the array's address up (a CUDA runtime call), so make
+ *    that call before capturing the stream into a graph.
+ * All calls, from every handle, share the one array. Nothing in it needs to start at zero, but
+ * calls whose work overlaps on the GPU race on it: issue them on one stream or one at a time.
+ * Results match maivs_search_batch_device(..., cell_major = 0, ...) exactly. */
+int maivs_search_batch_device_noalloc(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
+                                      float target_confidence, float beta, uint64_t* d_ids, float* d_scores,
+                                      void* stream);
+
 /* Host copy of one internal array, for persistence, inspection and parity tests: the pointer
  * stays valid until the next mutation of the index. Names: "vecs_f32", "scan_i8", "bits",
  * "ext_ids", "slot_cell", "slot_cells", "cell_members", "cell_member_off", "centroids",

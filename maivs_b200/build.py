@@ -33,6 +33,7 @@ SOURCES = [
     ("capi.cpp", "cxx"),
     ("cuda/kernels.cu", "nvcc"),
     ("cuda/engine.cu", "nvcc"),
+    ("cuda/static_search.cu", "nvcc"),
 ]
 HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/engine.h"]
 

@@ -449,6 +449,29 @@ int maivs_search_batch_device(maivs_index* ix, const float* dQ, size_t nq, size_
     return MAIVS_OK;
 }
 
+int maivs_search_batch_device_noalloc(maivs_index* ix, const float* dQ, size_t nq, size_t k, size_t nprobe,
+                                      float tc, float beta, uint64_t* d_ids, float* d_scores, void* stream) {
+    LOCK(ix);
+    if (nq == 0) return MAIVS_OK;
+    if (k == 0) return fail(ix, MAIVS_BAD_ARG, "k must be positive");
+    if (k > 4096) return fail(ix, MAIVS_UNSUPPORTED, "k above 4096 is not supported");
+    if (nq > 64) return fail(ix, MAIVS_BAD_ARG, "the allocation-free search takes at most 64 queries per call");
+    // uploading the index allocates, so the device image must already be current
+    if (!ix->d || ix->d->version() != ix->h.version || ix->d->device() != ix->device)
+        return fail(ix, MAIVS_BAD_STATE, "no current device image; call maivs_to_device() before this search");
+    maivs::SearchArgs a;
+    a.nq = (int)nq;
+    a.k = (int)k;
+    a.nprobe = (int)std::min<size_t>(nprobe, 1u << 30);
+    a.tc = tc;
+    a.beta = beta;
+    a.cell_major = false;
+    std::string err;
+    int rc = ix->d->search_static(ix->h, dQ, a, d_ids, d_scores, (cudaStream_t)stream, err);
+    if (rc != MAIVS_OK) return fail(ix, rc, err);
+    return MAIVS_OK;
+}
+
 int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags) {
     LOCK(ix);
     if (!ix->d) return fail(ix, MAIVS_BAD_STATE, "no device image");

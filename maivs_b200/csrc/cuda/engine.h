@@ -72,6 +72,11 @@ class DeviceIndex {
     // Returns a Status; `err` receives a message on failure.
     int search_device(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                       uint32_t* d_nout, cudaStream_t st, std::string& err);
+    // Per-query search of at most 64 device-resident queries whose scratch is a fixed 32 MiB
+    // device array defined in static_search.cu (allocates nothing; calls share the array, so
+    // overlapping calls race). Returns kBadArg when the search needs more scratch than that.
+    int search_static(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
+                      cudaStream_t st, std::string& err);
     // Host buffers: copies in, searches, copies out, synchronises, and retries with larger
     // candidate buffers if any query overflowed them.
     int search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
