@@ -292,12 +292,15 @@ def run_maivs(args):
     launches0 = launch_count()
     with ClockSampler(local) as clk:
         clk.wait_first()
+        # a profiler started with --profile-from-start off sees only the timed steps
+        torch.cuda.profiler.start()
         for s in range(args.steps):
             flush.zero_()
             evs[s][0].record(stream)
             step()
             evs[s][1].record(stream)
         torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
         clk.stop_mark()
     launches = launch_count() - launches0
     if dist:
@@ -336,6 +339,10 @@ def run_maivs(args):
     if name == "k_rerank":
         alg = stats.get("rerank_bytes", 0.0) + stats.get("candidates", 0.0) * 4
         what = "candidate rows gathered for the exact rerank (rows x 4d bytes) + candidate slots"
+    elif name == "k_seed":
+        alg = (stats.get("seed_code_bytes", 0.0) + stats.get("nq", 0.0) * (16 * 128 + 64)
+               + stats.get("seed_kept", 0.0) * 8)
+        what = "1-bit codes of the union of seed cells, each read once, + query LUTs and codes + kept entries"
     elif name == "k_scan_cm":
         alg = stats.get("scan_code_bytes", 0.0)
         what = "1-bit codes of every scanned cell, each read once (members x 64 B)"

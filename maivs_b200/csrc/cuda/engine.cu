@@ -286,7 +286,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     const int cand_cap = seed_cap + rest_cap;
     const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
 
-    float* rsc = nullptr;  // rerank scores (nq x cand_cap) of the pipelined gather
+    float* rsc = nullptr;       // rerank scores (nq x cand_cap) of the flattened gather
+    uint32_t* ritem = nullptr;  // its item numbering (nq + 1)
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
         e.qbits = bp.take<uint64_t>((size_t)nq * nw);
@@ -322,6 +323,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
         rsc = bp.take<float>((size_t)nq * cand_cap);
+        ritem = bp.take<uint32_t>((size_t)nq + 1);
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
@@ -371,8 +373,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
     }
     if (timing_) cudaEventRecord(ev_[3], st);
-    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, d_flags_ + 2,
-                       rsc, st);
+    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, rsc, ritem,
+                       st);
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
     return kOk;
@@ -389,7 +391,8 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     const bool tree_router = h.tree != nullptr;
     const int chunk = std::min(a.nq, kPerQueryChunk);
 
-    float* rsc = nullptr;  // rerank scores (chunk x cand_cap) of the pipelined gather
+    float* rsc = nullptr;       // rerank scores (chunk x cand_cap) of the flattened gather
+    uint32_t* ritem = nullptr;  // its item numbering (chunk + 1)
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
         int nq = chunk;
@@ -417,6 +420,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
         rsc = bp.take<float>((size_t)nq * cand_cap);
+        ritem = bp.take<uint32_t>((size_t)nq + 1);
     };
     dev::QueryEnc e{};
     uint32_t *sl, *sl_n, *tsc, *chosen, *nch;
@@ -460,7 +464,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         if (dbg && dbg->stage == 2) return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[3], st);
         dev::launch_rerank(view_, Qc, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids + (size_t)q0 * a.k,
-                           d_scores + (size_t)q0 * a.k, d_nout + q0, d_flags_ + 2, rsc, st);
+                           d_scores + (size_t)q0 * a.k, d_nout + q0, rsc, ritem, st);
     }
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
@@ -551,10 +555,6 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
             err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
             return kUnsupported;
         }
-        if (hF[2] != 0) {
-            err = "a rerank row copy did not complete within the wait limit";
-            return kCudaError;
-        }
         if (hF[0] == 0) break;
         if (attempt == 3) {
             err = "candidate buffers overflowed after enlarging them";
@@ -608,7 +608,8 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
                               rest_n = get(last_.rest_n, nq), rest_hi = get(last_.rest_hi, nq);
         double cells = 0, bytes = 0, pairs = 0, seed_pairs = 0, seed_kept = 0, rest_kept = 0, rest_probes = 0;
         std::vector<uint8_t> seen(M, 0);
-        double seed_bytes = 0;
+        double seed_bytes = 0, seed_union_bytes = 0;
+        std::vector<uint8_t> seed_seen(M, 0);
         for (int c = 0; c < M; ++c) {
             uint32_t nqc = start[c + 1] - start[c];
             double nc = (double)(moff_[c + 1] - moff_[c]);
@@ -625,6 +626,10 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
                 uint32_t c = chosen[(size_t)q * np + r];
                 double nc = (double)(moff_[c + 1] - moff_[c]);
                 seed_pairs += nc;
+                if (!seed_seen[c]) {
+                    seed_seen[c] = 1;
+                    seed_union_bytes += nc * code_bytes;
+                }
                 if (!seen[c]) {
                     seen[c] = 2;
                     seed_bytes += nc * code_bytes;
@@ -639,6 +644,7 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
         out.push_back({"scan_pairs", pairs});
         out.push_back({"seed_pairs", seed_pairs});
         out.push_back({"seed_extra_code_bytes", seed_bytes});
+        out.push_back({"seed_code_bytes", seed_union_bytes});
         out.push_back({"seed_kept", seed_kept});
         out.push_back({"rest_kept", rest_kept});
         out.push_back({"rest_probes", rest_probes});

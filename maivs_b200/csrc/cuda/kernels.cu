@@ -1331,307 +1331,6 @@ __global__ void __launch_bounds__(kBS) k_rerank(IndexView ix, const float* __res
     if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
 }
 
-// ---- exact rerank, TMA-staged rows -------------------------------------------------------------
-// Candidate rows are copied HBM -> shared memory by the bulk-copy engine (cp.async.bulk, one
-// thread issues a batch, completion on an mbarrier) into a double-buffered ring, so the gather
-// costs no per-thread load instructions. Eight threads then score one row from shared memory,
-// each running one SIMD lane's FMA chain of the reference's dot (index.rs:136-152, :278-294),
-// closed with the hsum_ps tree. Waits are bounded: a copy that does not land within the limit
-// sets err[0] and the block returns after draining.
-
-constexpr int kTmaRows = 32;          // rows per batch (8 threads per row, 256 threads)
-constexpr int kTmaSortChunk = 512;    // candidates scored between two top-k merges
-constexpr uint32_t kSpinLimit = 1u << 22;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait; false when the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-template <int kMode>  // 0: f32 rows, 1: per-dimension SQ8 rows, 2: global int8 rows
-__global__ void __launch_bounds__(kBS) k_rerank_tma(IndexView ix, const float* __restrict__ Q, QueryEnc e,
-                                                    const uint32_t* __restrict__ cand,
-                                                    const uint32_t* __restrict__ cand_n, int cand_cap, int k, int P,
-                                                    int row_bytes, int stride, uint64_t* ids, float* scores,
-                                                    uint32_t* out_n, uint32_t* err) {
-    extern __shared__ __align__(16) uint8_t tsm[];
-    uint64_t* bar = reinterpret_cast<uint64_t*>(tsm);               // 2 mbarriers
-    uint64_t* sid = reinterpret_cast<uint64_t*>(tsm + 16);          // P ids
-    float* ssc = reinterpret_cast<float*>(sid + P);                 // P scores
-    float* qv = ssc + P;                                            // dim, padded to 16 B
-    const int dim = ix.dim;
-    uint8_t* ring = reinterpret_cast<uint8_t*>(qv) + ((dim * 4 + 15) & ~15);  // 2 x kTmaRows x stride
-    const int q = blockIdx.x;
-    const int n = (int)cand_n[q];
-    const uint32_t* cq = cand + (size_t)q * cand_cap;
-    const float* qsrc = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
-    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
-    for (int t = threadIdx.x; t < dim; t += kBS) qv[t] = qsrc[t];
-    for (int i = threadIdx.x; i < P; i += kBS) {
-        sid[i] = ~0ull;
-        ssc[i] = -INFINITY;
-    }
-    if (threadIdx.x == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    const int nbatch = (n + kTmaRows - 1) / kTmaRows;
-    auto issue = [&](int b) {  // thread 0 only
-        const int r0 = b * kTmaRows, nr = min(kTmaRows, n - r0);
-        uint8_t* dst = ring + (size_t)(b & 1) * kTmaRows * stride;
-        mbar_expect_tx(&bar[b & 1], (uint32_t)(nr * row_bytes));
-        for (int r = 0; r < nr; ++r)
-            bulk_g2s(dst + (size_t)r * stride, base + (size_t)cq[r0 + r] * row_bytes, (uint32_t)row_bytes, &bar[b & 1]);
-    };
-    if (threadIdx.x == 0) {
-        if (nbatch > 0) issue(0);
-        if (nbatch > 1) issue(1);
-    }
-    const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
-    const int row = threadIdx.x >> 3, l8 = threadIdx.x & 7;
-    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
-    const int full = dim & ~7;
-    bool failed = false;
-    int filled = 0;  // candidates written at [k, k + filled) since the last merge
-    for (int b = 0; b < nbatch; ++b) {
-        const bool ok = mbar_wait(&bar[b & 1], (uint32_t)((b >> 1) & 1));
-        // every thread leaves together if any thread's wait ran out
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
-        const int r0 = b * kTmaRows, nr = min(kTmaRows, n - r0);
-        const uint8_t* buf = ring + (size_t)(b & 1) * kTmaRows * stride;
-        if (row < nr) {
-            const uint8_t* rp = buf + (size_t)row * stride;
-            float acc = 0.0f;
-            for (int i = l8; i < full; i += 8) {
-                float x;
-                if (kMode == 0)
-                    x = reinterpret_cast<const float*>(rp)[i];
-                else if (kMode == 1)
-                    x = (float)rp[i];
-                else
-                    x = (float)(int8_t)rp[i];
-                acc = __fmaf_rn(qv[i], x, acc);
-            }
-            float sc = hsum8_group(acc, gmask);
-            if (l8 == 0) {
-                for (int i = full; i < dim; ++i) {
-                    float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
-                                         : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
-                    sc = __fadd_rn(sc, __fmul_rn(qv[i], x));
-                }
-                if (kMode == 1) sc = __fadd_rn(rbase, sc);
-                sid[k + filled + row] = ix.ext_ids[cq[r0 + row]];
-                ssc[k + filled + row] = sc;
-            }
-        }
-        __syncthreads();  // every thread is done with this buffer
-        if (threadIdx.x == 0 && b + 2 < nbatch) issue(b + 2);
-        filled += nr;
-        if (filled + kTmaRows > kTmaSortChunk || b + 1 == nbatch) {
-            const int Pe = next_pow2(k + filled);
-            for (int kk = 2; kk <= Pe; kk <<= 1) {
-                for (int j = kk >> 1; j > 0; j >>= 1) {
-                    for (int i = threadIdx.x; i < Pe; i += kBS) {
-                        int ixj = i ^ j;
-                        if (ixj > i) {
-                            float sa = ssc[i], sb = ssc[ixj];
-                            uint64_t ia = sid[i], ib = sid[ixj];
-                            bool first = (i & kk) == 0;
-                            bool sw = first ? better(sb, ib, sa, ia) : better(sa, ia, sb, ib);
-                            if (sw) {
-                                ssc[i] = sb;
-                                ssc[ixj] = sa;
-                                sid[i] = ib;
-                                sid[ixj] = ia;
-                            }
-                        }
-                    }
-                    __syncthreads();
-                }
-            }
-            for (int i = k + threadIdx.x; i < Pe; i += kBS) {
-                sid[i] = ~0ull;
-                ssc[i] = -INFINITY;
-            }
-            __syncthreads();
-            filled = 0;
-        }
-    }
-    if (failed) {
-        // drain: wait (bounded) for every batch still in flight before the block exits
-        if (threadIdx.x == 0) {
-            atomicAdd(err, 1u);
-            // both ring slots may still be receiving: wait (bounded) for their current phases
-            for (int b = 0; b < 2; ++b) mbar_wait(&bar[b], 0), mbar_wait(&bar[b], 1);
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < k; i += kBS) {
-            ids[(size_t)q * k + i] = ~0ull;
-            scores[(size_t)q * k + i] = -INFINITY;
-        }
-        if (threadIdx.x == 0) out_n[q] = 0;
-        return;
-    }
-    const int m = min(k, n);
-    for (int i = threadIdx.x; i < k; i += kBS) {
-        bool v = i < m;
-        ids[(size_t)q * k + i] = v ? sid[i] : ~0ull;
-        scores[(size_t)q * k + i] = v ? ssc[i] : -INFINITY;
-    }
-    if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
-}
-
-// ---- exact rerank: persistent TMA pipeline ------------------------------------------------------
-// One CTA per SM. Warp 8 (producer) streams each of its queries' candidate rows HBM -> shared
-// memory with cp.async.bulk into a kStages-deep ring (full/empty mbarriers); warps 0-7 (consumers)
-// score 32 rows per stage, eight threads per row, each thread one SIMD lane's FMA chain of the
-// reference's dot, closed with the hsum_ps tree. Scores go to `out` (nq x cand_cap); k_topk picks
-// the best k. All waits are bounded: on a timeout err[0] is raised and the block drains and exits.
-
-constexpr int kPipeStages = 3;
-constexpr int kPipeRows = 32;
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-template <int kMode>
-__global__ void __launch_bounds__(288) k_rerank_pipe(IndexView ix, const float* __restrict__ Q, QueryEnc e,
-                                                     const uint32_t* __restrict__ cand,
-                                                     const uint32_t* __restrict__ cand_n, int cand_cap, int nq,
-                                                     int row_bytes, int stride, float* out, uint32_t* err) {
-    extern __shared__ __align__(16) uint8_t psm[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(psm);           // kPipeStages
-    uint64_t* empty = full + kPipeStages;                         // kPipeStages
-    uint8_t* ring = psm + 128;                                    // kPipeStages x kPipeRows x stride
-    const int dim = ix.dim;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < kPipeStages; ++st) {
-            mbar_init(&full[st], 1);
-            mbar_init(&empty[st], 8);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    __shared__ int s_fail;
-    if (threadIdx.x == 0) s_fail = 0;
-    __syncthreads();
-    if (warp == 8) {
-        // ---- producer: one elected lane issues every copy ----
-        if (lane == 0) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (int q = blockIdx.x; q < nq && ok; q += gridDim.x) {
-                const int n = (int)cand_n[q];
-                const uint32_t* cq = cand + (size_t)q * cand_cap;
-                for (int r0 = 0; r0 < n && ok; r0 += kPipeRows, ++it) {
-                    const int stg = it % kPipeStages;
-                    if (it >= (uint32_t)kPipeStages && !mbar_wait(&empty[stg], ((it / kPipeStages) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    const int nr = min(kPipeRows, n - r0);
-                    uint8_t* dst = ring + (size_t)stg * kPipeRows * stride;
-                    mbar_expect_tx(&full[stg], (uint32_t)(nr * row_bytes));
-                    for (int r = 0; r < nr; ++r)
-                        bulk_g2s(dst + (size_t)r * stride, base + (size_t)cq[r0 + r] * row_bytes, (uint32_t)row_bytes,
-                                 &full[stg]);
-                }
-            }
-            if (!ok) {
-                atomicAdd(err, 1u);
-                s_fail = 1;
-            }
-            // drain: every issued stage must have landed before the block may exit
-            for (int stg = 0; stg < kPipeStages && it > 0; ++stg) {
-                if ((uint32_t)stg >= it) break;
-                const uint32_t last = it - 1 - ((it - 1 - stg) % kPipeStages);  // last use of this stage
-                mbar_wait(&full[stg], (last / kPipeStages) & 1);
-            }
-        }
-        return;
-    }
-    // ---- consumers: 256 threads = 32 rows x 8 lanes ----
-    const int row = threadIdx.x >> 3, l8 = threadIdx.x & 7;
-    const unsigned gmask = 0xFFu << ((threadIdx.x & 31) & ~7);
-    const int full8 = dim & ~7;
-    uint32_t it = 0;
-    for (int q = blockIdx.x; q < nq; q += gridDim.x) {
-        const int n = (int)cand_n[q];
-        const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
-        const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
-        for (int r0 = 0; r0 < n; r0 += kPipeRows, ++it) {
-            const int stg = it % kPipeStages;
-            const bool ok = mbar_wait(&full[stg], (it / kPipeStages) & 1);
-            if (!ok || *(volatile int*)&s_fail) {
-                if (lane == 0 && !ok) atomicAdd(err, 1u);
-                return;
-            }
-            const int nr = min(kPipeRows, n - r0);
-            if (row < nr) {
-                const uint8_t* rp = ring + ((size_t)stg * kPipeRows + row) * stride;
-                float acc = 0.0f;
-                for (int i = l8; i < full8; i += 8) {
-                    float x;
-                    if (kMode == 0)
-                        x = reinterpret_cast<const float*>(rp)[i];
-                    else if (kMode == 1)
-                        x = (float)rp[i];
-                    else
-                        x = (float)(int8_t)rp[i];
-                    acc = __fmaf_rn(__ldg(qv + i), x, acc);
-                }
-                float sc = hsum8_group(acc, gmask);
-                if (l8 == 0) {
-                    for (int i = full8; i < dim; ++i) {
-                        float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
-                                             : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
-                        sc = __fadd_rn(sc, __fmul_rn(__ldg(qv + i), x));
-                    }
-                    if (kMode == 1) sc = __fadd_rn(rbase, sc);
-                    out[(size_t)q * cand_cap + r0 + row] = sc;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[stg]);
-        }
-    }
-}
-
 // Best k of each query's scored candidates by (score desc, external id asc), chunks of 1024
 // merged by a bitonic sort in shared memory (same order rule as k_rerank).
 __global__ void __launch_bounds__(kBS) k_topk(IndexView ix, const uint32_t* __restrict__ cand,
@@ -1686,23 +1385,6 @@ __global__ void __launch_bounds__(kBS) k_topk(IndexView ix, const uint32_t* __re
     if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
 }
 
-// ---- exact rerank: per-warp cp.async pipeline, fused top-k -----------------------------------------
-// One CTA per query, 8 warps. Warp w owns rows 32b + 4w .. 32b + 4w + 3 of batch b: it copies
-// them HBM -> its own double-buffered shared-memory slice with 16-byte cp.async (each warp
-// instruction moves 512 contiguous bytes of a row), then scores them, eight lanes per row, each
-// lane one SIMD lane's FMA chain of the reference's dot closed with the hsum_ps tree. Each warp
-// keeps its best k (k <= 32) in registers, lane j holding the j-th best; the 8 lists are merged
-// at the end. Order: score desc, external id asc.
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Insert (s, id) into the warp's sorted list (lane j < k holds the j-th best).
 __device__ __forceinline__ void warp_insert(float& ms, uint64_t& mid, float s, uint64_t id, int k) {
     const int lane = threadIdx.x & 31;
@@ -1721,107 +1403,270 @@ __device__ __forceinline__ void warp_insert(float& ms, uint64_t& mid, float s, u
     }
 }
 
-template <int kMode>
-__global__ void __launch_bounds__(kBS) k_rerank_async(IndexView ix, const float* __restrict__ Q, QueryEnc e,
-                                                      const uint32_t* __restrict__ cand,
-                                                      const uint32_t* __restrict__ cand_n, int cand_cap, int k,
-                                                      int row_bytes, int stride, uint64_t* ids, float* scores,
-                                                      uint32_t* out_n, float* score_out) {
-    extern __shared__ __align__(16) uint8_t asm_[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* mine = asm_ + (size_t)warp * 2 * 4 * stride;  // 2 stages x 4 rows
-    __shared__ float s_sc[8][32];
-    __shared__ uint64_t s_id[8][32];
-    const int q = blockIdx.x, dim = ix.dim;
-    const int n = (int)cand_n[q];
-    const uint32_t* cq = cand + (size_t)q * cand_cap;
-    const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
-    const float rbase = kMode == 1 ? e.rbase[q] : 0.0f;
-    const uint8_t* base = kMode == 0 ? reinterpret_cast<const uint8_t*>(ix.vecs_f32) : ix.rr_u8;
-    const int chunks = row_bytes / 16;
-    const int nbatch = n > 4 * warp ? (n - 4 * warp + 31) / 32 : 0;
-    auto issue = [&](int b) {
-        uint8_t* dst = mine + (size_t)(b & 1) * 4 * stride;
+// ---- exact rerank: flattened gather into registers ----------------------------------------------
+// The candidates of all queries are cut into items of R consecutive rows of one query (R = 16
+// for f32 rows, 32 for byte rows); k_rerank_items numbers them (exclusive prefix of
+// ceil(cand_n / R) per query) and every warp of a persistent grid takes an equal contiguous run
+// of items. Rows are read straight into registers with 128-bit loads at full occupancy, which is
+// what a random gather of ~1.5 KB rows needs to run at HBM speed; the warp keeps its query's
+// vector in shared memory and prefetches the next item's slots while it scores the current one.
+// f32 rows: two lanes per row, lane h running SIMD lanes 4h..4h+3 of the reference's 8-lane FMA
+// dot (elements 8i + 4h .. 8i + 4h + 3 at step i), the pair closing it with the hsum_ps tree
+// ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)). Byte rows: one lane per row running all eight SIMD
+// lanes, 16 elements (two steps) per load. The scalar tail is added sequentially, then the SQ8
+// base. Scores go to score_out[q * cand_cap + r]; k_topk_warp (k <= 32) or k_topk picks the best
+// k of each query.
+__global__ void __launch_bounds__(1024) k_rerank_items(const uint32_t* __restrict__ cand_n, int nq, int rows,
+                                                       uint32_t* __restrict__ item_off) {
+    __shared__ uint32_t wsum[32];
+    __shared__ uint32_t carry;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int q0 = 0; q0 < nq; q0 += 1024) {
+        const int q = q0 + threadIdx.x;
+        const uint32_t v = q < nq ? (cand_n[q] + rows - 1) / rows : 0u;
+        uint32_t x = v;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = 32 * b + 4 * warp + i;
-            if (r < n) {
-                const uint8_t* src = base + (size_t)__ldg(cq + r) * row_bytes;
-                for (int c = lane; c < chunks; c += 32) cp_async16(dst + (size_t)i * stride + 16 * c, src + 16 * c);
-            }
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+            if (lane >= o) x += y;
         }
-        cp_async_commit();
+        if (lane == 31) wsum[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+                if (lane >= o) w += y;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const uint32_t before = carry + (warp ? wsum[warp - 1] : 0u) + x - v;
+        if (q < nq) item_off[q] = before;
+        __syncthreads();
+        if (threadIdx.x == 1023) carry = before + v;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) item_off[nq] = carry;
+}
+
+__host__ __device__ constexpr int gather_rows(int mode) { return mode == 0 ? 16 : 32; }
+
+__device__ __forceinline__ float byte_val(uint32_t w, int b, bool sgn) {
+    const uint32_t v = (w >> (8 * b)) & 0xFFu;
+    return sgn ? (float)(int8_t)v : (float)v;
+}
+
+template <int kMode>  // 0: f32 rows, 1: per-dimension SQ8 rows, 2: global int8 rows
+__global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float* __restrict__ Q, QueryEnc e,
+                                                       const uint32_t* __restrict__ cand,
+                                                       const uint32_t* __restrict__ cand_n,
+                                                       const uint32_t* __restrict__ item_off, int nq, int cand_cap,
+                                                       float* __restrict__ score_out) {
+    constexpr int R = gather_rows(kMode);
+    extern __shared__ __align__(16) float gsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dim = ix.dim, full8 = dim & ~7, n8 = full8 >> 3;
+    float* sq = gsm + (size_t)warp * ((dim + 3) & ~3);
+    const long long total = item_off[nq];
+    const long long tw = (long long)gridDim.x * (blockDim.x >> 5), gw = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+    const uint32_t i0 = (uint32_t)(total * gw / tw), i1 = (uint32_t)(total * (gw + 1) / tw);
+    if (i0 >= i1) return;
+
+    // the query owning item i0: last q with item_off[q] <= i0
+    int lo = 0, hi = nq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (item_off[mid] <= i0) lo = mid; else hi = mid - 1;
+    }
+    int lq = lo;
+    uint32_t lq_end = item_off[lq + 1];
+    auto advance = [&](uint32_t it, int& q, int& r0) {
+        while (it >= lq_end) {
+            ++lq;
+            lq_end = item_off[lq + 1];
+        }
+        q = lq;
+        r0 = (int)(it - item_off[lq]) * R;
     };
-    const int i_row = lane >> 3, l8 = lane & 7;
-    const unsigned gmask = 0xFFu << (lane & ~7);
-    const int full8 = dim & ~7;
+    const int j = kMode == 0 ? lane >> 1 : lane;  // this lane's row within the item
+    const int h = lane & 1;
+    auto slot_of = [&](int q, int r0) -> uint32_t {
+        const int r = r0 + j;
+        return r < (int)__ldg(cand_n + q) ? __ldg(cand + (size_t)q * cand_cap + r) : ~0u;
+    };
+    int q_a, r_a;
+    advance(i0, q_a, r_a);
+    uint32_t s_a = slot_of(q_a, r_a);
+    int cur_q = -1;
+    for (uint32_t it = i0; it < i1; ++it) {
+        int q_n = 0, r_n = 0;
+        uint32_t s_n = ~0u;
+        if (it + 1 < i1) {
+            advance(it + 1, q_n, r_n);
+            s_n = slot_of(q_n, r_n);
+        }
+        const int q = q_a;
+        if (q != cur_q) {  // warp-uniform: stage this query's vector
+            __syncwarp();
+            const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+            for (int i = lane; i < dim; i += 32) sq[i] = __ldg(qv + i);
+            __syncwarp();
+            cur_q = q;
+        }
+        const bool valid = s_a != ~0u;
+        float sc = 0.0f;
+        if (kMode == 0) {
+            const float* row = ix.vecs_f32 + (size_t)(valid ? s_a : 0u) * dim;
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+            if (valid) {
+                const float4* rp = reinterpret_cast<const float4*>(row) + h;
+                const float4* qp = reinterpret_cast<const float4*>(sq) + h;
+#pragma unroll 8
+                for (int i = 0; i < n8; ++i) {
+                    const float4 xx = __ldg(rp + 2 * i);
+                    const float4 qq = qp[2 * i];
+                    a0 = __fmaf_rn(qq.x, xx.x, a0);
+                    a1 = __fmaf_rn(qq.y, xx.y, a1);
+                    a2 = __fmaf_rn(qq.z, xx.z, a2);
+                    a3 = __fmaf_rn(qq.w, xx.w, a3);
+                }
+            }
+            const float s0 = __fadd_rn(a0, __shfl_xor_sync(0xFFFFFFFFu, a0, 1));
+            const float s1 = __fadd_rn(a1, __shfl_xor_sync(0xFFFFFFFFu, a1, 1));
+            const float s2 = __fadd_rn(a2, __shfl_xor_sync(0xFFFFFFFFu, a2, 1));
+            const float s3 = __fadd_rn(a3, __shfl_xor_sync(0xFFFFFFFFu, a3, 1));
+            sc = __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+            if (valid && h == 0) {
+                for (int i = full8; i < dim; ++i) sc = __fadd_rn(sc, __fmul_rn(sq[i], __ldg(row + i)));
+                score_out[(size_t)q * cand_cap + r_a + j] = sc;
+            }
+        } else if (valid) {
+            constexpr bool sgn = kMode == 2;
+            const uint8_t* row = ix.rr_u8 + (size_t)s_a * dim;
+            const uint4* rp = reinterpret_cast<const uint4*>(row);
+            const float4* qp = reinterpret_cast<const float4*>(sq);
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, a4 = 0.0f, a5 = 0.0f, a6 = 0.0f, a7 = 0.0f;
+            const int m2 = n8 >> 1;
+#pragma unroll 4
+            for (int m = 0; m < m2; ++m) {
+                const uint4 w = __ldg(rp + m);
+                const float4 q0 = qp[4 * m], q1 = qp[4 * m + 1], q2 = qp[4 * m + 2], q3 = qp[4 * m + 3];
+                a0 = __fmaf_rn(q0.x, byte_val(w.x, 0, sgn), a0);
+                a1 = __fmaf_rn(q0.y, byte_val(w.x, 1, sgn), a1);
+                a2 = __fmaf_rn(q0.z, byte_val(w.x, 2, sgn), a2);
+                a3 = __fmaf_rn(q0.w, byte_val(w.x, 3, sgn), a3);
+                a4 = __fmaf_rn(q1.x, byte_val(w.y, 0, sgn), a4);
+                a5 = __fmaf_rn(q1.y, byte_val(w.y, 1, sgn), a5);
+                a6 = __fmaf_rn(q1.z, byte_val(w.y, 2, sgn), a6);
+                a7 = __fmaf_rn(q1.w, byte_val(w.y, 3, sgn), a7);
+                a0 = __fmaf_rn(q2.x, byte_val(w.z, 0, sgn), a0);
+                a1 = __fmaf_rn(q2.y, byte_val(w.z, 1, sgn), a1);
+                a2 = __fmaf_rn(q2.z, byte_val(w.z, 2, sgn), a2);
+                a3 = __fmaf_rn(q2.w, byte_val(w.z, 3, sgn), a3);
+                a4 = __fmaf_rn(q3.x, byte_val(w.w, 0, sgn), a4);
+                a5 = __fmaf_rn(q3.y, byte_val(w.w, 1, sgn), a5);
+                a6 = __fmaf_rn(q3.z, byte_val(w.w, 2, sgn), a6);
+                a7 = __fmaf_rn(q3.w, byte_val(w.w, 3, sgn), a7);
+            }
+            for (int i = 2 * m2; i < n8; ++i) {  // an odd last step (not reached with 16-byte rows)
+                const float* qs = sq + 8 * i;
+                const uint8_t* xs = row + 8 * i;
+                a0 = __fmaf_rn(qs[0], sgn ? (float)(int8_t)xs[0] : (float)xs[0], a0);
+                a1 = __fmaf_rn(qs[1], sgn ? (float)(int8_t)xs[1] : (float)xs[1], a1);
+                a2 = __fmaf_rn(qs[2], sgn ? (float)(int8_t)xs[2] : (float)xs[2], a2);
+                a3 = __fmaf_rn(qs[3], sgn ? (float)(int8_t)xs[3] : (float)xs[3], a3);
+                a4 = __fmaf_rn(qs[4], sgn ? (float)(int8_t)xs[4] : (float)xs[4], a4);
+                a5 = __fmaf_rn(qs[5], sgn ? (float)(int8_t)xs[5] : (float)xs[5], a5);
+                a6 = __fmaf_rn(qs[6], sgn ? (float)(int8_t)xs[6] : (float)xs[6], a6);
+                a7 = __fmaf_rn(qs[7], sgn ? (float)(int8_t)xs[7] : (float)xs[7], a7);
+            }
+            sc = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), __fadd_rn(a2, a6)), __fadd_rn(__fadd_rn(a1, a5), __fadd_rn(a3, a7)));
+            for (int i = full8; i < dim; ++i)
+                sc = __fadd_rn(sc, __fmul_rn(sq[i], sgn ? (float)(int8_t)row[i] : (float)row[i]));
+            if (kMode == 1) sc = __fadd_rn(__ldg(e.rbase + q), sc);
+            score_out[(size_t)q * cand_cap + r_a + j] = sc;
+        }
+        q_a = q_n;
+        r_a = r_n;
+        s_a = s_n;
+    }
+}
+
+// Best k (k <= 32) of each query's scored candidates, one warp per query. A chunk of up to 512
+// scores is held in registers (16 per lane); the warp finds the k-th largest score key of the
+// chunk by a bitwise search over the 32-bit order-preserving keys, loads the external ids of the
+// few candidates at or above it (and at or above the running list's k-th), and inserts them into
+// the sorted list (lane j holds the j-th best). Order: score desc, external id asc (as k_topk).
+__global__ void __launch_bounds__(256) k_topk_warp(IndexView ix, const uint32_t* __restrict__ cand,
+                                                   const uint32_t* __restrict__ cand_n,
+                                                   const float* __restrict__ sc_in, int nq, int cand_cap, int k,
+                                                   uint64_t* ids, float* scores, uint32_t* out_n) {
+    constexpr int T = 16;
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (q >= nq) return;  // warp-uniform
+    const int n = (int)cand_n[q];
+    const float* sp = sc_in + (size_t)q * cand_cap;
+    const uint32_t* cq = cand + (size_t)q * cand_cap;
     float ms = -INFINITY;
     uint64_t mid = ~0ull;
-    const bool fused = score_out == nullptr;
-    if (nbatch > 0) issue(0);
-    for (int b = 0; b < nbatch; ++b) {
-        if (b + 1 < nbatch) {
-            issue(b + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncwarp();
-        const int r = 32 * b + 4 * warp + i_row;
-        float sc = -INFINITY;
-        uint64_t id = ~0ull;
-        if (r < n) {
-            const uint8_t* rp = mine + (size_t)(b & 1) * 4 * stride + (size_t)i_row * stride;
-            float acc = 0.0f;
-            for (int i = l8; i < full8; i += 8) {
-                float x;
-                if (kMode == 0)
-                    x = reinterpret_cast<const float*>(rp)[i];
-                else if (kMode == 1)
-                    x = (float)rp[i];
-                else
-                    x = (float)(int8_t)rp[i];
-                acc = __fmaf_rn(__ldg(qv + i), x, acc);
-            }
-            sc = hsum8_group(acc, gmask);
-            if (l8 == 0) {
-                for (int i = full8; i < dim; ++i) {
-                    float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i]
-                                         : (kMode == 1 ? (float)rp[i] : (float)(int8_t)rp[i]);
-                    sc = __fadd_rn(sc, __fmul_rn(__ldg(qv + i), x));
-                }
-                if (kMode == 1) sc = __fadd_rn(rbase, sc);
-                id = ix.ext_ids[__ldg(cq + r)];
-                if (!fused) score_out[(size_t)q * cand_cap + r] = sc;
-            }
-        }
-        __syncwarp();  // the buffer of batch b is refilled by issue(b + 2)
-        if (fused) {
+    int filled = 0;
+    for (int c0 = 0; c0 < n; c0 += 32 * T) {
+        float s[T];
+        uint32_t key[T];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float cs = __shfl_sync(0xFFFFFFFFu, sc, 8 * i);
-                const uint64_t ci = __shfl_sync(0xFFFFFFFFu, id, 8 * i);
-                if (32 * b + 4 * warp + i < n) warp_insert(ms, mid, cs, ci, k);
+        for (int t = 0; t < T; ++t) {
+            const int r = c0 + 32 * t + lane;
+            s[t] = r < n ? __ldg(sp + r) : -INFINITY;
+        }
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            const int r = c0 + 32 * t + lane;
+            key[t] = r < n ? float_key(s[t] == 0.0f ? 0.0f : s[t]) : 0u;
+        }
+        uint32_t thr = 0;
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t c = thr | (1u << bit);
+            int cnt = 0;
+#pragma unroll
+            for (int t = 0; t < T; ++t) cnt += key[t] >= c ? 1 : 0;
+            if (__reduce_add_sync(0xFFFFFFFFu, cnt) >= k) thr = c;
+        }
+        if (filled >= k) {
+            const float ts = __shfl_sync(0xFFFFFFFFu, ms, k - 1);
+            thr = max(thr, float_key(ts == 0.0f ? 0.0f : ts));
+        }
+        uint64_t id[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            const int r = c0 + 32 * t + lane;
+            id[t] = (r < n && key[t] >= thr) ? ix.ext_ids[__ldg(cq + r)] : ~0ull;
+        }
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            const int r = c0 + 32 * t + lane;
+            unsigned m = __ballot_sync(0xFFFFFFFFu, r < n && key[t] >= thr);
+            while (m) {
+                const int src = __ffs(m) - 1;
+                m &= m - 1;
+                const float cs = __shfl_sync(0xFFFFFFFFu, s[t], src);
+                const uint64_t ci = __shfl_sync(0xFFFFFFFFu, id[t], src);
+                warp_insert(ms, mid, cs, ci, k);
+                ++filled;
             }
         }
     }
-    if (!fused) return;
-    s_sc[warp][lane] = ms;
-    s_id[warp][lane] = mid;
-    __syncthreads();
-    if (warp == 0) {
-        float fs = -INFINITY;
-        uint64_t fid = ~0ull;
-        for (int w = 0; w < 8; ++w)
-            for (int j = 0; j < k; ++j) warp_insert(fs, fid, s_sc[w][j], s_id[w][j], k);
-        const int m = min(k, n);
-        if (lane < k) {
-            const bool v = lane < m;
-            ids[(size_t)q * k + lane] = v ? fid : ~0ull;
-            scores[(size_t)q * k + lane] = v ? fs : -INFINITY;
-        }
-        if (lane == 0) out_n[q] = (uint32_t)m;
+    const int got = min(k, n);
+    if (lane < k) {
+        const bool v = lane < got;
+        ids[(size_t)q * k + lane] = v ? mid : ~0ull;
+        scores[(size_t)q * k + lane] = v ? ms : -INFINITY;
     }
+    if (lane == 0) out_n[q] = (uint32_t)got;
 }
 
 }  // namespace
@@ -1866,7 +1711,7 @@ const char* kernel_name(int id) {
     static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
                                              "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
-                                             "k_pq_fold", "k_rerank",    "k_topk"};
+                                             "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -2027,65 +1872,42 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   uint32_t* err, float* score_scratch, cudaStream_t st) {
+                   float* score_scratch, uint32_t* item_scratch, cudaStream_t st) {
     if (nq <= 0) return;
     const int row_bytes = ix.rerank_mode == 0 ? ix.dim * 4 : ix.dim;
-    if (row_bytes % 16 == 0) {
-        int words = row_bytes / 4;
-        int stride_words = words + ((8 - words % 32) + 32) % 32;
-        const int stride = stride_words * 4;
-        const size_t smem = (size_t)8 * 2 * 4 * stride;
-        const bool fused = k <= 32;
-        float* so = fused ? nullptr : score_scratch;
+    if (row_bytes % 16 == 0 && score_scratch && item_scratch && k <= 4096) {
+        const void* fn = ix.rerank_mode == 0   ? (const void*)k_rerank_gather<0>
+                         : ix.rerank_mode == 1 ? (const void*)k_rerank_gather<1>
+                                               : (const void*)k_rerank_gather<2>;
+        const size_t smem = (size_t)8 * ((ix.dim + 3) & ~3) * sizeof(float);
+        set_smem(fn, smem);
+        int dev = 0, sms = 148, per_sm = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        const int grid = sms * per_sm;
+        {
+            Tick tk(kKRerankItems, st);
+            k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
+        }
         {
             Tick tk(kKRerank, st);
-            if (ix.rerank_mode == 0) {
-                set_smem((const void*)k_rerank_async<0>, smem);
-                k_rerank_async<0><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
-                                                         scores, out_n, so);
-            } else if (ix.rerank_mode == 1) {
-                set_smem((const void*)k_rerank_async<1>, smem);
-                k_rerank_async<1><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
-                                                         scores, out_n, so);
-            } else {
-                set_smem((const void*)k_rerank_async<2>, smem);
-                k_rerank_async<2><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, row_bytes, stride, ids,
-                                                         scores, out_n, so);
-            }
+            if (ix.rerank_mode == 0)
+                k_rerank_gather<0><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                                                            score_scratch);
+            else if (ix.rerank_mode == 1)
+                k_rerank_gather<1><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                                                            score_scratch);
+            else
+                k_rerank_gather<2><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                                                            score_scratch);
         }
-        if (!fused) {
-            const int P = next_pow2(k + kRerankChunk);
-            const size_t tsm = (size_t)P * (sizeof(uint64_t) + sizeof(float));
-            set_smem((const void*)k_topk, tsm);
+        if (k <= 32) {
             Tick tk(kKTopk, st);
-            k_topk<<<nq, kBS, tsm, st>>>(ix, cand, cand_n, score_scratch, cand_cap, k, P, ids, scores, out_n);
-        }
-        return;
-    }
-    if (row_bytes % 16 == 0 && score_scratch && k <= 4096) {
-        int words = row_bytes / 4;
-        int stride_words = words + ((8 - words % 32) + 32) % 32;
-        const int stride = stride_words * 4;
-        const size_t smem = 128 + (size_t)kPipeStages * kPipeRows * stride;
-        int sms = 148, cur = 0;
-        cudaGetDevice(&cur);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur);
-        const int grid = std::min(nq, sms);
-        {
-            Tick tk(kKRerank, st);
-            if (ix.rerank_mode == 0) {
-                set_smem((const void*)k_rerank_pipe<0>, smem);
-                k_rerank_pipe<0><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
-                                                          score_scratch, err);
-            } else if (ix.rerank_mode == 1) {
-                set_smem((const void*)k_rerank_pipe<1>, smem);
-                k_rerank_pipe<1><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
-                                                          score_scratch, err);
-            } else {
-                set_smem((const void*)k_rerank_pipe<2>, smem);
-                k_rerank_pipe<2><<<grid, 288, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, nq, row_bytes, stride,
-                                                          score_scratch, err);
-            }
+            k_topk_warp<<<(nq + 7) / 8, 256, 0, st>>>(ix, cand, cand_n, score_scratch, nq, cand_cap, k, ids, scores,
+                                                      out_n);
+            return;
         }
         const int P = next_pow2(k + kRerankChunk);
         const size_t tsm = (size_t)P * (sizeof(uint64_t) + sizeof(float));
@@ -2094,30 +1916,7 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
         k_topk<<<nq, kBS, tsm, st>>>(ix, cand, cand_n, score_scratch, cand_cap, k, P, ids, scores, out_n);
         return;
     }
-    if (row_bytes % 16 == 0 && k <= 2048) {
-        // TMA-staged rows: padded stride keeps the 8-lane reads of 4 rows per warp on distinct banks
-        int words = row_bytes / 4;
-        int stride_words = words + ((8 - words % 32) + 32) % 32;
-        const int stride = stride_words * 4;
-        const int P = next_pow2(k + kTmaSortChunk);
-        size_t smem = 16 + (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (((size_t)ix.dim * 4 + 15) & ~size_t(15)) +
-                      2 * (size_t)kTmaRows * stride;
-        Tick tk(kKRerank, st);
-        if (ix.rerank_mode == 0) {
-            set_smem((const void*)k_rerank_tma<0>, smem);
-            k_rerank_tma<0><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
-                                                   scores, out_n, err);
-        } else if (ix.rerank_mode == 1) {
-            set_smem((const void*)k_rerank_tma<1>, smem);
-            k_rerank_tma<1><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
-                                                   scores, out_n, err);
-        } else {
-            set_smem((const void*)k_rerank_tma<2>, smem);
-            k_rerank_tma<2><<<nq, kBS, smem, st>>>(ix, Q, e, cand, cand_n, cand_cap, k, P, row_bytes, stride, ids,
-                                                   scores, out_n, err);
-        }
-        return;
-    }
+    // rows that are not 16-byte multiples (odd dimensions): one CTA per query, rows read in place
     int P = next_pow2(k + kRerankChunk);
     size_t smem = (size_t)P * (sizeof(uint64_t) + sizeof(float)) + (size_t)ix.dim * sizeof(float);
     set_smem((const void*)k_rerank, smem);

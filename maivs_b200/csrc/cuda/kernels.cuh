@@ -53,7 +53,7 @@ struct IndexView {
 // after synchronising. Every launch is counted whether or not a clock is installed.
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
-    kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kNumKernels
+    kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kNumKernels
 };
 const char* kernel_name(int id);
 struct KernelClock {
@@ -152,11 +152,12 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
                      uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st);
 
 // Exact rerank + top-k (index.rs:1309-1378); writes k ids/scores per query, padded.
-// `err` counts blocks whose row copies did not complete within the wait limit; `score_scratch`
-// (nq x cand_cap floats) enables the pipelined gather + separate top-k.
+// `score_scratch` (nq x cand_cap floats) and `item_scratch` (nq + 1 words) enable the flattened
+// register gather + separate top-k, used whenever rows are 16-byte multiples; other rows take a
+// one-CTA-per-query kernel.
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   uint32_t* err, float* score_scratch, cudaStream_t st);
+                   float* score_scratch, uint32_t* item_scratch, cudaStream_t st);
 
 }  // namespace dev
 }  // namespace maivs

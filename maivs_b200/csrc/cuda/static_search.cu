@@ -93,7 +93,7 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
 
     dev::QueryEnc e{};
     dev::PerQueryBufs b{};
-    uint32_t *sl, *sl_n, *tsc, *chosen, *nch, *nout;
+    uint32_t *sl, *sl_n, *tsc, *chosen, *nch, *nout, *ritem;
     uint16_t* hs;
     float *cscore, *rsc;
     auto carve = [&](Carve& c) {
@@ -122,6 +122,7 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
         b.overflow = d_flags_;
         rsc = c.take<float>((size_t)nq * cand_cap);
         nout = c.take<uint32_t>(nq);
+        ritem = c.take<uint32_t>((size_t)nq + 1);
     };
     Carve sizing{nullptr};
     carve(sizing);
@@ -143,7 +144,7 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
     if (rc != kOk) return rc;
     dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
                          h.filter_lo, h.filter_hi, b, st);
-    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, nout, d_flags_ + 2, rsc,
+    dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, nout, rsc, ritem,
                        st);
     int kid = -1;
     cudaError_t le = dev::take_launch_error(&kid);
