@@ -193,6 +193,20 @@ def measured_peaks() -> dict:
 
 # ---- arms ---------------------------------------------------------------------------------------
 
+def ncu_traffic(kernel: str, stats: dict):
+    """DRAM bytes per launch of `kernel` from the committed ncu capture, scaled to this run's work."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            ent = json.load(f).get(kernel)
+    except (OSError, ValueError):
+        return None
+    if not ent:
+        return None
+    now = stats.get(ent["scale_counter"], 0.0)
+    return round(ent["dram_bytes_per_launch"] * now / ent["counter_at_capture"]) if now else None
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -353,6 +367,7 @@ def run_maivs(args):
         alg = stats.get("scan_code_bytes", 0.0) + stats.get("rerank_bytes", 0.0)
         what = "scan codes + rerank rows"
     achieved = alg / (per_launch_ms / 1e3) / 1e9 if per_launch_ms > 0 else 0.0
+    traffic = ncu_traffic(name, stats)
     shares = {k: round(v[0] / max(sum(x[0] for x in ktimes.values()), 1e-9), 4) for k, v in ktimes.items() if v[1]}
 
     out = {
@@ -381,7 +396,7 @@ def run_maivs(args):
                 "d2h_bytes_per_step": args.nq * K * 12},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": round(alg), "avg_launch_ms": round(per_launch_ms, 5),
                      "what": what, "peak_src": peaks["src"]},
         "kernel_share": shares,
