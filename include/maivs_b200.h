@@ -121,6 +121,27 @@ int maivs_search_batch_device_noalloc(maivs_index* ix, const float* d_queries, s
                                       float target_confidence, float beta, uint64_t* d_ids, float* d_scores,
                                       void* stream);
 
+/* Cell-range sharding over the GPUs of one job (no counterpart in the reference, which runs in
+ * one process; the cell-range split is its stated unit of parallelism, docs/ARCHITECTURE.md:28-30).
+ * Rank r of `world` keeps the scan data of a contiguous range of cells holding ~1/world of the
+ * member entries, plus the whole routing tables and rerank rows. Every search on a sharded handle
+ * runs the cell-major join with three NCCL all-gathers (the seed cut-off, the candidate cut-off and
+ * the best-k lists, merged on the device), so every rank must issue the same searches with the same
+ * queries, and each rank's results equal the unsharded cell-major join's bit for bit.
+ * maivs_nccl_unique_id: 128 bytes that rank 0 makes and the host sends to every rank.
+ * maivs_shard: collective; world = 1 returns the handle to unsharded searching. NCCL is loaded
+ * (libnccl.so.2) only here; a rank that does not join ends the set-up with an error after 120 s.
+ * maivs_shard_range: the cells [lo, hi) of rank `rank` (host only).
+ * maivs_search_batch_sharded_emulated: the same protocol with `world` shards inside this process on
+ * the handle's device, exchanging through device copies (a one-GPU check of the sharded path; it
+ * keeps `world` device images). */
+int maivs_nccl_unique_id(uint8_t* id, size_t cap);
+int maivs_shard(maivs_index* ix, int rank, int world, const uint8_t* nccl_id, size_t id_len);
+int maivs_shard_range(maivs_index* ix, int rank, int world, uint32_t* lo, uint32_t* hi);
+int maivs_search_batch_sharded_emulated(maivs_index* ix, int world, const float* d_queries, size_t nq, size_t k,
+                                        size_t nprobe, float target_confidence, float beta, uint64_t* d_ids,
+                                        float* d_scores, void* stream);
+
 /* Host copy of one internal array, for persistence, inspection and parity tests: the pointer
  * stays valid until the next mutation of the index. Names: "vecs_f32", "scan_i8", "bits",
  * "ext_ids", "slot_cell", "slot_cells", "cell_members", "cell_member_off", "centroids",

@@ -14,7 +14,7 @@ import numpy as np
 
 from . import _lib
 
-__all__ = ["FlatCellIndex", "profile", "profile_read", "MaivsError"]
+__all__ = ["FlatCellIndex", "profile", "profile_read", "MaivsError", "nccl_unique_id", "shard_over_torch"]
 
 
 class MaivsError(RuntimeError):
@@ -208,6 +208,31 @@ class FlatCellIndex:
             self._h, C.c_void_p(d_queries), int(nq), int(k), int(nprobe), float(target_confidence), float(beta),
             int(bool(cell_major)), C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(stream or None)))
 
+    # ---- cell-range sharding (one rank per GPU; no counterpart in the reference) ----
+    def shard(self, rank: int, world: int, nccl_id: bytes = b"") -> None:
+        """Make this handle rank `rank` of `world` cell-range shards (collective over the ranks).
+
+        Every later search runs the sharded cell-major join with NCCL all-gathers, so all ranks
+        must issue the same searches with the same queries; results equal the unsharded join's.
+        `nccl_id` is rank 0's nccl_unique_id(), shared by the host. world=1 unshards."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(nccl_id.ljust(128, b"\0")[:128]) if nccl_id else None
+        self._check(_lib.lib().maivs_shard(self._h, int(rank), int(world), buf, 128 if nccl_id else 0))
+
+    def shard_range(self, rank: int, world: int) -> tuple[int, int]:
+        """Cells [lo, hi) that rank `rank` of `world` scans (balanced by member entries)."""
+        lo, hi = C.c_uint32(0), C.c_uint32(0)
+        self._check(_lib.lib().maivs_shard_range(self._h, int(rank), int(world), C.byref(lo), C.byref(hi)))
+        return int(lo.value), int(hi.value)
+
+    def search_batch_sharded_emulated(self, world: int, d_queries: int, nq: int, k: int, d_ids: int,
+                                      d_scores: int, nprobe: int = 16, target_confidence: float = 0.95,
+                                      beta: float = 8.0, stream: int = 0) -> None:
+        """The sharded protocol with `world` shards in this process on one GPU (device copies
+        stand in for NCCL); device pointers in and out, enqueued on `stream`."""
+        self._check(_lib.lib().maivs_search_batch_sharded_emulated(
+            self._h, int(world), C.c_void_p(d_queries), int(nq), int(k), int(nprobe), float(target_confidence),
+            float(beta), C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(stream or None)))
+
     def device_flags(self, stream: int = 0) -> int:
         f = C.c_uint32(0)
         self._check(_lib.lib().maivs_device_flags(self._h, C.c_void_p(stream or None), C.byref(f)))
@@ -329,6 +354,28 @@ CONFIG_FIELDS = ("dim", "dim_pad", "nw", "rerank_factor", "two_stage", "shortlis
                  "max_assign", "fastscan", "per_dim_sq", "i8_rerank", "keep_f32", "adaptive", "at_margin",
                  "quant_scale", "compacted", "n_live", "cm_min_batch", "has_filter", "filter_lo", "filter_hi",
                  "tree_beam_frac", "tree_n_leaf", "graph_route", "graph_min_cells")
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (rank 0 makes it; every rank passes it to shard())."""
+    buf = (C.c_uint8 * 128)()
+    rc = _lib.lib().maivs_nccl_unique_id(buf, 128)
+    if rc != _lib.OK:
+        raise MaivsError(f"nccl_unique_id failed: {_lib.lib().maivs_status_string(rc).decode()}")
+    return bytes(buf)
+
+
+def shard_over_torch(ix: "FlatCellIndex", group=None) -> None:
+    """Shard `ix` over the ranks of a torch.distributed group (rank r -> cells of rank r).
+
+    Rank 0 makes the NCCL id and the group broadcasts it; torch is only the rendezvous here,
+    the searches then run over the engine's own NCCL communicator."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    ix.shard(rank, world, obj[0])
 
 
 def launch_count() -> int:

@@ -34,6 +34,7 @@ SOURCES = [
     ("cuda/kernels.cu", "nvcc"),
     ("cuda/engine.cu", "nvcc"),
     ("cuda/static_search.cu", "nvcc"),
+    ("cuda/shard.cu", "nvcc"),
 ]
 HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/engine.h"]
 
@@ -79,7 +80,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             if verbose and warn.strip():
                 print(warn)
     if force or jobs or _stale(LIB, objs):
-        link = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-Xcompiler", "-fopenmp", "-lgomp"]
+        link = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-Xcompiler", "-fopenmp", "-lgomp", "-ldl"]
         run(link)
     return LIB
 

@@ -20,7 +20,14 @@ using maivs::HostIndex;
 
 struct maivs_index {
     HostIndex h;
+    // cell-range sharding (declared before `d`, which points at it, so it is destroyed after)
+    std::unique_ptr<maivs::Exchange> exch;
+    int shard_rank = 0, shard_world = 1;
     std::unique_ptr<DeviceIndex> d;
+    // shards of the in-process emulation of the sharded protocol
+    std::vector<std::unique_ptr<DeviceIndex>> emu;
+    uint64_t emu_version = ~0ull;
+    int emu_world = 0, emu_device = -1;
     int device = 0;
     std::string err;
     std::mutex mu;
@@ -59,8 +66,11 @@ int ensure_device(maivs_index* ix) {
         return fail(ix, MAIVS_NO_DEVICE, "no CUDA device is visible; the MAIVS GPU search has no CPU fallback");
     if (ix->d && ix->d->version() == ix->h.version && ix->d->device() == ix->device) return MAIVS_OK;
     auto d = std::make_unique<DeviceIndex>();
-    std::string e = d->upload(ix->h, ix->device);
+    uint32_t lo = 0, hi = 0xFFFFFFFFu;
+    if (ix->exch) maivs::shard_range(ix->h, ix->shard_rank, ix->shard_world, &lo, &hi);
+    std::string e = d->upload(ix->h, ix->device, lo, hi);
     if (!e.empty()) return fail(ix, MAIVS_BAD_STATE, e);
+    d->set_shard(ix->exch.get(), ix->shard_rank, ix->shard_world);
     d->set_timing(g_prof_on.load());
     ix->d = std::move(d);
     return MAIVS_OK;
@@ -456,6 +466,7 @@ int maivs_search_batch_device_noalloc(maivs_index* ix, const float* dQ, size_t n
     if (k == 0) return fail(ix, MAIVS_BAD_ARG, "k must be positive");
     if (k > 4096) return fail(ix, MAIVS_UNSUPPORTED, "k above 4096 is not supported");
     if (nq > 64) return fail(ix, MAIVS_BAD_ARG, "the allocation-free search takes at most 64 queries per call");
+    if (ix->exch) return fail(ix, MAIVS_UNSUPPORTED, "the allocation-free search does not run on a sharded index");
     // uploading the index allocates, so the device image must already be current
     if (!ix->d || ix->d->version() != ix->h.version || ix->d->device() != ix->device)
         return fail(ix, MAIVS_BAD_STATE, "no current device image; call maivs_to_device() before this search");
@@ -468,6 +479,92 @@ int maivs_search_batch_device_noalloc(maivs_index* ix, const float* dQ, size_t n
     a.cell_major = false;
     std::string err;
     int rc = ix->d->search_static(ix->h, dQ, a, d_ids, d_scores, (cudaStream_t)stream, err);
+    if (rc != MAIVS_OK) return fail(ix, rc, err);
+    return MAIVS_OK;
+}
+
+int maivs_nccl_unique_id(uint8_t* id, size_t cap) {
+    if (!id || cap < 128) return MAIVS_BAD_ARG;
+    std::string err;
+    return maivs::nccl_unique_id(id, err);
+}
+
+int maivs_shard(maivs_index* ix, int rank, int world, const uint8_t* nccl_id, size_t id_len) {
+    LOCK(ix);
+    if (world < 1 || rank < 0 || rank >= world) return fail(ix, MAIVS_BAD_ARG, "need 0 <= rank < world");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return fail(ix, MAIVS_NO_DEVICE, "no CUDA device is visible; the MAIVS GPU search has no CPU fallback");
+    ix->d.reset();
+    ix->exch.reset();
+    ix->shard_rank = 0;
+    ix->shard_world = 1;
+    if (world == 1) return MAIVS_OK;
+    if (!nccl_id || id_len != 128) return fail(ix, MAIVS_BAD_ARG, "the NCCL unique id is 128 bytes");
+    std::string err;
+    auto x = maivs::nccl_exchange(nccl_id, rank, world, ix->device, err);
+    if (!x) return fail(ix, MAIVS_CUDA_ERROR, err);
+    ix->exch = std::move(x);
+    ix->shard_rank = rank;
+    ix->shard_world = world;
+    return MAIVS_OK;
+}
+
+int maivs_shard_range(maivs_index* ix, int rank, int world, uint32_t* lo, uint32_t* hi) {
+    LOCK(ix);
+    if (world < 1 || rank < 0 || rank >= world) return fail(ix, MAIVS_BAD_ARG, "need 0 <= rank < world");
+    maivs::shard_range(ix->h, rank, world, lo, hi);
+    return MAIVS_OK;
+}
+
+int maivs_search_batch_sharded_emulated(maivs_index* ix, int world, const float* dQ, size_t nq, size_t k,
+                                        size_t nprobe, float tc, float beta, uint64_t* d_ids, float* d_scores,
+                                        void* stream) {
+    LOCK(ix);
+    if (nq == 0) return MAIVS_OK;
+    if (k == 0) return fail(ix, MAIVS_BAD_ARG, "k must be positive");
+    if (world < 1 || world > 64) return fail(ix, MAIVS_BAD_ARG, "world must be in 1..64");
+    if (ix->h.cells.empty() || ix->h.n_live == 0) return fail(ix, MAIVS_BAD_STATE, "the index is empty");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return fail(ix, MAIVS_NO_DEVICE, "no CUDA device is visible; the MAIVS GPU search has no CPU fallback");
+    if (ix->emu_version != ix->h.version || ix->emu_world != world || ix->emu_device != ix->device) {
+        ix->emu.clear();
+        ix->emu_version = ~0ull;
+        for (int r = 0; r < world; ++r) {
+            uint32_t lo, hi;
+            maivs::shard_range(ix->h, r, world, &lo, &hi);
+            auto d = std::make_unique<DeviceIndex>();
+            std::string e = d->upload(ix->h, ix->device, lo, hi);
+            if (!e.empty()) {
+                ix->emu.clear();
+                return fail(ix, MAIVS_BAD_STATE, e);
+            }
+            ix->emu.push_back(std::move(d));
+        }
+        ix->emu_version = ix->h.version;
+        ix->emu_world = world;
+        ix->emu_device = ix->device;
+    }
+    maivs::SearchArgs a;
+    a.nq = (int)nq;
+    a.k = (int)k;
+    a.nprobe = (int)std::min<size_t>(nprobe, 1u << 30);
+    a.tc = tc;
+    a.beta = beta;
+    a.cell_major = true;
+    cudaSetDevice(ix->device);
+    static thread_local uint32_t* d_nout = nullptr;
+    static thread_local size_t d_nout_cap = 0;
+    if (d_nout_cap < nq) {
+        if (d_nout) cudaFree(d_nout);
+        d_nout = nullptr;
+        if (cudaMalloc(&d_nout, nq * sizeof(uint32_t)) != cudaSuccess) return fail(ix, MAIVS_OOM, "cudaMalloc failed");
+        d_nout_cap = nq;
+    }
+    std::string err;
+    int rc = maivs::search_emulated_shards(ix->h, ix->emu, dQ, a, d_ids, d_scores, d_nout,
+                                           stream ? (cudaStream_t)stream : ix->emu[0]->stream(), err);
     if (rc != MAIVS_OK) return fail(ix, rc, err);
     return MAIVS_OK;
 }

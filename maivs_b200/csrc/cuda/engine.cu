@@ -63,7 +63,7 @@ T* DeviceIndex::upload_vec(const std::vector<T>& v) {
     return p;
 }
 
-std::string DeviceIndex::upload(const HostIndex& h, int device) {
+std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, uint32_t c_hi) {
     if (!h.compacted || !h.fastscan || h.fs_off.empty())
         return "the GPU search needs a compacted FastScan index: call set_fastscan(True) and compact() first";
     if (h.nw > 16) return "codes longer than 1024 bits are not supported";
@@ -93,7 +93,7 @@ std::string DeviceIndex::upload(const HostIndex& h, int device) {
     std::vector<uint32_t> moff(M + 1, 0), woff(M + 1, 0);
     max_members_ = 0;
     for (size_t c = 0; c < M; ++c) {
-        size_t n = h.cells[c].members.size();
+        size_t n = (c >= c_lo && c < c_hi) ? h.cells[c].members.size() : 0;
         max_members_ = std::max(max_members_, n);
         moff[c + 1] = moff[c] + (uint32_t)n;
         woff[c + 1] = woff[c] + (uint32_t)(npos * ((n + 7) / 8));
@@ -102,8 +102,8 @@ std::string DeviceIndex::upload(const HostIndex& h, int device) {
 #pragma omp parallel for schedule(dynamic, 16)
     for (long long c = 0; c < (long long)M; ++c) {
         const auto& mem = h.cells[c].members;
-        size_t n = mem.size(), ng = (n + 7) / 8;
-        std::copy(mem.begin(), mem.end(), slots.begin() + moff[c]);
+        size_t n = moff[c + 1] - moff[c], ng = (n + 7) / 8;
+        std::copy(mem.begin(), mem.begin() + n, slots.begin() + moff[c]);
         uint32_t* cw = codes.data() + woff[c];
         for (size_t g = 0; g < ng; ++g)
             for (size_t b = 0; b < 8 && 8 * g + b < n; ++b) {
@@ -490,8 +490,9 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
     if (!st) st = stream_;
     dev::take_launch_error(nullptr);
     cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
-    int rc = use_cell_major(h, a) ? run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err)
-                                  : run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+    int rc = exch_                  ? search_sharded(h, dQ, a, d_ids, d_scores, d_nout, st, err)
+             : use_cell_major(h, a) ? run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err)
+                                    : run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
     int kid = -1;
     cudaError_t le = dev::take_launch_error(&kid);
     if (le != cudaSuccess) {

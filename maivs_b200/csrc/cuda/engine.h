@@ -55,6 +55,29 @@ struct DebugOut {
     std::vector<uint32_t> seed_n, tau, rest_hi, rest_n;  // cell-major only (stage 2)
 };
 
+// All-gather used by the cell-range sharded search: `bytes` from every rank's `send` land in
+// `recv`, rank r's block at recv + r * bytes, ordered on stream `st`.
+class Exchange {
+   public:
+    virtual ~Exchange() = default;
+    virtual int all_gather(const void* send, void* recv, size_t bytes, cudaStream_t st, std::string& err) = 0;
+};
+
+// NCCL over NVLink / NVSwitch (libnccl.so.2 is loaded on first use). `id` is the 128-byte
+// ncclUniqueId that rank 0 made with nccl_unique_id and the host shared with every rank.
+int nccl_unique_id(uint8_t* id, std::string& err);
+std::unique_ptr<Exchange> nccl_exchange(const uint8_t* id, int rank, int world, int device, std::string& err);
+
+// Cells [lo, hi) of rank `rank` of `world`: contiguous ranges balanced by member entries.
+void shard_range(const HostIndex& h, int rank, int world, uint32_t* lo, uint32_t* hi);
+
+class DeviceIndex;
+// The sharded protocol with every shard in this process on one device, exchanging through device
+// copies: results equal the NCCL path's, which equal the unsharded cell-major join's.
+int search_emulated_shards(const HostIndex& h, std::vector<std::unique_ptr<DeviceIndex>>& shards, const float* dQ,
+                           const SearchArgs& a, uint64_t* d_ids, float* d_scores, uint32_t* d_nout, cudaStream_t st,
+                           std::string& err);
+
 class DeviceIndex {
    public:
     // When set, the next search stops after dbg->stage and fills *dbg (synchronous).
@@ -62,7 +85,16 @@ class DeviceIndex {
 
     ~DeviceIndex();
     // Builds the device image from a compacted FastScan host index; returns an error message.
-    std::string upload(const HostIndex& h, int device);
+    // With a cell range, only cells [c_lo, c_hi) keep their members (a cell-range shard); the
+    // routing tables and the rerank rows are always whole.
+    std::string upload(const HostIndex& h, int device, uint32_t c_lo = 0, uint32_t c_hi = 0xFFFFFFFFu);
+    // Makes this image rank `rank` of a sharded search over `x` (not owned; null: unsharded).
+    void set_shard(Exchange* x, int rank, int world) {
+        exch_ = x;
+        shard_rank_ = rank;
+        shard_world_ = x ? world : 1;
+    }
+    bool sharded() const { return exch_ != nullptr; }
     uint64_t version() const { return version_; }
     int device() const { return device_; }
     cudaStream_t stream() const { return stream_; }
@@ -98,7 +130,31 @@ class DeviceIndex {
     dev::KernelClock* kernel_clock() { return clock_.get(); }
     std::vector<std::pair<std::string, double>> last_stats();
 
+    // Phases of the cell-range sharded join (one shard's side); search_sharded and
+    // search_emulated_shards put the all-gathers between them.
+    struct ShardRun {
+        int nq = 0, k = 0, nprobe = 0, target = 0, xl = 0, W = 0;
+        bool rest = false;
+        size_t lb = 0, tb = 0;
+        const float* dQ = nullptr;
+        cudaStream_t st = nullptr;
+        dev::QueryEnc e{};
+        dev::CellMajorBufs b{};
+        uint32_t *chosen = nullptr, *nch = nullptr, *ritem = nullptr;
+        float *cscore = nullptr, *rsc = nullptr;
+        uint8_t *xsend = nullptr, *xrecv = nullptr, *tsend = nullptr, *trecv = nullptr;
+    };
+    int shard_begin(const HostIndex& h, const float* dQ, const SearchArgs& a, int W, cudaStream_t st, ShardRun& r,
+                    std::string& err);
+    void shard_after_seed(const HostIndex& h, ShardRun& r);
+    void shard_after_cut(const HostIndex& h, ShardRun& r);
+    void shard_merge(ShardRun& r, uint64_t* d_ids, float* d_scores, uint32_t* d_nout);
+
    private:
+    int search_sharded(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
+                       uint32_t* d_nout, cudaStream_t st, std::string& err);
+    Exchange* exch_ = nullptr;
+    int shard_rank_ = 0, shard_world_ = 1;
     void* alloc(size_t bytes);
     template <typename T>
     T* upload_vec(const std::vector<T>& v);

@@ -702,10 +702,94 @@ __global__ void __launch_bounds__(kBS) k_rescore_select(IndexView ix, QueryEnc e
 
 // ---- cell-major: seed + adaptive prune (index.rs:2126-2191) --------------------------------------
 
+// ---- cell-range shards: distance lists exchanged between shards -----------------------------------
+// A shard publishes, per query, how many entries it holds and the smallest min(count, xl) of their
+// distances (any order). The kth smallest distance of the union of all shards is then exact for
+// any kth <= xl: a shard holding kth or more entries at or below a value lists kth of them, and a
+// shard holding fewer lists them all. Rank r's block of an all-gathered buffer holds nq counts
+// (u32), then nq x xl distances (u16; distances are at most 255 x 256).
+
+__host__ __device__ inline size_t shard_list_bytes(int nq, int xl) {
+    return (((size_t)nq * 4 + (size_t)nq * xl * 2) + 15) & ~(size_t)15;
+}
+
+// Writes the smallest min(na + nb, L) distances (key >> 32) of two key segments to out.
+__device__ void emit_smallest_d(const uint64_t* a, int na, const uint64_t* b, int nb, int L, uint16_t* out,
+                                uint32_t* hist) {
+    __shared__ uint32_t s_cnt;
+    const int n = na + nb;
+    uint32_t dl = 0xFFFFFFFFu;
+    if (n > L) dl = (uint32_t)(block_select_kth(a, na, b, nb, L, 5, 4, hist) >> 32);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        const uint64_t k = i < na ? a[i] : (i < n ? b[i - na] : ~0ull);
+        const uint32_t d = (uint32_t)(k >> 32);
+        const bool take = i < n && d < dl;
+        const uint32_t p = warp_append(take, &s_cnt);
+        if (take) out[p] = (uint16_t)d;
+    }
+    __syncthreads();
+    const int m = min(n, L);
+    for (int i = (int)s_cnt + threadIdx.x; i < m; i += blockDim.x) out[i] = (uint16_t)dl;  // ties at the Lth
+    __syncthreads();
+}
+
+__device__ __forceinline__ uint32_t shard_count(const uint8_t* xall, size_t rank_bytes, int r, int q) {
+    return reinterpret_cast<const uint32_t*>(xall + (size_t)r * rank_bytes)[q];
+}
+__device__ __forceinline__ const uint16_t* shard_list(const uint8_t* xall, size_t rank_bytes, int r, int nq, int q,
+                                                      int xl) {
+    return reinterpret_cast<const uint16_t*>(xall + (size_t)r * rank_bytes + (size_t)nq * 4) + (size_t)q * xl;
+}
+
+// The kth smallest (1-based) distance of the union of W shards' lists for query q.
+__device__ uint32_t block_select_lists(const uint8_t* xall, size_t rank_bytes, int W, int nq, int q, int xl,
+                                       int kth, uint32_t* hist) {
+    __shared__ uint32_t s_digit;
+    __shared__ int s_rem;
+    if (threadIdx.x == 0) s_rem = kth;
+    uint32_t hi = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int r = 0; r < W; ++r) {
+            const int cnt = min((int)shard_count(xall, rank_bytes, r, q), xl);
+            const uint16_t* lst = shard_list(xall, rank_bytes, r, nq, q, xl);
+            for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
+                const uint32_t v = lst[j];
+                if (pass == 0)
+                    atomicAdd(&hist[v >> 8], 1u);
+                else if ((v >> 8) == hi)
+                    atomicAdd(&hist[v & 255u], 1u);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int rem = s_rem, digit = 255;
+            for (int t = 0; t < 256; ++t) {
+                if ((int)hist[t] >= rem) {
+                    digit = t;
+                    break;
+                }
+                rem -= (int)hist[t];
+            }
+            s_rem = rem;
+            s_digit = (uint32_t)digit;
+        }
+        __syncthreads();
+        if (pass == 0) hi = s_digit;
+    }
+    const uint32_t v = (hi << 8) | s_digit;
+    __syncthreads();
+    return v;
+}
+
 __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                               const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
                                               int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
-                                              int keys_in_smem) {
+                                              int keys_in_smem, uint16_t* xlist, uint32_t* xcnt, int xl) {
     extern __shared__ __align__(16) uint8_t lut_s[];  // npos x 16 LUT bytes, then (optionally) the keys
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_n;
@@ -787,6 +871,14 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
         if (threadIdx.x == 0) atomicAdd(b.overflow, 1u);
         n = b.seed_cap;
     }
+    if (xlist) {  // cell-range shard: publish this shard's seed distances; k_seed_finish goes on
+        emit_smallest_d(keys, n, nullptr, 0, xl, xlist + (size_t)q * xl, hist);
+        if (threadIdx.x == 0) {
+            xcnt[q] = (uint32_t)n;
+            b.seed_n[q] = (uint32_t)n;
+        }
+        return;
+    }
     uint32_t tau = maxk;
     if (n >= target) {
         uint64_t kk = block_select_kth(keys, n, nullptr, 0, target, 5, 4, hist);
@@ -846,6 +938,90 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
         b.rest_hi[q] = (uint32_t)rest_end;
         b.rest_n[q] = 0;
     }
+}
+
+// Cell-range shard, after the seed lists are all-gathered: the global seed cut-off tau (the
+// target-th smallest seed distance over all shards, index.rs:2150-2160), this shard's seed
+// survivors (d <= tau) and the adaptive end of the rest probes (index.rs:2162-2191), exactly as
+// k_seed computes them on a whole index.
+__global__ void __launch_bounds__(kBS) k_seed_finish(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                     const float* __restrict__ cscore,
+                                                     const uint32_t* __restrict__ nch, int nprobe, int target,
+                                                     int adaptive, float at_margin, CellMajorBufs b,
+                                                     const uint8_t* __restrict__ xall, size_t rank_bytes, int W,
+                                                     int nq, int xl) {
+    __shared__ uint32_t hist[256];
+    __shared__ int s_last;
+    __shared__ uint32_t s_out;
+    const int q = blockIdx.x;
+    const int n_ch = (int)nch[q];
+    const int ns = min(kSeedCells, n_ch);
+    const uint32_t* ch = chosen + (size_t)q * nprobe;
+    const uint32_t maxk = ix.maxk;
+    unsigned long long ng = 0;
+    for (int r = 0; r < W; ++r) ng += shard_count(xall, rank_bytes, r, q);
+    const bool full = ng >= (unsigned long long)target;
+    uint32_t tau = maxk;
+    if (full) tau = block_select_lists(xall, rank_bytes, W, nq, q, xl, target, hist);
+    uint64_t* sbuf = b.seed_buf + (size_t)q * b.seed_cap;
+    int n = (int)b.seed_n[q];
+    if (threadIdx.x == 0) {
+        s_out = 0;
+        s_last = -1;
+    }
+    __syncthreads();
+    if (full) {
+        using BS = cub::BlockScan<uint32_t, kBS>;
+        __shared__ typename BS::TempStorage scan;
+        for (int base = 0; base < n; base += kBS) {
+            int i = base + threadIdx.x;
+            uint64_t key = i < n ? sbuf[i] : 0;
+            uint32_t f = (i < n && (uint32_t)(key >> 32) <= tau) ? 1u : 0u;
+            uint32_t pos, agg;
+            BS(scan).ExclusiveSum(f, pos, agg);
+            __syncthreads();
+            uint32_t off = s_out;
+            if (f) sbuf[off + pos] = key;
+            __syncthreads();
+            if (threadIdx.x == 0) s_out = off + agg;
+            __syncthreads();
+        }
+        n = (int)s_out;
+    }
+    int rest_end = n_ch;
+    if (adaptive && full && ns < n_ch) {
+        const float norm = fs_norm(ix.dim_pad);
+        float thr = clampf(__fdiv_rn(fs_estimate(e.fs_delta[q], e.fs_bias[q], maxk - tau), norm), -1.0f, 1.0f);
+        float X = __fsub_rn(thr, at_margin);
+        for (int i = ns + threadIdx.x; i < n_ch; i += kBS) {
+            float bnd = cell_bound(cscore[(size_t)q * nprobe + i], ix.r_bound[ch[i]]);
+            if (bnd >= X) atomicMax(&s_last, i);
+        }
+        __syncthreads();
+        rest_end = s_last >= 0 ? s_last + 1 : ns;
+    }
+    if (threadIdx.x == 0) {
+        b.tau[q] = tau;
+        b.seed_n[q] = (uint32_t)n;
+        b.rest_hi[q] = (uint32_t)rest_end;
+        b.rest_n[q] = 0;
+    }
+}
+
+// Cell-range shard, after its rest scan: publish the smallest distances of its survivors (seed and
+// rest) for the global candidate cut.
+__global__ void __launch_bounds__(kBS) k_local_list(CellMajorBufs b, uint16_t* xlist, uint32_t* xcnt, int xl) {
+    __shared__ uint32_t hist[256];
+    const int q = blockIdx.x;
+    const int ns = (int)b.seed_n[q];
+    int nr = (int)b.rest_n[q];
+    if (nr > b.rest_cap) {
+        if (threadIdx.x == 0) atomicAdd(b.overflow, 1u);
+        nr = b.rest_cap;
+    }
+    emit_smallest_d(b.seed_buf + (size_t)q * b.seed_cap, ns, b.rest_buf + (size_t)q * b.rest_cap, nr, xl,
+                    xlist + (size_t)q * xl, hist);
+    if (threadIdx.x == 0) xcnt[q] = (uint32_t)(ns + nr);
 }
 
 // ---- cell-major: inversion (index.rs:2193-2213) ---------------------------------------------------
@@ -940,7 +1116,11 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
 
 // ---- cell-major: merge + exact global cut, ties kept (index.rs:2277-2306) ---------------------------
 
-__global__ void __launch_bounds__(kBS) k_final_cm(CellMajorBufs b, int target) {
+// With W > 0 (cell-range shard) the cut comes from all shards: the target-th smallest distance of
+// the all-gathered lists when the shards hold more than target entries together, else no cut
+// (xall == nullptr: no rest scan ran, so every shard's seed survivors are already within it).
+__global__ void __launch_bounds__(kBS) k_final_cm(CellMajorBufs b, int target, const uint8_t* __restrict__ xall,
+                                                  size_t rank_bytes, int W, int nq, int xl) {
     __shared__ uint32_t hist[256];
     const int q = blockIdx.x;
     const uint64_t* sb = b.seed_buf + (size_t)q * b.seed_cap;
@@ -953,7 +1133,13 @@ __global__ void __launch_bounds__(kBS) k_final_cm(CellMajorBufs b, int target) {
     }
     const int total = ns + nr;
     uint32_t D = 0xFFFFFFFFu;
-    if (total > target) D = (uint32_t)(block_select_kth(sb, ns, rb, nr, target, 5, 4, hist) >> 32);
+    if (W == 0) {
+        if (total > target) D = (uint32_t)(block_select_kth(sb, ns, rb, nr, target, 5, 4, hist) >> 32);
+    } else if (xall) {
+        unsigned long long tg = 0;
+        for (int r = 0; r < W; ++r) tg += shard_count(xall, rank_bytes, r, q);
+        if (tg > (unsigned long long)target) D = block_select_lists(xall, rank_bytes, W, nq, q, xl, target, hist);
+    }
     using BS = cub::BlockScan<uint32_t, kBS>;
     __shared__ typename BS::TempStorage scan;
     __shared__ uint32_t s_off;
@@ -1669,6 +1855,65 @@ __global__ void __launch_bounds__(256) k_topk_warp(IndexView ix, const uint32_t*
     if (lane == 0) out_n[q] = (uint32_t)got;
 }
 
+// Cell-range shards: merge the W shards' best-k lists of each query (rank r's block: nq x k ids,
+// nq x k scores, nq counts) into the global best k, by score desc, external id asc.
+__host__ __device__ inline size_t shard_topk_bytes(int nq, int k) {
+    return (((size_t)nq * k * 12 + (size_t)nq * 4) + 15) & ~(size_t)15;
+}
+
+__global__ void __launch_bounds__(128) k_merge_topk(const uint8_t* __restrict__ tall, size_t rank_bytes, int W,
+                                                    int nq, int k, int P, uint64_t* ids, float* scores,
+                                                    uint32_t* out_n) {
+    extern __shared__ uint64_t msh[];
+    uint64_t* sid = msh;
+    float* ssc = reinterpret_cast<float*>(sid + P);
+    const int q = blockIdx.x;
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        sid[i] = ~0ull;
+        ssc[i] = -INFINITY;
+    }
+    __syncthreads();
+    unsigned got = 0;
+    for (int r = 0; r < W; ++r) {
+        const uint8_t* blk = tall + (size_t)r * rank_bytes;
+        const uint64_t* ri = reinterpret_cast<const uint64_t*>(blk) + (size_t)q * k;
+        const float* rs = reinterpret_cast<const float*>(blk + (size_t)nq * k * 8) + (size_t)q * k;
+        const int n = min((int)reinterpret_cast<const uint32_t*>(blk + (size_t)nq * k * 12)[q], k);
+        got += (unsigned)n;
+        for (int j = threadIdx.x; j < n; j += blockDim.x) {
+            sid[r * k + j] = ri[j];
+            ssc[r * k + j] = rs[j];
+        }
+    }
+    __syncthreads();
+    for (int kk = 2; kk <= P; kk <<= 1) {
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const float sa = ssc[i], sb = ssc[ixj];
+                    const uint64_t ia = sid[i], ib = sid[ixj];
+                    const bool first = (i & kk) == 0;
+                    if (first ? better(sb, ib, sa, ia) : better(sa, ia, sb, ib)) {
+                        ssc[i] = sb;
+                        ssc[ixj] = sa;
+                        sid[i] = ib;
+                        sid[ixj] = ia;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const int m = min(k, (int)got);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const bool v = i < m;
+        ids[(size_t)q * k + i] = v ? sid[i] : ~0ull;
+        scores[(size_t)q * k + i] = v ? ssc[i] : -INFINITY;
+    }
+    if (threadIdx.x == 0) out_n[q] = (uint32_t)m;
+}
+
 }  // namespace
 
 // ---- launchers ----------------------------------------------------------------------------------------
@@ -1711,7 +1956,8 @@ const char* kernel_name(int id) {
     static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
                                              "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
-                                             "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items"};
+                                             "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
+                                             "k_seed_finish", "k_local_list", "k_merge_topk"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -1824,19 +2070,34 @@ void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* 
                                             cscore, nch, err);
 }
 
-void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
-                      const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
-                      const CellMajorBufs& b, cudaStream_t st) {
+void launch_seed(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                 const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin, const CellMajorBufs& b,
+                 uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st) {
     if (nq <= 0) return;
     size_t lut_bytes = (size_t)ix.npos * 16;
     const size_t key_bytes = (size_t)b.seed_cap * sizeof(uint64_t);
-    const int keys_in_smem = key_bytes <= 96 * 1024 ? 1 : 0;
+    // a shard keeps its seed keys in the global buffer: k_seed_finish filters them after the exchange
+    const int keys_in_smem = !xlist && key_bytes <= 96 * 1024 ? 1 : 0;
     const size_t smem = lut_bytes + (keys_in_smem ? key_bytes : 0);
     set_smem((const void*)k_seed, smem);
-    { Tick tk(kKSeed, st);
+    Tick tk(kKSeed, st);
     k_seed<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b,
-                                  keys_in_smem); }
-    if (nprobe > kSeedCells) {
+                                  keys_in_smem, xlist, xcnt, xl);
+}
+
+void launch_seed_finish(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                        const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
+                        const CellMajorBufs& b, const uint8_t* xall, size_t rank_bytes, int W, int xl,
+                        cudaStream_t st) {
+    if (nq <= 0) return;
+    Tick tk(kKSeedFinish, st);
+    k_seed_finish<<<nq, kBS, 0, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b,
+                                      xall, rank_bytes, W, nq, xl);
+}
+
+void launch_rest_scan(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const uint32_t* nch,
+                      int nprobe, const CellMajorBufs& b, cudaStream_t st) {
+    if (nq <= 0 || nprobe <= kSeedCells) return;
     // every probe beyond the seed cells goes through the inverted cell -> queries scan
     cudaMemsetAsync(b.cell_cnt, 0, sizeof(uint32_t) * (ix.M + 1), st);
     cudaMemsetAsync(b.cell_fill, 0, sizeof(uint32_t) * ix.M, st);
@@ -1849,9 +2110,41 @@ void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint
     k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof); }
     { Tick tk(kKScanCm, st);
     k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b); }
-    }
-    { Tick tk(kKFinalCm, st);
-    k_final_cm<<<nq, kBS, 0, st>>>(b, target); }
+}
+
+void launch_local_list(const CellMajorBufs& b, int nq, uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st) {
+    if (nq <= 0) return;
+    Tick tk(kKLocalList, st);
+    k_local_list<<<nq, kBS, 0, st>>>(b, xlist, xcnt, xl);
+}
+
+void launch_final(const CellMajorBufs& b, int nq, int target, const uint8_t* xall, size_t rank_bytes, int W, int xl,
+                  cudaStream_t st) {
+    if (nq <= 0) return;
+    Tick tk(kKFinalCm, st);
+    k_final_cm<<<nq, kBS, 0, st>>>(b, target, xall, rank_bytes, W, nq, xl);
+}
+
+void launch_merge_topk(const uint8_t* tall, size_t rank_bytes, int W, int nq, int k, uint64_t* ids, float* scores,
+                       uint32_t* out_n, cudaStream_t st) {
+    if (nq <= 0) return;
+    const int P = next_pow2(std::max(W * k, 2));
+    const size_t smem = (size_t)P * (sizeof(uint64_t) + sizeof(float));
+    set_smem((const void*)k_merge_topk, smem);
+    Tick tk(kKMergeTopk, st);
+    k_merge_topk<<<nq, 128, smem, st>>>(tall, rank_bytes, W, nq, k, P, ids, scores, out_n);
+}
+
+size_t shard_list_block_bytes(int nq, int xl) { return shard_list_bytes(nq, xl); }
+size_t shard_topk_block_bytes(int nq, int k) { return shard_topk_bytes(nq, k); }
+
+void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                      const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
+                      const CellMajorBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    launch_seed(ix, e, nq, chosen, cscore, nch, nprobe, target, adaptive, at_margin, b, nullptr, nullptr, 0, st);
+    launch_rest_scan(ix, e, nq, chosen, nch, nprobe, b, st);
+    launch_final(b, nq, target, nullptr, 0, 0, 0, st);
 }
 
 void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,

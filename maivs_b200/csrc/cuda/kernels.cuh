@@ -53,7 +53,8 @@ struct IndexView {
 // after synchronising. Every launch is counted whether or not a clock is installed.
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
-    kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kNumKernels
+    kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
+    kNumKernels
 };
 const char* kernel_name(int id);
 struct KernelClock {
@@ -135,6 +136,29 @@ struct CellMajorBufs {
 void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
                       const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
                       const CellMajorBufs& b, cudaStream_t st);
+
+// Cell-range shards run the cell-major join in pieces with all-gathers between them:
+// launch_seed (xlist set: publish the shard's seed distances) -> all-gather -> launch_seed_finish
+// -> launch_rest_scan -> launch_local_list -> all-gather -> launch_final (W > 0) -> rerank ->
+// all-gather of the best-k lists -> launch_merge_topk. Block sizes of one rank's share of the
+// gathered buffers: shard_list_block_bytes (nq counts + nq x xl distances) and
+// shard_topk_block_bytes (nq x k ids, nq x k scores, nq counts).
+void launch_seed(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                 const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin, const CellMajorBufs& b,
+                 uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st);
+void launch_seed_finish(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                        const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
+                        const CellMajorBufs& b, const uint8_t* xall, size_t rank_bytes, int W, int xl,
+                        cudaStream_t st);
+void launch_rest_scan(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const uint32_t* nch,
+                      int nprobe, const CellMajorBufs& b, cudaStream_t st);
+void launch_local_list(const CellMajorBufs& b, int nq, uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st);
+void launch_final(const CellMajorBufs& b, int nq, int target, const uint8_t* xall, size_t rank_bytes, int W, int xl,
+                  cudaStream_t st);
+void launch_merge_topk(const uint8_t* tall, size_t rank_bytes, int W, int nq, int k, uint64_t* ids, float* scores,
+                       uint32_t* out_n, cudaStream_t st);
+size_t shard_list_block_bytes(int nq, int xl);
+size_t shard_topk_block_bytes(int nq, int k);
 
 // Per-query path (index.rs:1381-1864, FastScan branch).
 struct PerQueryBufs {
