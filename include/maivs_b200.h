@@ -100,6 +100,9 @@ int maivs_search_batch(maivs_index* ix, const float* queries, size_t nq, size_t 
 int maivs_search_batch_device(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
                               float target_confidence, float beta, int cell_major, uint64_t* d_ids, float* d_scores,
                               void* stream);
+/* Overflow / routing-error counters of the last device search (synchronises `stream`); non-zero
+ * means: search again (the candidate buffers have been enlarged). On a sharded handle the call is
+ * collective and returns the sum over all ranks, so every rank takes the same decision. */
 int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags);
 
 /* Allocation-free search (no counterpart in the reference). For callers that must not allocate
@@ -120,6 +123,15 @@ int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags);
 int maivs_search_batch_device_noalloc(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
                                       float target_confidence, float beta, uint64_t* d_ids, float* d_scores,
                                       void* stream);
+
+/* save(path) / load(path) (index.rs:3594-3603, src/persist.rs): the reference's on-disk format
+ * "MAIVS2\0\1", so files move between the two implementations. A loaded index is not compacted
+ * and has FastScan off, as in the reference; call maivs_set_fastscan(1) and maivs_compact() before
+ * searching it on the GPU. maivs_load always returns a handle in *out (on failure it holds the
+ * message for maivs_last_error; free it with maivs_index_free). Only scan_mode "binary" files
+ * without f16 rerank rows load. */
+int maivs_save(maivs_index* ix, const char* path);
+int maivs_load(const char* path, maivs_index** out);
 
 /* Cell-range sharding over the GPUs of one job (no counterpart in the reference, which runs in
  * one process; the cell-range split is its stated unit of parallelism, docs/ARCHITECTURE.md:28-30).

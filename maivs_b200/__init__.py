@@ -208,6 +208,30 @@ class FlatCellIndex:
             self._h, C.c_void_p(d_queries), int(nq), int(k), int(nprobe), float(target_confidence), float(beta),
             int(bool(cell_major)), C.c_void_p(d_ids), C.c_void_p(d_scores), C.c_void_p(stream or None)))
 
+    # ---- persistence (index.rs:3594-3603) ----
+    def save(self, path: str) -> None:
+        """Write the index in the reference's on-disk format (MAIVS2, src/persist.rs)."""
+        self._check(_lib.lib().maivs_save(self._h, str(path).encode()))
+
+    @staticmethod
+    def load(path: str) -> "FlatCellIndex":
+        """Load an index written by save() here or by the reference. Like the reference, the loaded
+        index is not compacted and has FastScan off: call set_fastscan(True) and compact() before
+        searching it on the GPU."""
+        L = _lib.lib()
+        h = C.c_void_p()
+        rc = L.maivs_load(str(path).encode(), C.byref(h))
+        if rc != _lib.OK:
+            msg = L.maivs_last_error(h).decode() if h else "load failed"
+            if h:
+                L.maivs_index_free(h)
+            raise ValueError(msg)
+        ix = FlatCellIndex.__new__(FlatCellIndex)
+        ix._h = h
+        cfg = ix.array("config")
+        ix._dim = int(cfg[0])
+        return ix
+
     # ---- cell-range sharding (one rank per GPU; no counterpart in the reference) ----
     def shard(self, rank: int, world: int, nccl_id: bytes = b"") -> None:
         """Make this handle rank `rank` of `world` cell-range shards (collective over the ranks).

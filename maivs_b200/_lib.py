@@ -45,6 +45,8 @@ _SIGS = {
     "maivs_search_batch_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_float,
                                             C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "maivs_device_flags": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint32)]),
+    "maivs_save": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "maivs_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
     "maivs_nccl_unique_id": (C.c_int, [C.c_void_p, C.c_size_t]),
     "maivs_shard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
     "maivs_shard_range": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),

@@ -30,6 +30,7 @@ CUDA_INC = "/usr/local/cuda/include"
 SOURCES = [
     ("host/tree_host.cpp", "cxx"),
     ("host/index_build.cpp", "cxx"),
+    ("host/persist.cpp", "cxx"),
     ("capi.cpp", "cxx"),
     ("cuda/kernels.cu", "nvcc"),
     ("cuda/engine.cu", "nvcc"),

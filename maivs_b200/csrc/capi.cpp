@@ -238,6 +238,27 @@ int maivs_remove(maivs_index* ix, uint64_t id, int* removed) {
     return MAIVS_OK;
 }
 
+int maivs_save(maivs_index* ix, const char* path) {
+    LOCK(ix);
+    if (!path) return fail(ix, MAIVS_BAD_ARG, "path is null");
+    return check(ix, maivs::save_index(ix->h, path), MAIVS_BAD_STATE);
+}
+
+int maivs_load(const char* path, maivs_index** out) {
+    if (!out) return MAIVS_BAD_ARG;
+    *out = nullptr;
+    auto ix = std::make_unique<maivs_index>();
+    if (!path) return MAIVS_BAD_ARG;
+    std::string e = maivs::load_index(path, ix->h);
+    if (!e.empty()) {
+        ix->err = e;
+        *out = ix.release();  // the caller reads the message, then frees the handle
+        return MAIVS_BAD_ARG;
+    }
+    *out = ix.release();
+    return MAIVS_OK;
+}
+
 int maivs_compact(maivs_index* ix) {
     LOCK(ix);
     ix->h.compact();

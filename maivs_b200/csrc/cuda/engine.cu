@@ -222,9 +222,28 @@ int DeviceIndex::ensure_ws(size_t bytes, std::string& err) {
 
 uint32_t DeviceIndex::read_flags(cudaStream_t st) {
     uint32_t f[4] = {0, 0, 0, 0};
-    cudaMemcpyAsync(f, d_flags_, sizeof(f), cudaMemcpyDeviceToHost, st);
-    cudaStreamSynchronize(st);
+    global_flags(st, f);
     return f[0] + f[1];
+}
+
+int DeviceIndex::global_flags(cudaStream_t st, uint32_t out[4]) {
+    out[0] = out[1] = out[2] = out[3] = 0;
+    if (!exch_) {
+        cudaMemcpyAsync(out, d_flags_, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+        return cudaStreamSynchronize(st) == cudaSuccess ? kOk : kCudaError;
+    }
+    // a sharded search's retry decision must be the same on every rank: gather all ranks' flags
+    if (!d_flags_all_) d_flags_all_ = static_cast<uint32_t*>(alloc((size_t)shard_world_ * 4 * sizeof(uint32_t)));
+    if (!d_flags_all_) return kOom;
+    std::string err;
+    int rc = exch_->all_gather(d_flags_, d_flags_all_, 4 * sizeof(uint32_t), st, err);
+    if (rc != kOk) return rc;
+    std::vector<uint32_t> all((size_t)shard_world_ * 4);
+    cudaMemcpyAsync(all.data(), d_flags_all_, all.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return kCudaError;
+    for (int r = 0; r < shard_world_; ++r)
+        for (int i = 0; i < 4; ++i) out[i] += all[(size_t)r * 4 + i];
+    return kOk;
 }
 
 bool DeviceIndex::use_cell_major(const HostIndex& h, const SearchArgs& a) const {
@@ -552,6 +571,13 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
         CUDA_TRY(cudaMemcpyAsync(hN, dN, nb, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaMemcpyAsync(hF, d_flags_, fb, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaStreamSynchronize(stream_));
+        if (exch_) {
+            rc = global_flags(stream_, hF);
+            if (rc != kOk) {
+                err = "gathering the shards' overflow flags failed";
+                return rc;
+            }
+        }
         if (hF[1] != 0) {
             err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
             return kUnsupported;

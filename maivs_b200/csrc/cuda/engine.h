@@ -114,8 +114,10 @@ class DeviceIndex {
     int search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
                     uint32_t* nout, std::string& err);
 
-    // Overflow/error counters of the last device search (read after synchronising its stream).
+    // Overflow/error counters of the last device search (synchronises `st`). On a sharded image
+    // this is collective: the counters are summed over all ranks, so every rank decides alike.
     uint32_t read_flags(cudaStream_t st);
+    int global_flags(cudaStream_t st, uint32_t out[4]);
     bool use_cell_major(const HostIndex& h, const SearchArgs& a) const;
     void set_timing(bool on) { timing_ = on; }
     // Synchronises on the last timed search and returns its phase times.
@@ -133,7 +135,7 @@ class DeviceIndex {
     // Phases of the cell-range sharded join (one shard's side); search_sharded and
     // search_emulated_shards put the all-gathers between them.
     struct ShardRun {
-        int nq = 0, k = 0, nprobe = 0, target = 0, xl = 0, W = 0;
+        int nq = 0, k = 0, nprobe = 0, target = 0, xl = 0, W = 0, rank = 0, qb = 0;  // qb: queries routed per rank
         bool rest = false;
         size_t lb = 0, tb = 0;
         const float* dQ = nullptr;
@@ -144,8 +146,11 @@ class DeviceIndex {
         float *cscore = nullptr, *rsc = nullptr;
         uint8_t *xsend = nullptr, *xrecv = nullptr, *tsend = nullptr, *trecv = nullptr;
     };
-    int shard_begin(const HostIndex& h, const float* dQ, const SearchArgs& a, int W, cudaStream_t st, ShardRun& r,
-                    std::string& err);
+    // encode every query, route this rank's block of qb queries (rows rank*qb.. of chosen/cscore/nch)
+    int shard_begin(const HostIndex& h, const float* dQ, const SearchArgs& a, int W, int rank, cudaStream_t st,
+                    ShardRun& r, std::string& err);
+    // after the probe lists are all-gathered: scan this shard's seed probes, publish its distances
+    void shard_seed(const HostIndex& h, ShardRun& r);
     void shard_after_seed(const HostIndex& h, ShardRun& r);
     void shard_after_cut(const HostIndex& h, ShardRun& r);
     void shard_merge(ShardRun& r, uint64_t* d_ids, float* d_scores, uint32_t* d_nout);
@@ -154,6 +159,7 @@ class DeviceIndex {
     int search_sharded(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                        uint32_t* d_nout, cudaStream_t st, std::string& err);
     Exchange* exch_ = nullptr;
+    uint32_t* d_flags_all_ = nullptr;  // world x 4 counters gathered by global_flags
     int shard_rank_ = 0, shard_world_ = 1;
     void* alloc(size_t bytes);
     template <typename T>

@@ -1,8 +1,9 @@
 // Cell-range sharded search: each rank scans only its cells, three all-gathers keep the result
 // identical to the unsharded cell-major join (index.rs:1999-2311).
 //
-// Every rank routes the whole batch (the routing tables are replicated, so the probe lists and
-// the exactly-once rule agree everywhere), then:
+// Every rank encodes the whole batch and routes its block of ceil(nq / world) queries; the probe
+// lists are all-gathered (the routing tables are replicated, so every rank then holds the probe
+// lists and the exactly-once rule of the unsharded join). Then each rank:
 //   1. scans the seed probes that fall in its cells and publishes, per query, its entry count and
 //      its smallest `target` distances; all-gather -> every rank derives the global seed cut-off
 //      tau, its own seed survivors and the adaptive end of the rest probes;
@@ -173,13 +174,15 @@ void shard_range(const HostIndex& h, int rank, int world, uint32_t* lo, uint32_t
     *hi = bound(rank + 1);
 }
 
-int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchArgs& a, int W, cudaStream_t st,
-                             ShardRun& r, std::string& err) {
+int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchArgs& a, int W, int rank,
+                             cudaStream_t st, ShardRun& r, std::string& err) {
     const int nq = a.nq, M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
     r = ShardRun{};
     r.nq = nq;
     r.k = a.k;
     r.W = W;
+    r.rank = rank;
+    r.qb = (nq + W - 1) / W;
     r.dQ = dQ;
     r.st = st;
     r.nprobe = std::max(1, std::min(a.nprobe, M));
@@ -219,9 +222,9 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         sl_n = bp.take<uint32_t>(nq);
         hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
-        r.chosen = bp.take<uint32_t>((size_t)nq * nprobe);
-        r.cscore = bp.take<float>((size_t)nq * nprobe);
-        r.nch = bp.take<uint32_t>(nq);
+        r.chosen = bp.take<uint32_t>((size_t)W * r.qb * nprobe);
+        r.cscore = bp.take<float>((size_t)W * r.qb * nprobe);
+        r.nch = bp.take<uint32_t>((size_t)W * r.qb);
         b.mwords = mwords;
         b.probed = h.max_assign > 1 ? bp.take<uint64_t>((size_t)nq * mwords) : nullptr;
         b.seed_cap = seed_cap;
@@ -270,13 +273,30 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
     last_.st = st;
 
     dev::launch_encode(view_, dQ, nq, r.e, use_sq8_, view_.rerank_mode == 1, st);
-    rc = route(h, r.e, dQ, nq, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, r.chosen, r.cscore, r.nch, st, err);
-    if (rc != kOk) return rc;
+    // route_batch is per query: this rank routes its block, the probe lists are then all-gathered
+    const int q0 = rank * r.qb, qn = std::max(0, std::min(r.qb, nq - q0));
+    if (qn > 0) {
+        dev::QueryEnc eb = r.e;
+        eb.qbits += (size_t)q0 * nw;
+        eb.lut += (size_t)q0 * npos * 16;
+        eb.fs_delta += q0;
+        eb.fs_bias += q0;
+        eb.cqs += (size_t)q0 * dim;
+        eb.cqbase += q0;
+        eb.rqs += (size_t)q0 * dim;
+        eb.rbase += q0;
+        rc = route(h, eb, dQ + (size_t)q0 * dim, qn, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc,
+                   r.chosen + (size_t)q0 * nprobe, r.cscore + (size_t)q0 * nprobe, r.nch + q0, st, err);
+        if (rc != kOk) return rc;
+    }
     if (!r.rest) cudaMemsetAsync(r.b.cell_cnt, 0, sizeof(uint32_t) * ((size_t)M + 1), st);  // read by stats
-    dev::launch_seed(view_, r.e, nq, r.chosen, r.cscore, r.nch, nprobe, target, h.adaptive, h.at_margin, r.b,
-                     reinterpret_cast<uint16_t*>(r.xsend + (size_t)nq * 4), reinterpret_cast<uint32_t*>(r.xsend),
-                     r.xl, st);
     return kOk;
+}
+
+void DeviceIndex::shard_seed(const HostIndex& h, ShardRun& r) {
+    dev::launch_seed(view_, r.e, r.nq, r.chosen, r.cscore, r.nch, r.nprobe, r.target, h.adaptive, h.at_margin, r.b,
+                     reinterpret_cast<uint16_t*>(r.xsend + (size_t)r.nq * 4), reinterpret_cast<uint32_t*>(r.xsend),
+                     r.xl, r.st);
 }
 
 void DeviceIndex::shard_after_seed(const HostIndex& h, ShardRun& r) {
@@ -307,8 +327,15 @@ int DeviceIndex::search_sharded(const HostIndex& h, const float* dQ, const Searc
         ~Unset() { dev::set_thread_clock(nullptr); }
     } unset;
     ShardRun r;
-    int rc = shard_begin(h, dQ, a, shard_world_, st, r, err);
+    int rc = shard_begin(h, dQ, a, shard_world_, shard_rank_, st, r, err);
     if (rc != kOk) return rc;
+    // probe lists: in-place all-gathers of each rank's block of rows
+    const size_t rows = (size_t)r.qb * r.nprobe;
+    rc = exch_->all_gather(r.chosen + (size_t)r.rank * rows, r.chosen, rows * 4, st, err);
+    if (rc == kOk) rc = exch_->all_gather(r.cscore + (size_t)r.rank * rows, r.cscore, rows * 4, st, err);
+    if (rc == kOk) rc = exch_->all_gather(r.nch + (size_t)r.rank * r.qb, r.nch, (size_t)r.qb * 4, st, err);
+    if (rc != kOk) return rc;
+    shard_seed(h, r);
     rc = exch_->all_gather(r.xsend, r.xrecv, r.lb, st, err);
     if (rc != kOk) return rc;
     shard_after_seed(h, r);
@@ -343,9 +370,20 @@ int search_emulated_shards(const HostIndex& h, std::vector<std::unique_ptr<Devic
     };
     dev::take_launch_error(nullptr);
     for (int s = 0; s < W; ++s) {
-        int rc = shards[s]->shard_begin(h, dQ, a, W, st, runs[s], err);
+        int rc = shards[s]->shard_begin(h, dQ, a, W, s, st, runs[s], err);
         if (rc != kOk) return rc;
     }
+    // probe lists: shard r's block of rows to every shard
+    for (int s = 0; s < W; ++s)
+        for (int r = 0; r < W; ++r) {
+            if (r == s) continue;
+            const size_t rows = (size_t)runs[r].qb * runs[r].nprobe, o = (size_t)r * rows;
+            cudaMemcpyAsync(runs[s].chosen + o, runs[r].chosen + o, rows * 4, cudaMemcpyDeviceToDevice, st);
+            cudaMemcpyAsync(runs[s].cscore + o, runs[r].cscore + o, rows * 4, cudaMemcpyDeviceToDevice, st);
+            cudaMemcpyAsync(runs[s].nch + (size_t)r * runs[r].qb, runs[r].nch + (size_t)r * runs[r].qb,
+                            (size_t)runs[r].qb * 4, cudaMemcpyDeviceToDevice, st);
+        }
+    for (int s = 0; s < W; ++s) shards[s]->shard_seed(h, runs[s]);
     int rc = gather(false);
     if (rc != kOk) return rc;
     for (int s = 0; s < W; ++s) shards[s]->shard_after_seed(h, runs[s]);

@@ -164,4 +164,8 @@ struct HostIndex {
     void encode_i8(const float* v, int8_t* out) const;
 };
 
+// Reference on-disk format "MAIVS2\0\1" (src/persist.rs); empty string on success.
+std::string save_index(const HostIndex& h, const std::string& path);
+std::string load_index(const std::string& path, HostIndex& h);
+
 }  // namespace maivs
