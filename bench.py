@@ -520,6 +520,8 @@ def run_sharded(args):
         run(rf, np_)
     torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ix.kernel_clock(True)
+    ix.kernel_times(reset=True)
     if ws > 1:
         tdist.barrier()
     torch.cuda.synchronize(dev)
@@ -533,6 +535,10 @@ def run_sharded(args):
         torch.cuda.synchronize(dev)
         clk.stop_mark()
     overflow = ix.device_flags(stream.cuda_stream)
+    ktimes = ix.kernel_times(reset=True)
+    ix.kernel_clock(False)
+    ktot = max(sum(v[0] for v in ktimes.values()), 1e-9)
+    shares = {k: round(v[0] / ktot, 4) for k, v in ktimes.items() if v[1]}
     if ws > 1:
         tdist.barrier()
     total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
@@ -562,6 +568,7 @@ def run_sharded(args):
         "e2e": {"value": round(nq * args.steps / e2e_total, 1), "unit": "queries/s",
                 "h2d_bytes_per_step": nq * 384 * 4, "d2h_bytes_per_step": nq * K * 12},
         "clocks": clk.summary(),
+        "kernel_share_rank0": shares,
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
