@@ -513,7 +513,11 @@ def run_sharded(args):
                 break
         return d_ids.cpu().numpy().view(np.uint64)
 
-    rf, np_, rec = operating_point(search, truth)
+    if args.rf and args.nprobe:
+        rf, np_ = args.rf, args.nprobe
+        rec = recall(search(rf, np_), truth)
+    else:
+        rf, np_, rec = operating_point(search, truth)
     search(rf, np_)  # grows the candidate buffers if this point overflows them
     for _ in range(max(args.warmup, 3)):
         flush.zero_()
@@ -527,12 +531,14 @@ def run_sharded(args):
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
         clk.wait_first()
+        torch.cuda.profiler.start()  # a profiler started with --profile-from-start off sees the timed steps
         for s in range(args.steps):
             flush.zero_()
             evs[s][0].record(stream)
             run(rf, np_)
             evs[s][1].record(stream)
         torch.cuda.synchronize(dev)
+        torch.cuda.profiler.stop()
         clk.stop_mark()
     overflow = ix.device_flags(stream.cuda_stream)
     ktimes = ix.kernel_times(reset=True)
@@ -633,6 +639,8 @@ def main():
     ap.add_argument("--n", type=int, default=None, help="vectors (500,000; 5,200,000 for --workload sharded)")
     ap.add_argument("--nq", type=int, default=None, help="queries per batch (1,000; 10,000 sharded)")
     ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
+    ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
     ap.add_argument("--workload", choices=("config2", "sharded"), default="config2",
                     help="config2: the headline 500k batch (replicas for N > 1); sharded: configs[3], 5.2M "
                          "vectors with cells sharded by range over the N GPUs")

@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "umma.cuh"
 
 namespace maivs {
 namespace dev {
@@ -1074,10 +1075,10 @@ __global__ void k_inv_scatter(const uint32_t* __restrict__ chosen, const uint32_
 // a valid bound on the final cut (index.rs:2266-2269), and it is canonical.
 
 __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const uint32_t* __restrict__ start,
-                                                 const uint32_t* __restrict__ qof, CellMajorBufs b) {
+                                                 const uint32_t* __restrict__ qof, CellMajorBufs b, uint32_t max_q) {
     const uint32_t c = blockIdx.x;
     const uint32_t s0 = start[c], s1 = start[c + 1];
-    if (s0 == s1) return;
+    if (s0 == s1 || s1 - s0 >= max_q) return;  // high-batch cells go to k_scan_mma
     const uint32_t moff = ix.cell_moff[c];
     const int nc = (int)(ix.cell_moff[c + 1] - moff);
     if (nc == 0) return;
@@ -1112,6 +1113,184 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
             }
         }
     }
+}
+
+// ---- cell-major: the scan of high-batch cells on the tensor cores -----------------------------------
+// The FastScan sum of a (query, member) pair is sum_j LUT_q[16 j + nib_j(member)], i.e. the dot
+// product of the query's u8 table row (K = 16 x npos bytes) with the one-hot expansion of the
+// member's nibbles. For a cell that many queries probe this is a dense u8 x u8 -> s32 GEMM:
+// M = 128 queries x N = 256 members per tile, K in chunks of 128 bytes (8 nibble positions). A
+// (tables) is copied and B (one-hot nibbles) is built in shared memory in the K-major 128-byte
+// swizzled layout, one elected thread issues four kind::i8 tcgen05.mma per chunk into a TMEM
+// accumulator (128 lanes x 256 columns), two stages overlap building chunk k + 1 with the MMAs of
+// chunk k, and the epilogue reads the sums with tcgen05.ld and applies k_scan_cm's rule
+// (d = maxk - sum <= tau, canonical home) to append survivors. Sums are exact integers, so the
+// survivors equal k_scan_cm's. Every mbarrier wait is bounded; a timeout sets *err and the CTA
+// stops issuing MMAs.
+constexpr int kMmaQ = 128, kMmaN = 256, kMmaTmemCols = 256;
+constexpr uint32_t kMmaMinQueries = 16;  // cells probed by at least this many queries of the batch
+constexpr size_t kMmaStageBytes = (size_t)kMmaQ * 128 + (size_t)kMmaN * 128;  // A + B per stage
+constexpr size_t kMmaSmem = 2 * kMmaStageBytes + 1024;
+
+__global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, const uint32_t* __restrict__ start,
+                                                  const uint32_t* __restrict__ qof, CellMajorBufs b, uint32_t min_q,
+                                                  uint32_t* err) {
+    const uint32_t c = blockIdx.x;
+    const uint32_t s0 = start[c], s1 = start[c + 1];
+    const uint32_t nqc = s1 - s0;
+    if (nqc < min_q || nqc == 0) return;
+    const uint32_t moff = ix.cell_moff[c];
+    const int nc = (int)(ix.cell_moff[c + 1] - moff);
+    if (nc == 0) return;
+    extern __shared__ uint8_t mraw[];
+    __shared__ uint64_t bar[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ uint32_t s_q[kMmaQ];
+    const uint32_t sbase = umma::smem_addr(mraw);
+    uint8_t* tiles = mraw + (((sbase + 1023u) & ~1023u) - sbase);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int npos = ix.npos, kchunks = npos >> 3, ng = (nc + 7) >> 3;
+    const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
+    const uint32_t maxk = ix.maxk;
+    if (warp == 0) umma::tmem_alloc(&s_tmem, kMmaTmemCols);
+    if (tid == 0) {
+        umma::bar_init(&bar[0], 1);
+        umma::bar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = s_tmem;
+    const uint32_t idesc = umma::idesc_u8_s32(kMmaQ, kMmaN);
+    uint32_t it = 0;  // chunks issued so far (stage = it & 1)
+    bool ok = true;
+    // Thread roles in the operand builds: A rows ra + 32u (u < 4) at 16-byte chunk ch; B member
+    // group gl at position ch (the 8 lanes of a quarter-warp take the 8 positions of one group, so
+    // under the swizzle each store instruction hits all 32 banks once per 128 bytes).
+    const int ch = tid & 7, ra = tid >> 3, gl = tid >> 3;
+    for (uint32_t qt = 0; qt < nqc && ok; qt += kMmaQ) {
+        const int nq_t = (int)min((uint32_t)kMmaQ, nqc - qt);
+        for (int mt = 0; mt < nc && ok; mt += kMmaN) {
+            __syncthreads();  // the previous tile's epilogue is done with s_q and the accumulator
+            if (tid < nq_t) s_q[tid] = qof[s0 + qt + tid];
+            __syncthreads();
+            const uint8_t* arow[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int r = ra + 32 * u;
+                arow[u] = r < nq_t ? e.lut + (size_t)s_q[r] * npos * 16 + ch * 16 : nullptr;
+            }
+            const int g = (mt >> 3) + gl;
+            const uint32_t* bword = 8 * g < nc ? codes + (size_t)ch * ng + g : nullptr;
+            // operands of one chunk, loaded a chunk ahead of their use
+            struct Ops {
+                uint4 a[4];
+                uint32_t w;
+            };
+            auto load = [&](Ops& o, int kc) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (arow[u]) o.a[u] = __ldg(reinterpret_cast<const uint4*>(arow[u] + (size_t)kc * 128));
+                if (bword) o.w = __ldg(bword + (size_t)kc * 8 * ng);
+            };
+            // writes chunk kc into its stage and issues its MMAs; false when a wait ran out
+            auto step = [&](const Ops& o, Ops& nxt, int kc) -> bool {
+                const int st = (int)(it & 1);
+                bool good = true;
+                if (it >= 2) good = umma::bar_wait(&bar[st], ((it >> 1) - 1) & 1);  // stage free again
+                good = __syncthreads_and(good);
+                if (!good) return false;
+                umma::fence_after_sync();
+                uint8_t* sA = tiles + (size_t)st * kMmaStageBytes;
+                uint8_t* sB = sA + (size_t)kMmaQ * 128;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (arow[u]) *reinterpret_cast<uint4*>(sA + umma::sw128_offset(ra + 32 * u, ch)) = o.a[u];
+                if (bword) {
+#pragma unroll
+                    for (int bb = 0; bb < 8; ++bb) {
+                        const uint32_t nb = (o.w >> (4 * bb)) & 15u;
+                        const unsigned long long one = 1ull << (8 * (nb & 7u));
+                        ulonglong2 v;
+                        v.x = nb < 8 ? one : 0ull;
+                        v.y = nb < 8 ? 0ull : one;
+                        *reinterpret_cast<ulonglong2*>(sB + umma::sw128_offset(8 * gl + bb, ch)) = v;
+                    }
+                }
+                if (kc + 1 < kchunks) load(nxt, kc + 1);  // in flight while this chunk's MMAs run
+                umma::fence_smem_to_async();
+                __syncthreads();
+                if (tid == 0) {
+                    umma::fence_after_sync();
+                    const uint32_t a0 = umma::smem_addr(sA), b0 = umma::smem_addr(sB);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        umma::mma_i8(tmem, umma::desc_k_sw128(a0 + 32 * k), umma::desc_k_sw128(b0 + 32 * k), idesc,
+                                     (kc > 0 || k > 0) ? 1u : 0u);
+                    umma::mma_commit(&bar[st]);
+                }
+                ++it;
+                return true;
+            };
+            Ops o0, o1;
+            load(o0, 0);
+            for (int kc = 0; kc < kchunks && ok; kc += 2) {
+                ok = step(o0, o1, kc);
+                if (ok && kc + 1 < kchunks) ok = step(o1, o0, kc + 1);
+            }
+            if (!ok) break;
+            // epilogue: wait for the tile's last chunk, then every warp reads 32 queries x 128 members
+            ok = umma::bar_wait(&bar[(it - 1) & 1], ((it - 1) >> 1) & 1);
+            ok = __syncthreads_and(ok);
+            if (!ok) break;
+            umma::fence_after_sync();
+            const int lq = warp & 3, half = warp >> 2;
+            const int r = 32 * lq + lane;
+            const bool vq = r < nq_t;
+            const uint32_t q = vq ? s_q[r] : 0u;
+            const uint32_t t = vq ? b.tau[q] : 0u;
+            const uint64_t* pq = b.probed + (size_t)q * b.mwords;
+            for (int cb = 0; cb < 128; cb += 16) {
+                uint32_t v[16];
+                umma::tmem_ld16(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(128 * half + cb), v);
+                umma::tmem_wait_ld();
+                const int m0 = mt + 128 * half + cb;
+                uint32_t hit = 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (vq && m0 + j < nc && maxk - v[j] <= t) hit |= 1u << j;
+                if (!hit) continue;
+                // the survivors' slots and home checks, loads of all 16 in flight together
+                uint32_t sl[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) sl[j] = (hit >> j) & 1u ? __ldg(ix.cell_slots + moff + m0 + j) : 0u;
+                if (ix.ma > 1) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (((hit >> j) & 1u) && !canonical_cm(ix, sl[j], c, pq)) hit &= ~(1u << j);
+                }
+                if (!hit) continue;
+                uint32_t p = atomicAdd(&b.rest_n[q], (uint32_t)__popc(hit));
+                uint64_t* out = b.rest_buf + (size_t)q * b.rest_cap;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (!((hit >> j) & 1u)) continue;
+                    if (p < (uint32_t)b.rest_cap) out[p] = ((uint64_t)(maxk - v[j]) << 32) | sl[j];
+                    ++p;
+                }
+            }
+            umma::fence_before_sync();
+        }
+    }
+    if (!ok) {
+        if (tid == 0) atomicAdd(err, 1u);
+        // let MMAs still in flight finish (bounded) before the accumulator is released
+        if (tid == 0 && it > 0) umma::bar_wait(&bar[(it - 1) & 1], ((it - 1) >> 1) & 1);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_free(tmem, kMmaTmemCols);
 }
 
 // ---- cell-major: merge + exact global cut, ties kept (index.rs:2277-2306) ---------------------------
@@ -1957,7 +2136,7 @@ const char* kernel_name(int id) {
                                              "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
                                              "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
-                                             "k_seed_finish", "k_local_list", "k_merge_topk"};
+                                             "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -2109,7 +2288,10 @@ void launch_rest_scan(const IndexView& ix, const QueryEnc& e, int nq, const uint
     { Tick tk(kKInvScatter, st);
     k_inv_scatter<<<wb, kBS, 0, st>>>(chosen, nch, b.rest_hi, nq, nprobe, b.cell_cnt, b.cell_fill, b.qof); }
     { Tick tk(kKScanCm, st);
-    k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b); }
+    k_scan_cm<<<ix.M, kBS, 0, st>>>(ix, e, b.cell_cnt, b.qof, b, kMmaMinQueries); }
+    set_smem((const void*)k_scan_mma, kMmaSmem);
+    { Tick tk(kKScanMma, st);
+    k_scan_mma<<<ix.M, 256, kMmaSmem, st>>>(ix, e, b.cell_cnt, b.qof, b, kMmaMinQueries, b.overflow + 2); }
 }
 
 void launch_local_list(const CellMajorBufs& b, int nq, uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st) {

@@ -54,7 +54,7 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kNumKernels
+    kKScanMma, kNumKernels
 };
 const char* kernel_name(int id);
 struct KernelClock {
