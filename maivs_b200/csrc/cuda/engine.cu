@@ -12,6 +12,7 @@ namespace maivs {
 namespace {
 
 constexpr int kPerQueryChunk = 64;  // queries per per-query pipeline pass (bounds its scratch)
+constexpr uint32_t kNoCellHost = 0xFFFFFFFFu;  // an unused home in slot_cells
 
 struct Bump {
     char* base;
@@ -110,6 +111,17 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
                 const uint64_t* code = &h.bits[(size_t)mem[8 * g + b] * nw];
                 for (size_t j = 0; j < npos; ++j) cw[j * ng + g] |= (uint32_t)nib(code, j) << (4 * b);
             }
+    }
+    if (ma == 2) {
+        std::vector<uint32_t> lower(moff[M], kNoCellHost);
+#pragma omp parallel for schedule(dynamic, 64)
+        for (long long c = 0; c < (long long)M; ++c)
+            for (uint32_t i = moff[c]; i < moff[c + 1]; ++i) {
+                const uint32_t* hm = &h.slot_cells[(size_t)slots[i] * 2];
+                for (int j = 0; j < 2; ++j)
+                    if (hm[j] != kNoCellHost && hm[j] < (uint32_t)c) lower[i] = hm[j];
+            }
+        v.cell_lower = upload_vec(lower);
     }
     v.cell_moff = upload_vec(moff);
     moff_ = moff;

@@ -80,6 +80,11 @@ __device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot,
     return ok;
 }
 
+// canonical_cm for a member entry whose lower home is precomputed (IndexView::cell_lower).
+__device__ __forceinline__ bool canonical_lower(uint32_t lower, const uint64_t* probed) {
+    return lower == kNoCell || !((__ldg(probed + (lower >> 6)) >> (lower & 63)) & 1ull);
+}
+
 // The kth smallest (1-based) of up to two key segments, by radix selection on bytes [lo_byte,
 // hi_byte] of the 64-bit keys (higher bytes must be zero). Returns the selected key with the
 // unselected low bytes zero. All threads of the block must call it; `hist` is 256 shared words.
@@ -854,7 +859,14 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
             valid[bb] = act && pos < nc;
             slot[bb] = valid[bb] ? __ldg(ix.cell_slots + moff + pos) : 0u;
         }
-        if (ix.ma > 1) {
+        if (ix.ma > 1 && ix.cell_lower) {
+            uint32_t lw[8];
+#pragma unroll
+            for (int bb = 0; bb < 8; ++bb) lw[bb] = valid[bb] ? __ldg(ix.cell_lower + moff + 8 * g + bb) : kNoCell;
+#pragma unroll
+            for (int bb = 0; bb < 8; ++bb)
+                if (valid[bb]) valid[bb] = canonical_lower(lw[bb], probed);
+        } else if (ix.ma > 1) {
 #pragma unroll
             for (int bb = 0; bb < 8; ++bb)
                 if (valid[bb]) valid[bb] = canonical_cm(ix, slot[bb], c, probed);
@@ -1106,7 +1118,10 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
                 }
                 if (valid) {
                     slot = ix.cell_slots[moff + pos];
-                    if (ix.ma > 1) valid = canonical_cm(ix, slot, c, b.probed + (size_t)q * b.mwords);
+                    if (ix.ma > 1)
+                        valid = ix.cell_lower ? canonical_lower(__ldg(ix.cell_lower + moff + pos),
+                                                                b.probed + (size_t)q * b.mwords)
+                                              : canonical_cm(ix, slot, c, b.probed + (size_t)q * b.mwords);
                 }
                 uint32_t p = warp_append(valid, &b.rest_n[q]);
                 if (valid && p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)q * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
@@ -1129,6 +1144,7 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
 // stops issuing MMAs.
 constexpr int kMmaQ = 128, kMmaN = 256, kMmaTmemCols = 256;
 constexpr uint32_t kMmaMinQueries = 16;  // cells probed by at least this many queries of the batch
+constexpr int kHitCap = 256;  // survivors one warp collects before resolving them (>= 32 rows x 8 members)
 constexpr size_t kMmaStageBytes = (size_t)kMmaQ * 128 + (size_t)kMmaN * 128;  // A + B per stage
 constexpr size_t kMmaSmem = 2 * kMmaStageBytes + 1024;
 
@@ -1146,6 +1162,7 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
     __shared__ uint64_t bar[2];
     __shared__ uint32_t s_tmem;
     __shared__ uint32_t s_q[kMmaQ];
+    __shared__ uint32_t s_hit[8][kHitCap];
     const uint32_t sbase = umma::smem_addr(mraw);
     uint8_t* tiles = mraw + (((sbase + 1023u) & ~1023u) - sbase);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1248,38 +1265,67 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
             const int lq = warp & 3, half = warp >> 2;
             const int r = 32 * lq + lane;
             const bool vq = r < nq_t;
-            const uint32_t q = vq ? s_q[r] : 0u;
-            const uint32_t t = vq ? b.tau[q] : 0u;
-            const uint64_t* pq = b.probed + (size_t)q * b.mwords;
+            const uint32_t t = vq ? b.tau[s_q[r]] : 0u;
+            // Survivors (row, member, d) of the warp's 32 rows x 128 members are collected in its
+            // shared list and resolved by all 32 lanes together: one chain of dependent loads
+            // (slot, lower home, probed bit, counter) per batch instead of one per thread and block.
+            uint32_t* hb = s_hit[warp];
+            uint32_t cur = 0;  // entries in hb (warp-uniform)
+            auto resolve = [&](uint32_t n) {
+                __syncwarp();
+                for (uint32_t i = lane; i < n; i += 32) {
+                    const uint32_t en = hb[i];
+                    const uint32_t rr = en >> 24, mm = (en >> 16) & 255u, d = en & 0xFFFFu;
+                    const uint32_t qq = s_q[rr], mi = moff + (uint32_t)mt + mm;
+                    const uint32_t slot = __ldg(ix.cell_slots + mi);
+                    bool keep = true;
+                    if (ix.ma > 1) {
+                        const uint64_t* pq = b.probed + (size_t)qq * b.mwords;
+                        keep = ix.cell_lower ? canonical_lower(__ldg(ix.cell_lower + mi), pq)
+                                             : canonical_cm(ix, slot, c, pq);
+                    }
+                    if (keep) {
+                        const uint32_t p = atomicAdd(&b.rest_n[qq], 1u);
+                        if (p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)qq * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
+                    }
+                }
+                __syncwarp();
+            };
             for (int cb = 0; cb < 128; cb += 16) {
                 uint32_t v[16];
                 umma::tmem_ld16(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(128 * half + cb), v);
                 umma::tmem_wait_ld();
                 const int m0 = mt + 128 * half + cb;
-                uint32_t hit = 0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (vq && m0 + j < nc && maxk - v[j] <= t) hit |= 1u << j;
-                if (!hit) continue;
-                // the survivors' slots and home checks, loads of all 16 in flight together
-                uint32_t sl[16];
+                for (int hh = 0; hh < 2; ++hh) {  // 8 columns at a time: at most 256 survivors per batch
+                    uint32_t hit = 0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) sl[j] = (hit >> j) & 1u ? __ldg(ix.cell_slots + moff + m0 + j) : 0u;
-                if (ix.ma > 1) {
+                    for (int j = 0; j < 8; ++j)
+                        if (vq && m0 + 8 * hh + j < nc && maxk - v[8 * hh + j] <= t) hit |= 1u << j;
+                    const uint32_t nh = (uint32_t)__popc(hit);
+                    const uint32_t tot = __reduce_add_sync(0xFFFFFFFFu, nh);
+                    if (tot == 0) continue;
+                    if (cur + tot > (uint32_t)kHitCap) {
+                        resolve(cur);
+                        cur = 0;
+                    }
+                    uint32_t pre = nh;  // inclusive prefix over lanes
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (((hit >> j) & 1u) && !canonical_cm(ix, sl[j], c, pq)) hit &= ~(1u << j);
-                }
-                if (!hit) continue;
-                uint32_t p = atomicAdd(&b.rest_n[q], (uint32_t)__popc(hit));
-                uint64_t* out = b.rest_buf + (size_t)q * b.rest_cap;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, pre, o);
+                        if (lane >= o) pre += y;
+                    }
+                    uint32_t pos = cur + pre - nh;
+                    const uint32_t mbase = (uint32_t)(128 * half + cb + 8 * hh);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    if (!((hit >> j) & 1u)) continue;
-                    if (p < (uint32_t)b.rest_cap) out[p] = ((uint64_t)(maxk - v[j]) << 32) | sl[j];
-                    ++p;
+                    for (int j = 0; j < 8; ++j) {
+                        if (!((hit >> j) & 1u)) continue;
+                        hb[pos++] = ((uint32_t)r << 24) | ((mbase + j) << 16) | (maxk - v[8 * hh + j]);
+                    }
+                    cur += tot;
                 }
             }
+            resolve(cur);
             umma::fence_before_sync();
         }
     }

@@ -29,6 +29,9 @@ struct IndexView {
     const uint32_t* cell_codes;
     const uint32_t* cell_slots;
     const uint32_t* slot_cells;  // n_slots x ma
+    // per member entry of a cell c: its other home when that home's id is below c, else kNoCell
+    // (two homes at most; null otherwise). The exactly-once rule then needs one probed-bit test.
+    const uint32_t* cell_lower;
     const uint32_t* tags;        // n_slots or null
     // rerank store
     int rerank_mode;  // 0 f32, 1 per-dimension SQ8, 2 global int8
