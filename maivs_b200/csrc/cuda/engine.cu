@@ -266,15 +266,17 @@ bool DeviceIndex::use_cell_major(const HostIndex& h, const SearchArgs& a) const 
 
 int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc,
                        float beta, bool batch_router, uint16_t* hs, uint32_t* sl, uint32_t* sl_n,
-                       uint32_t* tree_scratch,
+                       uint32_t* tree_scratch, float* rs_scores, uint32_t* rs_items,
                        uint32_t* chosen, float* cscore, uint32_t* nch, cudaStream_t st, std::string& err) {
     const int M = view_.M;
     const size_t mult2 = std::max<size_t>(h.shortlist_mult, 2);
+    int expect = (int)std::min<size_t>(n_live_, 1u << 30);  // typical shortlist length
     bool have_codes = h.two_stage && !h.cent_bits.empty();
     if (batch_router && have_codes) {
         // route_batch (index.rs:1873-1980): exact flat Hamming shortlist for every query
         int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_live_);
         dev::launch_route_flat(view_, e, nq, want_c, hs, sl, sl_n, M, st);
+        expect = want_c;
     } else if (h.tree) {
         // route_query tree branch (index.rs:1188-1211)
         int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_leaf_);
@@ -282,6 +284,7 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
         int beams[dev::kMaxTreeLevels] = {0};
         for (size_t i = 0; i < b.size(); ++i) beams[i] = (int)b[i];
         dev::launch_route_tree(view_, e, nq, beams, want_c, tree_scratch, (int)tree_cap_, sl, sl_n, M, st);
+        expect = want_c;
     } else if (h.graph_route && n_live_ >= h.graph_min_cells) {
         err = "centroid-graph routing is not supported by the GPU search; call set_graph_route(False)";
         return kUnsupported;
@@ -289,11 +292,12 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
         // route_query two-stage branch (index.rs:1241-1259): note the multiplier is not floored at 2
         int want_c = (int)std::min<size_t>((size_t)nprobe * h.shortlist_mult, n_live_);
         dev::launch_route_flat(view_, e, nq, want_c, hs, sl, sl_n, M, st);
+        expect = want_c;
     } else {
         dev::launch_route_all(view_, nq, sl, sl_n, M, st);
     }
     dev::launch_rescore_select(view_, e, dQ, nq, sl, sl_n, M, nprobe, tc, beta, use_sq8_, chosen, cscore, nch,
-                               d_flags_ + 1, st);
+                               d_flags_ + 1, rs_scores, rs_items, expect, st);
     return kOk;
 }
 
@@ -318,6 +322,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
 
     float* rsc = nullptr;       // rerank scores (nq x cand_cap) of the flattened gather
+    float* rss = nullptr;       // centroid re-order scores of the shortlists (nq x M)
+    uint32_t* rsi = nullptr;    // their item numbering (nq + 1)
     uint32_t* ritem = nullptr;  // its item numbering (nq + 1)
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::CellMajorBufs& b) {
@@ -333,6 +339,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         sl_n = bp.take<uint32_t>(nq);
         hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        rss = bp.take<float>((size_t)nq * M);
+        rsi = bp.take<uint32_t>((size_t)nq + 1);
         chosen = bp.take<uint32_t>((size_t)nq * nprobe);
         cscore = bp.take<float>((size_t)nq * nprobe);
         nch = bp.take<uint32_t>(nq);
@@ -391,7 +399,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     dev::launch_encode(view_, dQ, nq, e, use_sq8_, view_.rerank_mode == 1, st);
     if (dbg && dbg->stage == 0) return debug_encode(e, nq, st);
     if (timing_) cudaEventRecord(ev_[1], st);
-    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, rss, rsi, chosen, cscore, nch, st, err);
     if (rc != kOk) return rc;
     if (dbg && dbg->stage == 1) return debug_route(chosen, cscore, nch, nq, nprobe, st);
     if (timing_) cudaEventRecord(ev_[2], st);
@@ -423,6 +431,8 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     const int chunk = std::min(a.nq, kPerQueryChunk);
 
     float* rsc = nullptr;       // rerank scores (chunk x cand_cap) of the flattened gather
+    float* rss = nullptr;       // centroid re-order scores of the shortlists (chunk x M)
+    uint32_t* rsi = nullptr;    // their item numbering (chunk + 1)
     uint32_t* ritem = nullptr;  // its item numbering (chunk + 1)
     auto carve = [&](Bump& bp, dev::QueryEnc& e, uint32_t*& sl, uint32_t*& sl_n, uint16_t*& hs, uint32_t*& tsc,
                      uint32_t*& chosen, float*& cscore, uint32_t*& nch, dev::PerQueryBufs& b) {
@@ -439,6 +449,8 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         sl_n = bp.take<uint32_t>(nq);
         hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        rss = bp.take<float>((size_t)nq * M);
+        rsi = bp.take<uint32_t>((size_t)nq + 1);
         chosen = bp.take<uint32_t>((size_t)nq * nprobe);
         cscore = bp.take<float>((size_t)nq * nprobe);
         nch = bp.take<uint32_t>(nq);
@@ -486,7 +498,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         dev::launch_encode(view_, Qc, nq, e, use_sq8_, view_.rerank_mode == 1, st);
         if (dbg && dbg->stage == 0) return debug_encode(e, nq, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[1], st);
-        rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+        rc = route(h, e, Qc, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, rss, rsi, chosen, cscore, nch, st, err);
         if (rc != kOk) return rc;
         if (dbg && dbg->stage == 1) return debug_route(chosen, cscore, nch, nq, nprobe, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[2], st);

@@ -174,7 +174,8 @@ class DeviceIndex {
     int run_perquery(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                      uint32_t* d_nout, cudaStream_t st, std::string& err);
     int route(const HostIndex& h, const dev::QueryEnc& e, const float* dQ, int nq, int nprobe, float tc, float beta,
-              bool batch_router, uint16_t* hs, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch, uint32_t* chosen,
+              bool batch_router, uint16_t* hs, uint32_t* sl, uint32_t* sl_n, uint32_t* tree_scratch,
+              float* rs_scores, uint32_t* rs_items, uint32_t* chosen,
               float* cscore, uint32_t* nch, cudaStream_t st, std::string& err);
 
     int device_ = -1;

@@ -80,6 +80,12 @@ __device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot,
     return ok;
 }
 
+// Byte b of w as a float (signed or unsigned).
+__device__ __forceinline__ float byte_val(uint32_t w, int b, bool sgn) {
+    const uint32_t v = (w >> (8 * b)) & 0xFFu;
+    return sgn ? (float)(int8_t)v : (float)v;
+}
+
 // canonical_cm for a member entry whose lower home is precomputed (IndexView::cell_lower).
 __device__ __forceinline__ bool canonical_lower(uint32_t lower, const uint64_t* probed) {
     return lower == kNoCell || !((__ldg(probed + (lower >> 6)) >> (lower & 63)) & 1ull);
@@ -703,6 +709,265 @@ __global__ void __launch_bounds__(kBS) k_rescore_select(IndexView ix, QueryEnc e
             }
         }
         nch[q] = (uint32_t)m;
+    }
+}
+
+// The kth smallest (1-based) of n 64-bit keys given by key(i), by radix selection on all 8 bytes.
+// All threads of the block call it; `hist` is 256 shared words.
+template <typename KeyFn>
+__device__ uint64_t block_select_kth_fn(KeyFn key, int n, int kth, uint32_t* hist) {
+    __shared__ uint64_t s_prefix;
+    __shared__ int s_rem;
+    if (threadIdx.x == 0) {
+        s_prefix = 0;
+        s_rem = kth;
+    }
+    __syncthreads();
+    uint64_t mask = 0;
+    for (int by = 7; by >= 0; --by) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const uint64_t prefix = s_prefix;
+        const int shift = by * 8;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint64_t k = key(i);
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int rem = s_rem, digit = 255;
+            for (int t = 0; t < 256; ++t) {
+                if ((int)hist[t] >= rem) {
+                    digit = t;
+                    break;
+                }
+                rem -= (int)hist[t];
+            }
+            s_rem = rem;
+            s_prefix = prefix | ((uint64_t)digit << shift);
+        }
+        mask |= 0xFFull << shift;
+        __syncthreads();
+    }
+    const uint64_t r = s_prefix;
+    __syncthreads();
+    return r;
+}
+
+// Probe selection after k_rescore_dots: the nprobe best shortlist cells by (score desc, cell asc),
+// best first, then the nucleus cut (index.rs:1931-1977, :1283-1301). Up to `small` entries are
+// sorted whole in shared memory; longer shortlists first select the nprobe-th key by radix and sort
+// only the keys at or before it.
+__global__ void __launch_bounds__(kBS) k_probe_select(const uint32_t* __restrict__ sl,
+                                                      const uint32_t* __restrict__ sl_n,
+                                                      const float* __restrict__ sc, int sl_cap, int nprobe, int small,
+                                                      float tc, float beta, uint32_t* chosen, float* cscore,
+                                                      uint32_t* nch, uint32_t* err) {
+    extern __shared__ uint64_t pk[];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_cnt;
+    const int q = blockIdx.x;
+    const int n = (int)sl_n[q];
+    const int cap = min(nprobe, n);
+    if (n > sl_cap || cap > small) {
+        if (threadIdx.x == 0) {
+            nch[q] = 0;
+            atomicAdd(err, 1u);
+        }
+        return;
+    }
+    const uint32_t* cq = sl + (size_t)q * sl_cap;
+    const float* sq = sc + (size_t)q * sl_cap;
+    auto key = [&](int i) -> uint64_t { return ((uint64_t)(~float_key(__ldg(sq + i))) << 32) | __ldg(cq + i); };
+    int m = n;  // keys to sort
+    if (n <= small) {
+        for (int i = threadIdx.x; i < n; i += kBS) pk[i] = key(i);
+    } else {
+        const uint64_t kk = block_select_kth_fn(key, n, cap, hist);
+        if (threadIdx.x == 0) s_cnt = 0;
+        __syncthreads();
+        for (int base = 0; base < n; base += kBS) {
+            const int i = base + threadIdx.x;
+            const uint64_t k = i < n ? key(i) : ~0ull;
+            const bool take = i < n && k <= kk;
+            const uint32_t p = warp_append(take, &s_cnt);
+            if (take) pk[p] = k;
+        }
+        __syncthreads();
+        m = cap;
+    }
+    const int P = next_pow2(max(m, 1));
+    for (int i = m + threadIdx.x; i < P; i += kBS) pk[i] = ~0ull;
+    __syncthreads();
+    block_bitonic_u64(pk, P);
+    for (int i = threadIdx.x; i < cap; i += kBS) {
+        const uint64_t k = pk[i];
+        chosen[(size_t)q * nprobe + i] = (uint32_t)k;
+        cscore[(size_t)q * nprobe + i] = key_float(~(uint32_t)(k >> 32));
+    }
+    if (threadIdx.x == 0) {
+        int mm = cap;
+        if (cap > 0 && tc < 1.0f) {
+            // nucleus over the capped, sorted candidates (index.rs:1289-1300)
+            float max_s = key_float(~(uint32_t)(pk[0] >> 32));
+            float z = 0.0f;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(pk[i] >> 32));
+                z = __fadd_rn(z, (float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)));
+            }
+            float cum = 0.0f;
+            mm = 0;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(pk[i] >> 32));
+                ++mm;
+                float p = __fdiv_rn((float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)), __fadd_rn(z, 1e-9f));
+                cum = __fadd_rn(cum, p);
+                if (cum >= tc) break;
+            }
+        }
+        nch[q] = (uint32_t)mm;
+    }
+}
+
+// One lane's exact dot of a query (shared memory, dim floats) with one row: the reference's 8-lane
+// FMA order (lane l takes elements l, l+8, ...), the hsum_ps tree, then the sequential tail.
+// Byte rows are read 16 bytes (two steps) at a time; `row` must be 16-byte aligned with dim % 16 == 0
+// for bytes and dim % 4 == 0 for f32.
+template <bool kBytes>
+__device__ __forceinline__ float lane_row_dot(const float* __restrict__ qs, const void* row, int dim) {
+    const int full8 = dim & ~7, n8 = full8 >> 3;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, a4 = 0.0f, a5 = 0.0f, a6 = 0.0f, a7 = 0.0f;
+    const float4* qp = reinterpret_cast<const float4*>(qs);
+    if (kBytes) {
+        const uint4* rp = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+        for (int m = 0; m < (n8 >> 1); ++m) {
+            const uint4 w = __ldg(rp + m);
+            const float4 q0 = qp[4 * m], q1 = qp[4 * m + 1], q2 = qp[4 * m + 2], q3 = qp[4 * m + 3];
+            a0 = __fmaf_rn(q0.x, byte_val(w.x, 0, false), a0);
+            a1 = __fmaf_rn(q0.y, byte_val(w.x, 1, false), a1);
+            a2 = __fmaf_rn(q0.z, byte_val(w.x, 2, false), a2);
+            a3 = __fmaf_rn(q0.w, byte_val(w.x, 3, false), a3);
+            a4 = __fmaf_rn(q1.x, byte_val(w.y, 0, false), a4);
+            a5 = __fmaf_rn(q1.y, byte_val(w.y, 1, false), a5);
+            a6 = __fmaf_rn(q1.z, byte_val(w.y, 2, false), a6);
+            a7 = __fmaf_rn(q1.w, byte_val(w.y, 3, false), a7);
+            a0 = __fmaf_rn(q2.x, byte_val(w.z, 0, false), a0);
+            a1 = __fmaf_rn(q2.y, byte_val(w.z, 1, false), a1);
+            a2 = __fmaf_rn(q2.z, byte_val(w.z, 2, false), a2);
+            a3 = __fmaf_rn(q2.w, byte_val(w.z, 3, false), a3);
+            a4 = __fmaf_rn(q3.x, byte_val(w.w, 0, false), a4);
+            a5 = __fmaf_rn(q3.y, byte_val(w.w, 1, false), a5);
+            a6 = __fmaf_rn(q3.z, byte_val(w.w, 2, false), a6);
+            a7 = __fmaf_rn(q3.w, byte_val(w.w, 3, false), a7);
+        }
+    } else {
+        const float4* rp = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+        for (int i = 0; i < n8; ++i) {
+            const float4 x0 = __ldg(rp + 2 * i), x1 = __ldg(rp + 2 * i + 1);
+            const float4 q0 = qp[2 * i], q1 = qp[2 * i + 1];
+            a0 = __fmaf_rn(q0.x, x0.x, a0);
+            a1 = __fmaf_rn(q0.y, x0.y, a1);
+            a2 = __fmaf_rn(q0.z, x0.z, a2);
+            a3 = __fmaf_rn(q0.w, x0.w, a3);
+            a4 = __fmaf_rn(q1.x, x1.x, a4);
+            a5 = __fmaf_rn(q1.y, x1.y, a5);
+            a6 = __fmaf_rn(q1.z, x1.z, a6);
+            a7 = __fmaf_rn(q1.w, x1.w, a7);
+        }
+    }
+    float sc = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), __fadd_rn(a2, a6)), __fadd_rn(__fadd_rn(a1, a5), __fadd_rn(a3, a7)));
+    for (int i = full8; i < dim; ++i) {
+        const float x = kBytes ? (float)reinterpret_cast<const uint8_t*>(row)[i] : reinterpret_cast<const float*>(row)[i];
+        sc = __fadd_rn(sc, __fmul_rn(qs[i], x));
+    }
+    return sc;
+}
+
+// Small shortlists (the re-order of index.rs:1931-1977 when nprobe x multiplier is small): one warp
+// per query scores up to kSmallShortlist cells, one lane per centroid row, then sorts the keys
+// (score desc, cell asc) in its slice of shared memory and takes the best nprobe, then the nucleus.
+constexpr int kSmallShortlist = 1024;
+constexpr int kSmallQ = 4;  // queries (warps) per CTA
+template <bool kBytes>
+__global__ void __launch_bounds__(32 * kSmallQ) k_rescore_small(IndexView ix, const float* __restrict__ qsrc,
+                                                               const float* __restrict__ qbase,
+                                                               const uint32_t* __restrict__ sl,
+                                                               const uint32_t* __restrict__ sl_n, int sl_cap, int nq,
+                                                               int nprobe, float tc, float beta, uint32_t* chosen,
+                                                               float* cscore, uint32_t* nch, uint32_t* err) {
+    extern __shared__ __align__(16) uint8_t ssm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, dim = ix.dim;
+    const int q = blockIdx.x * kSmallQ + warp;
+    const int qstride = (dim + 3) & ~3;
+    float* qs = reinterpret_cast<float*>(ssm) + (size_t)warp * qstride;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(ssm + (size_t)kSmallQ * qstride * 4) + (size_t)warp * kSmallShortlist;
+    if (q >= nq) return;  // warp-uniform
+    const int n = (int)sl_n[q];
+    if (n > kSmallShortlist || n > sl_cap) {
+        if (lane == 0) {
+            nch[q] = 0;
+            atomicAdd(err, 1u);
+        }
+        return;
+    }
+    for (int i = lane; i < dim; i += 32) qs[i] = qsrc[(size_t)q * dim + i];
+    __syncwarp();
+    const float base = kBytes ? qbase[q] : 0.0f;
+    const uint32_t* cq = sl + (size_t)q * sl_cap;
+    for (int i = lane; i < n; i += 32) {
+        const uint32_t c = __ldg(cq + i);
+        const void* row = kBytes ? (const void*)(ix.cent_sq8 + (size_t)c * dim) : (const void*)(ix.cent_f32 + (size_t)c * dim);
+        float s = lane_row_dot<kBytes>(qs, row, dim);
+        if (kBytes) s = __fadd_rn(s, base);
+        keys[i] = ((uint64_t)(~float_key(s)) << 32) | c;
+    }
+    const int P = next_pow2(max(n, 1));
+    for (int i = n + lane; i < P; i += 32) keys[i] = ~0ull;
+    __syncwarp();
+    for (int kk = 2; kk <= P; kk <<= 1) {
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < P; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t a = keys[i], b = keys[ixj];
+                    if ((a > b) == ((i & kk) == 0)) {
+                        keys[i] = b;
+                        keys[ixj] = a;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+    const int cap = min(nprobe, n);
+    for (int i = lane; i < cap; i += 32) {
+        const uint64_t k = keys[i];
+        chosen[(size_t)q * nprobe + i] = (uint32_t)k;
+        cscore[(size_t)q * nprobe + i] = key_float(~(uint32_t)(k >> 32));
+    }
+    if (lane == 0) {
+        int mm = cap;
+        if (cap > 0 && tc < 1.0f) {
+            // nucleus over the capped, sorted candidates (index.rs:1289-1300)
+            float max_s = key_float(~(uint32_t)(keys[0] >> 32));
+            float z = 0.0f;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(keys[i] >> 32));
+                z = __fadd_rn(z, (float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)));
+            }
+            float cum = 0.0f;
+            mm = 0;
+            for (int i = 0; i < cap; ++i) {
+                float s = key_float(~(uint32_t)(keys[i] >> 32));
+                ++mm;
+                float p = __fdiv_rn((float)exp((double)__fmul_rn(__fsub_rn(s, max_s), beta)), __fadd_rn(z, 1e-9f));
+                cum = __fadd_rn(cum, p);
+                if (cum >= tc) break;
+            }
+        }
+        nch[q] = (uint32_t)mm;
     }
 }
 
@@ -1866,21 +2131,25 @@ __global__ void __launch_bounds__(1024) k_rerank_items(const uint32_t* __restric
 
 __host__ __device__ constexpr int gather_rows(int mode) { return mode == 0 ? 16 : 32; }
 
-__device__ __forceinline__ float byte_val(uint32_t w, int b, bool sgn) {
-    const uint32_t v = (w >> (8 * b)) & 0xFFu;
-    return sgn ? (float)(int8_t)v : (float)v;
-}
 
-template <int kMode>  // 0: f32 rows, 1: per-dimension SQ8 rows, 2: global int8 rows
-__global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float* __restrict__ Q, QueryEnc e,
-                                                       const uint32_t* __restrict__ cand,
-                                                       const uint32_t* __restrict__ cand_n,
-                                                       const uint32_t* __restrict__ item_off, int nq, int cand_cap,
-                                                       float* __restrict__ score_out) {
+// Rows scored by row_dots: queries (nq x dim, f32), an optional per-query base added after the dot
+// (SQ8 rows), and the rows themselves (f32 or bytes).
+struct RowSrc {
+    int dim;
+    const float* qsrc;
+    const float* qbase;
+    const float* rows_f32;
+    const uint8_t* rows_u8;
+};
+
+template <int kMode>  // 0: f32 rows, 1: unsigned byte rows + base, 2: signed byte rows
+__device__ __forceinline__ void row_dots(const RowSrc& src, const uint32_t* __restrict__ cand,
+                                         const uint32_t* __restrict__ cand_n, const uint32_t* __restrict__ item_off,
+                                         int nq, int cand_cap, float* __restrict__ score_out) {
     constexpr int R = gather_rows(kMode);
     extern __shared__ __align__(16) float gsm[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int dim = ix.dim, full8 = dim & ~7, n8 = full8 >> 3;
+    const int dim = src.dim, full8 = dim & ~7, n8 = full8 >> 3;
     float* sq = gsm + (size_t)warp * ((dim + 3) & ~3);
     const long long total = item_off[nq];
     const long long tw = (long long)gridDim.x * (blockDim.x >> 5), gw = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
@@ -1923,7 +2192,7 @@ __global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float
         const int q = q_a;
         if (q != cur_q) {  // warp-uniform: stage this query's vector
             __syncwarp();
-            const float* qv = kMode == 1 ? e.rqs + (size_t)q * dim : Q + (size_t)q * dim;
+            const float* qv = src.qsrc + (size_t)q * dim;
             for (int i = lane; i < dim; i += 32) sq[i] = __ldg(qv + i);
             __syncwarp();
             cur_q = q;
@@ -1931,7 +2200,7 @@ __global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float
         const bool valid = s_a != ~0u;
         float sc = 0.0f;
         if (kMode == 0) {
-            const float* row = ix.vecs_f32 + (size_t)(valid ? s_a : 0u) * dim;
+            const float* row = src.rows_f32 + (size_t)(valid ? s_a : 0u) * dim;
             float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
             if (valid) {
                 const float4* rp = reinterpret_cast<const float4*>(row) + h;
@@ -1957,7 +2226,7 @@ __global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float
             }
         } else if (valid) {
             constexpr bool sgn = kMode == 2;
-            const uint8_t* row = ix.rr_u8 + (size_t)s_a * dim;
+            const uint8_t* row = src.rows_u8 + (size_t)s_a * dim;
             const uint4* rp = reinterpret_cast<const uint4*>(row);
             const float4* qp = reinterpret_cast<const float4*>(sq);
             float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, a4 = 0.0f, a5 = 0.0f, a6 = 0.0f, a7 = 0.0f;
@@ -1998,13 +2267,33 @@ __global__ void __launch_bounds__(256) k_rerank_gather(IndexView ix, const float
             sc = __fadd_rn(__fadd_rn(__fadd_rn(a0, a4), __fadd_rn(a2, a6)), __fadd_rn(__fadd_rn(a1, a5), __fadd_rn(a3, a7)));
             for (int i = full8; i < dim; ++i)
                 sc = __fadd_rn(sc, __fmul_rn(sq[i], sgn ? (float)(int8_t)row[i] : (float)row[i]));
-            if (kMode == 1) sc = __fadd_rn(__ldg(e.rbase + q), sc);
+            if (kMode == 1) sc = __fadd_rn(__ldg(src.qbase + q), sc);
             score_out[(size_t)q * cand_cap + r_a + j] = sc;
         }
         q_a = q_n;
         r_a = r_n;
         s_a = s_n;
     }
+}
+
+
+// Exact rerank rows (index.rs:1309-1378): score_out[q * cand_cap + r] for every candidate.
+template <int kMode>
+__global__ void __launch_bounds__(256) k_rerank_gather(RowSrc src, const uint32_t* __restrict__ cand,
+                                                       const uint32_t* __restrict__ cand_n,
+                                                       const uint32_t* __restrict__ item_off, int nq, int cand_cap,
+                                                       float* __restrict__ score_out) {
+    row_dots<kMode>(src, cand, cand_n, item_off, nq, cand_cap, score_out);
+}
+
+// Centroid re-order scores of the routing shortlist (index.rs:1931-1977, :782-800): SQ8 rows with
+// the query's base, or f32 rows; the same exact dot as the rerank.
+template <int kMode>
+__global__ void __launch_bounds__(256) k_rescore_dots(RowSrc src, const uint32_t* __restrict__ cells,
+                                                      const uint32_t* __restrict__ cells_n,
+                                                      const uint32_t* __restrict__ item_off, int nq, int cap,
+                                                      float* __restrict__ score_out) {
+    row_dots<kMode>(src, cells, cells_n, item_off, nq, cap, score_out);
 }
 
 // Best k (k <= 32) of each query's scored candidates, one warp per query. A chunk of up to 512
@@ -2285,8 +2574,57 @@ void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int
 
 void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
                            const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
-                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, cudaStream_t st) {
+                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, float* rs_scores,
+                           uint32_t* rs_items, int expect_n, cudaStream_t st) {
     if (nq <= 0) return;
+    const int mode = use_sq8 ? 1 : 0;
+    const int row_bytes = use_sq8 ? ix.dim : ix.dim * 4;
+    if (expect_n <= 128 && row_bytes % 16 == 0 && nprobe <= kSmallShortlist) {
+        // small shortlists: one launch, one warp per query
+        const size_t smem = (size_t)kSmallQ * (((ix.dim + 3) & ~3) * sizeof(float) + kSmallShortlist * sizeof(uint64_t));
+        const int grid = (nq + kSmallQ - 1) / kSmallQ;
+        Tick tk(kKRescore, st);
+        if (use_sq8) {
+            set_smem((const void*)k_rescore_small<true>, smem);
+            k_rescore_small<true><<<grid, 32 * kSmallQ, smem, st>>>(ix, e.cqs, e.cqbase, sl, sl_n, sl_cap, nq, nprobe,
+                                                                     tc, beta, chosen, cscore, nch, err);
+        } else {
+            set_smem((const void*)k_rescore_small<false>, smem);
+            k_rescore_small<false><<<grid, 32 * kSmallQ, smem, st>>>(ix, Q, e.cqbase, sl, sl_n, sl_cap, nq, nprobe,
+                                                                      tc, beta, chosen, cscore, nch, err);
+        }
+        return;
+    }
+    if (rs_scores && rs_items && row_bytes % 16 == 0) {
+        // scores of every (query, shortlist cell) pair by the flattened register gather, then a
+        // per-query selection
+        const void* fn = mode == 1 ? (const void*)k_rescore_dots<1> : (const void*)k_rescore_dots<0>;
+        const size_t smem = (size_t)8 * ((ix.dim + 3) & ~3) * sizeof(float);
+        set_smem(fn, smem);
+        int dev = 0, sms = 148, per_sm = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        const RowSrc src{ix.dim, use_sq8 ? e.cqs : Q, e.cqbase, ix.cent_f32, ix.cent_sq8};
+        {
+            Tick tk(kKRescore, st);
+            k_rerank_items<<<1, 1024, 0, st>>>(sl_n, nq, gather_rows(mode), rs_items);
+            if (mode == 1)
+                k_rescore_dots<1><<<sms * per_sm, 256, smem, st>>>(src, sl, sl_n, rs_items, nq, sl_cap, rs_scores);
+            else
+                k_rescore_dots<0><<<sms * per_sm, 256, smem, st>>>(src, sl, sl_n, rs_items, nq, sl_cap, rs_scores);
+        }
+        const int small = std::max(next_pow2(std::max(nprobe, 1)), 1024);
+        if (small <= kSortCap) {
+            const size_t psm = (size_t)small * sizeof(uint64_t);
+            set_smem((const void*)k_probe_select, psm);
+            Tick tk(kKRescore, st);
+            k_probe_select<<<nq, kBS, psm, st>>>(sl, sl_n, rs_scores, sl_cap, nprobe, small, tc, beta, chosen,
+                                                 cscore, nch, err);
+            return;
+        }
+    }
     int P = next_pow2(std::min(std::max(sl_cap, 1), kSortCap));
     size_t smem = (size_t)P * sizeof(uint64_t) + (size_t)ix.dim * sizeof(float);
     set_smem((const void*)k_rescore_select, smem);
@@ -2413,15 +2751,16 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
             k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
         }
         {
+            const RowSrc src{ix.dim, ix.rerank_mode == 1 ? e.rqs : Q, e.rbase, ix.vecs_f32, ix.rr_u8};
             Tick tk(kKRerank, st);
             if (ix.rerank_mode == 0)
-                k_rerank_gather<0><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                k_rerank_gather<0><<<grid, 256, smem, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap,
                                                             score_scratch);
             else if (ix.rerank_mode == 1)
-                k_rerank_gather<1><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                k_rerank_gather<1><<<grid, 256, smem, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap,
                                                             score_scratch);
             else
-                k_rerank_gather<2><<<grid, 256, smem, st>>>(ix, Q, e, cand, cand_n, item_scratch, nq, cand_cap,
+                k_rerank_gather<2><<<grid, 256, smem, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap,
                                                             score_scratch);
         }
         if (k <= 32) {

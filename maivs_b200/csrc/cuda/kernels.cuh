@@ -114,7 +114,8 @@ void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int
 // nucleus cut (index.rs:1931-1977, :1283-1301).
 void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
                            const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
-                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, cudaStream_t st);
+                           uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, float* rs_scores,
+                           uint32_t* rs_items, int expect_n, cudaStream_t st);
 
 // Cell-major batch (index.rs:1999-2311).
 struct CellMajorBufs {

@@ -205,7 +205,8 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
     const int rest_cap = std::max(32 * target, 16384) * grow_factor;
     const int cand_cap = seed_cap + rest_cap;
     const bool tree_router = !(h.two_stage && !h.cent_bits.empty()) && h.tree;
-    uint32_t *sl, *sl_n, *tsc;
+    uint32_t *sl, *sl_n, *tsc, *rsi;
+    float* rss;
     uint16_t* hs;
     auto carve = [&](Bump& bp) {
         dev::QueryEnc& e = r.e;
@@ -222,6 +223,8 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         sl_n = bp.take<uint32_t>(nq);
         hs = bp.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? bp.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        rss = bp.take<float>((size_t)r.qb * M);
+        rsi = bp.take<uint32_t>((size_t)r.qb + 1);
         r.chosen = bp.take<uint32_t>((size_t)W * r.qb * nprobe);
         r.cscore = bp.take<float>((size_t)W * r.qb * nprobe);
         r.nch = bp.take<uint32_t>((size_t)W * r.qb);
@@ -285,7 +288,7 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         eb.cqbase += q0;
         eb.rqs += (size_t)q0 * dim;
         eb.rbase += q0;
-        rc = route(h, eb, dQ + (size_t)q0 * dim, qn, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc,
+        rc = route(h, eb, dQ + (size_t)q0 * dim, qn, nprobe, a.tc, a.beta, true, hs, sl, sl_n, tsc, rss, rsi,
                    r.chosen + (size_t)q0 * nprobe, r.cscore + (size_t)q0 * nprobe, r.nch + q0, st, err);
         if (rc != kOk) return rc;
     }

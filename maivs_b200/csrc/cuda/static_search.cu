@@ -93,7 +93,8 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
 
     dev::QueryEnc e{};
     dev::PerQueryBufs b{};
-    uint32_t *sl, *sl_n, *tsc, *chosen, *nch, *nout, *ritem;
+    uint32_t *sl, *sl_n, *tsc, *chosen, *nch, *nout, *ritem, *rsi;
+    float* rss;
     uint16_t* hs;
     float *cscore, *rsc;
     auto carve = [&](Carve& c) {
@@ -109,6 +110,8 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
         sl_n = c.take<uint32_t>(nq);
         hs = c.take<uint16_t>((size_t)nq * M);
         tsc = tree_router ? c.take<uint32_t>((size_t)nq * 3 * tree_cap_) : nullptr;
+        rss = c.take<float>((size_t)nq * M);
+        rsi = c.take<uint32_t>((size_t)nq + 1);
         chosen = c.take<uint32_t>((size_t)nq * nprobe);
         cscore = c.take<float>((size_t)nq * nprobe);
         nch = c.take<uint32_t>(nq);
@@ -140,7 +143,7 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
     dev::take_launch_error(nullptr);
     cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
     dev::launch_encode(view_, dQ, nq, e, use_sq8_, view_.rerank_mode == 1, st);
-    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, chosen, cscore, nch, st, err);
+    rc = route(h, e, dQ, nq, nprobe, a.tc, a.beta, false, hs, sl, sl_n, tsc, rss, rsi, chosen, cscore, nch, st, err);
     if (rc != kOk) return rc;
     dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
                          h.filter_lo, h.filter_hi, b, st);
