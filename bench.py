@@ -95,16 +95,36 @@ def build_quality(X: np.ndarray, threads: int):
     return ix
 
 
-def operating_point(search, truth) -> tuple[int, int, float]:
-    """Smallest rerank factor (then smallest nprobe) on the grid with R@10 >= 0.99."""
+def build_memory(X: np.ndarray, threads: int):
+    """The reference's `memory` preset (bench/fair/fairbench.py:98-106): quality + per-dimension SQ8 rerank."""
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    import maivs_b200 as M
+
+    n, d = X.shape
+    ix = M.FlatCellIndex(d, "binary", 16, 0x5EED, 0)
+    ix.set_per_dim_sq(True)
+    ix.set_orthogonal_polysemy(2, 1.0)
+    ix.set_fastscan(True)
+    ix.set_two_stage(True, 2)
+    ix.set_graph_route(False, 10**9)
+    ix.set_tree_route(True, 2048, 16)
+    ix.set_adaptive(True, 0.02)
+    ix.train_centroids(X, max(16, n // 128))
+    ix.add_batch(np.arange(n, dtype=np.uint64), X)
+    ix.compact()
+    return ix
+
+
+def operating_point(search, truth, target: float = TARGET_RECALL) -> tuple[int, int, float]:
+    """Smallest rerank factor (then smallest nprobe) on the grid with R@10 >= target."""
     best = None
     for rf in RF_GRID:
-        if recall(search(rf, NP_GRID[-1]), truth) < TARGET_RECALL:
+        if recall(search(rf, NP_GRID[-1]), truth) < target:
             continue
         lo, hi = 0, len(NP_GRID) - 1
         while lo < hi:
             mid = (lo + hi) // 2
-            if recall(search(rf, NP_GRID[mid]), truth) >= TARGET_RECALL:
+            if recall(search(rf, NP_GRID[mid]), truth) >= target:
                 hi = mid
             else:
                 lo = mid + 1
@@ -584,6 +604,86 @@ def run_sharded(args):
         tdist.destroy_process_group()
 
 
+def run_lowbatch(args):
+    """500k x 384 `memory` preset, batches of 1 and 16 on the per-query path
+    (no cell-major batching), p50/p99 latency and QPS at R@10 >= 0.99 (or the best point)."""
+    import torch
+
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    X, Q, _ = mixture(args.seed, args.n, args.nq, 384, 1000, 0.35)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ix = build_memory(X, threads)
+    build_s = time.perf_counter() - t0
+    ix.to_device(0)
+    truth = brute_force_topk(X, Q, K, str(dev))
+
+    def search(rf, np_, q=Q):
+        ix.set_rerank_factor(rf)
+        ids, _ = ix.search_batch_arrays(q, K, np_, 1.0, 8.0, False)
+        return ids
+
+    # the memory preset's SQ8 rerank can top out below 0.99 (it does on the reference's own corpus,
+    # docs/RESULTS.md:49); then the point is the cheapest one within 0.002 of the best reachable recall
+    best = recall(search(RF_GRID[-1], NP_GRID[-1]), truth)
+    target = min(TARGET_RECALL, best - 0.002)
+    rf, np_, rec = operating_point(search, truth, target)
+    ix.set_rerank_factor(rf)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    out = {"metric": "p50/p99 latency and QPS at R@10=0.99, batch 1 and 16 (memory preset)",
+           "unit": "ms", "higher_is_better": False, "n_gpus": 1, "dtype": "u8", "data": "synthetic",
+           "config": {"workload": "BASELINE configs[2]: 500k x 384 Gaussian mixture (1000 comps, sigma 0.35), "
+                                  "memory preset (per-dimension SQ8 rerank), per-query path", "n": args.n,
+                      "rerank_factor": rf, "nprobe": np_, "recall_at_10": round(rec, 4),
+                      "best_reachable_recall_at_10": round(best, 4), "recall_target": round(target, 4),
+                      "build_s": round(build_s, 1)}}
+    calls = max(args.steps, 50)
+    for b in (1, 16):
+        # end to end through the host API (queries in, ids/scores out, one synchronisation)
+        lat = []
+        for i in range(args.warmup + calls):
+            q = Q[(i * b) % (args.nq - b + 1):][:b]
+            t = time.perf_counter()
+            ix.search_batch_arrays(q, K, np_, 1.0, 8.0, False)
+            if i >= args.warmup:
+                lat.append((time.perf_counter() - t) * 1e3)
+        # device-resident: CUDA events around each call on the search stream
+        dq = torch.from_numpy(Q[:b].copy()).to(dev)
+        d_ids = torch.empty(b * K, dtype=torch.int64, device=dev)
+        d_sc = torch.empty(b * K, dtype=torch.float32, device=dev)
+        dl = []
+        for i in range(args.warmup + calls):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ix.search_batch_device(dq.data_ptr(), b, K, d_ids.data_ptr(), d_sc.data_ptr(), np_, 1.0, 8.0, False,
+                                   stream.cuda_stream)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= args.warmup:
+                dl.append(e0.elapsed_time(e1))
+        lat, dl = np.asarray(lat), np.asarray(dl)
+        out[f"batch{b}"] = {"e2e_p50_ms": round(float(np.percentile(lat, 50)), 4),
+                            "e2e_p99_ms": round(float(np.percentile(lat, 99)), 4),
+                            "e2e_qps": round(b / (float(lat.mean()) / 1e3), 1),
+                            "device_p50_ms": round(float(np.percentile(dl, 50)), 4),
+                            "device_p99_ms": round(float(np.percentile(dl, 99)), 4), "calls": calls}
+    # the reference's single-thread latency (fairbench.py:61-67) on the oracle port
+    o = oracle.OracleIndex.from_index(ix)
+    cl = []
+    for i in range(min(calls, 200)):
+        t = time.perf_counter()
+        o.search_batch(Q[i:i + 1], K, np_, 1.0, 8.0, False, threads=1)
+        cl.append((time.perf_counter() - t) * 1e3)
+    out["cpu_baseline"] = {"value": round(float(np.percentile(cl, 50)), 4), "unit": "ms (p50, batch 1)", "cores": 1,
+                           "kind": "port", "sample": f"{len(cl)} single-query calls, one thread"}
+    out["value"] = out["batch1"]["e2e_p50_ms"]
+    print(json.dumps(out), flush=True)
+
+
 def run_reference(args):
     ws, rank, local = dist_env()
     if rank != 0:
@@ -641,9 +741,10 @@ def main():
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
     ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
-    ap.add_argument("--workload", choices=("config2", "sharded"), default="config2",
+    ap.add_argument("--workload", choices=("config2", "sharded", "lowbatch"), default="config2",
                     help="config2: the headline 500k batch (replicas for N > 1); sharded: configs[3], 5.2M "
-                         "vectors with cells sharded by range over the N GPUs")
+                         "vectors with cells sharded by range over the N GPUs; lowbatch: configs[2], memory "
+                         "preset at batch 1 and 16")
     args = ap.parse_args()
     sharded = args.workload == "sharded"
     if args.n is None:
@@ -654,6 +755,8 @@ def main():
         run_reference(args)
     elif sharded:
         run_sharded(args)
+    elif args.workload == "lowbatch":
+        run_lowbatch(args)
     else:
         run_maivs(args)
 

@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(kBS) k_encode_warp(IndexView ix, const float* 
                                                      int want_cqs, int want_rqs) {
     __shared__ float s_mins[kBS / 32][256];
     __shared__ uint32_t s_mask[kBS / 32][32];
+    __shared__ float s_x[kBS / 32][32 * E];
     const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * (kBS / 32) + wq;
     if (q >= nq) return;
@@ -377,25 +378,34 @@ __global__ void __launch_bounds__(kBS) k_encode_warp(IndexView ix, const float* 
         }
         *reinterpret_cast<uint4*>(e.lut + ((size_t)q * npos + j) * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
+    // the query row in shared memory for the sequential sums below
+    for (int t = lane; t < dim; t += 32) s_x[wq][t] = __ldg(x + t);
     __syncwarp();
-    // sequential sums: bias (lane 2), centroid SQ8 base (lane 0), rerank SQ8 base (lane 1)
-    if (lane == 2) {
-        float b = 0.0f;
-        for (int t = 0; t < npos; ++t) b = __fadd_rn(b, s_mins[wq][t]);
-        e.fs_delta[q] = delta;
-        e.fs_bias[q] = b;
-    }
-    if ((lane == 0 && want_cqs) || (lane == 1 && want_rqs)) {
+    // three left-to-right sums in one convergent loop: lane 0 the centroid SQ8 base sum(x * csq_min),
+    // lane 1 the rerank SQ8 base sum(x * sq_min), lane 2 the FastScan bias sum(mins)
+    {
         const float* mn = lane == 0 ? ix.csq_min : ix.sq_min;
+        const bool dot = (lane == 0 && want_cqs) || (lane == 1 && want_rqs);
+        const int len = lane == 2 ? npos : (dot ? dim : 0);
         float b = 0.0f;
-#pragma unroll 16
-        for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(mn + t)));
-        (lane == 0 ? e.cqbase : e.rbase)[q] = b;
+#pragma unroll 8
+        for (int t = 0; t < len; ++t) {
+            if (lane == 2)
+                b = __fadd_rn(b, s_mins[wq][t]);
+            else
+                b = __fadd_rn(b, __fmul_rn(s_x[wq][t], __ldg(mn + t)));
+        }
+        if (lane == 2) {
+            e.fs_delta[q] = delta;
+            e.fs_bias[q] = b;
+        } else if (dot) {
+            (lane == 0 ? e.cqbase : e.rbase)[q] = b;
+        }
     }
     if (want_cqs)
-        for (int t = lane; t < dim; t += 32) e.cqs[(size_t)q * dim + t] = __fmul_rn(__ldg(x + t), __ldg(ix.csq_step + t));
+        for (int t = lane; t < dim; t += 32) e.cqs[(size_t)q * dim + t] = __fmul_rn(s_x[wq][t], __ldg(ix.csq_step + t));
     if (want_rqs)
-        for (int t = lane; t < dim; t += 32) e.rqs[(size_t)q * dim + t] = __fmul_rn(__ldg(x + t), __ldg(ix.sq_step + t));
+        for (int t = lane; t < dim; t += 32) e.rqs[(size_t)q * dim + t] = __fmul_rn(s_x[wq][t], __ldg(ix.sq_step + t));
 }
 
 // ---- K2: flat Hamming shortlist ------------------------------------------------------------------
@@ -449,6 +459,35 @@ constexpr int kRouteSmemH = 160 * 1024;  // Hamming rows kept in shared memory u
 // Hamming values (0xFFFF for empty cells) go to shared memory, or to the `hs` scratch (nq x M)
 // when M is too large, plus a per-query histogram. Pass 2: warp j finds query j's counting
 // cut-off and compacts its shortlist in cell order with ballots.
+// Hamming distances of one centroid code to the CTA's queries; NW > 0: that many words, unrolled
+// and read 16 bytes at a time (rows of NW words are 16-byte aligned for even NW); NW = 0: any nw.
+template <int NW>
+__device__ __forceinline__ void ham_rows(const uint64_t (*qb)[16], const uint64_t* __restrict__ code, int nw,
+                                         uint32_t (&h)[kRouteQB]) {
+#pragma unroll
+    for (int j = 0; j < kRouteQB; ++j) h[j] = 0;
+    if (NW > 0) {
+        uint64_t cw[NW > 0 ? NW : 1];
+#pragma unroll
+        for (int w = 0; w < NW; w += 2) {
+            const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(code + w));
+            cw[w] = v.x;
+            cw[w + 1] = v.y;
+        }
+#pragma unroll
+        for (int w = 0; w < NW; ++w)
+#pragma unroll
+            for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw[w]);
+    } else {
+        for (int w = 0; w < nw; ++w) {
+            const uint64_t cw = __ldg(code + w);
+#pragma unroll
+            for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw);
+        }
+    }
+}
+
+template <int NW>
 __global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int nq, int want_c, int all,
                                                     int h_in_smem, uint16_t* hs, uint32_t* sl, uint32_t* sl_n,
                                                     int sl_cap) {
@@ -470,16 +509,7 @@ __global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, in
         for (int c = threadIdx.x; c < M; c += kBS) {
             uint32_t h[kRouteQB];
             const bool lv = ix.live[c] != 0;
-            if (lv) {
-                const uint64_t* src = ix.cent_bits + (size_t)c * nw;
-#pragma unroll
-                for (int j = 0; j < kRouteQB; ++j) h[j] = 0;
-                for (int w = 0; w < nw; ++w) {
-                    const uint64_t cw = __ldg(src + w);
-#pragma unroll
-                    for (int j = 0; j < kRouteQB; ++j) h[j] += __popcll(qb[j][w] ^ cw);
-                }
-            }
+            if (lv) ham_rows<NW>(qb, ix.cent_bits + (size_t)c * nw, nw, h);
 #pragma unroll
             for (int j = 0; j < kRouteQB; ++j) {
                 if (j < nqb) {
@@ -2549,17 +2579,30 @@ void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_
     const size_t h_b = (size_t)kRouteQB * ix.M * sizeof(uint16_t);
     const int in_smem = h_b <= (size_t)kRouteSmemH ? 1 : 0;
     const size_t smem = hist_b + (in_smem ? h_b : 0);
-    set_smem((const void*)k_route_flat, smem);
+    const int grid = (nq + kRouteQB - 1) / kRouteQB;
+    const void* fn = ix.nw == 8    ? (const void*)k_route_flat<8>
+                     : ix.nw == 4  ? (const void*)k_route_flat<4>
+                     : ix.nw == 2  ? (const void*)k_route_flat<2>
+                     : ix.nw == 12 ? (const void*)k_route_flat<12>
+                     : ix.nw == 16 ? (const void*)k_route_flat<16>
+                                   : (const void*)k_route_flat<0>;
+    set_smem(fn, smem);
     Tick tk(kKRouteFlat, st);
-    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n,
-                                                                      sl_cap);
+    switch (ix.nw) {
+        case 8: k_route_flat<8><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 4: k_route_flat<4><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 2: k_route_flat<2><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 12: k_route_flat<12><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 16: k_route_flat<16><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        default: k_route_flat<0><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+    }
 }
 
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
     QueryEnc e{};
     Tick tk(kKRouteFlat, st);
-    k_route_flat<<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, 0, nullptr, sl, sl_n, sl_cap);
+    k_route_flat<0><<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, 0, nullptr, sl, sl_n, sl_cap);
 }
 
 void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,
