@@ -563,6 +563,7 @@ def run_sharded(args):
     overflow = ix.device_flags(stream.cuda_stream)
     ktimes = ix.kernel_times(reset=True)
     ix.kernel_clock(False)
+    stats = ix.last_search_stats()
     ktot = max(sum(v[0] for v in ktimes.values()), 1e-9)
     shares = {k: round(v[0] / ktot, 4) for k, v in ktimes.items() if v[1]}
     if ws > 1:
@@ -595,6 +596,7 @@ def run_sharded(args):
                 "h2d_bytes_per_step": nq * 384 * 4, "d2h_bytes_per_step": nq * K * 12},
         "clocks": clk.summary(),
         "kernel_share_rank0": shares,
+        "work_rank0": {k: round(v, 1) for k, v in stats.items()},
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -656,7 +658,11 @@ def run_lowbatch(args):
         d_ids = torch.empty(b * K, dtype=torch.int64, device=dev)
         d_sc = torch.empty(b * K, dtype=torch.float32, device=dev)
         dl = []
+        ix.kernel_clock(True)
+        ix.kernel_times(reset=True)
         for i in range(args.warmup + calls):
+            if i == args.warmup:
+                ix.kernel_times(reset=True)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             ix.search_batch_device(dq.data_ptr(), b, K, d_ids.data_ptr(), d_sc.data_ptr(), np_, 1.0, 8.0, False,
@@ -665,12 +671,15 @@ def run_lowbatch(args):
             e1.synchronize()
             if i >= args.warmup:
                 dl.append(e0.elapsed_time(e1))
+        kt = ix.kernel_times(reset=True)
+        ix.kernel_clock(False)
         lat, dl = np.asarray(lat), np.asarray(dl)
         out[f"batch{b}"] = {"e2e_p50_ms": round(float(np.percentile(lat, 50)), 4),
                             "e2e_p99_ms": round(float(np.percentile(lat, 99)), 4),
                             "e2e_qps": round(b / (float(lat.mean()) / 1e3), 1),
                             "device_p50_ms": round(float(np.percentile(dl, 50)), 4),
-                            "device_p99_ms": round(float(np.percentile(dl, 99)), 4), "calls": calls}
+                            "device_p99_ms": round(float(np.percentile(dl, 99)), 4), "calls": calls,
+                            "kernel_us_per_call": {k: round(v[0] * 1e3 / calls, 2) for k, v in kt.items() if v[1]}}
     # the reference's single-thread latency (fairbench.py:61-67) on the oracle port
     o = oracle.OracleIndex.from_index(ix)
     cl = []

@@ -47,6 +47,39 @@ __device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, i
     }
 }
 
+// group_sums over positions [p0, p1) only (the packed 16-bit partial sums of a position slice).
+__device__ __forceinline__ void group_sums_range(const uint32_t* __restrict__ codes, int ng, int g, bool active,
+                                                 const uint8_t* lut, int p0, int p1, uint32_t acc[4]) {
+    acc[0] = acc[1] = acc[2] = acc[3] = 0;
+    const uint4* T = reinterpret_cast<const uint4*>(lut);
+    int j0 = p0;
+    for (; j0 + 8 <= p1; j0 += 8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint4 t = T[j0 + u];
+            const uint32_t r0 = lut16x4(t, w[u]);
+            const uint32_t r1 = lut16x4(t, w[u] >> 16);
+            acc[0] += __byte_perm(r0, 0, 0x4140);
+            acc[1] += __byte_perm(r0, 0, 0x4342);
+            acc[2] += __byte_perm(r1, 0, 0x4140);
+            acc[3] += __byte_perm(r1, 0, 0x4342);
+        }
+    }
+    for (; j0 < p1; ++j0) {
+        const uint32_t w = active ? __ldg(codes + (size_t)j0 * ng + g) : 0u;
+        const uint4 t = T[j0];
+        const uint32_t r0 = lut16x4(t, w);
+        const uint32_t r1 = lut16x4(t, w >> 16);
+        acc[0] += __byte_perm(r0, 0, 0x4140);
+        acc[1] += __byte_perm(r0, 0, 0x4342);
+        acc[2] += __byte_perm(r1, 0, 0x4140);
+        acc[3] += __byte_perm(r1, 0, 0x4342);
+    }
+}
+
 __device__ __forceinline__ uint32_t member_sum(const uint32_t acc[4], int b) {
     return (acc[b >> 1] >> (16 * (b & 1))) & 0xFFFFu;
 }
@@ -280,132 +313,141 @@ __global__ void __launch_bounds__(kBS) k_encode(IndexView ix, const float* __res
         for (int t = threadIdx.x; t < dim; t += kBS) e.rqs[(size_t)q * dim + t] = __fmul_rn(x[t], ix.sq_step[t]);
 }
 
-// One warp per query, E = dim_pad / 32 rotated coordinates per lane (lane l holds l*E .. l*E+E-1).
-// Butterflies of the FWHT with h < E stay inside a lane; h >= E pair lane l with l ^ (h / E).
-// Every level applies the reference's butterflies (quantize.rs:71-126), so the bits are the same.
+// Rotation layout: E = dim_pad / 32 rotated coordinates per lane of warp 0 (lane l holds l*E ..
+// l*E+E-1); butterflies of the FWHT with h < E stay inside a lane, h >= E pair lane l with l ^ (h / E),
+// every level applying the reference's butterflies (quantize.rs:71-126), so the bits are the same.
+// Query encoding with four warps per query: warp 0 rotates (two rounds of sign flip + FWHT in
+// registers and shuffles) and packs the sign bits while warps 1 and 2 compute the SQ8 pre-scales
+// and their left-to-right base sums; then every thread builds the FastScan table entries of its
+// nibble positions (rotated values from shared memory), the range reduction runs over the block,
+// and one thread adds the table minima in position order (quantize.rs:57-67, :152-163, :279-313;
+// index.rs:1177-1187), every float operation in the reference's order.
 template <int E>
-__global__ void __launch_bounds__(kBS) k_encode_warp(IndexView ix, const float* __restrict__ Q, QueryEnc e, int nq,
-                                                     int want_cqs, int want_rqs) {
-    __shared__ float s_mins[kBS / 32][256];
-    __shared__ uint32_t s_mask[kBS / 32][32];
-    __shared__ float s_x[kBS / 32][32 * E];
-    const int wq = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.x * (kBS / 32) + wq;
-    if (q >= nq) return;
+__global__ void __launch_bounds__(128) k_encode4(IndexView ix, const float* __restrict__ Q, QueryEnc e, int want_cqs,
+                                                int want_rqs) {
+    __shared__ float s_v[32 * E];
+    __shared__ float s_mins[256];
+    __shared__ float s_red[4];
+    __shared__ uint32_t s_mask[32];
+    const int q = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int dp = ix.dim_pad, dim = ix.dim, npos = ix.npos;
     const float* x = Q + (size_t)q * dim;
-    float v[E];
+    if (warp == 0) {
+        float v[E];
 #pragma unroll
-    for (int t = 0; t < E; ++t) {
-        const int i = lane * E + t;
-        v[t] = i < dim ? __ldg(x + i) : 0.0f;
-    }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dp));
+        for (int t = 0; t < E; ++t) {
+            const int i = lane * E + t;
+            v[t] = i < dim ? __ldg(x + i) : 0.0f;
+        }
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)dp));
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const float* sg = ix.signs + (size_t)r * dp + lane * E;
+        for (int r = 0; r < 2; ++r) {
+            const float* sg = ix.signs + (size_t)r * dp + lane * E;
 #pragma unroll
-        for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], __ldg(sg + t));
+            for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], __ldg(sg + t));
 #pragma unroll
-        for (int h = 1; h < E; h <<= 1) {
+            for (int h = 1; h < E; h <<= 1) {
 #pragma unroll
-            for (int t = 0; t < E; ++t) {
-                if ((t & h) == 0) {
-                    const float a = v[t], b = v[t + h];
-                    v[t] = __fadd_rn(a, b);
-                    v[t + h] = __fsub_rn(a, b);
+                for (int t = 0; t < E; ++t) {
+                    if ((t & h) == 0) {
+                        const float a = v[t], b = v[t + h];
+                        v[t] = __fadd_rn(a, b);
+                        v[t + h] = __fsub_rn(a, b);
+                    }
                 }
             }
-        }
-        for (int hl = 1; hl < 32; hl <<= 1) {  // h = hl * E
+            for (int hl = 1; hl < 32; hl <<= 1) {  // h = hl * E
 #pragma unroll
-            for (int t = 0; t < E; ++t) {
-                const float o = __shfl_xor_sync(0xFFFFFFFFu, v[t], hl);
-                v[t] = (lane & hl) ? __fsub_rn(o, v[t]) : __fadd_rn(v[t], o);
+                for (int t = 0; t < E; ++t) {
+                    const float o = __shfl_xor_sync(0xFFFFFFFFu, v[t], hl);
+                    v[t] = (lane & hl) ? __fsub_rn(o, v[t]) : __fadd_rn(v[t], o);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], scale);
+        }
+        uint32_t m = 0;
+#pragma unroll
+        for (int t = 0; t < E; ++t) {
+            s_v[lane * E + t] = v[t];
+            if (v[t] < 0.0f) m |= 1u << t;
+        }
+        s_mask[lane] = m;
+        __syncwarp();
+        if (lane < ix.nw) {
+            uint64_t w = 0;
+            const int per = 64 / E;  // lanes per word
+            for (int u = 0; u < per; ++u) w |= (uint64_t)s_mask[lane * per + u] << (u * E);
+            e.qbits[(size_t)q * ix.nw + lane] = w;
+        }
+    } else if (warp == 1 || warp == 2) {
+        // SQ8 pre-scales and the base sum(x * min) in dimension order (warp 1: centroid re-order,
+        // warp 2: rerank)
+        const bool want = warp == 1 ? want_cqs : want_rqs;
+        if (want) {
+            const float* mn = warp == 1 ? ix.csq_min : ix.sq_min;
+            const float* stp = warp == 1 ? ix.csq_step : ix.sq_step;
+            float* dst = (warp == 1 ? e.cqs : e.rqs) + (size_t)q * dim;
+            for (int t = lane; t < dim; t += 32) dst[t] = __fmul_rn(__ldg(x + t), __ldg(stp + t));
+            if (lane == 0) {
+                float b = 0.0f;
+#pragma unroll 8
+                for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(mn + t)));
+                (warp == 1 ? e.cqbase : e.rbase)[q] = b;
             }
         }
-#pragma unroll
-        for (int t = 0; t < E; ++t) v[t] = __fmul_rn(v[t], scale);
     }
-    // sign bits (quantize.rs:57-67): lane masks, then one 64-bit word per assembling lane
-    uint32_t m = 0;
+    __syncthreads();
+    // FsQuery::new (quantize.rs:279-313): positions j = threadIdx.x + 128 u
+    constexpr int PU = (8 * E + 127) / 128;  // positions per thread (npos <= 8 E)
+    float raw[PU][16], lo[PU];
+    float range = 0.0f;
 #pragma unroll
-    for (int t = 0; t < E; ++t)
-        if (v[t] < 0.0f) m |= 1u << t;
-    s_mask[wq][lane] = m;
-    __syncwarp();
-    if (lane < ix.nw) {
-        uint64_t w = 0;
-        const int per = 64 / E;  // lanes per word
-        for (int u = 0; u < per; ++u) w |= (uint64_t)s_mask[wq][lane * per + u] << (u * E);
-        e.qbits[(size_t)q * ix.nw + lane] = w;
-    }
-    // FsQuery::new (quantize.rs:279-313): this lane's E/4 nibble positions
-    constexpr int PP = E / 4;
-    float lo[PP], range = 0.0f;
-    float raw[PP][16];
-#pragma unroll
-    for (int pp = 0; pp < PP; ++pp) {
-        lo[pp] = INFINITY;
-        float hi = -INFINITY;
-#pragma unroll
-        for (int ev = 0; ev < 16; ++ev) {
-            float a = 0.0f;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) a = ((ev >> t) & 1) ? __fsub_rn(a, v[4 * pp + t]) : __fadd_rn(a, v[4 * pp + t]);
-            raw[pp][ev] = a;
-            lo[pp] = fminf(lo[pp], a);
-            hi = fmaxf(hi, a);
-        }
-        const int j = lane * PP + pp;
+    for (int u = 0; u < PU; ++u) {
+        const int j = threadIdx.x + 128 * u;
+        lo[u] = INFINITY;
         if (j < npos) {
-            range = fmaxf(range, __fsub_rn(hi, lo[pp]));
-            s_mins[wq][j] = lo[pp];
+            float hi = -INFINITY;
+            const float v0 = s_v[4 * j], v1 = s_v[4 * j + 1], v2 = s_v[4 * j + 2], v3 = s_v[4 * j + 3];
+#pragma unroll
+            for (int ev = 0; ev < 16; ++ev) {
+                float a = 0.0f;
+                a = (ev & 1) ? __fsub_rn(a, v0) : __fadd_rn(a, v0);
+                a = (ev & 2) ? __fsub_rn(a, v1) : __fadd_rn(a, v1);
+                a = (ev & 4) ? __fsub_rn(a, v2) : __fadd_rn(a, v2);
+                a = (ev & 8) ? __fsub_rn(a, v3) : __fadd_rn(a, v3);
+                raw[u][ev] = a;
+                lo[u] = fminf(lo[u], a);
+                hi = fmaxf(hi, a);
+            }
+            range = fmaxf(range, __fsub_rn(hi, lo[u]));
+            s_mins[j] = lo[u];
         }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) range = fmaxf(range, __shfl_xor_sync(0xFFFFFFFFu, range, o));
+    if (lane == 0) s_red[warp] = range;
+    __syncthreads();
+    range = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
     const float delta = fmaxf(__fdiv_rn(range, 255.0f), 1e-12f);
 #pragma unroll
-    for (int pp = 0; pp < PP; ++pp) {
-        const int j = lane * PP + pp;
+    for (int u = 0; u < PU; ++u) {
+        const int j = threadIdx.x + 128 * u;
         if (j >= npos) continue;
         uint32_t wv[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int ev = 0; ev < 16; ++ev) {
-            float qv = clampf(roundf(__fdiv_rn(__fsub_rn(raw[pp][ev], lo[pp]), delta)), 0.0f, 255.0f);
+            float qv = clampf(roundf(__fdiv_rn(__fsub_rn(raw[u][ev], lo[u]), delta)), 0.0f, 255.0f);
             wv[ev >> 2] |= ((uint32_t)qv) << (8 * (ev & 3));
         }
         *reinterpret_cast<uint4*>(e.lut + ((size_t)q * npos + j) * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
-    // the query row in shared memory for the sequential sums below
-    for (int t = lane; t < dim; t += 32) s_x[wq][t] = __ldg(x + t);
-    __syncwarp();
-    // three left-to-right sums in one convergent loop: lane 0 the centroid SQ8 base sum(x * csq_min),
-    // lane 1 the rerank SQ8 base sum(x * sq_min), lane 2 the FastScan bias sum(mins)
-    {
-        const float* mn = lane == 0 ? ix.csq_min : ix.sq_min;
-        const bool dot = (lane == 0 && want_cqs) || (lane == 1 && want_rqs);
-        const int len = lane == 2 ? npos : (dot ? dim : 0);
+    if (threadIdx.x == 96) {  // bias: the table minima in position order
         float b = 0.0f;
-#pragma unroll 8
-        for (int t = 0; t < len; ++t) {
-            if (lane == 2)
-                b = __fadd_rn(b, s_mins[wq][t]);
-            else
-                b = __fadd_rn(b, __fmul_rn(s_x[wq][t], __ldg(mn + t)));
-        }
-        if (lane == 2) {
-            e.fs_delta[q] = delta;
-            e.fs_bias[q] = b;
-        } else if (dot) {
-            (lane == 0 ? e.cqbase : e.rbase)[q] = b;
-        }
+        for (int t = 0; t < npos; ++t) b = __fadd_rn(b, s_mins[t]);
+        e.fs_delta[q] = delta;
+        e.fs_bias[q] = b;
     }
-    if (want_cqs)
-        for (int t = lane; t < dim; t += 32) e.cqs[(size_t)q * dim + t] = __fmul_rn(s_x[wq][t], __ldg(ix.csq_step + t));
-    if (want_rqs)
-        for (int t = lane; t < dim; t += 32) e.rqs[(size_t)q * dim + t] = __fmul_rn(s_x[wq][t], __ldg(ix.sq_step + t));
 }
 
 // ---- K2: flat Hamming shortlist ------------------------------------------------------------------
@@ -1717,9 +1759,16 @@ __global__ void __launch_bounds__(kBS) k_pq_prep(IndexView ix, const uint32_t* _
 
 // Every member of every chosen cell: (d << 32 | slot) when canonical under the first-ranked-home
 // rule (index.rs:1443-1460) and inside the tag filter (index.rs:1430-1439), else kInvalidEntry.
+// One CTA per (probe, query). The query's FastScan table sits in shared memory; for each chunk of
+// 32 member groups (256 members) the 8 warps sum disjoint slices of the nibble positions and
+// combine their packed 16-bit partials in shared memory (exact: a member's total is at most
+// 255 x npos), then every thread resolves one member (slot, tag filter, the per-query exactly-once
+// rule against the probe ranks), so the members' dependent loads run side by side.
 __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                                  const uint32_t* __restrict__ nch, int nprobe, int filtering,
                                                  uint32_t flo, uint32_t fhi, PerQueryBufs b) {
+    __shared__ __align__(16) uint8_t s_lut[16 * 16 * 16];  // npos <= 256 positions x 16 entries
+    __shared__ uint32_t s_part[kBS / 32][32][4];
     const int r = blockIdx.x, q = blockIdx.y;
     if (r >= (int)nch[q]) return;
     const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
@@ -1732,38 +1781,55 @@ __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const
     const uint32_t* crank = b.crank + (size_t)q * ix.M;
     uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
-    const uint8_t* lut = e.lut + (size_t)q * ix.npos * 16;
-    for (int chk = warp; chk * 32 < ng; chk += nwarps) {
-        int g = chk * 32 + lane;
-        bool act = g < ng;
+    const int npos = ix.npos;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(e.lut + (size_t)q * npos * 16);
+        for (int i = threadIdx.x; i < npos; i += kBS) reinterpret_cast<uint4*>(s_lut)[i] = src[i];
+    }
+    __syncthreads();
+    // this warp's slice of the positions
+    const int p0 = (int)((long long)npos * warp / nwarps), p1 = (int)((long long)npos * (warp + 1) / nwarps);
+    for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        const bool act = g < ng;
         uint32_t acc[4];
-        group_sums(codes, ng, g, act, lut, ix.npos, acc);
-        if (!act) continue;
-        for (int bb = 0; bb < 8; ++bb) {
-            int pos = 8 * g + bb;
-            if (pos >= nc) break;
-            uint32_t d = ix.maxk - member_sum(acc, bb);
-            uint32_t slot = ix.cell_slots[moff + pos];
-            bool ok = true;
-            if (filtering) {
-                uint32_t tg = ix.tags[slot];
-                ok = tg >= flo && tg <= fhi;
-            }
-            if (ok && ix.ma > 1) {
-                const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
-                for (int j = 0; j < ix.ma; ++j) {
-                    uint32_t h = hs[j];
-                    if (h != kNoCell && h != c) {
-                        uint32_t rh = crank[h];
-                        if (rh != kNoCell && rh < (uint32_t)r) {
-                            ok = false;
-                            break;
+        group_sums_range(codes, ng, g, act, s_lut, p0, p1, acc);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_part[warp][lane][i] = acc[i];
+        __syncthreads();
+        // thread t: member 8 * (g0 + t / 8) + t % 8 of this chunk
+        {
+            const int gl = threadIdx.x >> 3, bb = threadIdx.x & 7;
+            const int pos = 8 * (g0 + gl) + bb;
+            if (pos < nc) {
+                uint32_t tot = 0;
+#pragma unroll
+                for (int w = 0; w < nwarps; ++w) tot += s_part[w][gl][bb >> 1];
+                const uint32_t sum = (tot >> (16 * (bb & 1))) & 0xFFFFu;
+                const uint32_t d = ix.maxk - sum;
+                const uint32_t slot = __ldg(ix.cell_slots + moff + pos);
+                bool ok = true;
+                if (filtering) {
+                    const uint32_t tg = __ldg(ix.tags + slot);
+                    ok = tg >= flo && tg <= fhi;
+                }
+                if (ok && ix.ma > 1) {
+                    const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
+                    for (int j = 0; j < ix.ma; ++j) {
+                        const uint32_t h = __ldg(hs + j);
+                        if (h != kNoCell && h != c) {
+                            const uint32_t rh = __ldg(crank + h);
+                            if (rh != kNoCell && rh < (uint32_t)r) {
+                                ok = false;
+                                break;
+                            }
                         }
                     }
                 }
+                out[pos] = ok ? (((uint64_t)d << 32) | slot) : kInvalidEntry;
             }
-            out[pos] = ok ? (((uint64_t)d << 32) | slot) : kInvalidEntry;
         }
+        __syncthreads();  // s_part is rewritten by the next chunk
     }
 }
 
@@ -1824,16 +1890,32 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long kept = s_kept + s_add;
-            s_add = 0;
-            uint32_t t = s_tau;
-            while (t > 0 && kept - hist[t] >= (unsigned long long)target) {
-                kept -= hist[t];
-                --t;
+        // the falling cut-off: the smallest bucket t (not above the current one) whose prefix count
+        // still reaches target, i.e. the sequential walk down from tau done as one warp scan
+        if (threadIdx.x < 32) {
+            const unsigned long long kept0 = s_kept + s_add;
+            const uint32_t t0 = s_tau;
+            uint32_t t = t0;
+            unsigned long long kept = kept0;
+            if (kept0 >= (unsigned long long)target && t0 > 0) {
+                const int cut = warp_hist_cut(hist, (int)t0, (long long)target);
+                unsigned long long below = 0;  // prefix(cut), summed by the warp
+                for (int i = threadIdx.x; i <= cut; i += 32) below += hist[i];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) below += __shfl_xor_sync(0xFFFFFFFFu, below, o);
+                t = (uint32_t)cut;
+                kept = below;
             }
-            s_kept = kept;
-            s_tau = t;
+            if (threadIdx.x == 0) {
+                s_add = 0;
+                s_kept = kept;
+                s_tau = t;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned long long kept = s_kept;
+            const uint32_t t = s_tau;
             if (adaptive && kept >= (unsigned long long)target) {
                 uint32_t wsub = ((t + 1) << 6) - 1;
                 uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
@@ -2559,13 +2641,13 @@ void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& 
                    cudaStream_t st) {
     if (nq <= 0) return;
     Tick tk(kKEncode, st);
-    const int blocks = (nq + kBS / 32 - 1) / (kBS / 32);
     const int wc = want_cqs ? 1 : 0, wr = want_rqs ? 1 : 0;
     switch (ix.dim_pad) {
-        case 128: k_encode_warp<4><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
-        case 256: k_encode_warp<8><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
-        case 512: k_encode_warp<16><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
-        case 1024: k_encode_warp<32><<<blocks, kBS, 0, st>>>(ix, Q, e, nq, wc, wr); return;
+        case 64: k_encode4<2><<<nq, 128, 0, st>>>(ix, Q, e, wc, wr); return;
+        case 128: k_encode4<4><<<nq, 128, 0, st>>>(ix, Q, e, wc, wr); return;
+        case 256: k_encode4<8><<<nq, 128, 0, st>>>(ix, Q, e, wc, wr); return;
+        case 512: k_encode4<16><<<nq, 128, 0, st>>>(ix, Q, e, wc, wr); return;
+        case 1024: k_encode4<32><<<nq, 128, 0, st>>>(ix, Q, e, wc, wr); return;
         default: break;
     }
     size_t smem = (size_t)(ix.dim_pad + ix.npos) * sizeof(float);
