@@ -173,6 +173,10 @@ int maivs_profile_read(int reset, const char** names, double* values, size_t cap
  * and the work counters of the last search ("nq", "probes", "candidates", "rerank_bytes",
  * "scan_code_bytes", "scan_pairs", ...; names '\n'-separated in `names`). */
 int maivs_kernel_clock(maivs_index* ix, int on);
+/* Times only the named kernel ("k_rerank", "k_seed", ... as maivs_kernel_times names them), so
+ * that the events of the clock do not sit between every pair of kernels; NULL or "" times all.
+ * Turns the clock on. MAIVS_BAD_ARG for an unknown name. */
+int maivs_kernel_clock_only(maivs_index* ix, const char* kernel);
 int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* ms, uint64_t* launches, size_t cap,
                        size_t* n_out);
 uint64_t maivs_launch_count(void);

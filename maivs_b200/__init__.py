@@ -263,9 +263,13 @@ class FlatCellIndex:
         return int(f.value)
 
     # ---- instrumentation ----
-    def kernel_clock(self, on: bool) -> None:
-        """Time every kernel of subsequent searches with CUDA events on their launch stream."""
-        self._check(_lib.lib().maivs_kernel_clock(self._h, int(bool(on))))
+    def kernel_clock(self, on: bool, only: str | None = None) -> None:
+        """Time every kernel of subsequent searches (or only the kernel named `only`) with CUDA
+        events on their launch stream."""
+        if on and only:
+            self._check(_lib.lib().maivs_kernel_clock_only(self._h, only.encode()))
+        else:
+            self._check(_lib.lib().maivs_kernel_clock(self._h, int(bool(on))))
 
     def kernel_times(self, reset: bool = False) -> dict:
         """{kernel name: (total ms, launches)} accumulated while the clock was on."""

@@ -58,6 +58,7 @@ _SIGS = {
     "maivs_array": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t),
                               C.POINTER(C.c_size_t)]),
     "maivs_kernel_clock": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_kernel_clock_only": (C.c_int, [C.c_void_p, C.c_char_p]),
     "maivs_kernel_times": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
                                      C.POINTER(C.c_uint64), C.c_size_t, C.POINTER(C.c_size_t)]),
     "maivs_launch_count": (C.c_uint64, []),

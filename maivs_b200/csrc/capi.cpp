@@ -626,6 +626,22 @@ int maivs_kernel_clock(maivs_index* ix, int on) {
     int rc = ensure_device(ix);
     if (rc != MAIVS_OK) return rc;
     ix->d->enable_kernel_clock(on != 0);
+    if (on) ix->d->kernel_clock()->only = -1;
+    return MAIVS_OK;
+}
+
+int maivs_kernel_clock_only(maivs_index* ix, const char* kernel) {
+    LOCK(ix);
+    int rc = ensure_device(ix);
+    if (rc != MAIVS_OK) return rc;
+    int id = -1;
+    if (kernel && *kernel) {
+        for (int i = 0; i < maivs::dev::kNumKernels; ++i)
+            if (std::strcmp(maivs::dev::kernel_name(i), kernel) == 0) id = i;
+        if (id < 0) return fail(ix, MAIVS_BAD_ARG, std::string("unknown kernel name: ") + kernel);
+    }
+    ix->d->enable_kernel_clock(true);
+    ix->d->kernel_clock()->only = id;
     return MAIVS_OK;
 }
 

@@ -94,15 +94,5 @@ __device__ __forceinline__ float fs_norm(int dim_pad) {
     return __fsqrt_rn(__fdiv_rn(__fmul_rn(2.0f, (float)dim_pad), 3.14159274101257324f));
 }
 
-// 16-entry u8 table lookup for 4 nibbles at once: `t` holds the table as 4 little-endian words,
-// `sel` the 4 indices in its low 16 bits (one per nibble). Returns the 4 looked-up bytes.
-__device__ __forceinline__ uint32_t lut16x4(uint4 t, uint32_t sel) {
-    uint32_t s3 = sel & 0x7777u;
-    uint32_t lo = __byte_perm(t.x, t.y, s3);
-    uint32_t hi = __byte_perm(t.z, t.w, s3);
-    uint32_t pick = ((sel >> 1) & 0x4444u) | 0x3210u;
-    return __byte_perm(lo, hi, pick);
-}
-
 }  // namespace dev
 }  // namespace maivs

@@ -2,6 +2,7 @@
 #include <omp.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "../host/hostmath.h"
@@ -98,6 +99,14 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
         max_members_ = std::max(max_members_, n);
         moff[c + 1] = moff[c] + (uint32_t)n;
         woff[c + 1] = woff[c] + (uint32_t)(npos * ((n + 7) / 8));
+    }
+    {
+        // seed scan blocks per query: the seed cells' groups of an average live cell, 128 a block,
+        // with room for larger cells
+        size_t live = 0;
+        for (size_t c = 0; c < M; ++c) live += moff[c + 1] > moff[c] ? 1 : 0;
+        const double groups = live ? (double)woff[M] / (double)std::max<size_t>(npos, 1) / (double)live : 1.0;
+        v.seed_parts = (int)std::min(16.0, std::max(1.0, std::ceil(1.15 * dev::kSeedCells * groups / 128.0)));
     }
     std::vector<uint32_t> slots(moff[M]), codes(woff[M], 0);
 #pragma omp parallel for schedule(dynamic, 16)
@@ -235,7 +244,7 @@ int DeviceIndex::ensure_ws(size_t bytes, std::string& err) {
 uint32_t DeviceIndex::read_flags(cudaStream_t st) {
     uint32_t f[4] = {0, 0, 0, 0};
     global_flags(st, f);
-    return f[0] + f[1];
+    return f[0] + f[1] + f[2];
 }
 
 int DeviceIndex::global_flags(cudaStream_t st, uint32_t out[4]) {
@@ -348,6 +357,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         b.probed = h.max_assign > 1 ? bp.take<uint64_t>((size_t)nq * mwords) : nullptr;
         b.seed_cap = seed_cap;
         b.seed_buf = bp.take<uint64_t>((size_t)nq * seed_cap);
+        b.seed_dcap = (int)(dev::kSeedCells * 8 * ((max_members_ + 7) / 8));
+        b.seed_d = bp.take<uint16_t>((size_t)nq * b.seed_dcap);
         b.seed_n = bp.take<uint32_t>(nq);
         b.tau = bp.take<uint32_t>(nq);
         b.rest_hi = bp.take<uint32_t>(nq);
@@ -413,7 +424,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     }
     if (timing_) cudaEventRecord(ev_[3], st);
     dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, d_nout, rsc, ritem,
-                       st);
+                       d_flags_ + 2, st);
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
     return kOk;
@@ -507,7 +518,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
         if (dbg && dbg->stage == 2) return debug_cands(b.cand, b.cand_n, nq, cand_cap, st);
         if (timing_ && q0 == 0) cudaEventRecord(ev_[3], st);
         dev::launch_rerank(view_, Qc, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids + (size_t)q0 * a.k,
-                           d_scores + (size_t)q0 * a.k, d_nout + q0, rsc, ritem, st);
+                           d_scores + (size_t)q0 * a.k, d_nout + q0, rsc, ritem, d_flags_ + 2, st);
     }
     if (timing_) cudaEventRecord(ev_[4], st);
     CUDA_TRY(cudaGetLastError());
@@ -621,6 +632,10 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
         if (hF[1] != 0) {
             err = "a routing shortlist exceeded 16384 cells; lower nprobe or the shortlist multiplier";
             return kUnsupported;
+        }
+        if (hF[2] != 0) {
+            err = "a bounded wait for the GPU's copy or tensor-core engines ran out; the results are not valid";
+            return kCudaError;
         }
         if (hF[0] == 0) break;
         if (attempt == 3) {

@@ -21,13 +21,56 @@ constexpr int kBS = 256;
 
 // ---- block utilities ----------------------------------------------------------------------------
 
+// prmt.b32 in its generic mode: byte i of the result is byte (sel nibble i) & 7 of {b, a}; every
+// selector here keeps bit 3 of its nibbles clear (copy, no sign replication).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// FastScan table lookups of one code word: nibble b of w (member b of the group) selects entry
+// nib of the 16-byte table t. r0 holds members 0-3 and r1 members 4-7, one byte each. The byte
+// selectors of both halves come from one mask and one shift of w.
+__device__ __forceinline__ void lut16x8(uint4 t, uint32_t w, uint32_t& r0, uint32_t& r1) {
+    const uint32_t s3 = w & 0x77777777u;                         // entry within the 8-byte half
+    const uint32_t pk = ((w >> 1) & 0x44444444u) | 0x32103210u;  // pick the half by bit 3
+    r0 = prmt(prmt(t.x, t.y, s3), prmt(t.z, t.w, s3), pk);
+    const uint32_t s3h = s3 >> 16, pkh = pk >> 16;
+    r1 = prmt(prmt(t.x, t.y, s3h), prmt(t.z, t.w, s3h), pkh);
+}
+
+// Running sums of a group's 8 members without widening every byte: `all` adds the four looked-up
+// bytes as one 32-bit word (bytes 1 and 3 carry into their neighbours, modulo 2^32) and `odd`
+// adds bytes 1 and 3 widened to 16-bit halves. Because every member's total stays below 2^16
+// (255 x npos with npos <= 256), all - (odd << 8) is exactly bytes 0 and 2 widened, modulo 2^32.
+struct GroupAcc {
+    uint32_t all0 = 0, odd0 = 0, all1 = 0, odd1 = 0;
+    __device__ __forceinline__ void add(uint4 t, uint32_t w) {
+        uint32_t r0, r1;
+        lut16x8(t, w, r0, r1);
+        all0 += r0;
+        odd0 += prmt(r0, 0, 0x4341);
+        all1 += r1;
+        odd1 += prmt(r1, 0, 0x4341);
+    }
+    // acc[b >> 1] holds member b's sum in half (b & 1)
+    __device__ __forceinline__ void finish(uint32_t acc[4]) const {
+        const uint32_t e0 = all0 - (odd0 << 8), e1 = all1 - (odd1 << 8);  // members 0|2, 4|6
+        acc[0] = prmt(e0, odd0, 0x5410);
+        acc[1] = prmt(e0, odd0, 0x7632);
+        acc[2] = prmt(e1, odd1, 0x5410);
+        acc[3] = prmt(e1, odd1, 0x7632);
+    }
+};
+
 // Sum of each lane's 8 FastScan table sums of group g over npos positions. Word (j, g) of the
 // cell holds nibble j of members 8g..8g+7; `lut` is npos x 16 bytes (layout of
 // src/quantize.rs:303-311: entry e of position j at byte 16j + e). acc[b>>1] holds member b's
 // 16-bit sum in half (b & 1). Sums never exceed 255 * npos <= 65280.
 __device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, int ng, int g, bool active,
                                            const uint8_t* lut, int npos, uint32_t acc[4]) {
-    acc[0] = acc[1] = acc[2] = acc[3] = 0;
+    GroupAcc a;
     const uint4* T = reinterpret_cast<const uint4*>(lut);
     // npos is a multiple of 16; eight independent code-word loads are issued before their lookups
     for (int j0 = 0; j0 < npos; j0 += 8) {
@@ -35,22 +78,15 @@ __device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, i
 #pragma unroll
         for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint4 t = T[j0 + u];
-            const uint32_t r0 = lut16x4(t, w[u]);
-            const uint32_t r1 = lut16x4(t, w[u] >> 16);
-            acc[0] += __byte_perm(r0, 0, 0x4140);
-            acc[1] += __byte_perm(r0, 0, 0x4342);
-            acc[2] += __byte_perm(r1, 0, 0x4140);
-            acc[3] += __byte_perm(r1, 0, 0x4342);
-        }
+        for (int u = 0; u < 8; ++u) a.add(T[j0 + u], w[u]);
     }
+    a.finish(acc);
 }
 
 // group_sums over positions [p0, p1) only (the packed 16-bit partial sums of a position slice).
 __device__ __forceinline__ void group_sums_range(const uint32_t* __restrict__ codes, int ng, int g, bool active,
                                                  const uint8_t* lut, int p0, int p1, uint32_t acc[4]) {
-    acc[0] = acc[1] = acc[2] = acc[3] = 0;
+    GroupAcc a;
     const uint4* T = reinterpret_cast<const uint4*>(lut);
     int j0 = p0;
     for (; j0 + 8 <= p1; j0 += 8) {
@@ -58,26 +94,10 @@ __device__ __forceinline__ void group_sums_range(const uint32_t* __restrict__ co
 #pragma unroll
         for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint4 t = T[j0 + u];
-            const uint32_t r0 = lut16x4(t, w[u]);
-            const uint32_t r1 = lut16x4(t, w[u] >> 16);
-            acc[0] += __byte_perm(r0, 0, 0x4140);
-            acc[1] += __byte_perm(r0, 0, 0x4342);
-            acc[2] += __byte_perm(r1, 0, 0x4140);
-            acc[3] += __byte_perm(r1, 0, 0x4342);
-        }
+        for (int u = 0; u < 8; ++u) a.add(T[j0 + u], w[u]);
     }
-    for (; j0 < p1; ++j0) {
-        const uint32_t w = active ? __ldg(codes + (size_t)j0 * ng + g) : 0u;
-        const uint4 t = T[j0];
-        const uint32_t r0 = lut16x4(t, w);
-        const uint32_t r1 = lut16x4(t, w >> 16);
-        acc[0] += __byte_perm(r0, 0, 0x4140);
-        acc[1] += __byte_perm(r0, 0, 0x4342);
-        acc[2] += __byte_perm(r1, 0, 0x4140);
-        acc[3] += __byte_perm(r1, 0, 0x4342);
-    }
+    for (; j0 < p1; ++j0) a.add(T[j0], active ? __ldg(codes + (size_t)j0 * ng + g) : 0u);
+    a.finish(acc);
 }
 
 __device__ __forceinline__ uint32_t member_sum(const uint32_t acc[4], int b) {
@@ -100,6 +120,14 @@ __device__ __forceinline__ uint32_t warp_append(bool valid, uint32_t* counter) {
 
 // Exactly-once rule of the cell-major join: a multi-home vector is scored only at its lowest-id
 // probed home (index.rs:2036-2045).
+// A probed-bitmap word. A kernel that wrote the bitmap itself reads it through L2 (kFresh): the
+// read-only path may hold a line of it cached before the writes.
+template <bool kFresh = false>
+__device__ __forceinline__ uint64_t probed_word(const uint64_t* probed, uint32_t cell) {
+    return kFresh ? __ldcg(probed + (cell >> 6)) : __ldg(probed + (cell >> 6));
+}
+
+template <bool kFresh = false>
 __device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot, uint32_t c, const uint64_t* probed) {
     // branch-free over the homes so the loads of several members can be in flight together
     const uint32_t* h = ix.slot_cells + (size_t)slot * ix.ma;
@@ -107,7 +135,7 @@ __device__ __forceinline__ bool canonical_cm(const IndexView& ix, uint32_t slot,
     for (int j = 0; j < ix.ma; ++j) {
         const uint32_t hc = __ldg(h + j);
         const bool lower = hc != kNoCell && hc < c;
-        const uint64_t word = lower ? __ldg(probed + (hc >> 6)) : 0ull;
+        const uint64_t word = lower ? probed_word<kFresh>(probed, hc) : 0ull;
         ok = ok && !(lower && ((word >> (hc & 63)) & 1ull));
     }
     return ok;
@@ -120,8 +148,22 @@ __device__ __forceinline__ float byte_val(uint32_t w, int b, bool sgn) {
 }
 
 // canonical_cm for a member entry whose lower home is precomputed (IndexView::cell_lower).
+template <bool kFresh = false>
 __device__ __forceinline__ bool canonical_lower(uint32_t lower, const uint64_t* probed) {
-    return lower == kNoCell || !((__ldg(probed + (lower >> 6)) >> (lower & 63)) & 1ull);
+    return lower == kNoCell || !((probed_word<kFresh>(probed, lower) >> (lower & 63)) & 1ull);
+}
+
+// canonical_cm against a bitmap in shared memory.
+__device__ __forceinline__ bool canonical_cm_bits(const IndexView& ix, uint32_t slot, uint32_t c,
+                                                  const uint64_t* bits) {
+    const uint32_t* h = ix.slot_cells + (size_t)slot * ix.ma;
+    bool ok = true;
+    for (int j = 0; j < ix.ma; ++j) {
+        const uint32_t hc = __ldg(h + j);
+        const bool lower = hc != kNoCell && hc < c;
+        ok = ok && !(lower && ((bits[hc >> 6] >> (hc & 63)) & 1ull));
+    }
+    return ok;
 }
 
 // The kth smallest (1-based) of up to two key segments, by radix selection on bytes [lo_byte,
@@ -183,6 +225,98 @@ __device__ uint64_t block_select_kth(const uint64_t* a, int na, const uint64_t* 
     uint64_t r = s_prefix;
     __syncthreads();
     return r;
+}
+
+// Warp 0 (all its lanes): the bin of `hist` (256 counts) where the running count reaches rem
+// (1-based); *rem_out = rem less the counts of the bins before it. Nothing else is synchronised.
+__device__ __forceinline__ void hist_find_warp0(const uint32_t* hist, int rem, uint32_t* bin_out, int* rem_out) {
+    const int lane = threadIdx.x;
+    int local = 0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) local += (int)hist[lane * 8 + t];
+    int inc = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    const int excl = inc - local;
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, excl < rem && inc >= rem);
+    const int src = hit ? __ffs(hit) - 1 : 31;
+    if (lane == src) {
+        int r = rem - excl, bin = lane * 8 + 7;
+        for (int t = 0; t < 8; ++t) {
+            const int hv = (int)hist[lane * 8 + t];
+            if (hv >= r) {
+                bin = lane * 8 + t;
+                break;
+            }
+            r -= hv;
+        }
+        *bin_out = (uint32_t)bin;
+        *rem_out = r;
+    }
+}
+
+// The kth smallest (1-based, kth <= na + nb) distance d = key >> 32 of up to two key segments,
+// d < 2^16. Three passes over the keys: the block's smallest and largest d; a histogram of
+// (d - lo) >> s, s the fewest bits that fit the range in 256 bins; and a histogram of the low s
+// bits of the keys in the bin that holds the kth. Bins over the keys' own range spread the
+// shared-memory atomics (fixed byte digits would pile most distances onto a few bins). All
+// threads of the block call it; `hist` is 256 shared words.
+__device__ uint32_t block_select_d(const uint64_t* a, int na, const uint64_t* b, int nb, int kth, uint32_t* hist) {
+    __shared__ uint32_t s_lo, s_hi, s_bin;
+    __shared__ int s_rem;
+    const int n = na + nb;
+    uint32_t lo = 0xFFFFFFFFu, hi = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t d = (uint32_t)((i < na ? a[i] : b[i - na]) >> 32);
+        lo = min(lo, d);
+        hi = max(hi, d);
+    }
+    lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+    hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+    if (threadIdx.x == 0) {
+        s_lo = 0xFFFFFFFFu;
+        s_hi = 0;
+        s_rem = kth;
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(&s_lo, lo);
+        atomicMax(&s_hi, hi);
+    }
+    __syncthreads();
+    lo = s_lo;
+    const uint32_t range = s_hi - lo;
+    int sh = 0;
+    while ((range >> sh) > 255u) ++sh;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t d = (uint32_t)((i < na ? a[i] : b[i - na]) >> 32);
+        atomicAdd(&hist[(d - lo) >> sh], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) hist_find_warp0(hist, s_rem, &s_bin, &s_rem);
+    __syncthreads();
+    const uint32_t bin = s_bin;
+    if (sh == 0) {
+        __syncthreads();
+        return lo + bin;
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t mask = (1u << sh) - 1u;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t d = (uint32_t)((i < na ? a[i] : b[i - na]) >> 32) - lo;
+        if ((d >> sh) == bin) atomicAdd(&hist[d & mask], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) hist_find_warp0(hist, s_rem, &s_bin, &s_rem);
+    __syncthreads();
+    const uint32_t v = lo + (bin << sh) + s_bin;
+    __syncthreads();
+    return v;
 }
 
 // Bitonic sort, ascending, of P (power of two) 64-bit keys in shared memory.
@@ -1062,7 +1196,7 @@ __device__ void emit_smallest_d(const uint64_t* a, int na, const uint64_t* b, in
     __shared__ uint32_t s_cnt;
     const int n = na + nb;
     uint32_t dl = 0xFFFFFFFFu;
-    if (n > L) dl = (uint32_t)(block_select_kth(a, na, b, nb, L, 5, 4, hist) >> 32);
+    if (n > L) dl = block_select_d(a, na, b, nb, L, hist);
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (int base = 0; base < n; base += blockDim.x) {
@@ -1129,90 +1263,174 @@ __device__ uint32_t block_select_lists(const uint8_t* xall, size_t rank_bytes, i
     return v;
 }
 
-__global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
-                                              const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
-                                              int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
-                                              int keys_in_smem, uint16_t* xlist, uint32_t* xcnt, int xl) {
-    extern __shared__ __align__(16) uint8_t lut_s[];  // npos x 16 LUT bytes, then (optionally) the keys
-    __shared__ uint32_t hist[256];
-    __shared__ uint32_t s_n;
-    __shared__ int s_last;
-    const int q = blockIdx.x, npos = ix.npos;
-    const int n_ch = (int)nch[q];
-    const int ns = min(kSeedCells, n_ch);
-    const uint32_t* ch = chosen + (size_t)q * nprobe;
-    uint64_t* probed = b.probed + (size_t)q * b.mwords;
-    if (ix.ma > 1) {
-        for (int w = threadIdx.x; w < b.mwords; w += kBS) probed[w] = 0;
-        __syncthreads();
-        for (int i = threadIdx.x; i < n_ch; i += kBS) atomicOr((unsigned long long*)&probed[ch[i] >> 6], 1ull << (ch[i] & 63));
+// FastScan sums of every member of a query's seed cells (the first kSeedCells probes,
+// index.rs:2131-2148). The member groups of the seed cells are numbered consecutively, cell after
+// cell, and dealt to the query's gridDim.y blocks, one group of 8 members per thread, so warps
+// stay full whatever the cells' sizes. Member b of numbered group f gets its distance
+// maxk - sum at seed_d[8 f + b] (members past the end of their cell get a value nobody reads).
+constexpr int kSeedScanThreads = 128;
+// Seed keys k_seed keeps in shared memory (48 KB: four 256-thread CTAs per SM); a query whose seed
+// cells hold more members keeps them in its global seed buffer.
+constexpr int kSeedSmemKeys = 6144;
+// Probed-cell bitmaps up to this many words (M <= 65,536 cells) are built in shared memory.
+constexpr int kSeedSmemBitmapWords = 1024;
+
+// Group prefix of the query's seed cells in shared memory: g[r] = groups of the seed cells
+// before r, ng/woff/moff/nc of cell r. Warp 0 computes it; the caller synchronises.
+struct SeedCells {
+    int g[kSeedCells + 1];
+    int ng[kSeedCells], nc[kSeedCells];
+    uint32_t woff[kSeedCells], moff[kSeedCells], c[kSeedCells];
+};
+__device__ __forceinline__ void seed_cells_prefix(const IndexView& ix, const uint32_t* ch, int ns, SeedCells& sc) {
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    int ng = 0, nc = 0;
+    uint32_t c = 0, m0 = 0, woff = 0;
+    if (lane < ns) {
+        c = ch[lane];
+        m0 = ix.cell_moff[c];
+        nc = (int)(ix.cell_moff[c + 1] - m0);
+        ng = (nc + 7) >> 3;
+        woff = ix.cell_woff[c];
     }
+    int inc = ng;
+#pragma unroll
+    for (int o = 1; o < kSeedCells; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    if (lane < kSeedCells) {
+        sc.g[lane + 1] = inc;
+        sc.ng[lane] = ng;
+        sc.nc[lane] = nc;
+        sc.woff[lane] = woff;
+        sc.moff[lane] = m0;
+        sc.c[lane] = c;
+    }
+    if (lane == 0) sc.g[0] = 0;
+}
+// The seed cell holding numbered group f (cells without members hold none).
+__device__ __forceinline__ int seed_cell_of(const SeedCells& sc, int f) {
+    int r = 0;
+    while (r + 1 < kSeedCells && sc.g[r + 1] <= f) ++r;
+    return r;
+}
+
+__global__ void __launch_bounds__(kSeedScanThreads) k_seed_scan(IndexView ix, QueryEnc e,
+                                                                const uint32_t* __restrict__ chosen,
+                                                                const uint32_t* __restrict__ nch, int nprobe,
+                                                                CellMajorBufs b) {
+    extern __shared__ __align__(16) uint8_t lut_s[];  // npos x 16 LUT bytes
+    __shared__ SeedCells sc;
+    const int q = blockIdx.x, npos = ix.npos;
+    const int ns = min(kSeedCells, (int)nch[q]);
+    seed_cells_prefix(ix, chosen + (size_t)q * nprobe, ns, sc);
+    __syncthreads();
+    const int G = sc.g[kSeedCells];
+    const int first = blockIdx.y * kSeedScanThreads;
+    if (first >= G) return;
     {
         const uint4* src = reinterpret_cast<const uint4*>(e.lut + (size_t)q * npos * 16);
         uint4* dst = reinterpret_cast<uint4*>(lut_s);
-        for (int i = threadIdx.x; i < npos; i += kBS) dst[i] = src[i];
+        for (int i = threadIdx.x; i < npos; i += kSeedScanThreads) dst[i] = src[i];
     }
+    __syncthreads();
+    const uint32_t maxk = ix.maxk;
+    uint4* out = reinterpret_cast<uint4*>(b.seed_d + (size_t)q * b.seed_dcap);
+    for (int f = first + (int)threadIdx.x; f < G; f += (int)gridDim.y * kSeedScanThreads) {
+        const int r = seed_cell_of(sc, f);
+        uint32_t acc[4];
+        group_sums(ix.cell_codes + sc.woff[r], sc.ng[r], f - sc.g[r], true, lut_s, npos, acc);
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = (maxk - (acc[i] & 0xFFFFu)) | ((maxk - (acc[i] >> 16)) << 16);
+        out[f] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// The seed step of the cell-major join (index.rs:2131-2191), one CTA per query, after
+// k_seed_scan: keeps the canonical seed entries (the exactly-once rule against every probed cell),
+// selects the seed cut-off tau = the target-th smallest seed distance (ties kept), retains
+// d <= tau in the seed buffer and finds the adaptive end of the rest probes. The entries stay in
+// shared memory when the seed cells' members fit in `smem_keys` keys.
+__global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                              const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
+                                              int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
+                                              int smem_keys, int smem_bits, uint16_t* xlist, uint32_t* xcnt, int xl) {
+    extern __shared__ __align__(16) uint64_t key_s[];  // smem_keys keys, then (smem_bits) the bitmap
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_n;
+    __shared__ int s_last;
+    __shared__ SeedCells sc;
+    const int q = blockIdx.x;
+    const int n_ch = (int)nch[q];
+    const int ns = min(kSeedCells, n_ch);
+    const uint32_t* ch = chosen + (size_t)q * nprobe;
+    // the probed-cell bitmap of the exactly-once rule: built in shared memory when it fits and
+    // stored for the rest scan, else built in the global buffer and read back through L2
+    uint64_t* probed = b.probed + (size_t)q * b.mwords;
+    uint64_t* bits = smem_bits ? key_s + smem_keys : probed;
+    if (ix.ma > 1) {
+        for (int w = threadIdx.x; w < b.mwords; w += kBS) bits[w] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n_ch; i += kBS) atomicOr((unsigned long long*)&bits[ch[i] >> 6], 1ull << (ch[i] & 63));
+    }
+    seed_cells_prefix(ix, ch, ns, sc);
     if (threadIdx.x == 0) {
         s_n = 0;
         s_last = -1;
     }
     __syncthreads();
+    if (ix.ma > 1 && smem_bits)
+        for (int w = threadIdx.x; w < b.mwords; w += kBS) probed[w] = bits[w];
     uint64_t* sbuf = b.seed_buf + (size_t)q * b.seed_cap;
+    int members = 0;
+    for (int r = 0; r < ns; ++r) members += sc.nc[r];
     // all canonical seed entries go to `keys`: shared memory when they fit, else the global buffer
-    uint64_t* keys = keys_in_smem ? reinterpret_cast<uint64_t*>(lut_s + (size_t)npos * 16) : sbuf;
+    const bool keys_in_smem = members <= smem_keys;
+    uint64_t* keys = keys_in_smem ? key_s : sbuf;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
     const uint32_t maxk = ix.maxk;
-    // (cell, 32-group chunk) work items of the seed cells, spread over all warps
-    __shared__ int s_items[kSeedCells + 1];
-    if (threadIdx.x == 0) {
-        s_items[0] = 0;
-        for (int r = 0; r < ns; ++r) {
-            uint32_t c = ch[r];
-            int ng = (int)((ix.cell_moff[c + 1] - ix.cell_moff[c] + 7) >> 3);
-            s_items[r + 1] = s_items[r] + (ng + 31) / 32;
-        }
-    }
-    __syncthreads();
-    const int n_items = s_items[ns];
-    for (int it = warp; it < n_items; it += nwarps) {
-        int r = 0;
-        while (s_items[r + 1] <= it) ++r;
-        const int chk = it - s_items[r];
-        const uint32_t c = ch[r];
-        const uint32_t moff = ix.cell_moff[c];
-        const int nc = (int)(ix.cell_moff[c + 1] - moff);
-        const int ng = (nc + 7) >> 3;
-        const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
-        const int g = chk * 32 + lane;
-        const bool act = g < ng;
-        uint32_t acc[4];
-        group_sums(codes, ng, g, act, lut_s, npos, acc);
-        // all eight members' slots first, then their home checks, so the loads overlap
-        uint32_t slot[8];
-        bool valid[8];
+    const uint16_t* sd = b.seed_d + (size_t)q * b.seed_dcap;
+    const int nslots = 8 * sc.g[kSeedCells];
+    constexpr int U = 4;  // member entries per thread and round: their loads are issued together
+    for (int base = 0; base < nslots; base += kBS * U) {
+        uint32_t slot[U], d[U], lw[U];
+        int rr[U];
+        bool valid[U];
 #pragma unroll
-        for (int bb = 0; bb < 8; ++bb) {
-            const int pos = 8 * g + bb;
-            valid[bb] = act && pos < nc;
-            slot[bb] = valid[bb] ? __ldg(ix.cell_slots + moff + pos) : 0u;
-        }
-        if (ix.ma > 1 && ix.cell_lower) {
-            uint32_t lw[8];
-#pragma unroll
-            for (int bb = 0; bb < 8; ++bb) lw[bb] = valid[bb] ? __ldg(ix.cell_lower + moff + 8 * g + bb) : kNoCell;
-#pragma unroll
-            for (int bb = 0; bb < 8; ++bb)
-                if (valid[bb]) valid[bb] = canonical_lower(lw[bb], probed);
-        } else if (ix.ma > 1) {
-#pragma unroll
-            for (int bb = 0; bb < 8; ++bb)
-                if (valid[bb]) valid[bb] = canonical_cm(ix, slot[bb], c, probed);
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * kBS + (int)threadIdx.x;
+            valid[u] = false;
+            slot[u] = d[u] = 0;
+            lw[u] = kNoCell;
+            rr[u] = 0;
+            if (i < nslots) {
+                const int f = i >> 3, r = seed_cell_of(sc, f);
+                const int pos = 8 * (f - sc.g[r]) + (i & 7);
+                if (pos < sc.nc[r]) {
+                    const uint32_t m = sc.moff[r] + (uint32_t)pos;
+                    valid[u] = true;
+                    rr[u] = r;
+                    slot[u] = __ldg(ix.cell_slots + m);
+                    d[u] = sd[i];
+                    if (ix.ma > 1 && ix.cell_lower) lw[u] = __ldg(ix.cell_lower + m);
+                }
+            }
         }
 #pragma unroll
-        for (int bb = 0; bb < 8; ++bb) {
-            const uint32_t d = maxk - member_sum(acc, bb);
-            const uint32_t p = warp_append(valid[bb], &s_n);
-            if (valid[bb] && p < (uint32_t)b.seed_cap) keys[p] = ((uint64_t)d << 32) | slot[bb];
+        for (int u = 0; u < U; ++u) {
+            if (valid[u] && ix.ma > 1) {
+                if (smem_bits)
+                    valid[u] = ix.cell_lower ? lw[u] == kNoCell || !((bits[lw[u] >> 6] >> (lw[u] & 63)) & 1ull)
+                                             : canonical_cm_bits(ix, slot[u], sc.c[rr[u]], bits);
+                else
+                    valid[u] = ix.cell_lower ? canonical_lower<true>(lw[u], probed)
+                                             : canonical_cm<true>(ix, slot[u], sc.c[rr[u]], probed);
+            }
+            const uint32_t p = warp_append(valid[u], &s_n);
+            if (valid[u] && p < (uint32_t)b.seed_cap) keys[p] = ((uint64_t)d[u] << 32) | slot[u];
         }
     }
     __syncthreads();
@@ -1231,8 +1449,7 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     }
     uint32_t tau = maxk;
     if (n >= target) {
-        uint64_t kk = block_select_kth(keys, n, nullptr, 0, target, 5, 4, hist);
-        tau = (uint32_t)(kk >> 32);
+        tau = block_select_d(keys, n, nullptr, 0, target, hist);
     }
     // retain d <= tau (ties kept): warps append the survivors to the global seed buffer
     __shared__ uint32_t s_out;
@@ -1696,7 +1913,7 @@ __global__ void __launch_bounds__(kBS) k_final_cm(CellMajorBufs b, int target, c
     const int total = ns + nr;
     uint32_t D = 0xFFFFFFFFu;
     if (W == 0) {
-        if (total > target) D = (uint32_t)(block_select_kth(sb, ns, rb, nr, target, 5, 4, hist) >> 32);
+        if (total > target) D = block_select_d(sb, ns, rb, nr, target, hist);
     } else if (xall) {
         unsigned long long tg = 0;
         for (int r = 0; r < W; ++r) tg += shard_count(xall, rank_bytes, r, q);
@@ -2398,6 +2615,145 @@ __global__ void __launch_bounds__(256) k_rerank_gather(RowSrc src, const uint32_
     row_dots<kMode>(src, cand, cand_n, item_off, nq, cand_cap, score_out);
 }
 
+// ---- exact f32 rerank, streamed through shared memory --------------------------------------------
+// Each CTA walks a contiguous range of the flattened candidate items (k_rerank_items numbering,
+// 16 rows an item) in stages of two items (32 rows). Lanes 0-3 of every warp each move one row of
+// a stage with a bulk copy (cp.async.bulk, completion counted on the stage's mbarrier), so the
+// gather is issued by the copy engine as whole rows, kS stages in flight. Then 8 threads own a
+// row: thread c runs the chain of elements c, c + 8, c + 16, ... (the eight FMA chains of
+// row_dots, same order, the query's chain held in registers) and shuffles combine them as
+// ((c0 + c4) + (c2 + c6)) + ((c1 + c5) + (c3 + c7)). Every mbarrier wait is bounded: on a timeout
+// the CTA sets *err, waits (bounded) for the copies it has in flight and returns.
+constexpr int kStreamRows = 32;
+constexpr size_t kStreamSmemMax = 210 * 1024;
+
+__device__ __forceinline__ void bulk_row_copy(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            umma::smem_addr(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(umma::smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bar_arrive_expect(uint64_t* bar, uint32_t bytes) {
+    uint64_t state;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;\n"
+                 : "=l"(state)
+                 : "r"(umma::smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    (void)state;
+}
+
+// The query holding item `it`: the last q with item_off[q] <= it (queries without items are
+// skipped because the next one starts at the same offset).
+__device__ __forceinline__ int query_of_item(const uint32_t* item_off, int nq, uint32_t it) {
+    int lo = 0, hi = nq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (item_off[mid] <= it) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <int kS, int N8>
+__global__ void __launch_bounds__(256, 1) k_rerank_stream(RowSrc src, const uint32_t* __restrict__ cand,
+                                                          const uint32_t* __restrict__ cand_n,
+                                                          const uint32_t* __restrict__ item_off, int nq,
+                                                          int cand_cap, int rstride, float* __restrict__ score_out,
+                                                          uint32_t* err) {
+    extern __shared__ __align__(128) float rbuf[];
+    __shared__ __align__(8) uint64_t full[kS];
+    constexpr int R = 16;  // rows an item
+    constexpr int dim = N8 * 8;
+    constexpr uint32_t row_bytes = dim * 4;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t items = item_off[nq];
+    const uint32_t nst = (items + 1) >> 1;
+    const uint32_t s0 = (uint32_t)((unsigned long long)nst * blockIdx.x / gridDim.x);
+    const uint32_t s1 = (uint32_t)((unsigned long long)nst * (blockIdx.x + 1) / gridDim.x);
+    if (s0 >= s1) return;
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < kS; ++i) umma::bar_init(&full[i], 32);  // lanes 0-3 of the 8 warps
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const size_t stage_floats = (size_t)kStreamRows * rstride;
+    const int half = tid >> 7;  // this thread's item of a stage (its copy row and its compute row)
+    // monotone cursors over the queries: one for the copies (kS stages ahead), one for compute
+    int qm = query_of_item(item_off, nq, min(2 * s0 + half, items - 1));
+    int qc = qm;
+    auto advance = [&](int& q, uint32_t it) {
+        while (item_off[q + 1] <= it) ++q;
+    };
+    const bool issuer = lane < 4;
+    const int crow = warp * 4 + lane;  // the row an issuing lane copies
+    // the slot of this lane's row of stage `stg` (~0 where there is no row)
+    auto slot_for = [&](uint32_t stg) -> uint32_t {
+        const uint32_t it = 2 * stg + half;
+        if (!issuer || stg >= s1 || it >= items) return ~0u;
+        advance(qm, it);
+        const int q = qm;
+        const int r = (int)(it - item_off[q]) * R + (crow & (R - 1));
+        return r < (int)__ldg(cand_n + q) ? __ldg(cand + (size_t)q * cand_cap + r) : ~0u;
+    };
+    auto copy = [&](uint32_t stg, uint32_t sl) {
+        if (!issuer || stg >= s1) return;
+        const int b = (int)((stg - s0) % kS);
+        bar_arrive_expect(&full[b], sl != ~0u ? row_bytes : 0u);
+        if (sl != ~0u)
+            bulk_row_copy(rbuf + (size_t)b * stage_floats + (size_t)crow * rstride,
+                          src.rows_f32 + (size_t)sl * dim, row_bytes, &full[b]);
+    };
+    uint32_t issued = s0;  // stages [s0, issued) have their copies issued
+#pragma unroll
+    for (int i = 0; i < kS - 1; ++i) copy(s0 + i, slot_for(s0 + i));
+    issued = min(s1, s0 + kS - 1);
+    uint32_t pslot = slot_for(s0 + kS - 1);
+    const int row = tid >> 3, c = tid & 7;
+    float qreg[N8];  // this thread's chain of the current query: q[c + 8k]
+    int qcur = -1;
+    bool bad = false;
+    uint32_t st = s0;
+    for (; st < s1; ++st) {
+        copy(st + kS - 1, pslot);       // its slot was loaded during the previous stage
+        if (st + kS - 1 < s1) issued = st + kS;
+        pslot = slot_for(st + kS);      // in flight while this stage is summed
+        const int b = (int)((st - s0) % kS);
+        if (!umma::bar_wait(&full[b], ((st - s0) / kS) & 1u)) bad = true;
+        const uint32_t it = 2 * st + half;
+        bool valid = false;
+        int q = 0, r = 0;
+        if (!bad && it < items) {
+            advance(qc, it);
+            q = qc;
+            r = (int)(it - item_off[q]) * R + (row & (R - 1));
+            valid = r < (int)__ldg(cand_n + q);
+        }
+        if (valid && q != qcur) {
+            const float* qv = src.qsrc + (size_t)q * dim + c;
+#pragma unroll
+            for (int k = 0; k < N8; ++k) qreg[k] = __ldg(qv + 8 * k);
+            qcur = q;
+        }
+        float acc = 0.0f;
+        if (valid) {
+            const float* sr = rbuf + (size_t)b * stage_floats + (size_t)row * rstride + c;
+#pragma unroll
+            for (int k = 0; k < N8; ++k) acc = __fmaf_rn(qreg[k], sr[8 * k], acc);
+        }
+        float v = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 4));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+        if (valid && c == 0) score_out[(size_t)q * cand_cap + r] = v;
+        // every thread is done with this stage's buffer before the next copy into it
+        if (__syncthreads_or(bad)) break;
+    }
+    if (st < s1) {  // a wait ran out: report, then let the copies in flight land before leaving
+        if (tid == 0) atomicAdd(err, 1u);
+        for (uint32_t t = st + 1; t < issued; ++t) umma::bar_wait(&full[(t - s0) % kS], ((t - s0) / kS) & 1u);
+    }
+}
+
 // Centroid re-order scores of the routing shortlist (index.rs:1931-1977, :782-800): SQ8 rows with
 // the query's base, or f32 rows; the same exact dot as the rerank.
 template <int kMode>
@@ -2555,9 +2911,10 @@ std::atomic<unsigned long long> g_launches{0};
 struct Tick {
     cudaStream_t st;
     int id;
-    Tick(int i, cudaStream_t s) : st(s), id(i) {
+    bool timed;
+    Tick(int i, cudaStream_t s) : st(s), id(i), timed(t_clock && t_clock->wants(i)) {
         g_launches.fetch_add(1, std::memory_order_relaxed);
-        if (t_clock) t_clock->begin(id, st);
+        if (timed) t_clock->begin(id, st);
     }
     ~Tick() {
         cudaError_t e = cudaGetLastError();
@@ -2565,7 +2922,7 @@ struct Tick {
             t_launch_err = e;
             t_launch_err_kernel = id;
         }
-        if (t_clock) t_clock->end(st);
+        if (timed) t_clock->end(st);
     }
 };
 }  // namespace
@@ -2583,7 +2940,8 @@ const char* kernel_name(int id) {
                                              "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
                                              "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
-                                             "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma"};
+                                             "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma",
+                                             "k_seed_scan"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -2762,15 +3120,19 @@ void launch_seed(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t*
                  const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin, const CellMajorBufs& b,
                  uint16_t* xlist, uint32_t* xcnt, int xl, cudaStream_t st) {
     if (nq <= 0) return;
-    size_t lut_bytes = (size_t)ix.npos * 16;
-    const size_t key_bytes = (size_t)b.seed_cap * sizeof(uint64_t);
+    {
+        Tick tk(kKSeedScan, st);
+        k_seed_scan<<<dim3(nq, std::max(ix.seed_parts, 1)), kSeedScanThreads, (size_t)ix.npos * 16, st>>>(
+            ix, e, chosen, nch, nprobe, b);
+    }
     // a shard keeps its seed keys in the global buffer: k_seed_finish filters them after the exchange
-    const int keys_in_smem = !xlist && key_bytes <= 96 * 1024 ? 1 : 0;
-    const size_t smem = lut_bytes + (keys_in_smem ? key_bytes : 0);
+    const int smem_keys = xlist ? 0 : std::min(b.seed_cap, kSeedSmemKeys);
+    const int smem_bits = ix.ma > 1 && b.mwords <= kSeedSmemBitmapWords ? 1 : 0;
+    const size_t smem = ((size_t)smem_keys + (smem_bits ? (size_t)b.mwords : 0)) * sizeof(uint64_t);
     set_smem((const void*)k_seed, smem);
     Tick tk(kKSeed, st);
     k_seed<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b,
-                                  keys_in_smem, xlist, xcnt, xl);
+                                  smem_keys, smem_bits, xlist, xcnt, xl);
 }
 
 void launch_seed_finish(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
@@ -2856,7 +3218,7 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   float* score_scratch, uint32_t* item_scratch, cudaStream_t st) {
+                   float* score_scratch, uint32_t* item_scratch, uint32_t* err, cudaStream_t st) {
     if (nq <= 0) return;
     const int row_bytes = ix.rerank_mode == 0 ? ix.dim * 4 : ix.dim;
     if (row_bytes % 16 == 0 && score_scratch && item_scratch && k <= 4096) {
@@ -2875,8 +3237,30 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
             Tick tk(kKRerankItems, st);
             k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
         }
-        {
-            const RowSrc src{ix.dim, ix.rerank_mode == 1 ? e.rqs : Q, e.rbase, ix.vecs_f32, ix.rr_u8};
+        const RowSrc src{ix.dim, ix.rerank_mode == 1 ? e.rqs : Q, e.rbase, ix.vecs_f32, ix.rr_u8};
+        // f32 rows of 384 or 768 dimensions: the streamed kernel (the query chain in registers)
+        const int rstride = ix.dim + ((8 - ix.dim % 32) + 32) % 32;  // rows of a warp on distinct banks
+        const size_t stage_bytes = (size_t)kStreamRows * rstride * sizeof(float);
+        const void* sf = nullptr;
+        int stages = 0;
+        if (ix.rerank_mode == 0 && ix.dim == 384) {
+            sf = (const void*)k_rerank_stream<4, 48>;
+            stages = 4;
+        } else if (ix.rerank_mode == 0 && ix.dim == 768) {
+            sf = (const void*)k_rerank_stream<2, 96>;
+            stages = 2;
+        }
+        if (sf && (size_t)stages * stage_bytes <= kStreamSmemMax) {
+            const size_t ssm = (size_t)stages * stage_bytes;
+            set_smem(sf, ssm);
+            Tick tk(kKRerank, st);
+            if (ix.dim == 384)
+                k_rerank_stream<4, 48><<<sms, 256, ssm, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap, rstride,
+                                                              score_scratch, err);
+            else
+                k_rerank_stream<2, 96><<<sms, 256, ssm, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap, rstride,
+                                                              score_scratch, err);
+        } else {
             Tick tk(kKRerank, st);
             if (ix.rerank_mode == 0)
                 k_rerank_gather<0><<<grid, 256, smem, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap,

@@ -13,6 +13,7 @@ namespace dev {
 struct IndexView {
     int dim, dim_pad, nw, npos, M, ma;
     uint32_t maxk;  // 255 * npos, the largest FastScan table sum
+    int seed_parts;  // blocks per query of the seed scan (about the seed cells' groups / 128)
     // routing tables
     const uint64_t* cent_bits;  // M x nw
     const uint8_t* cent_sq8;    // M x dim (null when the SQ8 re-order is off)
@@ -57,7 +58,7 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kKScanMma, kNumKernels
+    kKScanMma, kKSeedScan, kNumKernels
 };
 const char* kernel_name(int id);
 struct KernelClock {
@@ -69,6 +70,8 @@ struct KernelClock {
     std::vector<cudaEvent_t> pool;
     double ms[kNumKernels] = {0};
     unsigned long long launches[kNumKernels] = {0};
+    int only = -1;  // >= 0: time only this kernel
+    bool wants(int id) const { return only < 0 || only == id; }
     ~KernelClock();
     cudaEvent_t take();
     void begin(int id, cudaStream_t st);
@@ -123,6 +126,8 @@ struct CellMajorBufs {
     int mwords;
     uint64_t* seed_buf;   // nq x seed_cap
     int seed_cap;
+    uint16_t* seed_d;     // nq x seed_dcap: FastScan distances of the seed cells' member groups
+    int seed_dcap;        // a multiple of 8, >= 8 x the seed cells' groups
     uint32_t* seed_n;     // nq
     uint32_t* tau;        // nq
     uint32_t* rest_hi;    // nq (rest range is [min(8, nch), rest_hi))
@@ -185,7 +190,7 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 // one-CTA-per-query kernel.
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
-                   float* score_scratch, uint32_t* item_scratch, cudaStream_t st);
+                   float* score_scratch, uint32_t* item_scratch, uint32_t* err, cudaStream_t st);
 
 }  // namespace dev
 }  // namespace maivs

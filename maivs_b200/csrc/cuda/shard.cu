@@ -232,6 +232,8 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         b.probed = h.max_assign > 1 ? bp.take<uint64_t>((size_t)nq * mwords) : nullptr;
         b.seed_cap = seed_cap;
         b.seed_buf = bp.take<uint64_t>((size_t)nq * seed_cap);
+        b.seed_dcap = (int)(dev::kSeedCells * 8 * ((max_members_ + 7) / 8));
+        b.seed_d = bp.take<uint16_t>((size_t)nq * b.seed_dcap);
         b.seed_n = bp.take<uint32_t>(nq);
         b.tau = bp.take<uint32_t>(nq);
         b.rest_hi = bp.take<uint32_t>(nq);
@@ -316,7 +318,7 @@ void DeviceIndex::shard_after_cut(const HostIndex&, ShardRun& r) {
     const size_t nk = (size_t)r.nq * r.k;
     dev::launch_rerank(view_, r.dQ, r.e, r.nq, r.b.cand, r.b.cand_n, r.b.cand_cap, r.k,
                        reinterpret_cast<uint64_t*>(r.tsend), reinterpret_cast<float*>(r.tsend + nk * 8),
-                       reinterpret_cast<uint32_t*>(r.tsend + nk * 12), r.rsc, r.ritem, r.st);
+                       reinterpret_cast<uint32_t*>(r.tsend + nk * 12), r.rsc, r.ritem, r.b.overflow + 2, r.st);
 }
 
 void DeviceIndex::shard_merge(ShardRun& r, uint64_t* d_ids, float* d_scores, uint32_t* d_nout) {

@@ -148,7 +148,7 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
     dev::launch_perquery(view_, e, nq, chosen, cscore, nch, nprobe, want0, h.adaptive, h.at_margin, filtering,
                          h.filter_lo, h.filter_hi, b, st);
     dev::launch_rerank(view_, dQ, e, nq, b.cand, b.cand_n, cand_cap, a.k, d_ids, d_scores, nout, rsc, ritem,
-                       st);
+                       d_flags_ + 2, st);
     int kid = -1;
     cudaError_t le = dev::take_launch_error(&kid);
     if (le != cudaSuccess) {

@@ -162,3 +162,41 @@ def test_odd_dims(dim, preset):
     ix = build_index(X, preset, rf=8)
     _compare(ix, Q, K, 12, cell_major=True)
     _compare(ix, Q[:12], K, 12, cell_major=False)
+
+
+@pytest.mark.parametrize("homes", [1, 2])
+def test_large_cells(data, homes):
+    """About 1,000 vectors a cell (2,000 member entries with two homes): the seed cells of a query
+    then hold more members than the seed step keeps in shared memory, so its entries go through
+    the global seed buffer; ragged last groups in every cell."""
+    X, Q = data
+    ix = build_index(X[:30_000], "quality", rf=8, n_cells=30, tree_min_cells=10**9, homes=homes)
+    for nprobe in (8, 12):
+        _compare(ix, Q[:120], K, nprobe)
+
+
+def test_kernel_clock_only_times_one_kernel(data, quality):
+    """The bench times only its dominant kernel inside the timed steps: no other kernel gets events."""
+    _, Q = data
+    quality.kernel_clock(True, only="k_rerank")
+    quality.kernel_times(reset=True)
+    quality.search_batch_arrays(Q[:64], K, 8, 1.0, 8.0, True)
+    kt = quality.kernel_times(reset=True)
+    quality.kernel_clock(True)
+    quality.search_batch_arrays(Q[:64], K, 8, 1.0, 8.0, True)
+    every = quality.kernel_times(reset=True)
+    quality.kernel_clock(False)
+    assert {k for k, v in kt.items() if v[0] > 0} == {"k_rerank"}
+    assert {"k_seed_scan", "k_seed", "k_rerank"} <= {k for k, v in every.items() if v[0] > 0}
+    with pytest.raises(ValueError, match="unknown kernel"):
+        quality.kernel_clock(True, only="k_nothing")
+
+
+def test_d768_quality_rerank():
+    """f32 rows of 768 dimensions: the streamed rerank's second instantiation."""
+    rng = np.random.default_rng(12)
+    X, c = mixture(rng, 12_000, 768, 100, sigma=0.3)
+    Q, _ = mixture(rng, 64, 768, 100, sigma=0.3, centers=c)
+    ix = build_index(X, "quality", rf=8)
+    _compare(ix, Q, K, 16, cell_major=True)
+    _compare(ix, Q[:16], K, 16, cell_major=False)
