@@ -73,10 +73,12 @@ __device__ __forceinline__ void group_sums(const uint32_t* __restrict__ codes, i
     GroupAcc a;
     const uint4* T = reinterpret_cast<const uint4*>(lut);
     // npos is a multiple of 16; eight independent code-word loads are issued before their lookups
+    uint32_t off = (uint32_t)g;
     for (int j0 = 0; j0 < npos; j0 += 8) {
         uint32_t w[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
+        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + off + (uint32_t)u * (uint32_t)ng) : 0u;
+        off += 8u * (uint32_t)ng;
 #pragma unroll
         for (int u = 0; u < 8; ++u) a.add(T[j0 + u], w[u]);
     }
@@ -89,14 +91,16 @@ __device__ __forceinline__ void group_sums_range(const uint32_t* __restrict__ co
     GroupAcc a;
     const uint4* T = reinterpret_cast<const uint4*>(lut);
     int j0 = p0;
+    uint32_t off = (uint32_t)p0 * (uint32_t)ng + (uint32_t)g;
     for (; j0 + 8 <= p1; j0 += 8) {
         uint32_t w[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + (size_t)(j0 + u) * ng + g) : 0u;
+        for (int u = 0; u < 8; ++u) w[u] = active ? __ldg(codes + off + (uint32_t)u * (uint32_t)ng) : 0u;
+        off += 8u * (uint32_t)ng;
 #pragma unroll
         for (int u = 0; u < 8; ++u) a.add(T[j0 + u], w[u]);
     }
-    for (; j0 < p1; ++j0) a.add(T[j0], active ? __ldg(codes + (size_t)j0 * ng + g) : 0u);
+    for (; j0 < p1; ++j0, off += (uint32_t)ng) a.add(T[j0], active ? __ldg(codes + off) : 0u);
     a.finish(acc);
 }
 
@@ -1357,7 +1361,8 @@ __global__ void __launch_bounds__(kSeedScanThreads) k_seed_scan(IndexView ix, Qu
 __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                               const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
                                               int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
-                                              int smem_keys, int smem_bits, uint16_t* xlist, uint32_t* xcnt, int xl) {
+                                              int smem_keys, int smem_bits, int final_cand, uint16_t* xlist,
+                                              uint32_t* xcnt, int xl) {
     extern __shared__ __align__(16) uint64_t key_s[];  // smem_keys keys, then (smem_bits) the bitmap
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_n;
@@ -1395,6 +1400,7 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     const uint16_t* sd = b.seed_d + (size_t)q * b.seed_dcap;
     const int nslots = 8 * sc.g[kSeedCells];
     constexpr int U = 4;  // member entries per thread and round: their loads are issued together
+    int rcur = 0;         // a thread's slots rise, so the seed cell of the last one is a start
     for (int base = 0; base < nslots; base += kBS * U) {
         uint32_t slot[U], d[U], lw[U];
         int rr[U];
@@ -1407,7 +1413,9 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
             lw[u] = kNoCell;
             rr[u] = 0;
             if (i < nslots) {
-                const int f = i >> 3, r = seed_cell_of(sc, f);
+                const int f = i >> 3;
+                while (rcur + 1 < kSeedCells && sc.g[rcur + 1] <= f) ++rcur;
+                const int r = rcur;
                 const int pos = 8 * (f - sc.g[r]) + (i & 7);
                 if (pos < sc.nc[r]) {
                     const uint32_t m = sc.moff[r] + (uint32_t)pos;
@@ -1451,8 +1459,11 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
     if (n >= target) {
         tau = block_select_d(keys, n, nullptr, 0, target, hist);
     }
-    // retain d <= tau (ties kept): warps append the survivors to the global seed buffer
+    // retain d <= tau (ties kept): warps append the survivors to the global seed buffer. With no
+    // probes beyond the seed cells (final_cand) the survivors are the exact cut already (the
+    // target-th smallest of all entries is tau) and their slots go straight to the candidate list.
     __shared__ uint32_t s_out;
+    uint32_t* cand = b.cand + (size_t)q * b.cand_cap;
     if (keys_in_smem) {
         if (threadIdx.x == 0) s_out = 0;
         __syncthreads();
@@ -1463,7 +1474,10 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
             const uint64_t key = i < i1 ? keys[i] : ~0ull;
             const bool keep = i < i1 && (uint32_t)(key >> 32) <= tau;
             const uint32_t p = warp_append(keep, &s_out);
-            if (keep) sbuf[p] = key;
+            if (keep) {
+                if (final_cand) cand[p] = (uint32_t)key;
+                else sbuf[p] = key;
+            }
         }
         __syncthreads();
         n = (int)s_out;
@@ -1480,12 +1494,27 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
             BS(scan).ExclusiveSum(f, pos, agg);
             __syncthreads();
             uint32_t off = s_out;
-            if (f) sbuf[off + pos] = key;
+            if (f) {
+                if (final_cand) cand[off + pos] = (uint32_t)key;
+                else sbuf[off + pos] = key;
+            }
             __syncthreads();
             if (threadIdx.x == 0) s_out = off + agg;
             __syncthreads();
         }
         n = (int)s_out;
+    } else if (final_cand) {
+        for (int i = threadIdx.x; i < n; i += kBS) cand[i] = (uint32_t)sbuf[i];
+    }
+    if (final_cand) {
+        if (threadIdx.x == 0) {
+            b.tau[q] = tau;
+            b.seed_n[q] = (uint32_t)n;
+            b.rest_hi[q] = (uint32_t)ns;
+            b.rest_n[q] = 0;
+            b.cand_n[q] = (uint32_t)n;
+        }
+        return;
     }
     int rest_end = n_ch;
     if (adaptive && n >= target && ns < n_ch) {
@@ -3131,8 +3160,9 @@ void launch_seed(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t*
     const size_t smem = ((size_t)smem_keys + (smem_bits ? (size_t)b.mwords : 0)) * sizeof(uint64_t);
     set_smem((const void*)k_seed, smem);
     Tick tk(kKSeed, st);
+    const int final_cand = !xlist && nprobe <= kSeedCells ? 1 : 0;
     k_seed<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b,
-                                  smem_keys, smem_bits, xlist, xcnt, xl);
+                                  smem_keys, smem_bits, final_cand, xlist, xcnt, xl);
 }
 
 void launch_seed_finish(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
@@ -3196,6 +3226,7 @@ void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint
                       const CellMajorBufs& b, cudaStream_t st) {
     if (nq <= 0) return;
     launch_seed(ix, e, nq, chosen, cscore, nch, nprobe, target, adaptive, at_margin, b, nullptr, nullptr, 0, st);
+    if (nprobe <= kSeedCells) return;  // k_seed wrote the candidates: no probes beyond the seed cells
     launch_rest_scan(ix, e, nq, chosen, nch, nprobe, b, st);
     launch_final(b, nq, target, nullptr, 0, 0, 0, st);
 }
