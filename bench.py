@@ -78,8 +78,9 @@ def recall(ids: np.ndarray, truth: np.ndarray) -> float:
 
 
 def build_quality(X: np.ndarray, threads: int):
-    os.environ["OMP_NUM_THREADS"] = str(threads)
     import maivs_b200 as M
+
+    M.set_num_threads(threads)  # torchrun exports OMP_NUM_THREADS=1
 
     n, d = X.shape
     ix = M.FlatCellIndex(d, "binary", 16, 0x5EED, 0)
@@ -97,8 +98,9 @@ def build_quality(X: np.ndarray, threads: int):
 
 def build_memory(X: np.ndarray, threads: int):
     """The reference's `memory` preset (bench/fair/fairbench.py:98-106): quality + per-dimension SQ8 rerank."""
-    os.environ["OMP_NUM_THREADS"] = str(threads)
     import maivs_b200 as M
+
+    M.set_num_threads(threads)
 
     n, d = X.shape
     ix = M.FlatCellIndex(d, "binary", 16, 0x5EED, 0)

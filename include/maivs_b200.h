@@ -180,6 +180,10 @@ int maivs_kernel_clock_only(maivs_index* ix, const char* kernel);
 int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* ms, uint64_t* launches, size_t cap,
                        size_t* n_out);
 uint64_t maivs_launch_count(void);
+/* Host threads of the index build and host-side search staging for the calling thread
+ * (omp_set_num_threads; no counterpart in the reference). Under launchers that export
+ * OMP_NUM_THREADS=1 (torchrun) this restores the build's parallelism. MAIVS_BAD_ARG for n < 1. */
+int maivs_set_num_threads(int n);
 int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, double* values, size_t cap,
                             size_t* n_out);
 

@@ -406,6 +406,12 @@ def shard_over_torch(ix: "FlatCellIndex", group=None) -> None:
     ix.shard(rank, world, obj[0])
 
 
+def set_num_threads(n: int) -> None:
+    """Host threads of the index build and of the host search's staging (calling thread)."""
+    if _lib.lib().maivs_set_num_threads(int(n)) != _lib.OK:
+        raise ValueError("the thread count must be at least 1")
+
+
 def launch_count() -> int:
     """Kernels this library has launched in this process."""
     return int(_lib.lib().maivs_launch_count())

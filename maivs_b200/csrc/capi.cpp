@@ -1,5 +1,6 @@
 // C ABI of the B200 MAIVS engine (declared in include/maivs_b200.h).
 #include <cuda_runtime.h>
+#include <omp.h>
 
 #include <algorithm>
 #include <atomic>
@@ -666,6 +667,12 @@ int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* m
 }
 
 uint64_t maivs_launch_count(void) { return maivs::dev::total_launches(); }
+
+int maivs_set_num_threads(int n) {
+    if (n < 1) return MAIVS_BAD_ARG;
+    omp_set_num_threads(n);
+    return MAIVS_OK;
+}
 
 int maivs_last_search_stats(maivs_index* ix, char* names, size_t names_cap, double* values, size_t cap,
                             size_t* n_out) {
