@@ -88,3 +88,12 @@ def test_profile_names_match_the_reference():
     names = [n for n, _ in M.profile_read(True)]
     for n in ("q.route", "q.scan", "q.rerank", "q.count", "b.compact"):  # src/prof.rs:35-42
         assert n in names
+
+
+def test_set_num_threads():
+    import maivs_b200 as M
+
+    M.set_num_threads(2)
+    with pytest.raises(ValueError):
+        M.set_num_threads(0)
+    M.set_num_threads(os.cpu_count() or 1)

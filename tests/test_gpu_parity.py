@@ -200,3 +200,13 @@ def test_d768_quality_rerank():
     ix = build_index(X, "quality", rf=8)
     _compare(ix, Q, K, 16, cell_major=True)
     _compare(ix, Q[:16], K, 16, cell_major=False)
+
+
+@pytest.mark.parametrize("k,rf", [(1, 1), (7, 3), (33, 5)])
+def test_ragged_candidate_counts(data, k, rf):
+    """Candidate lists that are not whole 16-row items (k x rf = 1, 21, 165) through the streamed
+    f32 rerank, with k above the warp top-k's 32 in the last case; batch at the cell-major floor."""
+    X, Q = data
+    ix = build_index(X[:20_000], "quality", rf=rf, tree_min_cells=64)
+    _compare(ix, Q[:32], k, 8)
+    _compare(ix, Q[:40], k, 24)
