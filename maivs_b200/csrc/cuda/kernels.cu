@@ -1273,9 +1273,9 @@ __device__ uint32_t block_select_lists(const uint8_t* xall, size_t rank_bytes, i
 // stay full whatever the cells' sizes. Member b of numbered group f gets its distance
 // maxk - sum at seed_d[8 f + b] (members past the end of their cell get a value nobody reads).
 constexpr int kSeedScanThreads = 128;
-// Seed keys k_seed keeps in shared memory (48 KB: four 256-thread CTAs per SM); a query whose seed
-// cells hold more members keeps them in its global seed buffer.
-constexpr int kSeedSmemKeys = 6144;
+// Seed keys k_seed keeps in shared memory (32 KB: five 256-thread CTAs per SM, the register
+// limit); a query whose seed cells hold more members keeps them in its global seed buffer.
+constexpr int kSeedSmemKeys = 4096;
 // Probed-cell bitmaps up to this many words (M <= 65,536 cells) are built in shared memory.
 constexpr int kSeedSmemBitmapWords = 1024;
 
@@ -2654,7 +2654,7 @@ __global__ void __launch_bounds__(256) k_rerank_gather(RowSrc src, const uint32_
 // ((c0 + c4) + (c2 + c6)) + ((c1 + c5) + (c3 + c7)). Every mbarrier wait is bounded: on a timeout
 // the CTA sets *err, waits (bounded) for the copies it has in flight and returns.
 constexpr int kStreamRows = 32;
-constexpr size_t kStreamSmemMax = 210 * 1024;
+constexpr size_t kStreamSmemMax = 222 * 1024;
 
 __device__ __forceinline__ void bulk_row_copy(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
     asm volatile(
@@ -2683,18 +2683,48 @@ __device__ __forceinline__ int query_of_item(const uint32_t* item_off, int nq, u
     return lo;
 }
 
+// Exclusive prefix over queries of ceil(cand_n / 16) into out[0..nq], out[nq] the total (the
+// numbering of k_rerank_items), computed by one 256-thread CTA.
+__device__ void block_items_prefix(const uint32_t* __restrict__ cand_n, int nq, uint32_t* out) {
+    using BS = cub::BlockScan<uint32_t, 256>;
+    __shared__ typename BS::TempStorage tmp;
+    __shared__ uint32_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < nq; base += 256) {
+        const int q = base + (int)threadIdx.x;
+        const uint32_t v = q < nq ? (__ldg(cand_n + q) + 15u) / 16u : 0u;
+        uint32_t ex, agg;
+        BS(tmp).ExclusiveSum(v, ex, agg);
+        const uint32_t c = carry;
+        if (q < nq) out[q] = c + ex;
+        __syncthreads();
+        if (threadIdx.x == 0) carry = c + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[nq] = carry;
+    __syncthreads();
+}
+
 template <int kS, int N8>
 __global__ void __launch_bounds__(256, 1) k_rerank_stream(RowSrc src, const uint32_t* __restrict__ cand,
                                                           const uint32_t* __restrict__ cand_n,
-                                                          const uint32_t* __restrict__ item_off, int nq,
-                                                          int cand_cap, int rstride, float* __restrict__ score_out,
-                                                          uint32_t* err) {
+                                                          const uint32_t* item_off_g, int nq, int cand_cap,
+                                                          int rstride, float* __restrict__ score_out, uint32_t* err) {
     extern __shared__ __align__(128) float rbuf[];
     __shared__ __align__(8) uint64_t full[kS];
     constexpr int R = 16;  // rows an item
     constexpr int dim = N8 * 8;
     constexpr uint32_t row_bytes = dim * 4;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t stage_floats = (size_t)kStreamRows * rstride;
+    // the item numbering: from k_rerank_items, or (item_off_g null) computed here after the stages
+    const uint32_t* item_off = item_off_g;
+    if (!item_off_g) {
+        uint32_t* s_io = reinterpret_cast<uint32_t*>(rbuf + (size_t)kS * stage_floats);
+        block_items_prefix(cand_n, nq, s_io);
+        item_off = s_io;
+    }
     const uint32_t items = item_off[nq];
     const uint32_t nst = (items + 1) >> 1;
     const uint32_t s0 = (uint32_t)((unsigned long long)nst * blockIdx.x / gridDim.x);
@@ -2706,7 +2736,6 @@ __global__ void __launch_bounds__(256, 1) k_rerank_stream(RowSrc src, const uint
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    const size_t stage_floats = (size_t)kStreamRows * rstride;
     const int half = tid >> 7;  // this thread's item of a stage (its copy row and its compute row)
     // monotone cursors over the queries: one for the copies (kS stages ahead), one for compute
     int qm = query_of_item(item_off, nq, min(2 * s0 + half, items - 1));
@@ -2804,7 +2833,7 @@ __global__ void __launch_bounds__(256) k_topk_warp(IndexView ix, const uint32_t*
                                                    uint64_t* ids, float* scores, uint32_t* out_n) {
     constexpr int T = 16;
     const int lane = threadIdx.x & 31;
-    const int q = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int q = blockIdx.x * (int)(blockDim.x >> 5) + (int)(threadIdx.x >> 5);
     if (q >= nq) return;  // warp-uniform
     const int n = (int)cand_n[q];
     const float* sp = sc_in + (size_t)q * cand_cap;
@@ -3264,10 +3293,6 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess || per_sm < 1)
             per_sm = 1;
         const int grid = sms * per_sm;
-        {
-            Tick tk(kKRerankItems, st);
-            k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
-        }
         const RowSrc src{ix.dim, ix.rerank_mode == 1 ? e.rqs : Q, e.rbase, ix.vecs_f32, ix.rr_u8};
         // f32 rows of 384 or 768 dimensions: the streamed kernel (the query chain in registers)
         const int rstride = ix.dim + ((8 - ix.dim % 32) + 32) % 32;  // rows of a warp on distinct banks
@@ -3281,15 +3306,23 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
             sf = (const void*)k_rerank_stream<2, 96>;
             stages = 2;
         }
+        // the item numbering goes into the stream kernel's shared memory when it fits beside the stages
+        const size_t items_bytes = ((size_t)nq + 1) * sizeof(uint32_t);
+        const bool local_items = sf && (size_t)stages * stage_bytes + items_bytes <= kStreamSmemMax;
+        if (!local_items) {
+            Tick tk(kKRerankItems, st);
+            k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
+        }
         if (sf && (size_t)stages * stage_bytes <= kStreamSmemMax) {
-            const size_t ssm = (size_t)stages * stage_bytes;
+            const size_t ssm = (size_t)stages * stage_bytes + (local_items ? items_bytes : 0);
+            const uint32_t* io = local_items ? nullptr : item_scratch;
             set_smem(sf, ssm);
             Tick tk(kKRerank, st);
             if (ix.dim == 384)
-                k_rerank_stream<4, 48><<<sms, 256, ssm, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap, rstride,
+                k_rerank_stream<4, 48><<<sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
                                                               score_scratch, err);
             else
-                k_rerank_stream<2, 96><<<sms, 256, ssm, st>>>(src, cand, cand_n, item_scratch, nq, cand_cap, rstride,
+                k_rerank_stream<2, 96><<<sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
                                                               score_scratch, err);
         } else {
             Tick tk(kKRerank, st);
@@ -3305,8 +3338,9 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
         }
         if (k <= 32) {
             Tick tk(kKTopk, st);
-            k_topk_warp<<<(nq + 7) / 8, 256, 0, st>>>(ix, cand, cand_n, score_scratch, nq, cand_cap, k, ids, scores,
-                                                      out_n);
+            // two queries (warps) a CTA: the CTAs spread over every SM even for small batches
+            k_topk_warp<<<(nq + 1) / 2, 64, 0, st>>>(ix, cand, cand_n, score_scratch, nq, cand_cap, k, ids, scores,
+                                                     out_n);
             return;
         }
         const int P = next_pow2(k + kRerankChunk);
