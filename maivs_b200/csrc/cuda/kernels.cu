@@ -467,6 +467,7 @@ __global__ void __launch_bounds__(128) k_encode4(IndexView ix, const float* __re
     __shared__ float s_mins[256];
     __shared__ float s_red[4];
     __shared__ uint32_t s_mask[32];
+    __shared__ float s_prod[2][32 * E];  // x[t] * min[t] of the two SQ8 bases
     const int q = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int dp = ix.dim_pad, dim = ix.dim, npos = ix.npos;
     const float* x = Q + (size_t)q * dim;
@@ -519,20 +520,29 @@ __global__ void __launch_bounds__(128) k_encode4(IndexView ix, const float* __re
             e.qbits[(size_t)q * ix.nw + lane] = w;
         }
     } else if (warp == 1 || warp == 2) {
-        // SQ8 pre-scales and the base sum(x * min) in dimension order (warp 1: centroid re-order,
-        // warp 2: rerank)
-        const bool want = warp == 1 ? want_cqs : want_rqs;
+        // SQ8 pre-scales x * step and the products x * min (warp 1: centroid re-order, warp 2:
+        // rerank); then lanes 0 and 1 of warp 1 fold the two bases sum(x * min) in dimension order,
+        // side by side on one instruction stream (the products are the same rounded values the
+        // fold would compute inline)
+        const int which = warp - 1;
+        const bool want = which == 0 ? want_cqs : want_rqs;
         if (want) {
-            const float* mn = warp == 1 ? ix.csq_min : ix.sq_min;
-            const float* stp = warp == 1 ? ix.csq_step : ix.sq_step;
-            float* dst = (warp == 1 ? e.cqs : e.rqs) + (size_t)q * dim;
-            for (int t = lane; t < dim; t += 32) dst[t] = __fmul_rn(__ldg(x + t), __ldg(stp + t));
-            if (lane == 0) {
-                float b = 0.0f;
-#pragma unroll 8
-                for (int t = 0; t < dim; ++t) b = __fadd_rn(b, __fmul_rn(__ldg(x + t), __ldg(mn + t)));
-                (warp == 1 ? e.cqbase : e.rbase)[q] = b;
+            const float* mn = which == 0 ? ix.csq_min : ix.sq_min;
+            const float* stp = which == 0 ? ix.csq_step : ix.sq_step;
+            float* dst = (which == 0 ? e.cqs : e.rqs) + (size_t)q * dim;
+            for (int t = lane; t < dim; t += 32) {
+                const float xv = __ldg(x + t);
+                dst[t] = __fmul_rn(xv, __ldg(stp + t));
+                s_prod[which][t] = __fmul_rn(xv, __ldg(mn + t));
             }
+        }
+        asm volatile("bar.sync 1, 64;" ::: "memory");  // warps 1 and 2
+        if (warp == 1 && lane < 2 && (lane == 0 ? want_cqs : want_rqs)) {
+            const float* pr = s_prod[lane];
+            float b = 0.0f;
+#pragma unroll 8
+            for (int t = 0; t < dim; ++t) b = __fadd_rn(b, pr[t]);
+            (lane == 0 ? e.cqbase : e.rbase)[q] = b;
         }
     }
     __syncthreads();
