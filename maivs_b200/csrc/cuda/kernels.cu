@@ -1277,11 +1277,7 @@ __device__ uint32_t block_select_lists(const uint8_t* xall, size_t rank_bytes, i
     return v;
 }
 
-// FastScan sums of every member of a query's seed cells (the first kSeedCells probes,
-// index.rs:2131-2148). The member groups of the seed cells are numbered consecutively, cell after
-// cell, and dealt to the query's gridDim.y blocks, one group of 8 members per thread, so warps
-// stay full whatever the cells' sizes. Member b of numbered group f gets its distance
-// maxk - sum at seed_d[8 f + b] (members past the end of their cell get a value nobody reads).
+// ---- cell-major: the seed step (index.rs:2126-2191) --------------------------------------------------
 constexpr int kSeedScanThreads = 128;
 // Seed keys k_seed keeps in shared memory (32 KB: five 256-thread CTAs per SM, the register
 // limit); a query whose seed cells hold more members keeps them in its global seed buffer.
@@ -1331,6 +1327,11 @@ __device__ __forceinline__ int seed_cell_of(const SeedCells& sc, int f) {
     return r;
 }
 
+// FastScan sums of every member of a query's seed cells (the first kSeedCells probes,
+// index.rs:2131-2148). The member groups of the seed cells are numbered consecutively, cell after
+// cell, and dealt to the query's gridDim.y blocks, one group of 8 members per thread, so warps
+// stay full whatever the cells' sizes. Member b of numbered group f gets its distance
+// maxk - sum at seed_d[8 f + b] (members past the end of their cell get a value nobody reads).
 __global__ void __launch_bounds__(kSeedScanThreads) k_seed_scan(IndexView ix, QueryEnc e,
                                                                 const uint32_t* __restrict__ chosen,
                                                                 const uint32_t* __restrict__ nch, int nprobe,
@@ -1364,10 +1365,13 @@ __global__ void __launch_bounds__(kSeedScanThreads) k_seed_scan(IndexView ix, Qu
 }
 
 // The seed step of the cell-major join (index.rs:2131-2191), one CTA per query, after
-// k_seed_scan: keeps the canonical seed entries (the exactly-once rule against every probed cell),
-// selects the seed cut-off tau = the target-th smallest seed distance (ties kept), retains
-// d <= tau in the seed buffer and finds the adaptive end of the rest probes. The entries stay in
-// shared memory when the seed cells' members fit in `smem_keys` keys.
+// k_seed_scan: keeps the canonical seed entries (the exactly-once rule against every probed cell,
+// whose bitmap it builds, in shared memory when smem_bits, and stores for the rest scan), selects
+// the seed cut-off tau = the target-th smallest seed distance (ties kept), retains d <= tau and
+// finds the adaptive end of the rest probes. The entries stay in shared memory when the seed
+// cells' members fit in `smem_keys` keys. With final_cand (no probe beyond the seed cells) the
+// survivors are already the exact cut of index.rs:2277-2306 and their slots become the candidate
+// list; a cell-range shard (xlist) publishes its smallest distances instead.
 __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                               const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
                                               int nprobe, int target, int adaptive, float at_margin, CellMajorBufs b,
