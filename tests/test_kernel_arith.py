@@ -118,3 +118,61 @@ def test_select_d_is_the_kth_smallest():
             d[: n // 2] = d[0]
         kth = int(rng.integers(1, n + 1))
         assert select_d(d, kth) == int(np.sort(d)[kth - 1])
+
+
+def test_rerank_stream_covers_every_candidate_once():
+    """k_rerank_stream's work split: items of 16 candidate rows numbered by an exclusive prefix
+    over the queries, stages of two items dealt to the CTAs in equal runs, thread t of a stage
+    copying row 4 (t >> 5) + (t & 31) (lanes 0-3) and summing row t >> 3, both in item t >> 7.
+    Every (query, candidate) pair is copied and summed exactly once, whatever the counts."""
+    rng = np.random.default_rng(11)
+    for trial in range(200):
+        nq = int(rng.integers(1, 60))
+        cand_n = rng.integers(0, 70, nq)
+        if trial % 4 == 0:
+            cand_n[rng.random(nq) < 0.5] = 0  # queries without candidates
+        grid = int(rng.integers(1, 40))
+        item_off = np.concatenate([[0], np.cumsum((cand_n + 15) // 16)])
+        items = int(item_off[-1])
+        nst = (items + 1) // 2
+        copied, summed = {}, {}
+        for b in range(grid):
+            s0, s1 = nst * b // grid, nst * (b + 1) // grid
+            for st in range(s0, s1):
+                for t in range(256):
+                    half = t >> 7
+                    it = 2 * st + half
+                    if it >= items:
+                        continue
+                    q = int(np.searchsorted(item_off, it, side="right") - 1)  # last q with item_off[q] <= it
+                    lane, warp = t & 31, t >> 5
+                    if lane < 4:
+                        crow = warp * 4 + lane
+                        assert crow >> 4 == half
+                        r = (it - int(item_off[q])) * 16 + (crow & 15)
+                        if r < cand_n[q]:
+                            copied[(q, r)] = copied.get((q, r), 0) + 1
+                    row = t >> 3
+                    assert row >> 4 == half
+                    if t & 7 == 0:  # the lane that stores the row's score
+                        r = (it - int(item_off[q])) * 16 + (row & 15)
+                        if r < cand_n[q]:
+                            summed[(q, r)] = summed.get((q, r), 0) + 1
+        want = {(q, r) for q in range(nq) for r in range(int(cand_n[q]))}
+        assert set(copied) == want and set(copied.values()) <= {1}
+        assert set(summed) == want and set(summed.values()) <= {1}
+
+
+def test_shuffle_tree_is_the_reference_hsum_order():
+    """k_rerank_stream closes a row's eight FMA chains (one per thread c of 8) with xor-shuffles
+    over 4, 2, 1; lane 0 ends with ((c0 + c4) + (c2 + c6)) + ((c1 + c5) + (c3 + c7)), the
+    reference's horizontal sum (index.rs:58-65), in f32 with the same roundings."""
+    rng = np.random.default_rng(5)
+    f32 = np.float32
+    for _ in range(2000):
+        c = (rng.standard_normal(8) * 10.0 ** rng.integers(-6, 6, 8)).astype(f32)
+        v = c.copy()
+        for off in (4, 2, 1):
+            v = np.array([f32(v[i]) + f32(v[i ^ off]) for i in range(8)], dtype=f32)
+        want = f32(f32(f32(c[0] + c[4]) + f32(c[2] + c[6])) + f32(f32(c[1] + c[5]) + f32(c[3] + c[7])))
+        assert v[0].tobytes() == want.tobytes()
