@@ -210,3 +210,18 @@ def test_ragged_candidate_counts(data, k, rf):
     ix = build_index(X[:20_000], "quality", rf=rf, tree_min_cells=64)
     _compare(ix, Q[:32], k, 8)
     _compare(ix, Q[:40], k, 24)
+
+
+def test_batch_above_the_stream_item_table():
+    """7,000 queries: the streamed rerank's item numbering (4 bytes a query) no longer fits beside
+    its 4 x 49 KB stages, so it comes from k_rerank_items; each query's result equals its row in
+    two 3,500-query batches, which number their items inside the rerank kernel."""
+    rng = np.random.default_rng(21)
+    X, c = mixture(rng, 20_000, 384, 200)
+    Q, _ = mixture(rng, 7_000, 384, 200, centers=c)
+    ix = build_index(X, "quality", rf=8, tree_min_cells=64)
+    ids, sc = ix.search_batch_arrays(Q, K, 8, 1.0, 8.0, True)
+    ids_a, sc_a = ix.search_batch_arrays(Q[:3500], K, 8, 1.0, 8.0, True)
+    ids_b, sc_b = ix.search_batch_arrays(Q[3500:], K, 8, 1.0, 8.0, True)
+    assert np.array_equal(ids, np.concatenate([ids_a, ids_b]))
+    assert np.array_equal(sc.view(np.uint32), np.concatenate([sc_a, sc_b]).view(np.uint32))
