@@ -246,7 +246,8 @@ def kernel_profile(ix, step, n, flush, dev):
     tot = max(sum(v[0] for v in kt.values()), 1e-9)
     shares = {k: round(v[0] / tot, 4) for k, v in kt.items() if v[1]}
     dom = max(kt.items(), key=lambda kv: kv[1][0])[0]
-    return shares, dom, round(tot / max(n, 1), 4)
+    per_step = {k: v[0] / max(n, 1) for k, v in kt.items() if v[1]}
+    return shares, dom, round(tot / max(n, 1), 4), per_step
 
 
 def dist_env():
@@ -256,25 +257,72 @@ def dist_env():
     return ws, rank, local
 
 
-def cpu_baseline(ix, Q, rf, np_, budget_s=12.0) -> dict:
-    """The oracle (reference CPU path port) on the host cores, on a bounded sample of the batch."""
+def oracle_index(X: np.ndarray, rf: int, threads: int):
+    """The oracle's own build of the `quality` preset (its restatement of the reference build,
+    independent of the product's host build) and its query path over it."""
     import oracle
 
-    ix.set_rerank_factor(rf)
-    o = oracle.OracleIndex.from_index(ix)
-    sample = Q[:250]
-    threads = os.cpu_count() or 1
-    o.search_batch(sample, K, np_, 1.0, 8.0, True, threads=threads)  # warm-up
-    done, t0 = 0, time.perf_counter()
-    best = float("inf")
-    while time.perf_counter() - t0 < budget_s or done == 0:
+    b = oracle.build_preset(X, "quality", rf, threads=threads)
+    return b.index()
+
+
+def time_cpu_batches(o, Q, rf, np_, threads, budget_s=None, steps=None, warmup=1):
+    """Full cell-major batches through the oracle on `threads` host threads: (mean s, best s, calls)."""
+    o.set_rerank_factor(rf)
+    for _ in range(max(warmup, 1)):
+        o.search_batch(Q, K, np_, 1.0, 8.0, True, threads=threads)
+    ts, t0 = [], time.perf_counter()
+    while (steps is not None and len(ts) < steps) or (steps is None and (time.perf_counter() - t0 < budget_s or not ts)):
         t = time.perf_counter()
-        o.search_batch(sample, K, np_, 1.0, 8.0, True, threads=threads)
-        best = min(best, time.perf_counter() - t)
-        done += 1
-    return {"value": round(sample.shape[0] / best, 1), "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{sample.shape[0]} of the 1000 IND queries per call, cell-major, same index and "
-                      f"(rf={rf}, nprobe={np_}); best of {done} calls"}
+        o.search_batch(Q, K, np_, 1.0, 8.0, True, threads=threads)
+        ts.append(time.perf_counter() - t)
+    return float(np.mean(ts)), float(np.min(ts)), len(ts)
+
+
+def cpu_baseline(o, Q, rf, np_, budget_s=12.0) -> dict:
+    """The reference's CPU path (the oracle port) on every host core, over the same full batch."""
+    threads = os.cpu_count() or 1
+    mean_s, best_s, calls = time_cpu_batches(o, Q, rf, np_, threads, budget_s=budget_s)
+    return {"value": round(Q.shape[0] / mean_s, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+            "best_of_calls": round(Q.shape[0] / best_s, 1),
+            "sample": f"the full batch of {Q.shape[0]} IND queries per call, cell-major, the oracle's own build of "
+                      f"the same vectors, (rf={rf}, nprobe={np_}); mean of {calls} calls (~{budget_s:.0f} s)"}
+
+
+# ---- matched-recall frontier (bench/fair/summarise.py:26-45 of the reference) -------------------
+
+TARGETS = (0.95, 0.98, 0.99, 0.995)
+SWEEP_RF = (16, 32, 48, 64, 96)
+SWEEP_NP = (8, 16, 32, 64, 128, 256, 512)
+
+
+def frontier(pts):
+    """Points not dominated in (recall up, qps up), ascending recall."""
+    s = sorted(pts, key=lambda p: (-p["recall"], -p["qps"]))
+    out, best = [], None
+    for p in s:
+        if best is None or p["qps"] > best:
+            out.append(p)
+            best = p["qps"]
+    return sorted(out, key=lambda p: p["recall"])
+
+
+def interp(front, t):
+    """QPS at recall t, log-interpolated along the frontier, never extrapolated (None if unreached)."""
+    import math
+
+    for a, b in zip(front, front[1:]):
+        if a["recall"] <= t <= b["recall"]:
+            f = (t - a["recall"]) / max(b["recall"] - a["recall"], 1e-12)
+            return round(math.exp(math.log(a["qps"]) + f * (math.log(b["qps"]) - math.log(a["qps"]))), 1)
+    if front and abs(front[-1]["recall"] - t) < 1e-9:
+        return front[-1]["qps"]
+    return None
+
+
+def matched(points):
+    f = frontier(points)
+    return {str(t): interp(f, t) for t in TARGETS}
 
 
 def run_maivs(args):
@@ -341,7 +389,7 @@ def run_maivs(args):
 
     # kernel shares from a separate pass; inside the timed region only the dominant kernel carries
     # CUDA events (its live duration is the roofline's denominator)
-    shares, dom_kernel, kernel_ms_per_step = kernel_profile(ix, step, min(args.steps, 100), flush, dev)
+    shares, dom_kernel, kernel_ms_per_step, kms_step = kernel_profile(ix, step, min(args.steps, 100), flush, dev)
     ix.kernel_clock(True, only=dom_kernel)
     ix.kernel_times(reset=True)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -389,15 +437,50 @@ def run_maivs(args):
     queries = args.nq * args.steps * ws
     qps = queries / (total_ms / 1e3)
     e2e_qps = queries / e2e_total
+    got_ids = d_ids.cpu().numpy().view(np.uint64).copy()
+    got_sc = d_sc.cpu().numpy().copy()
+
+    # the union of candidate rows the batch reranks (each row is needed once per batch), from the
+    # GPU path's own candidate lists
+    cand = ix.debug_stage(2, Q, K, np_, 1.0, 8.0, True, cand_cap=4096)
+    rows = np.concatenate([cand["cand"][i, :cand["cand_n"][i]] for i in range(args.nq)])
+    union_rows = int(np.unique(rows).size)
+
+    # recall sweep over (rf, nprobe) for in-distribution and shifted queries, device-resident
+    sweep = {"IND": [], "OOD": []}
+    if not args.no_sweep:
+        dqs = torch.from_numpy(Qs).to(dev)
+        for tag, qh, qd, tr in (("IND", Q, dq, truth), ("OOD", Qs, dqs, truth_s)):
+            for srf in SWEEP_RF:
+                for snp in SWEEP_NP:
+                    ix.set_rerank_factor(srf)
+                    rec_p = recall(ix.search_batch_arrays(qh, K, snp, 1.0, 8.0, True)[0], tr)
+                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                    ms = []
+                    for it in range(8):
+                        flush.zero_()
+                        ev[0].record(stream)
+                        ix.search_batch_device(qd.data_ptr(), args.nq, K, d_ids.data_ptr(), d_sc.data_ptr(), snp,
+                                               1.0, 8.0, True, stream.cuda_stream)
+                        ev[1].record(stream)
+                        ev[1].synchronize()
+                        if it >= 2:
+                            ms.append(ev[0].elapsed_time(ev[1]))
+                    ix.device_flags(stream.cuda_stream)
+                    sweep[tag].append({"rf": srf, "nprobe": snp, "recall": round(rec_p, 4),
+                                       "qps": round(args.nq / (float(np.mean(ms)) / 1e3), 1)})
+        ix.set_rerank_factor(rf)
 
     # roofline of the dominant kernel
     peaks = measured_peaks()
     name = dom_kernel
     kms, kl = ktimes.get(name, (0.0, 0))
     per_launch_ms = kms / max(kl, 1)
+    row_bytes = stats.get("rerank_row_bytes", 1536.0)
     if name == "k_rerank":
-        alg = stats.get("rerank_bytes", 0.0) + stats.get("candidates", 0.0) * 4
-        what = "candidate rows gathered for the exact rerank (rows x 4d bytes) + candidate slots"
+        alg = union_rows * row_bytes
+        what = (f"union of the batch's candidate rows x {row_bytes:.0f} B (each row once per batch); "
+                f"{union_rows} distinct of {int(stats.get('candidates', 0))} (query, candidate) pairs")
     elif name == "k_seed":
         alg = (stats.get("seed_code_bytes", 0.0) + stats.get("nq", 0.0) * (16 * 128 + 64)
                + stats.get("seed_kept", 0.0) * 8)
@@ -413,6 +496,20 @@ def run_maivs(args):
         what = "scan codes + rerank rows"
     achieved = alg / (per_launch_ms / 1e3) / 1e9 if per_launch_ms > 0 else 0.0
     traffic = ncu_traffic(name, stats)
+
+    # the scan: algorithmic code bytes (union of scanned cells, each once per batch) over the scan
+    # kernels' device time from the all-kernel pass
+    scan_k = [k for k in ("k_seed_scan", "k_scan_cm", "k_scan_mma") if k in kms_step]
+    scan_ms = sum(kms_step[k] for k in scan_k)
+    scan_bytes = stats.get("seed_code_bytes", 0.0) + stats.get("scan_code_bytes", 0.0)
+    scan_gbs = scan_bytes / (scan_ms / 1e3) / 1e9 if scan_ms > 0 else 0.0
+
+    # parity: the timed batch's ids and scores against the oracle's own build + search of the
+    # same vectors and queries
+    threads_cpu = os.cpu_count() or 1
+    o = oracle_index(X, rf, threads_cpu)
+    ref_ids, ref_sc, *_ = o.search_batch(Q, K, np_, 1.0, 8.0, True, threads=threads_cpu)
+    parity = bool(np.array_equal(got_ids, ref_ids) and np.array_equal(got_sc.view(np.uint32), ref_sc.view(np.uint32)))
 
     out = {
         "metric": METRIC,
@@ -443,14 +540,26 @@ def run_maivs(args):
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                      "algorithmic_bytes_per_launch": round(alg), "avg_launch_ms": round(per_launch_ms, 5),
                      "what": what, "peak_src": peaks["src"]},
+        "scan": {"kernels": scan_k, "bytes_per_step": round(scan_bytes), "ms_per_step": round(scan_ms, 5),
+                 "achieved": round(scan_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                 "frac": round(scan_gbs / peaks["hbm_gbs"], 4),
+                 "what": "1-bit codes of the union of the batch's scanned cells, 64 B per member entry, each cell "
+                         "once per batch, over the scan kernels' device time (all-kernel pass)"},
+        "parity": parity,
+        "parity_src": f"ids and f32 scores of the timed batch ({args.nq} queries) bit-identical to the oracle's "
+                      "own build and search of the same vectors",
+        "sweep": sweep,
+        "qps_at_recall": {t: matched(p) for t, p in sweep.items() if p},
+        "sweep_src": "device-resident batch QPS per (rf, nprobe), mean of 6 timed batches, L2 flushed; QPS at "
+                     "R@10 targets log-interpolated on the Pareto frontier (reference bench/fair/summarise.py)",
         "kernel_share": shares,
         "kernel_share_src": f"separate pass of {min(args.steps, 100)} steps with every kernel timed: "
                             f"{kernel_ms_per_step} ms of kernel time per step",
-        "work": {k: round(v, 1) for k, v in stats.items()},
+        "work": {**{k: round(v, 1) for k, v in stats.items()}, "rerank_union_rows": union_rows},
         "clocks": clk.summary(),
     }
     if rank == 0 and ws == 1:
-        out["cpu_baseline"] = cpu_baseline(ix, Q, rf, np_)
+        out["cpu_baseline"] = cpu_baseline(o, Q, rf, np_)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if dist:
@@ -571,7 +680,8 @@ def run_sharded(args):
     torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     # every rank runs the same number of profiled steps (they hold collectives)
-    shares, dom_kernel, kernel_ms_per_step = kernel_profile(ix, lambda: run(rf, np_), min(args.steps, 10), flush, dev)
+    shares, dom_kernel, kernel_ms_per_step, _ = kernel_profile(ix, lambda: run(rf, np_), min(args.steps, 10), flush,
+                                                               dev)
     ix.kernel_clock(True, only=dom_kernel)
     ix.kernel_times(reset=True)
     if ws > 1:
@@ -714,8 +824,9 @@ def run_lowbatch(args):
                             "device_p50_ms": round(float(np.percentile(dl, 50)), 4),
                             "device_p99_ms": round(float(np.percentile(dl, 99)), 4), "calls": calls,
                             "kernel_us_per_call": {k: round(v[0] * 1e3 / calls, 2) for k, v in kt.items() if v[1]}}
-    # the reference's single-thread latency (fairbench.py:61-67) on the oracle port
-    o = oracle.OracleIndex.from_index(ix)
+    # the reference's single-thread latency (fairbench.py:61-67) on the oracle port, over the
+    # oracle's own build of the same vectors
+    o = oracle.build_preset(X, "memory", rf, threads=threads).index()
     cl = []
     for i in range(min(calls, 200)):
         t = time.perf_counter()
@@ -728,45 +839,40 @@ def run_lowbatch(args):
 
 
 def run_reference(args):
+    """The reference's CPU path (the oracle: a C++ restatement of the reference's Rust build and
+    query path; the reference itself cannot be built here) on every host core. The index is the
+    oracle's own build; nothing of the product is loaded. Each step is one full cell-major batch
+    of the same queries at the same operating point as the GPU arm."""
     ws, rank, local = dist_env()
     if rank != 0:
         return
-    import oracle
-
-    X, Q, _ = mixture(args.seed, args.n, args.nq, 384, 1000, 0.35)
+    X, Q, Qs = mixture(args.seed, args.n, args.nq, 384, 1000, 0.35)
     threads = os.cpu_count() or 1
-    ix = build_quality(X, threads)
+    t0 = time.perf_counter()
+    o = oracle_index(X, RF_GRID[0], threads)
+    build_s = time.perf_counter() - t0
     truth = brute_force_topk(X, Q, K, "cpu")
-    cache = {}
 
-    def search(rf, np_):
-        if rf not in cache:
-            ix.set_rerank_factor(rf)
-            cache.clear()
-            cache[rf] = oracle.OracleIndex.from_index(ix)
-        ids, *_ = cache[rf].search_batch(Q, K, np_, 1.0, 8.0, True, threads=threads)
+    def search(rf, np_, q=Q):
+        o.set_rerank_factor(rf)
+        ids, *_ = o.search_batch(q, K, np_, 1.0, 8.0, True, threads=threads)
         return ids
 
     rf, np_, rec = operating_point(search, truth)
-    ix.set_rerank_factor(rf)
-    o = oracle.OracleIndex.from_index(ix)
-    sample = Q[:250]
-    for _ in range(max(args.warmup, 1)):
-        o.search_batch(sample, K, np_, 1.0, 8.0, True, threads=threads)
-    t = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        o.search_batch(sample, K, np_, 1.0, 8.0, True, threads=threads)
-        t.append(time.perf_counter() - t0)
-    total = float(sum(t))
-    qps = sample.shape[0] * args.steps / total
-    desc = f"{sample.shape[0]} of the 1000 IND queries per step, cell-major, (rf={rf}, nprobe={np_})"
+    mean_s, best_s, steps = time_cpu_batches(o, Q, rf, np_, threads, steps=args.steps, warmup=args.warmup)
+    qps = args.nq / mean_s
+    desc = (f"the full batch of {args.nq} IND queries per step, cell-major, (rf={rf}, nprobe={np_}), "
+            f"mean of {steps} steps")
     print(json.dumps({
         "metric": METRIC, "impl": "reference", "value": round(qps, 1), "unit": "queries/s", "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean_s * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": "BASELINE configs[1]: 500k x 384, quality preset, k=10", "rerank_factor": rf,
-                   "nprobe": np_, "recall_at_10": round(rec, 4), "n": args.n},
+        "config": {"workload": "BASELINE configs[1]: 500k x 384 Gaussian mixture (1000 comps, sigma 0.35), quality "
+                               "preset, cell-major batches of 1000 queries, k=10",
+                   "n": args.n, "dim": 384, "nq_per_step": args.nq, "k": K, "rerank_factor": rf, "nprobe": np_,
+                   "recall_at_10": round(rec, 4), "build_s": round(build_s, 1),
+                   "index": "the oracle's own build (restated reference build), no product code"},
+        "best_step_qps": round(args.nq / best_s, 1),
         "cpu_baseline": {"value": round(qps, 1), "unit": "queries/s", "cores": threads, "kind": "port",
                          "sample": desc},
         "e2e": {"value": round(qps, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -784,6 +890,7 @@ def main():
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
     ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
+    ap.add_argument("--no-sweep", action="store_true", help="config2: skip the (rf, nprobe) recall sweep")
     ap.add_argument("--workload", choices=("config2", "sharded", "lowbatch"), default="config2",
                     help="config2: the headline 500k batch (replicas for N > 1); sharded: configs[3], 5.2M "
                          "vectors with cells sharded by range over the N GPUs; lowbatch: configs[2], memory "

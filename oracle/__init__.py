@@ -64,6 +64,7 @@ def lib() -> C.CDLL:
         L.oracle_index_new.argtypes = [C.POINTER(_Arrays)]
         L.oracle_index_free.argtypes = [vp]
         L.oracle_set_threads.argtypes = [C.c_int]
+        L.oracle_index_set_rerank_factor.argtypes = [vp, u64]
         L.oracle_search_batch.restype = C.c_int
         L.oracle_search_batch.argtypes = [vp, vp, u64, u64, u64, f32, f32, C.c_int, vp, vp, vp, u64, vp, vp]
         L.oracle_route.restype = C.c_int
@@ -85,6 +86,19 @@ def lib() -> C.CDLL:
         L.oracle_hamming_cutoff.argtypes = [vp, u64, u64, u64]
         L.oracle_keep_smallest.restype = u64
         L.oracle_keep_smallest.argtypes = [vp, vp, u64, u64, u64, vp]
+        L.oracle_build_new.restype = vp
+        L.oracle_build_new.argtypes = [u64, u64, u64, u64]
+        L.oracle_build_free.argtypes = [vp]
+        L.oracle_build_set.restype = C.c_int
+        L.oracle_build_set.argtypes = [vp, C.c_char_p, C.c_double, C.c_double, C.c_double, C.c_double]
+        L.oracle_build_train.restype = C.c_int
+        L.oracle_build_train.argtypes = [vp, vp, u64, u64, u64, u64]
+        L.oracle_build_add.restype = C.c_int
+        L.oracle_build_add.argtypes = [vp, vp, vp, u64]
+        L.oracle_build_compact.argtypes = [vp]
+        L.oracle_build_export.argtypes = [vp]
+        L.oracle_build_array.restype = C.c_int
+        L.oracle_build_array.argtypes = [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64), C.POINTER(u64)]
         _lib = L
     return _lib
 
@@ -132,12 +146,21 @@ class OracleIndex:
 
     @classmethod
     def from_index(cls, ix) -> "OracleIndex":
+        """Search the arrays of a product-built index (for stage-by-stage checks)."""
         return cls({n: ix.array(n) for n in cls.NAMES})
+
+    @classmethod
+    def from_build(cls, b: "OracleBuild") -> "OracleIndex":
+        """Search an index the oracle built itself from the raw vectors (independent of the product)."""
+        return cls({n: b.array(n) for n in cls.NAMES})
 
     def __del__(self):
         if getattr(self, "h", None):
             lib().oracle_index_free(self.h)
             self.h = None
+
+    def set_rerank_factor(self, rf: int) -> None:
+        lib().oracle_index_set_rerank_factor(self.h, int(rf))
 
     def search_batch(self, Q: np.ndarray, k: int, nprobe: int = 16, tc: float = 0.95, beta: float = 8.0,
                      cell_major: bool = True, cand_cap: int = 0, threads: int | None = None):
@@ -250,3 +273,142 @@ def keep_smallest(h: np.ndarray, ids: np.ndarray, keep: int, bits: int) -> np.nd
     out = np.empty(max(h.size, 1), np.uint32)
     n = lib().oracle_keep_smallest(h.ctypes.data, ids.ctypes.data, h.size, keep, bits, out.ctypes.data)
     return out[:n]
+
+
+# ---- the reference's index build, restated (independent of the product's host build) -----------
+
+_ARRAY_DTYPES = {
+    "vecs_f32": np.float32, "scan_i8": np.int8, "ext_ids": np.uint64, "slot_cell": np.uint32,
+    "slot_cells": np.uint32, "cell_members": np.uint32, "cell_member_off": np.uint32, "centroids": np.float32,
+    "r_bound": np.float32, "prim_len": np.uint32, "rep_off": np.uint32, "fs_codes": np.uint8, "fs_off": np.uint32,
+    "cent_bits": np.uint64, "cent_sq8": np.uint8, "csq_min": np.float32, "csq_step": np.float32,
+    "sq_min": np.float32, "sq_step": np.float32, "signs": np.float32, "tags": np.uint32,
+    "tree_level_n": np.uint64, "tree_codes": np.uint64, "tree_code_off": np.uint64, "tree_child_start": np.uint64,
+    "tree_child_len": np.uint64, "tree_child_off": np.uint64, "tree_leaf_codes": np.uint64,
+    "tree_leaf_ids": np.uint32, "config": np.float64,
+}
+
+
+class OracleBuild:
+    """FlatCellIndex's build path (train_centroids, add_batch, compact and the derived routing
+    state) restated from the reference (index.rs:684-1112, :2442-2667, :2761-2804, :2987-3212;
+    tree.rs:160-540). Method names and arguments follow the reference's pymethods, so a preset
+    reads the same on either side. Only the binary scan mode is restated."""
+
+    def __init__(self, dim: int, scan_mode: str = "binary", rerank_factor: int = 4, seed: int = 0x5EED,
+                 code_bits: int = 0):
+        if scan_mode != "binary":
+            raise ValueError("the oracle restates the binary scan mode only")
+        self.dim = int(dim)
+        self.h = lib().oracle_build_new(self.dim, int(code_bits), int(seed), int(rerank_factor))
+        self._exported = False
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().oracle_build_free(self.h)
+            self.h = None
+
+    def _set(self, key: str, a=0.0, b=0.0, c=0.0, d=0.0):
+        if lib().oracle_build_set(self.h, key.encode(), float(a), float(b), float(c), float(d)) != 0:
+            raise ValueError(key)
+        self._exported = False
+
+    def set_two_stage(self, on: bool, mult: int) -> None:
+        self._set("two_stage", on, mult)
+
+    def set_tree_route(self, on: bool, min_cells: int = 0, fanout: int = 0, beam_frac: float = 0.0) -> None:
+        self._set("tree_route", on, min_cells, fanout, beam_frac)
+
+    def set_graph_route(self, on: bool, min_cells: int = 0) -> None:
+        self._set("graph_route", on, min_cells)
+
+    def set_orthogonal_polysemy(self, homes: int = 2, lam: float = 1.0) -> None:
+        self._set("orthogonal_polysemy", homes, lam)
+
+    def set_replication(self, max_assign: int, spill_margin: float) -> None:
+        self._set("replication", max_assign, spill_margin)
+
+    def set_fastscan(self, on: bool) -> None:
+        self._set("fastscan", on)
+
+    def set_per_dim_sq(self, on: bool) -> None:
+        self._set("per_dim_sq", on)
+
+    def set_i8_rerank(self, on: bool) -> None:
+        self._set("i8_rerank", on)
+
+    def set_adaptive(self, on: bool, margin: float) -> None:
+        self._set("adaptive", on, margin)
+
+    def set_centroid_sq8(self, on: bool) -> None:
+        self._set("centroid_sq8", on)
+
+    def set_rerank_factor(self, rf: int) -> None:
+        self._set("rerank_factor", rf)
+
+    def set_cell_major_min_batch(self, n: int) -> None:
+        self._set("cm_min_batch", n)
+
+    def train_centroids(self, vectors: np.ndarray, n_cells: int, sample: int = 262_144, seed: int = 0x5EED) -> None:
+        X = np.ascontiguousarray(vectors, dtype=np.float32)
+        if X.ndim != 2 or X.shape[1] != self.dim:
+            raise ValueError("dim mismatch")
+        if lib().oracle_build_train(self.h, X.ctypes.data, X.shape[0], int(n_cells), int(sample), int(seed)) != 0:
+            raise ValueError("no training vectors")
+        self._exported = False
+
+    def add_batch(self, ids, vectors: np.ndarray) -> None:
+        X = np.ascontiguousarray(vectors, dtype=np.float32)
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.uint64))
+        if X.ndim != 2 or X.shape[1] != self.dim or ids.shape[0] != X.shape[0]:
+            raise ValueError("shape mismatch")
+        if lib().oracle_build_add(self.h, ids.ctypes.data, X.ctypes.data, X.shape[0]) != 0:
+            raise ValueError("call train_centroids() before add_batch()")
+        self._exported = False
+
+    def compact(self) -> None:
+        lib().oracle_build_compact(self.h)
+        self._exported = False
+
+    def array(self, name: str) -> np.ndarray:
+        """A copy of one index array, under FlatCellIndex.array()'s name and layout."""
+        if not self._exported:
+            lib().oracle_build_export(self.h)
+            self._exported = True
+        p, n, e = C.c_void_p(), C.c_uint64(), C.c_uint64()
+        if lib().oracle_build_array(self.h, name.encode(), C.byref(p), C.byref(n), C.byref(e)) != 0:
+            raise KeyError(name)
+        dt = np.dtype(_ARRAY_DTYPES[name])
+        if n.value == 0:
+            return np.empty(0, dt)
+        buf = (C.c_uint8 * (n.value * e.value)).from_address(p.value)
+        return np.frombuffer(buf, dtype=dt).copy()
+
+    def index(self) -> "OracleIndex":
+        return OracleIndex.from_build(self)
+
+
+def build_preset(X: np.ndarray, preset: str = "quality", rerank_factor: int = 16, ids=None,
+                 threads: int | None = None, n_cells: int | None = None) -> OracleBuild:
+    """The reference benchmark presets (bench/fair/fairbench.py:98-119) built by the oracle:
+    `quality` = two homes (orthogonal polysemy), FastScan, two-stage routing, tree routing from
+    2,048 cells with fanout 16, adaptive probing with margin 0.02, N/128 cells; `memory` adds the
+    per-dimension SQ8 rerank store."""
+    if threads is not None:
+        lib().oracle_set_threads(int(threads))
+    n, d = X.shape
+    b = OracleBuild(d, "binary", rerank_factor, 0x5EED, 0)
+    if preset == "memory":
+        b.set_per_dim_sq(True)
+    elif preset != "quality":
+        raise ValueError(preset)
+    b.set_orthogonal_polysemy(2, 1.0)
+    b.set_fastscan(True)
+    b.set_two_stage(True, 2)
+    b.set_graph_route(False, 10**9)
+    b.set_tree_route(True, 2048, 16)
+    b.set_adaptive(True, 0.02)
+    b.train_centroids(X, n_cells if n_cells is not None else max(16, n // 128))
+    b.add_batch(np.arange(n, dtype=np.uint64) if ids is None else ids, X)
+    b.compact()
+    return b

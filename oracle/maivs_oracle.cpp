@@ -27,6 +27,8 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <map>
+#include <string>
 #include <vector>
 
 namespace {
@@ -899,6 +901,783 @@ int search_cellmajor(const OIndex& ix, const float* data, size_t nq, size_t k, s
     return 0;
 }
 
+// ---- index build: an independent restatement of the reference's build path --------------------
+//
+// train_centroids (index.rs:2761-2804) -> hierarchical_kmeans / kmeans_spherical
+// (tree.rs:160-348); add_batch (index.rs:2987-3212) with assign_cells_routed / assign_cells /
+// pick_orthogonal / append_parallel (index.rs:2442-2667); refresh_derived (index.rs:684-878:
+// radii, centroid codes, SQ8 centroids, tree via CentroidTree::build + compact_layout,
+// tree.rs:354-540); compact (index.rs:3565-3569 -> compact_arena :929-1112). Written from the
+// reference source, not from the product's host build, so that a mistake in either shows up as
+// an array mismatch (tests/test_oracle_build.py). Only first-batch builds (no deletes, no reused
+// slots) are restated: that is all any benchmark or test here builds.
+
+void normalize_rows(float* v, size_t n) {  // tree.rs:163-172 and the loop in index.rs:2787-2794
+    float s = 0.0f;
+    for (size_t i = 0; i < n; ++i) s += v[i] * v[i];
+    s = std::sqrt(s);
+    if (s > 1e-12f)
+        for (size_t i = 0; i < n; ++i) v[i] /= s;
+}
+
+// kmeans_spherical (tree.rs:179-248): strided seeding, Lloyd iterations with the AVX2 dot, first
+// maximum wins; per-cluster sums accumulated in point order (grouped by cluster so clusters sum in
+// parallel: every cluster still adds its points in ascending index order, as the serial loop does);
+// empty clusters reseeded from a xorshift64 stream seeded with seed | 1.
+void kmeans_spherical(const float* x, size_t n, size_t dim, size_t k_in, size_t iters, uint64_t seed,
+                      std::vector<uint32_t>& assign, std::vector<float>& cents) {
+    size_t k = std::min(std::max<size_t>(k_in, 1), n);
+    cents.assign(k * dim, 0.0f);
+    size_t stride = std::max<size_t>(n / k, 1);
+    for (size_t j = 0; j < k; ++j) {
+        size_t src = std::min(j * stride, n - 1);
+        std::memcpy(&cents[j * dim], x + src * dim, dim * sizeof(float));
+    }
+    assign.assign(n, 0);
+    uint64_t state = seed | 1;
+    auto next_u = [&state]() {
+        state ^= state << 13;
+        state ^= state >> 7;
+        state ^= state << 17;
+        return state;
+    };
+    std::vector<size_t> start(k + 1), order(n);
+    std::vector<float> sums(k * dim);
+    for (size_t it = 0; it < iters; ++it) {
+#pragma omp parallel for schedule(static)
+        for (size_t i = 0; i < n; ++i) {
+            const float* v = x + i * dim;
+            uint32_t best = 0;
+            float best_s = -INFINITY;
+            for (size_t j = 0; j < k; ++j) {
+                float s = dot_f32(v, &cents[j * dim], dim);
+                if (s > best_s) {
+                    best_s = s;
+                    best = (uint32_t)j;
+                }
+            }
+            assign[i] = best;
+        }
+        std::fill(start.begin(), start.end(), 0);
+        for (size_t i = 0; i < n; ++i) ++start[assign[i] + 1];
+        for (size_t j = 0; j < k; ++j) start[j + 1] += start[j];
+        {
+            std::vector<size_t> pos(start.begin(), start.end() - 1);
+            for (size_t i = 0; i < n; ++i) order[pos[assign[i]]++] = i;
+        }
+#pragma omp parallel for schedule(dynamic, 16)
+        for (size_t j = 0; j < k; ++j) {
+            float* s = &sums[j * dim];
+            std::fill(s, s + dim, 0.0f);
+            for (size_t r = start[j]; r < start[j + 1]; ++r) {
+                const float* v = x + order[r] * dim;
+                for (size_t t = 0; t < dim; ++t) s[t] += v[t];
+            }
+        }
+        for (size_t j = 0; j < k; ++j) {
+            if (start[j + 1] == start[j]) {
+                size_t src = (size_t)(next_u() % (uint64_t)n);
+                std::memcpy(&cents[j * dim], x + src * dim, dim * sizeof(float));
+                continue;
+            }
+            std::memcpy(&cents[j * dim], &sums[j * dim], dim * sizeof(float));
+            normalize_rows(&cents[j * dim], dim);
+        }
+    }
+}
+
+// hierarchical_kmeans (tree.rs:257-348): sqrt(k) top-level groups (8 iterations), sub-cluster
+// counts proportional to group size by the sequential budget rule, 12 iterations per group with
+// seed ^ (g + 1) * 0x9E3779B9, shortfall rows filled from the data at (fill * 7919) % n.
+std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, size_t k_in, uint64_t seed) {
+    size_t k = std::min(std::max<size_t>(k_in, 1), n);
+    std::vector<uint32_t> asg;
+    std::vector<float> c;
+    if (k <= 64 || n <= k * 4) {
+        kmeans_spherical(x, n, dim, k, 12, seed, asg, c);
+        return c;
+    }
+    size_t k1 = (size_t)std::ceil(std::sqrt((double)k));
+    kmeans_spherical(x, n, dim, k1, 8, seed, asg, c);
+    std::vector<std::vector<uint32_t>> groups(k1);
+    for (size_t i = 0; i < n; ++i) groups[asg[i]].push_back((uint32_t)i);
+    std::vector<size_t> subs(k1, 0), offs(k1, 0);
+    size_t written = 0, before = 0;
+    for (size_t g = 0; g < k1; ++g) {
+        size_t glen = groups[g].size();
+        size_t seen = before;  // points in groups[..g]
+        before += glen;
+        if (glen == 0 || written >= k) continue;
+        size_t remaining_groups = k1 - g;
+        double denom = (double)std::max<size_t>(n - seen, 1);
+        size_t want = (size_t)std::round((double)(k - written) * (double)glen / denom);
+        size_t sub = std::min(std::min(std::max<size_t>(want, 1), k - written), glen);
+        if (remaining_groups == 1) sub = std::max<size_t>(std::min(k - written, glen), 1);
+        if (sub == 0) continue;
+        subs[g] = std::min(sub, k - written);
+        offs[g] = written;
+        written += subs[g];
+    }
+    std::vector<float> out(k * dim, 0.0f);
+    std::vector<size_t> todo;
+    for (size_t g = 0; g < k1; ++g)
+        if (subs[g] > 0) todo.push_back(g);
+    // Sub-clusterings are independent and write disjoint rows (inner parallel regions run serially).
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t t = 0; t < todo.size(); ++t) {
+        size_t g = todo[t];
+        const auto& idx = groups[g];
+        std::vector<float> buf(idx.size() * dim);
+        for (size_t r = 0; r < idx.size(); ++r) std::memcpy(&buf[r * dim], x + (size_t)idx[r] * dim, dim * 4);
+        std::vector<uint32_t> a2;
+        std::vector<float> cs;
+        kmeans_spherical(buf.data(), idx.size(), dim, subs[g], 12, seed ^ ((uint64_t)g + 1) * 0x9E3779B9ull, a2, cs);
+        std::memcpy(&out[offs[g] * dim], cs.data(), subs[g] * dim * sizeof(float));
+    }
+    size_t fill = 0;
+    while (written < k) {
+        size_t src = (fill * 7919) % n;
+        std::memcpy(&out[written * dim], x + src * dim, dim * sizeof(float));
+        ++written;
+        ++fill;
+    }
+    return out;
+}
+
+struct BLevel {  // tree.rs:74-83
+    size_t n = 0;
+    std::vector<float> cents;
+    std::vector<uint64_t> codes;
+    std::vector<uint32_t> child_start, child_len, child_idx;
+};
+
+struct BCell {  // index.rs:361-395
+    std::vector<uint32_t> members;
+    std::vector<float> sum, centroid;
+    float r_bound = 0.0f, r_max = 0.0f;
+};
+
+// The index under construction, with the reference's defaults (index.rs:2672-2755).
+struct OBuild {
+    size_t dim = 0, dim_pad = 0, nw = 0, rerank_factor = 4;
+    uint64_t seed = 0x5EED;
+    std::vector<float> signs;
+    bool two_stage = false, centroid_sq8 = true, tree_route = true, graph_route = true, fastscan = false;
+    bool per_dim_sq = false, i8_rerank = false, keep_f32 = true, adaptive = false, compacted = false;
+    size_t shortlist_mult = 4, tree_min_cells = 2048, tree_fanout = 64, graph_min_cells = 65536;
+    size_t max_assign = 1, cm_min_batch = 32, n_live = 0, tree_cells = 0;
+    float tree_beam_frac = 0.5f, spill_margin = 0.0f, spill_lambda = 0.0f, at_margin = 0.02f, quant_scale = 0.0f;
+    // arena
+    std::vector<uint64_t> bits, ext_ids;
+    std::vector<int8_t> scan_i8;
+    std::vector<float> vecs_f32, sq_min, sq_step;
+    std::vector<uint32_t> slot_cell, slot_cells;
+    // cells and derived state
+    std::vector<BCell> cells;
+    std::vector<uint64_t> cent_bits;
+    std::vector<uint8_t> cent_sq8;
+    std::vector<float> csq_min, csq_step;
+    bool has_tree = false;
+    std::vector<BLevel> levels;  // coarsest first, after compact_layout
+    std::vector<uint64_t> leaf_codes;
+    std::vector<uint32_t> leaf_ids;
+    float tree_bf = 0.5f;
+    // compacted layout
+    std::vector<uint32_t> prim_len, rep_off;
+    std::vector<uint8_t> fs_codes;
+    std::vector<uint32_t> fs_off;
+    // the tree as tree_search reads it
+    OIndex tview;
+
+    void code_of(const float* v, std::vector<float>& rot, uint64_t* out) const {
+        rotate(v, dim, signs.data(), dim_pad, rot.data());
+        pack_signs_trunc(rot.data(), dim_pad, out, nw);
+    }
+    size_t live_cells() const {
+        size_t c = 0;
+        for (auto& cl : cells) c += !cl.members.empty();
+        return c;
+    }
+};
+
+// CentroidTree::build (tree.rs:354-453) and compact_layout / permute_level / permute_leaves
+// (tree.rs:455-540).
+void tree_build(OBuild& b, const std::vector<uint32_t>& ids) {
+    b.has_tree = false;
+    b.levels.clear();
+    b.leaf_codes.clear();
+    b.leaf_ids.clear();
+    size_t m = ids.size(), dim = b.dim, nw = b.nw;
+    if (m < 2 || nw == 0) return;
+    size_t fanout = std::max<size_t>(b.tree_fanout, 2);
+    std::vector<float> rot(b.dim_pad), cur((size_t)m * dim);
+    for (size_t i = 0; i < m; ++i) std::memcpy(&cur[i * dim], b.cells[ids[i]].centroid.data(), dim * 4);
+    std::vector<uint64_t> leaf(m * nw);
+    for (size_t i = 0; i < m; ++i) b.code_of(&cur[i * dim], rot, &leaf[i * nw]);
+    std::vector<BLevel> rev;
+    size_t cur_n = m;
+    while (cur_n > 256) {  // TOP_MAX, tree.rs:41
+        size_t k = std::max<size_t>((cur_n + fanout - 1) / fanout, 1);
+        if (k >= cur_n) break;
+        std::vector<uint32_t> asg;
+        std::vector<float> parents;
+        kmeans_spherical(cur.data(), cur_n, dim, k, 10, 0x9E3779B97F4A7C15ull, asg, parents);
+        BLevel L;
+        L.n = k;
+        L.child_len.assign(k, 0);
+        for (uint32_t a : asg) ++L.child_len[a];
+        L.child_start.assign(k, 0);
+        uint32_t acc = 0;
+        for (size_t j = 0; j < k; ++j) {
+            L.child_start[j] = acc;
+            acc += L.child_len[j];
+        }
+        std::vector<uint32_t> fillp = L.child_start;
+        L.child_idx.assign(cur_n, 0);
+        for (size_t i = 0; i < cur_n; ++i) L.child_idx[fillp[asg[i]]++] = (uint32_t)i;
+        L.codes.resize(k * nw);
+        for (size_t j = 0; j < k; ++j) b.code_of(&parents[j * dim], rot, &L.codes[j * nw]);
+        L.cents = parents;
+        rev.push_back(std::move(L));
+        cur = std::move(parents);
+        cur_n = k;
+    }
+    if (rev.empty()) return;
+    std::reverse(rev.begin(), rev.end());
+    std::vector<uint32_t> lids = ids;
+    for (size_t i = 0; i < rev.size(); ++i) {
+        std::vector<uint32_t> order = rev[i].child_idx;
+        if (i + 1 < rev.size()) {
+            BLevel& l = rev[i + 1];
+            if (order.size() == l.n) {
+                BLevel p;
+                p.n = l.n;
+                p.cents.resize(l.n * dim);
+                p.codes.resize(l.n * nw);
+                p.child_start.resize(l.n);
+                p.child_len.resize(l.n);
+                uint32_t acc = 0;
+                for (size_t np_ = 0; np_ < order.size(); ++np_) {
+                    size_t o = order[np_];
+                    std::memcpy(&p.cents[np_ * dim], &l.cents[o * dim], dim * 4);
+                    std::memcpy(&p.codes[np_ * nw], &l.codes[o * nw], nw * 8);
+                    p.child_start[np_] = acc;
+                    p.child_len[np_] = l.child_len[o];
+                    acc += l.child_len[o];
+                    p.child_idx.insert(p.child_idx.end(), l.child_idx.begin() + l.child_start[o],
+                                       l.child_idx.begin() + l.child_start[o] + l.child_len[o]);
+                }
+                l = std::move(p);
+            }
+        } else {
+            std::vector<uint64_t> codes(order.size() * nw);
+            std::vector<uint32_t> nids(order.size());
+            for (size_t np_ = 0; np_ < order.size(); ++np_) {
+                std::memcpy(&codes[np_ * nw], &leaf[(size_t)order[np_] * nw], nw * 8);
+                nids[np_] = lids[order[np_]];
+            }
+            leaf = std::move(codes);
+            lids = std::move(nids);
+        }
+        for (size_t t = 0; t < rev[i].child_idx.size(); ++t) rev[i].child_idx[t] = (uint32_t)t;
+    }
+    b.levels = std::move(rev);
+    b.leaf_codes = std::move(leaf);
+    b.leaf_ids = std::move(lids);
+    b.tree_bf = b.tree_beam_frac > 0.0f ? b.tree_beam_frac : 0.5f;
+    b.has_tree = true;
+    // the view tree_search reads (tree.rs:574-628)
+    OIndex& t = b.tview;
+    t.nw = nw;
+    t.beam_frac = b.tree_bf;
+    t.levels.clear();
+    for (auto& L : b.levels) {
+        Level v;
+        v.n = L.n;
+        v.codes = L.codes;
+        v.child_start = L.child_start;
+        v.child_len = L.child_len;
+        t.levels.push_back(std::move(v));
+    }
+    t.leaf_codes = b.leaf_codes;
+    t.leaf_ids = b.leaf_ids;
+    t.n_leaf = b.leaf_ids.size();
+}
+
+// rebuild_centroid_tree (index.rs:684-708)
+void rebuild_tree(OBuild& b) {
+    b.tree_cells = b.live_cells();
+    std::vector<uint32_t> live;
+    for (size_t i = 0; i < b.cells.size(); ++i)
+        if (!b.cells[i].members.empty()) live.push_back((uint32_t)i);
+    if (live.empty() && !b.cells.empty())
+        for (size_t i = 0; i < b.cells.size(); ++i) live.push_back((uint32_t)i);
+    if (!b.tree_route || live.size() < b.tree_min_cells) {
+        b.has_tree = false;
+        b.levels.clear();
+        return;
+    }
+    tree_build(b, live);
+}
+
+// recompute_radii (index.rs:817-861): p99 and max of the member angles acos(clamp(mu . v)).
+void recompute_radii(OBuild& b) {
+    size_t dim = b.dim;
+    float inv = b.quant_scale > 0.0f ? 1.0f / b.quant_scale : 1.0f;
+#pragma omp parallel for schedule(dynamic, 8)
+    for (size_t ci = 0; ci < b.cells.size(); ++ci) {
+        BCell& c = b.cells[ci];
+        if (c.members.empty()) {
+            c.r_bound = c.r_max = 0.0f;
+            continue;
+        }
+        const float* mu = c.centroid.data();
+        std::vector<float> w;
+        float base = 0.0f;
+        if (b.per_dim_sq) {
+            w.resize(dim);
+            for (size_t j = 0; j < dim; ++j) w[j] = b.sq_step[j] * mu[j];
+            for (size_t j = 0; j < dim; ++j) base += b.sq_min[j] * mu[j];
+        }
+        std::vector<float> angs;
+        angs.reserve(c.members.size());
+        for (uint32_t s : c.members) {
+            size_t off = (size_t)s * dim;
+            float dot;
+            if (b.per_dim_sq)
+                dot = dot_f32_u8(w.data(), &b.scan_i8[off], dim) + base;
+            else if (b.keep_f32)
+                dot = dot_f32(mu, &b.vecs_f32[off], dim);
+            else
+                dot = dot_f32_i8(mu, &b.scan_i8[off], dim) * inv;
+            dot = std::min(std::max(dot, -1.0f), 1.0f);
+            angs.push_back(std::acos(dot));
+        }
+        size_t len = angs.size();
+        size_t p99 = (size_t)std::ceil((float)len * 0.99f);
+        p99 = std::min(p99 == 0 ? 0 : p99 - 1, len - 1);
+        float mx = -INFINITY;
+        for (float a : angs) mx = std::max(mx, a);
+        std::nth_element(angs.begin(), angs.begin() + p99, angs.end());
+        c.r_bound = angs[p99];
+        c.r_max = mx;
+    }
+}
+
+// rebuild_centroid_codes (index.rs:711-723)
+void rebuild_codes(OBuild& b) {
+    std::vector<float> rot(b.dim_pad);
+    b.cent_bits.assign(b.cells.size() * b.nw, 0);
+    for (size_t ci = 0; ci < b.cells.size(); ++ci) b.code_of(b.cells[ci].centroid.data(), rot, &b.cent_bits[ci * b.nw]);
+}
+
+// rebuild_centroid_sq8 (index.rs:730-770): range over live centroids, step floor 1e-12,
+// round-half-away codes clamped to [0, 255], one row for every cell.
+void rebuild_sq8(OBuild& b) {
+    size_t d = b.dim;
+    std::vector<float> lo(d, INFINITY), hi(d, -INFINITY);
+    bool any = false;
+    for (auto& c : b.cells) {
+        if (c.members.empty()) continue;
+        any = true;
+        for (size_t j = 0; j < d; ++j) {
+            float v = c.centroid[j];
+            if (v < lo[j]) lo[j] = v;
+            if (v > hi[j]) hi[j] = v;
+        }
+    }
+    b.cent_sq8.clear();
+    b.csq_min.clear();
+    b.csq_step.clear();
+    if (!any) return;
+    b.csq_step.resize(d);
+    for (size_t j = 0; j < d; ++j) {
+        float s = (hi[j] - lo[j]) / 255.0f;
+        b.csq_step[j] = s > 1e-12f ? s : 1e-12f;
+    }
+    b.csq_min = lo;
+    b.cent_sq8.assign(b.cells.size() * d, 0);
+    for (size_t ci = 0; ci < b.cells.size(); ++ci)
+        for (size_t j = 0; j < d; ++j) {
+            float q = std::round((b.cells[ci].centroid[j] - b.csq_min[j]) / b.csq_step[j]);
+            b.cent_sq8[ci * d + j] = (uint8_t)std::min(std::max(q, 0.0f), 255.0f);
+        }
+}
+
+// refresh_derived (index.rs:864-878); the centroid graph is not restated (off in both presets).
+void refresh_derived(OBuild& b) {
+    recompute_radii(b);
+    if (b.two_stage) rebuild_codes(b);
+    if (b.centroid_sq8) rebuild_sq8(b);
+    if (!(b.has_tree && b.tree_cells == b.live_cells())) rebuild_tree(b);  // maybe_rebuild, :667-677
+}
+
+// Descending score; exact ties by ascending cell id (the reference's unstable sorts leave them in
+// an unspecified order; the product uses the same rule).
+inline bool by_score_then_id(const std::pair<uint32_t, float>& a, const std::pair<uint32_t, float>& b) {
+    if (a.second != b.second) return a.second > b.second;
+    return a.first < b.first;
+}
+
+// pick_orthogonal (index.rs:2523-2560): nearest cell first, then greedily the lowest
+// ||r||^2 + lambda * sum_h (r . r_h / ||r_h||)^2 over the 16 best candidates.
+std::vector<uint32_t> pick_orthogonal(const OBuild& b, std::vector<std::pair<uint32_t, float>>& scored) {
+    size_t pool = std::min<size_t>(16, scored.size());
+    std::sort(scored.begin(), scored.end(), by_score_then_id);
+    scored.resize(pool);
+    size_t r = std::min(b.max_assign, scored.size());
+    std::vector<std::pair<uint32_t, float>> homes{scored[0]};
+    std::vector<uint8_t> taken(scored.size(), 0);
+    taken[0] = 1;
+    while (homes.size() < r) {
+        size_t bj = SIZE_MAX;
+        float bl = INFINITY;
+        for (size_t j = 0; j < scored.size(); ++j) {
+            if (taken[j]) continue;
+            uint32_t cj = scored[j].first;
+            float sj = scored[j].second;
+            float loss = 2.0f - 2.0f * sj;
+            for (auto& h : homes) {
+                float sh = h.second;
+                float rn = std::sqrt(std::max(2.0f - 2.0f * sh, 1e-12f));
+                float g = dot_f32(b.cells[h.first].centroid.data(), b.cells[cj].centroid.data(), b.dim);
+                float p = (1.0f - sh - sj + g) / rn;
+                loss += b.spill_lambda * p * p;
+            }
+            if (loss < bl) {
+                bl = loss;
+                bj = j;
+            }
+        }
+        if (bj == SIZE_MAX) break;
+        taken[bj] = 1;
+        homes.push_back(scored[bj]);
+    }
+    std::vector<uint32_t> out;
+    for (auto& h : homes) out.push_back(h.first);
+    return out;
+}
+
+// The home choice shared by assign_cells and assign_cells_routed once candidates are scored
+// (index.rs:2466-2477, :2489-2504).
+std::vector<uint32_t> choose_homes(const OBuild& b, std::vector<std::pair<uint32_t, float>>& scored) {
+    if (b.max_assign <= 1) {
+        auto best = scored[0];
+        for (auto& s : scored)
+            if (s.second > best.second) best = s;
+        return {best.first};
+    }
+    if (b.spill_lambda > 0.0f) return pick_orthogonal(b, scored);
+    size_t r = std::min(b.max_assign, scored.size());
+    std::sort(scored.begin(), scored.end(), by_score_then_id);
+    scored.resize(r);
+    float cutoff = scored[0].second - b.spill_margin;
+    std::vector<uint32_t> out;
+    for (auto& s : scored)
+        if (s.second >= cutoff) out.push_back(s.first);
+    return out;
+}
+
+// assign_cells_routed (index.rs:2442-2478) with its flat fallback assign_cells (:2480-2505).
+std::vector<uint32_t> assign_cells(const OBuild& b, const float* v, std::vector<float>& rot,
+                                   std::vector<uint64_t>& qb, std::vector<uint32_t>& tout) {
+    std::vector<std::pair<uint32_t, float>> scored;
+    if (b.has_tree) {
+        b.code_of(v, rot, qb.data());
+        size_t want = std::max<size_t>(64, b.max_assign * 8);  // ASSIGN_CANDIDATES, index.rs:401
+        tree_search(b.tview, qb.data(), want, tout);
+        for (uint32_t ci : tout) scored.push_back({ci, dot_f32(v, b.cells[ci].centroid.data(), b.dim)});
+    }
+    if (scored.empty())
+        for (size_t ci = 0; ci < b.cells.size(); ++ci)
+            scored.push_back({(uint32_t)ci, dot_f32(v, b.cells[ci].centroid.data(), b.dim)});
+    return choose_homes(b, scored);
+}
+
+// train_centroids (index.rs:2761-2804)
+int build_train(OBuild& b, const float* data, size_t n_all, size_t n_cells, size_t sample, uint64_t sd) {
+    if (n_all == 0) return 1;
+    size_t dim = b.dim;
+    std::vector<float> train;
+    size_t n_train = n_all;
+    const float* tp = data;
+    if (sample > 0 && n_all > sample) {
+        size_t stride = n_all / sample;
+        train.resize(sample * dim);
+        for (size_t i = 0; i < sample; ++i) {
+            size_t s = std::min(i * stride, n_all - 1);
+            std::memcpy(&train[i * dim], data + s * dim, dim * 4);
+        }
+        n_train = sample;
+        tp = train.data();
+    }
+    std::vector<float> cents = hierarchical_kmeans(tp, n_train, dim, n_cells, sd);
+    size_t m = cents.size() / dim;
+    b.cells.assign(m, BCell());
+    for (size_t c = 0; c < m; ++c) {
+        normalize_rows(&cents[c * dim], dim);
+        b.cells[c].sum.assign(dim, 0.0f);
+        b.cells[c].centroid.assign(cents.begin() + c * dim, cents.begin() + (c + 1) * dim);
+    }
+    refresh_derived(b);
+    return 0;
+}
+
+// add_batch (index.rs:2987-3212) for a build with no reused slots: scale and SQ8 fit from the
+// first batch, parallel placement, append_parallel (:2566-2667), centroid update, derived state.
+int build_add(OBuild& b, const uint64_t* ids, const float* data, size_t n) {
+    if (b.cells.empty()) return 1;
+    size_t dim = b.dim, nw = b.nw, ma = b.max_assign;
+    b.compacted = false;
+    if (b.quant_scale == 0.0f) {
+        float mx = 0.0f;
+        for (size_t i = 0; i < n * dim; ++i) mx = std::max(mx, std::fabs(data[i]));
+        b.quant_scale = mx > 0.0f ? 127.0f / mx : 1.0f;
+    }
+    if (b.per_dim_sq && b.sq_min.empty()) {
+        std::vector<float> lo(dim, INFINITY), hi(dim, -INFINITY);
+        for (size_t i = 0; i < n; ++i)
+            for (size_t j = 0; j < dim; ++j) {
+                float x = data[i * dim + j];
+                lo[j] = std::min(lo[j], x);
+                hi[j] = std::max(hi[j], x);
+            }
+        b.sq_step.resize(dim);
+        for (size_t j = 0; j < dim; ++j) b.sq_step[j] = std::max(hi[j] - lo[j], 1e-9f) / 255.0f;
+        b.sq_min = lo;
+    }
+    std::vector<std::vector<uint32_t>> asg(n);
+#pragma omp parallel
+    {
+        std::vector<float> rot(b.dim_pad);
+        std::vector<uint64_t> qb(nw);
+        std::vector<uint32_t> tout;
+#pragma omp for schedule(dynamic, 256)
+        for (size_t i = 0; i < n; ++i) asg[i] = assign_cells(b, data + i * dim, rot, qb, tout);
+    }
+    size_t base = b.ext_ids.size();
+    bool store_i8 = b.i8_rerank;
+    if (b.keep_f32) b.vecs_f32.insert(b.vecs_f32.end(), data, data + n * dim);
+    b.bits.resize((base + n) * nw);
+    if (store_i8) b.scan_i8.resize((base + n) * dim);
+#pragma omp parallel
+    {
+        std::vector<float> rot(b.dim_pad);
+#pragma omp for schedule(static)
+        for (size_t i = 0; i < n; ++i) {
+            const float* v = data + i * dim;
+            b.code_of(v, rot, &b.bits[(base + i) * nw]);
+            if (store_i8) {
+                int8_t* o = &b.scan_i8[(base + i) * dim];
+                for (size_t j = 0; j < dim; ++j) {
+                    if (b.per_dim_sq) {
+                        float q = std::round((v[j] - b.sq_min[j]) / b.sq_step[j]);
+                        o[j] = (int8_t)(uint8_t)std::min(std::max(q, 0.0f), 255.0f);
+                    } else {
+                        float q = std::round(v[j] * b.quant_scale);
+                        o[j] = (int8_t)std::min(std::max(q, -127.0f), 127.0f);
+                    }
+                }
+            }
+        }
+    }
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t slot = (uint32_t)(base + i);
+        b.ext_ids.push_back(ids[i]);
+        b.slot_cell.push_back(asg[i][0]);
+        for (size_t j = 0; j < ma; ++j) b.slot_cells.push_back(j < asg[i].size() ? asg[i][j] : UINT32_MAX);
+        for (uint32_t ci : asg[i]) b.cells[ci].members.push_back(slot);
+    }
+    b.n_live += n;
+    // primary sums: each cell adds its own vectors in input order
+    size_t m = b.cells.size();
+    std::vector<size_t> st(m + 1, 0), ord(n);
+    for (size_t i = 0; i < n; ++i) ++st[asg[i][0] + 1];
+    for (size_t c = 0; c < m; ++c) st[c + 1] += st[c];
+    {
+        std::vector<size_t> pos(st.begin(), st.end() - 1);
+        for (size_t i = 0; i < n; ++i) ord[pos[asg[i][0]]++] = i;
+    }
+#pragma omp parallel for schedule(dynamic, 16)
+    for (size_t c = 0; c < m; ++c) {
+        float* s = b.cells[c].sum.data();
+        for (size_t r = st[c]; r < st[c + 1]; ++r) {
+            const float* v = data + ord[r] * dim;
+            for (size_t j = 0; j < dim; ++j) s[j] += v[j];
+        }
+    }
+    // Cell::recompute_centroid (index.rs:379-392)
+    for (auto& c : b.cells) {
+        if (c.members.empty()) continue;
+        float nrm = 0.0f;
+        for (float v : c.sum) nrm += v * v;
+        nrm = std::sqrt(nrm);
+        if (nrm > 1e-12f)
+            for (size_t j = 0; j < dim; ++j) c.centroid[j] = c.sum[j] / nrm;
+    }
+    refresh_derived(b);
+    return 0;
+}
+
+// compact_arena (index.rs:929-1112): cluster-major renumbering by primary cell, member lists
+// remapped and sorted, polysemic runs (primaries ascending, then replicas ascending), FastScan
+// blocks of 32 members per cell.
+void build_compact(OBuild& b) {
+    size_t old_n = b.ext_ids.size();
+    if (old_n == 0) return;
+    size_t dim = b.dim, nw = b.nw, ma = b.max_assign;
+    std::vector<uint32_t> new_of_old(old_n, UINT32_MAX), old_of_new;
+    old_of_new.reserve(b.n_live);
+    for (size_t ci = 0; ci < b.cells.size(); ++ci)
+        for (uint32_t s : b.cells[ci].members) {
+            if (b.slot_cell[s] != ci || new_of_old[s] != UINT32_MAX) continue;
+            new_of_old[s] = (uint32_t)old_of_new.size();
+            old_of_new.push_back(s);
+        }
+    for (size_t s = 0; s < old_n; ++s)  // every slot is live in a first-batch build
+        if (new_of_old[s] == UINT32_MAX) {
+            new_of_old[s] = (uint32_t)old_of_new.size();
+            old_of_new.push_back((uint32_t)s);
+        }
+    size_t nn = old_of_new.size();
+    auto permute = [&](auto& arr, size_t w) {
+        if (arr.empty()) return;
+        std::remove_reference_t<decltype(arr)> v(nn * w);
+        for (size_t ns = 0; ns < nn; ++ns)
+            std::copy(arr.begin() + (size_t)old_of_new[ns] * w, arr.begin() + ((size_t)old_of_new[ns] + 1) * w,
+                      v.begin() + ns * w);
+        arr.swap(v);
+    };
+    if (b.keep_f32) permute(b.vecs_f32, dim);
+    permute(b.scan_i8, dim);
+    permute(b.bits, nw);
+    permute(b.ext_ids, 1);
+    permute(b.slot_cell, 1);
+    permute(b.slot_cells, ma);
+    for (auto& c : b.cells) {
+        for (auto& mbr : c.members) mbr = new_of_old[mbr];
+        std::sort(c.members.begin(), c.members.end());
+    }
+    b.prim_len.clear();
+    b.rep_off.clear();
+    if (ma > 1 && nw > 0) {
+        b.rep_off.push_back(0);
+        for (size_t ci = 0; ci < b.cells.size(); ++ci) {
+            std::vector<uint32_t> prim, repl;
+            for (uint32_t mbr : b.cells[ci].members) (b.slot_cell[mbr] == ci ? prim : repl).push_back(mbr);
+            std::sort(prim.begin(), prim.end());
+            std::sort(repl.begin(), repl.end());
+            b.prim_len.push_back((uint32_t)prim.size());
+            b.rep_off.push_back(b.rep_off.back() + (uint32_t)repl.size());
+            prim.insert(prim.end(), repl.begin(), repl.end());
+            b.cells[ci].members = std::move(prim);
+        }
+    }
+    b.fs_codes.clear();
+    b.fs_off.clear();
+    if (b.fastscan && nw > 0) {
+        size_t bb = nw * 256;
+        b.fs_off.push_back(0);
+        for (auto& c : b.cells) {
+            size_t nb = (c.members.size() + 31) / 32;
+            size_t at = b.fs_codes.size();
+            b.fs_codes.resize(at + nb * bb);
+            for (size_t blk = 0; blk < nb; ++blk) {
+                size_t lo = blk * 32, hi = std::min(lo + 32, c.members.size());
+                std::vector<const uint64_t*> lanes;
+                for (size_t r = lo; r < hi; ++r) lanes.push_back(&b.bits[(size_t)c.members[r] * nw]);
+                fs_pack_block(lanes.data(), lanes.size(), nw, &b.fs_codes[at + blk * bb]);
+            }
+            b.fs_off.push_back((uint32_t)(b.fs_codes.size() / bb));
+        }
+    }
+    b.compacted = true;
+}
+
+// ---- index build API (tests and the reference arm of bench.py) ---------------------------------
+
+struct OBuildHandle {
+    OBuild b;
+    std::map<std::string, std::vector<uint8_t>> arrays;
+    std::map<std::string, size_t> elem;
+};
+
+template <typename T>
+void bput(OBuildHandle* h, const char* name, const T* p, size_t n) {
+    auto& v = h->arrays[name];
+    v.resize(n * sizeof(T));
+    if (n) std::memcpy(v.data(), p, n * sizeof(T));
+    h->elem[name] = sizeof(T);
+}
+
+// The arrays under the names and in the layouts FlatCellIndex.array() uses, so one OracleIndex
+// constructor serves both sources and the test can compare them name by name.
+void bexport(OBuildHandle* h) {
+    OBuild& b = h->b;
+    h->arrays.clear();
+    double cfg[] = {(double)b.dim,          (double)b.dim_pad,       (double)b.nw,
+                    (double)b.rerank_factor, (double)b.two_stage,     (double)b.shortlist_mult,
+                    (double)b.centroid_sq8,  (double)b.has_tree,      (double)b.max_assign,
+                    (double)b.fastscan,      (double)b.per_dim_sq,    (double)b.i8_rerank,
+                    (double)b.keep_f32,      (double)b.adaptive,      (double)b.at_margin,
+                    (double)b.quant_scale,   (double)b.compacted,     (double)b.n_live,
+                    (double)b.cm_min_batch,  0.0,                     0.0,
+                    (double)0xFFFFFFFFu,     (double)(b.has_tree ? b.tree_bf : 0.0f),
+                    (double)(b.has_tree ? b.leaf_ids.size() : 0), (double)b.graph_route,
+                    (double)b.graph_min_cells};
+    bput(h, "config", cfg, sizeof(cfg) / sizeof(double));
+    bput(h, "vecs_f32", b.vecs_f32.data(), b.vecs_f32.size());
+    bput(h, "scan_i8", b.scan_i8.data(), b.scan_i8.size());
+    bput(h, "ext_ids", b.ext_ids.data(), b.ext_ids.size());
+    bput(h, "slot_cell", b.slot_cell.data(), b.slot_cell.size());
+    bput(h, "slot_cells", b.slot_cells.data(), b.slot_cells.size());
+    std::vector<uint32_t> mem, moff{0};
+    std::vector<float> cents, rb;
+    for (auto& c : b.cells) {
+        mem.insert(mem.end(), c.members.begin(), c.members.end());
+        moff.push_back((uint32_t)mem.size());
+        cents.insert(cents.end(), c.centroid.begin(), c.centroid.end());
+        rb.push_back(c.r_bound);
+    }
+    bput(h, "cell_members", mem.data(), mem.size());
+    bput(h, "cell_member_off", moff.data(), moff.size());
+    bput(h, "centroids", cents.data(), cents.size());
+    bput(h, "r_bound", rb.data(), rb.size());
+    bput(h, "prim_len", b.prim_len.data(), b.prim_len.size());
+    bput(h, "rep_off", b.rep_off.data(), b.rep_off.size());
+    bput(h, "fs_codes", b.fs_codes.data(), b.fs_codes.size());
+    bput(h, "fs_off", b.fs_off.data(), b.fs_off.size());
+    bput(h, "cent_bits", b.cent_bits.data(), b.cent_bits.size());
+    bput(h, "cent_sq8", b.cent_sq8.data(), b.cent_sq8.size());
+    bput(h, "csq_min", b.csq_min.data(), b.csq_min.size());
+    bput(h, "csq_step", b.csq_step.data(), b.csq_step.size());
+    bput(h, "sq_min", b.sq_min.data(), b.sq_min.size());
+    bput(h, "sq_step", b.sq_step.data(), b.sq_step.size());
+    bput(h, "signs", b.signs.data(), b.signs.size());
+    std::vector<uint32_t> tags;
+    bput(h, "tags", tags.data(), 0);
+    std::vector<uint64_t> lvn, tcodes, tcoff{0}, tcs, tcl, tchoff{0};
+    if (b.has_tree)
+        for (auto& l : b.levels) {
+            lvn.push_back(l.n);
+            tcodes.insert(tcodes.end(), l.codes.begin(), l.codes.end());
+            tcoff.push_back(tcodes.size());
+            tcs.insert(tcs.end(), l.child_start.begin(), l.child_start.end());
+            tcl.insert(tcl.end(), l.child_len.begin(), l.child_len.end());
+            tchoff.push_back(tcs.size());
+        }
+    bput(h, "tree_level_n", lvn.data(), lvn.size());
+    bput(h, "tree_codes", tcodes.data(), tcodes.size());
+    bput(h, "tree_code_off", tcoff.data(), tcoff.size());
+    bput(h, "tree_child_start", tcs.data(), tcs.size());
+    bput(h, "tree_child_len", tcl.data(), tcl.size());
+    bput(h, "tree_child_off", tchoff.data(), tchoff.size());
+    std::vector<uint64_t> lc = b.has_tree ? b.leaf_codes : std::vector<uint64_t>();
+    std::vector<uint32_t> li = b.has_tree ? b.leaf_ids : std::vector<uint32_t>();
+    bput(h, "tree_leaf_codes", lc.data(), lc.size());
+    bput(h, "tree_leaf_ids", li.data(), li.size());
+}
+
 }  // namespace
 
 // ---- C API used by the tests and the CPU-baseline arm of bench.py ------------------------------
@@ -1018,6 +1797,11 @@ void* oracle_index_new(const oracle_arrays* a) {
 void oracle_index_free(void* p) { delete static_cast<OIndex*>(p); }
 
 void oracle_set_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
+
+// set_rerank_factor (index.rs:2949-2951): query-time only, so a sweep needs one index.
+void oracle_index_set_rerank_factor(void* p, uint64_t rf) {
+    static_cast<OIndex*>(p)->rerank_factor = rf > 0 ? rf : 1;
+}
 
 // search_batch (index.rs:3316-3391): ids/scores nq*k padded; cand_out (optional) receives per
 // query the candidate slots sent to the rerank, sorted, as nq rows of cand_cap (UINT32_MAX pad)
@@ -1159,6 +1943,109 @@ uint64_t oracle_keep_smallest(const uint32_t* h, const uint32_t* id, uint64_t n,
     keep_smallest(v, keep, bits);
     for (size_t i = 0; i < v.size(); ++i) out[i] = v[i].second;
     return v.size();
+}
+
+// FlatCellIndex(dim, "binary", rerank_factor, seed, code_bits) (index.rs:2674-2755).
+void* oracle_build_new(uint64_t dim, uint64_t code_bits, uint64_t seed, uint64_t rerank_factor) {
+    if (dim == 0) return nullptr;
+    auto* h = new OBuildHandle();
+    OBuild& b = h->b;
+    b.dim = dim;
+    size_t p = 1;
+    while (p < dim) p <<= 1;
+    b.dim_pad = std::max<size_t>(p, 64);  // pad_dim, quantize.rs:38-40
+    size_t bits = code_bits == 0 ? b.dim_pad : std::min<size_t>(code_bits, b.dim_pad);
+    b.nw = std::max<size_t>(bits / 64, 1);  // code_words, quantize.rs:50-53
+    b.seed = seed;
+    b.rerank_factor = std::max<uint64_t>(rerank_factor, 1);
+    b.signs.resize(2 * b.dim_pad);
+    make_signs(b.dim_pad, seed, b.signs.data());
+    return h;
+}
+
+void oracle_build_free(void* p) { delete static_cast<OBuildHandle*>(p); }
+
+// The setters the presets call (index.rs:2823-2984); returns 0, or 1 for an unknown key.
+int oracle_build_set(void* p, const char* key, double a, double b2, double c, double d) {
+    OBuild& b = static_cast<OBuildHandle*>(p)->b;
+    std::string k(key);
+    if (k == "two_stage") {  // :2882-2888
+        b.two_stage = a != 0;
+        b.shortlist_mult = std::max<size_t>((size_t)b2, 1);
+        if (b.two_stage) rebuild_codes(b);
+    } else if (k == "tree_route") {  // :2839-2852
+        if (d > 0.0) b.tree_beam_frac = (float)d;
+        b.tree_route = a != 0;
+        if (b2 > 0) b.tree_min_cells = (size_t)b2;
+        if (c > 1) b.tree_fanout = (size_t)c;
+        rebuild_tree(b);
+    } else if (k == "graph_route") {  // :2859-2865
+        b.graph_route = a != 0;
+        if (b2 > 0) b.graph_min_cells = (size_t)b2;
+    } else if (k == "orthogonal_polysemy") {  // :2979-2984
+        b.max_assign = std::max<size_t>((size_t)a, 1);
+        b.spill_margin = 0.0f;
+        b.spill_lambda = std::max((float)b2, 1e-6f);
+    } else if (k == "replication") {  // :2966-2970
+        b.max_assign = std::max<size_t>((size_t)a, 1);
+        b.spill_margin = std::max((float)b2, 0.0f);
+        b.spill_lambda = 0.0f;
+    } else if (k == "fastscan") {  // :2962-2968
+        b.fastscan = a != 0;
+        if (!b.fastscan) {
+            b.fs_codes.clear();
+            b.fs_off.clear();
+        }
+    } else if (k == "per_dim_sq") {  // :2908-2915
+        b.per_dim_sq = a != 0;
+        if (b.per_dim_sq) {
+            b.i8_rerank = true;
+            b.keep_f32 = false;
+        }
+    } else if (k == "i8_rerank") {  // :2825-2831
+        b.i8_rerank = a != 0;
+        b.keep_f32 = !b.i8_rerank;
+    } else if (k == "adaptive") {  // :2899-2902
+        b.adaptive = a != 0;
+        b.at_margin = (float)b2;
+    } else if (k == "centroid_sq8") {  // :2872-2879
+        b.centroid_sq8 = a != 0;
+        if (b.centroid_sq8)
+            rebuild_sq8(b);
+        else
+            b.cent_sq8.clear();
+    } else if (k == "rerank_factor") {  // :2949-2951
+        b.rerank_factor = std::max<size_t>((size_t)a, 1);
+    } else if (k == "cm_min_batch") {
+        b.cm_min_batch = std::max<size_t>((size_t)a, 1);
+    } else {
+        return 1;
+    }
+    return 0;
+}
+
+int oracle_build_train(void* p, const float* data, uint64_t n, uint64_t n_cells, uint64_t sample, uint64_t seed) {
+    return build_train(static_cast<OBuildHandle*>(p)->b, data, n, n_cells, sample, seed);
+}
+
+int oracle_build_add(void* p, const uint64_t* ids, const float* data, uint64_t n) {
+    return build_add(static_cast<OBuildHandle*>(p)->b, ids, data, n);
+}
+
+void oracle_build_compact(void* p) { build_compact(static_cast<OBuildHandle*>(p)->b); }
+
+// Snapshot of every array (call after the build steps), then one array by name.
+void oracle_build_export(void* p) { bexport(static_cast<OBuildHandle*>(p)); }
+
+int oracle_build_array(void* p, const char* name, const void** data, uint64_t* count, uint64_t* elem_bytes) {
+    auto* h = static_cast<OBuildHandle*>(p);
+    auto it = h->arrays.find(name);
+    if (it == h->arrays.end()) return 1;
+    size_t e = h->elem[name];
+    *data = it->second.empty() ? nullptr : it->second.data();
+    *count = it->second.size() / e;
+    *elem_bytes = e;
+    return 0;
 }
 
 }  // extern "C"

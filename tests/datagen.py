@@ -66,7 +66,7 @@ def recall(ids, truth, k=10):
 
 
 def build_index(X, preset="quality", rf=16, n_cells=None, tree_min_cells=2048, ids=None, code_bits=0,
-                fanout=16, homes=2, adaptive=True, two_stage=True):
+                fanout=16, homes=2, adaptive=True, two_stage=True, replication=None):
     """The reference's benchmark presets (bench/fair/fairbench.py:98-119)."""
     import maivs_b200 as M
 
@@ -74,7 +74,9 @@ def build_index(X, preset="quality", rf=16, n_cells=None, tree_min_cells=2048, i
     ix = M.FlatCellIndex(d, "binary", rf, 0x5EED, code_bits)
     if preset == "memory":
         ix.set_per_dim_sq(True)
-    if homes > 1:
+    if replication is not None:
+        ix.set_replication(*replication)
+    elif homes > 1:
         ix.set_orthogonal_polysemy(homes, 1.0)
     ix.set_fastscan(True)
     if two_stage:
@@ -87,3 +89,30 @@ def build_index(X, preset="quality", rf=16, n_cells=None, tree_min_cells=2048, i
     ix.add_batch(list(range(n)) if ids is None else ids, X)
     ix.compact()
     return ix
+
+
+def oracle_build_index(X, preset="quality", rf=16, n_cells=None, tree_min_cells=2048, ids=None, code_bits=0,
+                       fanout=16, homes=2, adaptive=True, two_stage=True, replication=None):
+    """The same presets built by the oracle's own restatement of the reference build (test
+    infrastructure; shares no code with the product's host build)."""
+    import oracle
+
+    n, d = X.shape
+    b = oracle.OracleBuild(d, "binary", rf, 0x5EED, code_bits)
+    if preset == "memory":
+        b.set_per_dim_sq(True)
+    if replication is not None:
+        b.set_replication(*replication)
+    elif homes > 1:
+        b.set_orthogonal_polysemy(homes, 1.0)
+    b.set_fastscan(True)
+    if two_stage:
+        b.set_two_stage(True, 2)
+    b.set_graph_route(False, 10**9)
+    b.set_tree_route(True, tree_min_cells, fanout)
+    if adaptive:
+        b.set_adaptive(True, 0.02)
+    b.train_centroids(X, n_cells or max(16, n // 128))
+    b.add_batch(np.arange(n, dtype=np.uint64) if ids is None else np.asarray(ids, np.uint64), X)
+    b.compact()
+    return b
