@@ -601,6 +601,49 @@ def _scratch_dir(need_bytes: int) -> str:
     return "/tmp"
 
 
+def sharded_paths(args):
+    """Scratch files of the sharded workload, shared by the runs of one box: the MAIVS2 index, the
+    queries and their exact top-k."""
+    tag = f"maivs_cfg4_{args.n}_{args.nq}_{args.seed}"
+    d0 = _scratch_dir(args.n * 384 * 6)
+    path, qpath, tpath = (os.path.join(d0, tag + ext) for ext in (".maivs", ".q.npy", ".truth.npy"))
+    return path, qpath, tpath, d0, tag
+
+
+def sharded_queries(args, X, Q, dev):
+    """The batch and its exact top-k (brute force on the GPU), computed once and cached."""
+    _, qpath, tpath, _, _ = sharded_paths(args)
+    if not (os.path.exists(qpath) and os.path.exists(tpath)):
+        if X is None:
+            X, Q = mixture_torch(args.seed, args.n, args.nq, 384, 10_000, 0.35, dev)
+        truth = brute_force_topk(X, Q, K, str(dev))
+        np.save(qpath + ".part.npy", Q)
+        np.save(tpath + ".part.npy", truth)
+        os.replace(qpath + ".part.npy", qpath)
+        os.replace(tpath + ".part.npy", tpath)
+    return np.load(qpath), np.load(tpath)
+
+
+def sharded_oracle_answers(args, rf, np_, sample, dev):
+    """The oracle's answers (its own build of the same vectors, cell-major search) for the first
+    `sample` queries of the sharded batch; cached, since an oracle build of 5.2M vectors takes
+    minutes on the host cores. Cell-major results do not depend on the other queries of a batch."""
+    import oracle
+
+    _, qpath, _, d0, tag = sharded_paths(args)
+    cache = os.path.join(d0, f"{tag}.oracle_{rf}_{np_}_{sample}.npz")
+    if not os.path.exists(cache):
+        X, _ = mixture_torch(args.seed, args.n, args.nq, 384, 10_000, 0.35, dev)
+        o = oracle.build_preset(X, "quality", rf, threads=os.cpu_count() or 1).take_index()
+        del X
+        Q = np.load(qpath)[:sample]
+        ids, sc, *_ = o.search_batch(Q, K, np_, 1.0, 8.0, True, threads=os.cpu_count() or 1)
+        np.savez(cache + ".part.npz", ids=ids, sc=sc)
+        os.replace(cache + ".part.npz", cache)
+    z = np.load(cache)
+    return z["ids"], z["sc"]
+
+
 def run_sharded(args):
     """5.2M x 384 (10,000-component mixture), quality preset, 10,000-query
     batches, cells sharded by range over the ranks (one per GPU), NCCL all-gathers + device merge.
@@ -619,26 +662,24 @@ def run_sharded(args):
     if ws > 1:
         tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
     n, nq = args.n, args.nq
-    tag = f"maivs_cfg4_{n}_{nq}_{args.seed}"
-    d0 = _scratch_dir(n * 384 * 6)
-    path, qpath, tpath = (os.path.join(d0, tag + ext) for ext in (".maivs", ".q.npy", ".truth.npy"))
+    path, qpath, tpath, d0, tag = sharded_paths(args)
+    M.set_num_threads(max(1, (os.cpu_count() or 1) // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", ws)))))
     build_s = 0.0
-    if rank == 0 and not (os.path.exists(path) and os.path.exists(qpath) and os.path.exists(tpath)):
+    if rank == 0 and not os.path.exists(path):
         X, Q = mixture_torch(args.seed, n, nq, 384, 10_000, 0.35, dev)
         t0 = time.perf_counter()
         ix0 = build_quality(X, os.cpu_count() or 1)
         build_s = time.perf_counter() - t0
         ix0.save(path + ".part")
         del ix0
-        truth = brute_force_topk(X, Q, K, str(dev))
+        sharded_queries(args, X, Q, dev)
         del X
-        np.save(qpath, Q)
-        np.save(tpath, truth)
         os.replace(path + ".part", path)
+    elif rank == 0:
+        sharded_queries(args, None, None, dev)
     if ws > 1:
         tdist.barrier()
-    Q = np.load(qpath)
-    truth = np.load(tpath)
+    Q, truth = sharded_queries(args, None, None, dev)
     ix = M.FlatCellIndex.load(path)
     ix.set_graph_route(False, 10**9)
     ix.set_fastscan(True)
@@ -680,8 +721,10 @@ def run_sharded(args):
     torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     # every rank runs the same number of profiled steps (they hold collectives)
-    shares, dom_kernel, kernel_ms_per_step, _ = kernel_profile(ix, lambda: run(rf, np_), min(args.steps, 10), flush,
-                                                               dev)
+    shares, dom_kernel, kernel_ms_per_step, kms_step = kernel_profile(ix, lambda: run(rf, np_), min(args.steps, 10),
+                                                                      flush, dev)
+    if dom_kernel == "nccl_all_gather":  # the roofline's kernel is one of this library's
+        dom_kernel = max(((k, v) for k, v in kms_step.items() if k != "nccl_all_gather"), key=lambda kv: kv[1])[0]
     ix.kernel_clock(True, only=dom_kernel)
     ix.kernel_times(reset=True)
     if ws > 1:
@@ -703,6 +746,8 @@ def run_sharded(args):
     ix.kernel_clock(False)
     stats = ix.last_search_stats()
     dom_ms = ktimes.get(dom_kernel, (0.0, 0))
+    got_ids = d_ids.cpu().numpy().view(np.uint64).copy()
+    got_sc = d_sc.cpu().numpy().copy()
     if ws > 1:
         tdist.barrier()
     total_ms = float(sum(a.elapsed_time(b) for a, b in evs))
@@ -718,6 +763,16 @@ def run_sharded(args):
         t = torch.tensor([total_ms, e2e_total], dtype=torch.float64)
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         total_ms, e2e_total = float(t[0]), float(t[1])
+    parity = None
+    sample = min(args.parity_sample, nq)
+    if rank == 0 and sample > 0:
+        rid, rsc = sharded_oracle_answers(args, rf, np_, sample, dev)
+        parity = bool(np.array_equal(got_ids[:sample * K], rid) and
+                      np.array_equal(got_sc[:sample * K].view(np.uint32), rsc.view(np.uint32)))
+    if ws > 1:
+        tdist.barrier()
+    replicated = ("k_encode", "k_seed_finish", "k_local_list", "k_final_cm", "k_merge_topk", "k_topk")
+    tot_ms = max(sum(kms_step.values()), 1e-9)
     out = {
         "metric": METRIC, "value": round(nq * args.steps / (total_ms / 1e3), 1), "unit": "queries/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
@@ -737,6 +792,13 @@ def run_sharded(args):
                             f"{kernel_ms_per_step} ms of kernel time per step on rank 0",
         "dominant_kernel_rank0": {"name": dom_kernel, "ms_per_launch": round(dom_ms[0] / max(dom_ms[1], 1), 4),
                                   "launches": dom_ms[1]},
+        "ms_per_step_rank0": {k: round(v, 4) for k, v in sorted(kms_step.items(), key=lambda kv: -kv[1])},
+        "collective_ms_per_step_rank0": round(kms_step.get("nccl_all_gather", 0.0), 4),
+        "replicated_share_rank0": round(sum(kms_step.get(k, 0.0) for k in replicated) / tot_ms, 4),
+        "replicated_src": "kernels whose work is per query on every rank (not divided by N): " + ", ".join(replicated),
+        "parity": parity,
+        "parity_src": f"ids and f32 scores of the first {sample} queries of the timed batch bit-identical to the "
+                      "oracle's own build and cell-major search of the same vectors (rank 0)",
         "work_rank0": {k: round(v, 1) for k, v in stats.items()},
     }
     if rank == 0:
@@ -879,30 +941,96 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_reference_sharded(args):
+    """The reference's CPU path on the sharded workload's data (5.2M x 384,
+    10,000-query batches): the oracle's own build of the same vectors, cell-major search on every
+    host core, on rank 0 only (the reference is one process; there is nothing to shard on a CPU).
+    The operating point follows the same rule as the GPU arm. A step is the full batch, or a prefix
+    of it when K full batches would not end within a few minutes (then the line says so)."""
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    import oracle
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    threads = os.cpu_count() or 1
+    X, Q = mixture_torch(args.seed, args.n, args.nq, 384, 10_000, 0.35, dev)
+    Q, truth = sharded_queries(args, X, Q, dev)
+    t0 = time.perf_counter()
+    o = oracle.build_preset(X, "quality", RF_GRID[0], threads=threads).take_index()
+    build_s = time.perf_counter() - t0
+    del X
+
+    def search(rf, np_, q=Q):
+        o.set_rerank_factor(rf)
+        ids, *_ = o.search_batch(q, K, np_, 1.0, 8.0, True, threads=threads)
+        return ids
+
+    if args.rf and args.nprobe:
+        rf, np_ = args.rf, args.nprobe
+        rec = recall(search(rf, np_), truth)
+    else:
+        rf, np_, rec = operating_point(search, truth)
+    o.set_rerank_factor(rf)
+    t = time.perf_counter()
+    o.search_batch(Q, K, np_, 1.0, 8.0, True, threads=threads)
+    full_s = time.perf_counter() - t
+    budget = 150.0
+    nq_s = args.nq if full_s * args.steps <= budget else max(1000, int(args.nq * budget / (full_s * args.steps)))
+    Qs = np.ascontiguousarray(Q[:nq_s])
+    mean_s, best_s, steps = time_cpu_batches(o, Qs, rf, np_, threads, steps=args.steps, warmup=args.warmup)
+    qps = nq_s / mean_s
+    desc = (f"{nq_s} of the {args.nq} queries per step (cell-major, rf={rf}, nprobe={np_}), mean of {steps} "
+            f"steps; the full batch takes {full_s:.2f} s on these cores")
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": round(qps, 1), "unit": "queries/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": "BASELINE configs[3]: 5.2M x 384 Gaussian mixture (10,000 comps, sigma 0.35), quality "
+                               "preset, 10,000-query cell-major batches, k=10 (one process on the host cores)",
+                   "n": args.n, "dim": 384, "nq_per_step": nq_s, "k": K, "rerank_factor": rf, "nprobe": np_,
+                   "recall_at_10": round(rec, 4), "build_s": round(build_s, 1),
+                   "index": "the oracle's own build (restated reference build), no product code"},
+        "cpu_baseline": {"value": round(qps, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(qps, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("maivs", "reference"), default="maivs")
-    ap.add_argument("--n", type=int, default=None, help="vectors (500,000; 5,200,000 for --workload sharded)")
-    ap.add_argument("--nq", type=int, default=None, help="queries per batch (1,000; 10,000 sharded)")
+    ap.add_argument("--vectors", "--n", dest="n", type=int, default=None,
+                    help="vectors (500,000; 5,200,000 for --workload sharded)")
+    ap.add_argument("--batch", "--nq", dest="nq", type=int, default=None,
+                    help="queries per batch (1,000; 10,000 sharded)")
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
     ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
     ap.add_argument("--no-sweep", action="store_true", help="config2: skip the (rf, nprobe) recall sweep")
-    ap.add_argument("--workload", choices=("config2", "sharded", "lowbatch"), default="config2",
-                    help="config2: the headline 500k batch (replicas for N > 1); sharded: configs[3], 5.2M "
-                         "vectors with cells sharded by range over the N GPUs; lowbatch: configs[2], memory "
-                         "preset at batch 1 and 16")
+    ap.add_argument("--workload", choices=("auto", "config2", "sharded", "lowbatch"), default="auto",
+                    help="auto: sharded under torchrun (WORLD_SIZE set), else config2. config2: the headline 500k "
+                         "batch on one GPU (replicas when forced under torchrun); sharded: configs[3], 5.2M vectors "
+                         "with cells sharded by range over the N GPUs; lowbatch: configs[2], memory preset at "
+                         "batch 1 and 16")
+    ap.add_argument("--parity-sample", type=int, default=1000,
+                    help="sharded: queries of the timed batch checked against the oracle (0: none)")
     args = ap.parse_args()
+    if args.workload == "auto":
+        args.workload = "sharded" if "WORLD_SIZE" in os.environ else "config2"
     sharded = args.workload == "sharded"
     if args.n is None:
         args.n = 5_200_000 if sharded else 500_000
     if args.nq is None:
         args.nq = 10_000 if sharded else 1000
     if args.impl == "reference":
-        run_reference(args)
+        run_reference_sharded(args) if sharded else run_reference(args)
     elif sharded:
         run_sharded(args)
     elif args.workload == "lowbatch":

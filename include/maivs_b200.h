@@ -115,11 +115,20 @@ int maivs_device_flags(maivs_index* ix, void* stream, uint32_t* flags);
  *    MAIVS_BAD_STATE;
  *  - more than 64 queries, or a search whose buffers (about nq x nprobe x 1 KiB for 128-member
  *    cells) exceed 32 MiB, is rejected with MAIVS_BAD_ARG and a message giving the size;
- *  - the first call on a device looks the array's address up (a CUDA runtime call), so make
- *    that call before capturing the stream into a graph.
+ *  - the first call on a device looks the array's address up (a CUDA runtime call; under CUDA's
+ *    lazy module loading that is also when the 32 MiB are reserved on that device), so make that
+ *    call before capturing the stream into a graph. The address is kept per device ordinal: after
+ *    a context reset (cudaDeviceReset) the next call does not look it up again, so a caller that
+ *    resets a device must not use this entry point on it afterwards;
+ *  - after the work completes, read maivs_device_flags(ix, stream, &f): non-zero means this
+ *    call's ids and scores are invalid. Either a routing shortlist was longer than 16,384 cells
+ *    (only with nprobe above 8,192: lower nprobe) or a bounded wait of the rerank ran out (the
+ *    call may be repeated). Unlike maivs_search_batch_device, repeating the call enlarges
+ *    nothing here; the array's size is fixed.
  * All calls, from every handle, share the one array. Nothing in it needs to start at zero, but
  * calls whose work overlaps on the GPU race on it: issue them on one stream or one at a time.
- * Results match maivs_search_batch_device(..., cell_major = 0, ...) exactly. */
+ * For every request it accepts, the results match maivs_search_batch_device(..., cell_major = 0,
+ * ...) exactly. */
 int maivs_search_batch_device_noalloc(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
                                       float target_confidence, float beta, uint64_t* d_ids, float* d_scores,
                                       void* stream);

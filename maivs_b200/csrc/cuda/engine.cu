@@ -372,6 +372,8 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
+        b.gtau = bp.take<uint32_t>(nq);
+        b.lad = bp.take<uint32_t>((size_t)nq * dev::kLadStride);
         rsc = bp.take<float>((size_t)nq * cand_cap);
         ritem = bp.take<uint32_t>((size_t)nq + 1);
     };

@@ -323,6 +323,155 @@ __device__ uint32_t block_select_d(const uint64_t* a, int na, const uint64_t* b,
     return v;
 }
 
+// ---- the rest scan's falling cut-off (index.rs:2231-2275) ----------------------------------------
+// The reference scans the rest cells against a per-query cut-off shared by its workers: a worker
+// holding `target` entries of a query publishes their target-th smallest distance with
+// AtomicU32::fetch_min (index.rs:2266-2269) and later cells are tested against the lower value.
+// Here one CTA scans one cell for all its queries and never holds `target` entries of one query, so
+// the lower bound is proven by counting. For each query k_seed sets rungs e_0 > e_1 > ... below the
+// seed cut-off tau, with s_l = the query's seed survivors at or below e_l; the scans count the
+// canonical rest survivors at or below each rung (c_l), and once s_l + c_l >= target there are
+// `target` distinct entries at or below e_l, so the exact target-th smallest distance is at most
+// e_l and atomicMin lowers the query's cut-off gtau[q] to it. Entries above gtau can no longer be
+// in the exact cut of k_final_cm (ties at the cut are kept, as before), so the result is unchanged
+// while fewer entries are appended. Rungs sit near ranks m (3/4)^(l+1), m = min(seed survivors,
+// target), rounded up to the edge of a 256-bin histogram over [lowest seed distance, tau].
+
+// Writes the rungs of one query from its seed entries (keys[0..n), only d <= tau counted): per
+// rung its distance, the count still needed (target - s_l, 0 when the seed alone has target) and a
+// zeroed counter. All threads of the block call it; `hist` is 256 shared words.
+__device__ void build_ladder(const uint64_t* keys, int n, uint32_t tau, int target, uint32_t* lad,
+                             uint32_t* hist) {
+    __shared__ uint32_t s_lo, s_cnt;
+    __shared__ uint32_t s_bin[kLad];
+    __shared__ int s_rem[kLad];
+    uint32_t lo = 0xFFFFFFFFu, cnt = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t d = (uint32_t)(keys[i] >> 32);
+        if (d <= tau) {
+            lo = min(lo, d);
+            ++cnt;
+        }
+    }
+    lo = __reduce_min_sync(0xFFFFFFFFu, lo);
+    cnt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+    if (threadIdx.x == 0) {
+        s_lo = 0xFFFFFFFFu;
+        s_cnt = 0;
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(&s_lo, lo);
+        atomicAdd(&s_cnt, cnt);
+    }
+    __syncthreads();
+    lo = s_lo;
+    const int m = (int)s_cnt;
+    if (m == 0) {  // no seed survivors: the rungs can never be proven
+        if (threadIdx.x < kLad) {
+            lad[threadIdx.x] = 0;
+            lad[kLad + threadIdx.x] = 0xFFFFFFFFu;
+            lad[2 * kLad + threadIdx.x] = 0;
+        }
+        __syncthreads();
+        return;
+    }
+    int sh = 0;
+    while (((tau - lo) >> sh) > 255u) ++sh;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t d = (uint32_t)(keys[i] >> 32);
+        if (d <= tau) atomicAdd(&hist[(d - lo) >> sh], 1u);
+    }
+    __syncthreads();
+    const int mm = min(m, target);
+    if (threadIdx.x < 32) {  // one warp scan of the bins serves every rung
+        const int lane = threadIdx.x;
+        int local = 0;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) local += (int)hist[lane * 8 + t];
+        int inc = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+            if (lane >= o) inc += v;
+        }
+        const int excl = inc - local;
+        int r = mm;
+        for (int l = 0; l < kLad; ++l) {
+            r = max((r * 3) >> 2, 1);
+            const unsigned hit = __ballot_sync(0xFFFFFFFFu, excl < r && inc >= r);
+            if (lane == (hit ? __ffs(hit) - 1 : 31)) {
+                int rr = r - excl, bin = lane * 8 + 7;
+                for (int t = 0; t < 8; ++t) {
+                    const int hv = (int)hist[lane * 8 + t];
+                    if (hv >= rr) {
+                        bin = lane * 8 + t;
+                        break;
+                    }
+                    rr -= hv;
+                }
+                s_bin[l] = (uint32_t)bin;
+                s_rem[l] = rr;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < kLad) {
+        const int l = threadIdx.x;
+        int r = mm;
+        for (int t = 0; t <= l; ++t) r = max((r * 3) >> 2, 1);
+        const uint32_t bin = s_bin[l];
+        const uint32_t below = (uint32_t)(r - s_rem[l]) + hist[bin];  // seed survivors in bins <= bin
+        const uint32_t e = min(lo + (bin << sh) + ((1u << sh) - 1u), tau);
+        lad[l] = e;
+        lad[kLad + l] = below >= (uint32_t)target ? 0u : (uint32_t)target - below;
+        lad[2 * kLad + l] = 0;
+    }
+    __syncthreads();
+}
+
+// Adds a tile's counts (two u16 per word, zeroed here) to query q's rungs and lowers its cut-off
+// to the lowest rung proven. Loads and atomics are independent so that they overlap.
+__device__ __forceinline__ void ladder_flush(const CellMajorBufs& b, uint32_t q, uint32_t* packed) {
+    uint32_t v[kLad];
+    bool any = false;
+#pragma unroll
+    for (int w = 0; w < kLad / 2; ++w) {
+        const uint32_t pair = packed[w];
+        packed[w] = 0;
+        v[2 * w] = pair & 0xFFFFu;
+        v[2 * w + 1] = pair >> 16;
+        any |= pair != 0;
+    }
+    if (!any) return;
+    uint32_t* lq = b.lad + (size_t)q * kLadStride;
+    const uint32_t g = *reinterpret_cast<volatile const uint32_t*>(b.gtau + q);
+    uint32_t e[kLad], need[kLad], old[kLad];
+#pragma unroll
+    for (int l = 0; l < kLad; ++l) {
+        e[l] = lq[l];
+        need[l] = lq[kLad + l];
+    }
+#pragma unroll
+    for (int l = 0; l < kLad; ++l) old[l] = (v[l] && e[l] < g) ? atomicAdd(lq + 2 * kLad + l, v[l]) : 0u;
+    uint32_t best = g;
+#pragma unroll
+    for (int l = 0; l < kLad; ++l)
+        if (v[l] && e[l] < g && old[l] + v[l] >= need[l]) best = min(best, e[l]);
+    if (best < g) atomicMin(b.gtau + q, best);
+}
+
+// Adds v rest survivors at or below rung l of query q; lowers the query's cut-off once the rung is
+// proven. Skips rungs at or above the current cut-off.
+__device__ __forceinline__ void ladder_add(const CellMajorBufs& b, uint32_t q, int l, uint32_t v) {
+    uint32_t* lq = b.lad + (size_t)q * kLadStride;
+    const uint32_t e = lq[l];
+    if (e >= *reinterpret_cast<volatile const uint32_t*>(b.gtau + q)) return;
+    const uint32_t old = atomicAdd(lq + 2 * kLad + l, v);
+    if (old + v >= lq[kLad + l]) atomicMin(b.gtau + q, e);
+}
+
 // Bitonic sort, ascending, of P (power of two) 64-bit keys in shared memory.
 __device__ void block_bitonic_u64(uint64_t* keys, int P) {
     for (int k = 2; k <= P; k <<= 1) {
@@ -1542,8 +1691,10 @@ __global__ void __launch_bounds__(kBS) k_seed(IndexView ix, QueryEnc e, const ui
         __syncthreads();
         rest_end = s_last >= 0 ? s_last + 1 : ns;
     }
+    if (rest_end > ns) build_ladder(sbuf, n, tau, target, b.lad + (size_t)q * kLadStride, hist);
     if (threadIdx.x == 0) {
         b.tau[q] = tau;
+        b.gtau[q] = tau;
         b.seed_n[q] = (uint32_t)n;
         b.rest_hi[q] = (uint32_t)rest_end;
         b.rest_n[q] = 0;
@@ -1610,8 +1761,12 @@ __global__ void __launch_bounds__(kBS) k_seed_finish(IndexView ix, QueryEnc e, c
         __syncthreads();
         rest_end = s_last >= 0 ? s_last + 1 : ns;
     }
+    // the rungs count this shard's seed survivors only: fewer than the global ones, so a rung this
+    // shard proves with them and its own rest survivors holds for the union too
+    if (rest_end > ns) build_ladder(sbuf, n, tau, target, b.lad + (size_t)q * kLadStride, hist);
     if (threadIdx.x == 0) {
         b.tau[q] = tau;
+        b.gtau[q] = tau;
         b.seed_n[q] = (uint32_t)n;
         b.rest_hi[q] = (uint32_t)rest_end;
         b.rest_n[q] = 0;
@@ -1680,8 +1835,9 @@ __global__ void k_inv_scatter(const uint32_t* __restrict__ chosen, const uint32_
 
 // ---- cell-major: the scan (index.rs:2231-2275) ------------------------------------------------------
 // One CTA per cell; each warp scores one interested query against 32 member groups (256 members)
-// at a time. A member survives when its distance is within the query's seed cut-off tau, which is
-// a valid bound on the final cut (index.rs:2266-2269), and it is canonical.
+// at a time. A member survives when its distance is within the query's falling cut-off gtau (at
+// most the seed cut-off tau, always at least the exact final cut, index.rs:2266-2269) and it is
+// canonical. Each warp counts its survivors under the query's rungs and proves rungs as it goes.
 
 __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const uint32_t* __restrict__ start,
                                                  const uint32_t* __restrict__ qof, CellMajorBufs b, uint32_t max_q) {
@@ -1701,9 +1857,15 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
         const bool act = g < ng;
         for (uint32_t qi = s0 + warp; qi < s1; qi += nwarps) {
             const uint32_t q = qof[qi];
-            const uint32_t t = b.tau[q];
+            const uint32_t t = *reinterpret_cast<volatile const uint32_t*>(b.gtau + q);
+            const uint32_t rung = lane < kLad ? b.lad[(size_t)q * kLadStride + lane] : 0u;  // lane l: e_l
+            uint32_t el[kLad];
+#pragma unroll
+            for (int l = 0; l < kLad; ++l) el[l] = __shfl_sync(0xFFFFFFFFu, rung, l);
             uint32_t acc[4];
             group_sums(codes, ng, g, act, e.lut + (size_t)q * npos * 16, npos, acc);
+            uint32_t below[kLad] = {0, 0, 0, 0, 0, 0, 0, 0};
+            bool any = false;
 #pragma unroll
             for (int bb = 0; bb < 8; ++bb) {
                 const int pos = 8 * g + bb;
@@ -1722,6 +1884,18 @@ __global__ void __launch_bounds__(kBS) k_scan_cm(IndexView ix, QueryEnc e, const
                 }
                 uint32_t p = warp_append(valid, &b.rest_n[q]);
                 if (valid && p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)q * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
+                if (valid) {
+                    any = true;
+#pragma unroll
+                    for (int l = 0; l < kLad; ++l) below[l] += (el[l] < t && d <= el[l]) ? 1u : 0u;
+                }
+            }
+            if (__any_sync(0xFFFFFFFFu, any)) {
+#pragma unroll
+                for (int l = 0; l < kLad; ++l) {
+                    const uint32_t v = __reduce_add_sync(0xFFFFFFFFu, below[l]);
+                    if (lane == l && v) ladder_add(b, q, l, v);
+                }
             }
         }
     }
@@ -1760,6 +1934,8 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
     __shared__ uint32_t s_tmem;
     __shared__ uint32_t s_q[kMmaQ];
     __shared__ uint32_t s_hit[8][kHitCap];
+    __shared__ uint32_t s_lc[kMmaQ][kLad / 2];  // per row: survivors under each rung, two u16 per word
+    __shared__ uint8_t s_r0[kMmaQ];             // per row: the first rung below its cut-off
     const uint32_t sbase = umma::smem_addr(mraw);
     uint8_t* tiles = mraw + (((sbase + 1023u) & ~1023u) - sbase);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1767,6 +1943,7 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
     const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
     const uint32_t maxk = ix.maxk;
     if (warp == 0) umma::tmem_alloc(&s_tmem, kMmaTmemCols);
+    for (int i = tid; i < kMmaQ * (kLad / 2); i += 256) (&s_lc[0][0])[i] = 0;
     if (tid == 0) {
         umma::bar_init(&bar[0], 1);
         umma::bar_init(&bar[1], 1);
@@ -1855,14 +2032,21 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
             }
             if (!ok) break;
             // epilogue: wait for the tile's last chunk, then every warp reads 32 queries x 128 members
+            const int lq = warp & 3, half = warp >> 2;
+            const int r = 32 * lq + lane;
+            const bool vq = r < nq_t;
+            const uint32_t t = vq ? *reinterpret_cast<volatile const uint32_t*>(b.gtau + s_q[r]) : 0u;
+            if (vq && half == 0) {  // rungs at or above the cut-off are proven already: skip them
+                const uint32_t* eq = b.lad + (size_t)s_q[r] * kLadStride;
+                int r0 = 0;
+#pragma unroll
+                for (int l = 0; l < kLad; ++l) r0 += __ldg(eq + l) >= t ? 1 : 0;  // rungs descend
+                s_r0[r] = (uint8_t)r0;
+            }
             ok = umma::bar_wait(&bar[(it - 1) & 1], ((it - 1) >> 1) & 1);
             ok = __syncthreads_and(ok);
             if (!ok) break;
             umma::fence_after_sync();
-            const int lq = warp & 3, half = warp >> 2;
-            const int r = 32 * lq + lane;
-            const bool vq = r < nq_t;
-            const uint32_t t = vq ? b.tau[s_q[r]] : 0u;
             // Survivors (row, member, d) of the warp's 32 rows x 128 members are collected in its
             // shared list and resolved by all 32 lanes together: one chain of dependent loads
             // (slot, lower home, probed bit, counter) per batch instead of one per thread and block.
@@ -1884,6 +2068,9 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
                     if (keep) {
                         const uint32_t p = atomicAdd(&b.rest_n[qq], 1u);
                         if (p < (uint32_t)b.rest_cap) b.rest_buf[(size_t)qq * b.rest_cap + p] = ((uint64_t)d << 32) | slot;
+                        const uint32_t* eq = b.lad + (size_t)qq * kLadStride;
+                        for (int l = s_r0[rr]; l < kLad && d <= __ldg(eq + l); ++l)
+                            atomicAdd(&s_lc[rr][l >> 1], 1u << (16 * (l & 1)));
                     }
                 }
                 __syncwarp();
@@ -1924,6 +2111,10 @@ __global__ void __launch_bounds__(256) k_scan_mma(IndexView ix, QueryEnc e, cons
             }
             resolve(cur);
             umma::fence_before_sync();
+            // the tile's survivors under each rung go to the queries' counters (at most 256 per row
+            // and rung, so two u16 counts share a word)
+            __syncthreads();
+            if (tid < nq_t) ladder_flush(b, s_q[tid], s_lc[tid]);
         }
     }
     if (!ok) {
@@ -2822,7 +3013,8 @@ __global__ void __launch_bounds__(256, 1) k_rerank_stream(RowSrc src, const uint
     }
     if (st < s1) {  // a wait ran out: report, then let the copies in flight land before leaving
         if (tid == 0) atomicAdd(err, 1u);
-        for (uint32_t t = st + 1; t < issued; ++t) umma::bar_wait(&full[(t - s0) % kS], ((t - s0) / kS) & 1u);
+        // from stage st itself: its copies may still be in flight (a completed phase returns at once)
+        for (uint32_t t = st; t < issued; ++t) umma::bar_wait(&full[(t - s0) % kS], ((t - s0) / kS) & 1u);
     }
 }
 
@@ -3013,7 +3205,7 @@ const char* kernel_name(int id) {
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
                                              "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
                                              "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma",
-                                             "k_seed_scan"};
+                                             "k_seed_scan", "nccl_all_gather"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 
@@ -3059,6 +3251,12 @@ void KernelClock::collect() {
 }
 
 void set_thread_clock(KernelClock* c) { t_clock = c; }
+void clock_begin(int id, cudaStream_t st) {
+    if (t_clock && t_clock->wants(id)) t_clock->begin(id, st);
+}
+void clock_end(int id, cudaStream_t st) {
+    if (t_clock && t_clock->wants(id)) t_clock->end(st);
+}
 unsigned long long total_launches() { return g_launches.load(); }
 
 // The 48 KiB default covers static plus dynamic shared memory, so any dynamic request opts in to

@@ -58,9 +58,13 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kKScanMma, kKSeedScan, kNumKernels
+    kKScanMma, kKSeedScan, kKAllGather, kNumKernels
 };
 const char* kernel_name(int id);
+// Brackets a step that is not one of this library's kernels (an NCCL collective) on the thread's
+// clock, when one is installed; it is timed but not counted as a launch.
+void clock_begin(int id, cudaStream_t st);
+void clock_end(int id, cudaStream_t st);
 struct KernelClock {
     struct Mark {
         int id;
@@ -141,7 +145,13 @@ struct CellMajorBufs {
     int cand_cap;
     uint32_t* cand_n;     // nq
     uint32_t* overflow;   // 1: queries whose buffers overflowed
+    uint32_t* gtau;       // nq: the rest scan's falling cut-off (starts at tau)
+    uint32_t* lad;        // nq x kLadStride: rungs below tau, seed shortfalls, rest counts
 };
+// Rungs of the falling cut-off per query (see k_seed): 8 rungs at about (3/4)^(l+1) of the seed
+// survivors' rank, then as many "needed" counts and as many running counters.
+constexpr int kLad = 8;
+constexpr int kLadStride = 3 * kLad;
 void launch_cellmajor(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
                       const uint32_t* nch, int nprobe, int target, bool adaptive, float at_margin,
                       const CellMajorBufs& b, cudaStream_t st);

@@ -247,6 +247,8 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         b.cand = bp.take<uint32_t>((size_t)nq * cand_cap);
         b.cand_n = bp.take<uint32_t>(nq);
         b.overflow = d_flags_;
+        b.gtau = bp.take<uint32_t>(nq);
+        b.lad = bp.take<uint32_t>((size_t)nq * dev::kLadStride);
         r.rsc = bp.take<float>((size_t)nq * cand_cap);
         r.ritem = bp.take<uint32_t>((size_t)nq + 1);
         r.xsend = bp.take<uint8_t>(r.lb);
@@ -334,22 +336,29 @@ int DeviceIndex::search_sharded(const HostIndex& h, const float* dQ, const Searc
     ShardRun r;
     int rc = shard_begin(h, dQ, a, shard_world_, shard_rank_, st, r, err);
     if (rc != kOk) return rc;
+    // every exchange is an NCCL all-gather on the search stream, timed as one step on the clock
+    auto gather = [&](const void* src, void* dst, size_t bytes) {
+        dev::clock_begin(dev::kKAllGather, st);
+        int g = exch_->all_gather(src, dst, bytes, st, err);
+        dev::clock_end(dev::kKAllGather, st);
+        return g;
+    };
     // probe lists: in-place all-gathers of each rank's block of rows
     const size_t rows = (size_t)r.qb * r.nprobe;
-    rc = exch_->all_gather(r.chosen + (size_t)r.rank * rows, r.chosen, rows * 4, st, err);
-    if (rc == kOk) rc = exch_->all_gather(r.cscore + (size_t)r.rank * rows, r.cscore, rows * 4, st, err);
-    if (rc == kOk) rc = exch_->all_gather(r.nch + (size_t)r.rank * r.qb, r.nch, (size_t)r.qb * 4, st, err);
+    rc = gather(r.chosen + (size_t)r.rank * rows, r.chosen, rows * 4);
+    if (rc == kOk) rc = gather(r.cscore + (size_t)r.rank * rows, r.cscore, rows * 4);
+    if (rc == kOk) rc = gather(r.nch + (size_t)r.rank * r.qb, r.nch, (size_t)r.qb * 4);
     if (rc != kOk) return rc;
     shard_seed(h, r);
-    rc = exch_->all_gather(r.xsend, r.xrecv, r.lb, st, err);
+    rc = gather(r.xsend, r.xrecv, r.lb);
     if (rc != kOk) return rc;
     shard_after_seed(h, r);
     if (r.rest) {
-        rc = exch_->all_gather(r.xsend, r.xrecv, r.lb, st, err);
+        rc = gather(r.xsend, r.xrecv, r.lb);
         if (rc != kOk) return rc;
     }
     shard_after_cut(h, r);
-    rc = exch_->all_gather(r.tsend, r.trecv, r.tb, st, err);
+    rc = gather(r.tsend, r.trecv, r.tb);
     if (rc != kOk) return rc;
     shard_merge(r, d_ids, d_scores, d_nout);
     return kOk;

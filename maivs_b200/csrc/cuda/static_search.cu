@@ -5,11 +5,15 @@
 // of the device), or a latency-critical serving loop that must not pay cudaMalloc's implicit
 // device-wide synchronisation and unpredictable latency. For them this file runs the per-query
 // search pipeline (the same kernels as search_batch with cell_major = false) with all of its
-// scratch carved from one file-scope device array of kStaticScratchBytes. Every GPU that loads
-// the library holds that array until the process exits.
+// scratch carved from one file-scope device array of kStaticScratchBytes. A GPU holds that array
+// from the first allocation-free call made on it (under CUDA's lazy module loading the module,
+// and with it the array, is loaded on that device when the first call looks the address up)
+// until the process exits.
 //
 // The array's address is fetched with cudaGetSymbolAddress once per device, on the first call
-// made with that device current (so that first call should come before any stream capture).
+// made with that device current (so that first call should come before any stream capture). The
+// address is cached per device ordinal, so a device whose context is reset must not serve this
+// path again in the same process.
 // All calls share the array and it keeps the previous call's contents; no part of it has to
 // start at zero (every kernel writes what it later reads), but two calls whose work overlaps on
 // the GPU race on it, so a caller must serialise them (one stream, or one call at a time).

@@ -96,6 +96,8 @@ def lib() -> C.CDLL:
         L.oracle_build_add.restype = C.c_int
         L.oracle_build_add.argtypes = [vp, vp, vp, u64]
         L.oracle_build_compact.argtypes = [vp]
+        L.oracle_build_take_index.restype = vp
+        L.oracle_build_take_index.argtypes = [vp]
         L.oracle_build_export.argtypes = [vp]
         L.oracle_build_array.restype = C.c_int
         L.oracle_build_array.argtypes = [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64), C.POINTER(u64)]
@@ -386,6 +388,15 @@ class OracleBuild:
 
     def index(self) -> "OracleIndex":
         return OracleIndex.from_build(self)
+
+    def take_index(self) -> "OracleIndex":
+        """The searchable index, moving the build's large arrays into it (no copies; the build
+        cannot export or be searched afterwards). For large builds."""
+        o = OracleIndex.__new__(OracleIndex)
+        o.a = {}
+        o.h = lib().oracle_build_take_index(self.h)
+        self._exported = False
+        return o
 
 
 def build_preset(X: np.ndarray, preset: str = "quality", rerank_factor: int = 16, ids=None,

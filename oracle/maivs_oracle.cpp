@@ -2034,6 +2034,70 @@ int oracle_build_add(void* p, const uint64_t* ids, const float* data, uint64_t n
 
 void oracle_build_compact(void* p) { build_compact(static_cast<OBuildHandle*>(p)->b); }
 
+// The searchable index straight from a finished build, moving the large arrays instead of copying
+// them (the build handle keeps its configuration but no longer its arena). Same contents as
+// oracle_index_new over the exported arrays.
+void* oracle_build_take_index(void* p) {
+    OBuild& b = static_cast<OBuildHandle*>(p)->b;
+    auto* ix = new OIndex();
+    ix->dim = b.dim;
+    ix->dim_pad = b.dim_pad;
+    ix->nw = b.nw;
+    ix->M = b.cells.size();
+    ix->ma = b.max_assign;
+    ix->n_slots = b.ext_ids.size();
+    ix->signs = b.signs;
+    ix->mem_off.push_back(0);
+    for (auto& c : b.cells) {
+        ix->centroids.insert(ix->centroids.end(), c.centroid.begin(), c.centroid.end());
+        ix->r_bound.push_back(c.r_bound);
+        ix->mem.insert(ix->mem.end(), c.members.begin(), c.members.end());
+        ix->mem_off.push_back((uint32_t)ix->mem.size());
+    }
+    ix->fs_codes = std::move(b.fs_codes);
+    ix->fs_off = std::move(b.fs_off);
+    ix->slot_cells = std::move(b.slot_cells);
+    ix->ext_ids = std::move(b.ext_ids);
+    ix->cent_bits = b.cent_bits;
+    ix->cent_sq8 = b.cent_sq8;
+    if (!b.cent_sq8.empty()) {
+        ix->csq_min = b.csq_min;
+        ix->csq_step = b.csq_step;
+    }
+    ix->vecs_f32 = std::move(b.vecs_f32);
+    ix->scan_i8 = std::move(b.scan_i8);
+    ix->sq_min = b.sq_min;
+    ix->sq_step = b.sq_step;
+    ix->rerank_factor = b.rerank_factor;
+    ix->two_stage = b.two_stage;
+    ix->shortlist_mult = b.shortlist_mult;
+    ix->centroid_sq8 = b.centroid_sq8;
+    ix->has_tree = b.has_tree;
+    ix->fastscan = b.fastscan;
+    ix->per_dim_sq = b.per_dim_sq;
+    ix->i8_rerank = b.i8_rerank;
+    ix->adaptive = b.adaptive;
+    ix->at_margin = b.at_margin;
+    ix->compacted = b.compacted;
+    ix->n_live = b.n_live;
+    ix->cm_min_batch = b.cm_min_batch;
+    ix->has_filter = false;
+    ix->flo = 0;
+    ix->fhi = 0xFFFFFFFFu;
+    ix->beam_frac = b.has_tree ? b.tree_bf : 0.0f;
+    ix->n_leaf = b.has_tree ? b.leaf_ids.size() : 0;
+    ix->graph_route = b.graph_route;
+    ix->graph_min_cells = b.graph_min_cells;
+    if (b.has_tree) {
+        ix->levels = b.tview.levels;
+        ix->leaf_codes = b.leaf_codes;
+        ix->leaf_ids = b.leaf_ids;
+    }
+    b.bits.clear();
+    b.bits.shrink_to_fit();
+    return ix;
+}
+
 // Snapshot of every array (call after the build steps), then one array by name.
 void oracle_build_export(void* p) { bexport(static_cast<OBuildHandle*>(p)); }
 

@@ -103,3 +103,17 @@ def test_load_rejects_bad_files(tmp_path):
         M.FlatCellIndex.load(str(p))
     with pytest.raises(ValueError):
         M.FlatCellIndex.load(str(tmp_path / "missing"))
+
+
+def test_loaded_index_has_the_saved_arrays(saved):
+    """Load rebuilds the derived state (centroid codes, SQ8 centroids, radii, tree) as the reference
+    does (persist.rs:279); after compact() every array the GPU reads equals the saved index's."""
+    ix, _, path = saved
+    ld = M.FlatCellIndex.load(path)
+    ld.set_fastscan(True)
+    ld.compact()
+    for name in oracle.OracleIndex.NAMES:
+        a, b = ix.array(name), ld.array(name)
+        if name == "config":
+            continue
+        assert a.shape == b.shape and np.array_equal(a.view(np.uint8), b.view(np.uint8)), name

@@ -113,3 +113,57 @@ def test_rejects_requests_beyond_the_scratch():
     rc = _noalloc(ix, dq.data_ptr(), 4, K, 8, ids.data_ptr(), sc.data_ptr(), 0)
     assert rc == _lib.OK, _error(ix)
     torch.cuda.synchronize()
+
+
+@pytest.mark.gpu
+def test_allocates_nothing_across_calls(built):
+    """Free device memory is the same before and after repeated calls once the first call has set
+    the array up (the ordinary device search would have grown its workspace here)."""
+    import torch
+
+    ix, Q = built
+    ix.to_device(0)
+    dq = torch.from_numpy(np.ascontiguousarray(Q[:64])).cuda()
+    ids = torch.empty(64 * K, dtype=torch.int64, device="cuda")
+    sc = torch.empty(64 * K, dtype=torch.float32, device="cuda")
+    assert _noalloc(ix, dq.data_ptr(), 64, K, 16, ids.data_ptr(), sc.data_ptr(), 0) == _lib.OK, _error(ix)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for nprobe in (8, 16, 32, 8):
+        assert _noalloc(ix, dq.data_ptr(), 64, K, nprobe, ids.data_ptr(), sc.data_ptr(), 0) == _lib.OK, _error(ix)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert ix.device_flags(0) == 0
+
+
+@pytest.mark.gpu
+def test_flags_report_a_shortlist_beyond_the_sort_limit():
+    """A routing shortlist longer than 16,384 cells cannot be ordered; the call still returns OK
+    (the work is only enqueued) and the caller learns it from the device flags."""
+    import maivs_b200 as M
+    import torch
+
+    rng = np.random.default_rng(11)
+    d = 64
+    cents = rng.standard_normal((20_000, d)).astype(np.float32)
+    cents /= np.linalg.norm(cents, axis=1, keepdims=True)
+    X = cents[rng.integers(0, len(cents), 40_000)] + 0.02 * rng.standard_normal((40_000, d)).astype(np.float32)
+    X = np.ascontiguousarray((X / np.linalg.norm(X, axis=1, keepdims=True)).astype(np.float32))
+    ix = M.FlatCellIndex(d, "binary", 4, 0x5EED, 0)
+    ix.set_fastscan(True)
+    ix.set_graph_route(False, 10**9)
+    ix.set_centroids(cents)
+    ix.add_batch(list(range(len(X))), X)
+    ix.compact()
+    ix.to_device(0)
+    dq = torch.from_numpy(X[:1].copy()).cuda()
+    ids = torch.empty(K, dtype=torch.int64, device="cuda")
+    sc = torch.empty(K, dtype=torch.float32, device="cuda")
+    nprobe = 16_500  # the tree shortlist asks for 2 x nprobe cells: all live cells, above 16,384
+    assert _noalloc(ix, dq.data_ptr(), 1, K, nprobe, ids.data_ptr(), sc.data_ptr(), 0) == _lib.OK, _error(ix)
+    torch.cuda.synchronize()
+    assert ix.device_flags(0) != 0
+    # a request within the limits on the same handle comes back clean
+    assert _noalloc(ix, dq.data_ptr(), 1, K, 64, ids.data_ptr(), sc.data_ptr(), 0) == _lib.OK, _error(ix)
+    torch.cuda.synchronize()
+    assert ix.device_flags(0) == 0
