@@ -32,12 +32,18 @@ SOURCES = [
     ("host/index_build.cpp", "cxx"),
     ("host/persist.cpp", "cxx"),
     ("capi.cpp", "cxx"),
-    ("cuda/kernels.cu", "nvcc"),
+    ("cuda/clock.cu", "nvcc"),
+    ("cuda/k_route.cu", "nvcc"),
+    ("cuda/k_cellmajor.cu", "nvcc"),
+    ("cuda/k_scan_mma.cu", "nvcc"),
+    ("cuda/k_perquery.cu", "nvcc"),
+    ("cuda/k_rerank.cu", "nvcc"),
     ("cuda/engine.cu", "nvcc"),
     ("cuda/static_search.cu", "nvcc"),
     ("cuda/shard.cu", "nvcc"),
 ]
-HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/engine.h"]
+HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/dev_common.cuh",
+           "cuda/umma.cuh", "cuda/engine.h"]
 
 
 def _cmd(src: str, kind: str, obj: str) -> list[str]:

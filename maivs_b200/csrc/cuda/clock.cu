@@ -1,0 +1,106 @@
+// Per-kernel device clock, launch counter and first-launch-error record of the query kernels.
+#include <atomic>
+
+#include "dev_common.cuh"
+
+namespace maivs {
+namespace dev {
+
+namespace {
+thread_local KernelClock* t_clock = nullptr;
+thread_local cudaError_t t_launch_err = cudaSuccess;
+thread_local int t_launch_err_kernel = -1;
+std::atomic<unsigned long long> g_launches{0};
+
+}  // namespace
+
+bool tick_begin(int id, cudaStream_t st) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const bool timed = t_clock && t_clock->wants(id);
+    if (timed) t_clock->begin(id, st);
+    return timed;
+}
+
+void tick_end(int id, cudaStream_t st, bool timed) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && t_launch_err == cudaSuccess) {
+        t_launch_err = e;
+        t_launch_err_kernel = id;
+    }
+    if (timed) t_clock->end(st);
+}
+
+cudaError_t take_launch_error(int* kernel) {
+    cudaError_t e = t_launch_err;
+    if (kernel) *kernel = t_launch_err_kernel;
+    t_launch_err = cudaSuccess;
+    t_launch_err_kernel = -1;
+    return e;
+}
+
+const char* kernel_name(int id) {
+    static const char* names[kNumKernels] = {"k_encode", "k_route_flat", "k_route_tree", "k_rescore_select",
+                                             "k_seed",   "k_inv_count",  "k_inv_scan",   "k_inv_scatter",
+                                             "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
+                                             "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
+                                             "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma",
+                                             "k_seed_scan", "nccl_all_gather"};
+    return id >= 0 && id < kNumKernels ? names[id] : "?";
+}
+
+KernelClock::~KernelClock() {
+    for (auto& m : pending) {
+        cudaEventDestroy(m.a);
+        cudaEventDestroy(m.b);
+    }
+    for (auto e : pool) cudaEventDestroy(e);
+}
+
+cudaEvent_t KernelClock::take() {
+    if (!pool.empty()) {
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void KernelClock::begin(int id, cudaStream_t st) {
+    Mark m{id, take(), take()};
+    cudaEventRecord(m.a, st);
+    pending.push_back(m);
+    launches[id] += 1;
+}
+
+void KernelClock::end(cudaStream_t st) {
+    if (!pending.empty()) cudaEventRecord(pending.back().b, st);
+}
+
+void KernelClock::collect() {
+    for (auto& m : pending) {
+        float t = 0.0f;
+        if (cudaEventSynchronize(m.b) == cudaSuccess && cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess)
+            ms[m.id] += t;
+        pool.push_back(m.a);
+        pool.push_back(m.b);
+    }
+    pending.clear();
+}
+
+void set_thread_clock(KernelClock* c) { t_clock = c; }
+void clock_begin(int id, cudaStream_t st) {
+    if (t_clock && t_clock->wants(id)) t_clock->begin(id, st);
+}
+void clock_end(int id, cudaStream_t st) {
+    if (t_clock && t_clock->wants(id)) t_clock->end(st);
+}
+unsigned long long total_launches() { return g_launches.load(); }
+
+void set_smem(const void* f, size_t bytes) {
+    if (bytes > 0) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace dev
+}  // namespace maivs

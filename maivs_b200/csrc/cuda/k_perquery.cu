@@ -1,0 +1,276 @@
+// The per-query path (index.rs search_one :1381-1864, FastScan branch): probe ranks, the scan of
+// every probed cell, and the sequential bucket queue with the adaptive stop.
+#include "dev_common.cuh"
+
+namespace maivs {
+namespace dev {
+
+namespace {
+
+// ---- per-query path (index.rs:1381-1864, FastScan branch) -------------------------------------------
+
+// Probe ranks and the entry segment of every chosen cell.
+__global__ void __launch_bounds__(kBS) k_pq_prep(IndexView ix, const uint32_t* __restrict__ chosen,
+                                                 const uint32_t* __restrict__ nch, int nprobe, PerQueryBufs b) {
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    __shared__ uint32_t s_run;
+    const int q = blockIdx.x, M = ix.M;
+    const int n = (int)nch[q];
+    uint32_t* crank = b.crank + (size_t)q * M;
+    for (int c = threadIdx.x; c < M; c += kBS) crank[c] = kNoCell;
+    if (threadIdx.x == 0) s_run = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kBS) crank[chosen[(size_t)q * nprobe + i]] = (uint32_t)i;
+    uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    for (int base = 0; base < n; base += kBS) {
+        int i = base + threadIdx.x;
+        uint32_t len = 0;
+        if (i < n) {
+            uint32_t c = chosen[(size_t)q * nprobe + i];
+            len = ix.cell_moff[c + 1] - ix.cell_moff[c];
+        }
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(len, pos, agg);
+        uint32_t run = s_run;
+        if (i < n) so[i] = run + pos;
+        __syncthreads();
+        if (threadIdx.x == 0) s_run = run + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) so[n] = s_run;
+}
+
+// Every member of every chosen cell: (d << 32 | slot) when canonical under the first-ranked-home
+// rule (index.rs:1443-1460) and inside the tag filter (index.rs:1430-1439), else kInvalidEntry.
+// One CTA per (probe, query). The query's FastScan table sits in shared memory; for each chunk of
+// 32 member groups (256 members) the 8 warps sum disjoint slices of the nibble positions and
+// combine their packed 16-bit partials in shared memory (exact: a member's total is at most
+// 255 x npos), then every thread resolves one member (slot, tag filter, the per-query exactly-once
+// rule against the probe ranks), so the members' dependent loads run side by side.
+__global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                 const uint32_t* __restrict__ nch, int nprobe, int filtering,
+                                                 uint32_t flo, uint32_t fhi, PerQueryBufs b) {
+    __shared__ __align__(16) uint8_t s_lut[16 * 16 * 16];  // npos <= 256 positions x 16 entries
+    __shared__ uint32_t s_part[kBS / 32][32][4];
+    const int r = blockIdx.x, q = blockIdx.y;
+    if (r >= (int)nch[q]) return;
+    const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    if (so[r + 1] > (uint32_t)b.ent_cap) return;  // reported by the fold
+    const uint32_t c = chosen[(size_t)q * nprobe + r];
+    const uint32_t moff = ix.cell_moff[c];
+    const int nc = (int)(ix.cell_moff[c + 1] - moff);
+    const int ng = (nc + 7) >> 3;
+    const uint32_t* codes = ix.cell_codes + ix.cell_woff[c];
+    const uint32_t* crank = b.crank + (size_t)q * ix.M;
+    uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
+    const int npos = ix.npos;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(e.lut + (size_t)q * npos * 16);
+        for (int i = threadIdx.x; i < npos; i += kBS) reinterpret_cast<uint4*>(s_lut)[i] = src[i];
+    }
+    __syncthreads();
+    // this warp's slice of the positions
+    const int p0 = (int)((long long)npos * warp / nwarps), p1 = (int)((long long)npos * (warp + 1) / nwarps);
+    for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        const bool act = g < ng;
+        uint32_t acc[4];
+        group_sums_range(codes, ng, g, act, s_lut, p0, p1, acc);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_part[warp][lane][i] = acc[i];
+        __syncthreads();
+        // thread t: member 8 * (g0 + t / 8) + t % 8 of this chunk
+        {
+            const int gl = threadIdx.x >> 3, bb = threadIdx.x & 7;
+            const int pos = 8 * (g0 + gl) + bb;
+            if (pos < nc) {
+                uint32_t tot = 0;
+#pragma unroll
+                for (int w = 0; w < nwarps; ++w) tot += s_part[w][gl][bb >> 1];
+                const uint32_t sum = (tot >> (16 * (bb & 1))) & 0xFFFFu;
+                const uint32_t d = ix.maxk - sum;
+                const uint32_t slot = __ldg(ix.cell_slots + moff + pos);
+                bool ok = true;
+                if (filtering) {
+                    const uint32_t tg = __ldg(ix.tags + slot);
+                    ok = tg >= flo && tg <= fhi;
+                }
+                if (ok && ix.ma > 1) {
+                    const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
+                    for (int j = 0; j < ix.ma; ++j) {
+                        const uint32_t h = __ldg(hs + j);
+                        if (h != kNoCell && h != c) {
+                            const uint32_t rh = __ldg(crank + h);
+                            if (rh != kNoCell && rh < (uint32_t)r) {
+                                ok = false;
+                                break;
+                            }
+                        }
+                    }
+                }
+                out[pos] = ok ? (((uint64_t)d << 32) | slot) : kInvalidEntry;
+            }
+        }
+        __syncthreads();  // s_part is rewritten by the next chunk
+    }
+}
+
+// The sequential part of the per-query scan: cells in probe order feed a bucket queue on d >> 6
+// with a falling cut-off tau, and the scan stops once no later cell can reach the current
+// want0-th best (index.rs:1630-1679). tau after any prefix of cells is the target-th smallest
+// bucket among that prefix's surviving entries, so whole cells are folded at once.
+__global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                 const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
+                                                 int nprobe, int target, int adaptive, float at_margin,
+                                                 PerQueryBufs b) {
+    extern __shared__ uint32_t sh[];
+    const int nb = (int)(ix.maxk >> 6) + 1;
+    uint32_t* hist = sh;              // nb buckets
+    float* suffix = reinterpret_cast<float*>(sh + nb);  // nprobe + 1
+    __shared__ uint32_t s_add, s_tau, s_stop, s_cnt;
+    __shared__ unsigned long long s_kept;
+    __shared__ uint32_t hist256[256];
+    const int q = blockIdx.x;
+    const int n = (int)nch[q];
+    const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    const uint64_t* ent = b.ent + (size_t)q * b.ent_cap;
+    if (so[n] > (uint32_t)b.ent_cap) {
+        if (threadIdx.x == 0) {
+            atomicAdd(b.overflow, 1u);
+            b.cand_n[q] = 0;
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < nb; i += kBS) hist[i] = 0;
+    if (adaptive) {
+        // suffix[i] = max bound over cells i..n-1 (index.rs:1467-1490)
+        for (int i = threadIdx.x; i < n; i += kBS)
+            suffix[i] = cell_bound(cscore[(size_t)q * nprobe + i], ix.r_bound[chosen[(size_t)q * nprobe + i]]);
+        if (threadIdx.x == 0) suffix[n] = -INFINITY;
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int i = n - 1; i >= 0; --i) suffix[i] = fmaxf(suffix[i], suffix[i + 1]);
+    }
+    if (threadIdx.x == 0) {
+        s_tau = ix.maxk >> 6;
+        s_kept = 0;
+        s_add = 0;
+        s_stop = (uint32_t)n;
+    }
+    __syncthreads();
+    const float norm = fs_norm(ix.dim_pad);
+    const float delta = e.fs_delta[q], bias = e.fs_bias[q];
+    for (int r = 0; r < n; ++r) {
+        const uint32_t tau = s_tau;
+        for (uint32_t i = so[r] + threadIdx.x; i < so[r + 1]; i += kBS) {
+            uint64_t k = ent[i];
+            if (k == kInvalidEntry) continue;
+            uint32_t hc = (uint32_t)(k >> 32) >> 6;
+            if (hc <= tau) {
+                atomicAdd(&hist[hc], 1u);
+                atomicAdd(&s_add, 1u);
+            }
+        }
+        __syncthreads();
+        // the falling cut-off: the smallest bucket t (not above the current one) whose prefix count
+        // still reaches target, i.e. the sequential walk down from tau done as one warp scan
+        if (threadIdx.x < 32) {
+            const unsigned long long kept0 = s_kept + s_add;
+            const uint32_t t0 = s_tau;
+            uint32_t t = t0;
+            unsigned long long kept = kept0;
+            if (kept0 >= (unsigned long long)target && t0 > 0) {
+                const int cut = warp_hist_cut(hist, (int)t0, (long long)target);
+                unsigned long long below = 0;  // prefix(cut), summed by the warp
+                for (int i = threadIdx.x; i <= cut; i += 32) below += hist[i];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) below += __shfl_xor_sync(0xFFFFFFFFu, below, o);
+                t = (uint32_t)cut;
+                kept = below;
+            }
+            if (threadIdx.x == 0) {
+                s_add = 0;
+                s_kept = kept;
+                s_tau = t;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned long long kept = s_kept;
+            const uint32_t t = s_tau;
+            if (adaptive && kept >= (unsigned long long)target) {
+                uint32_t wsub = ((t + 1) << 6) - 1;
+                uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
+                float thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+                if (suffix[r + 1] < __fsub_rn(thr, at_margin)) s_stop = (uint32_t)(r + 1);
+            }
+        }
+        __syncthreads();
+        if (s_stop != (uint32_t)n) break;
+    }
+    // candidates: entries of the scanned cells with bucket <= tau (index.rs:1680-1685)
+    const uint32_t tau = s_tau, end = so[s_stop];
+    uint64_t* keys = b.ent + (size_t)q * b.ent_cap;  // compacted in place (order-free)
+    using BS = cub::BlockScan<uint32_t, kBS>;
+    __shared__ typename BS::TempStorage scan;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (uint32_t base = 0; base < end; base += kBS) {
+        uint32_t i = base + threadIdx.x;
+        uint64_t k = i < end ? ent[i] : kInvalidEntry;
+        uint32_t f = (k != kInvalidEntry && ((uint32_t)(k >> 32) >> 6) <= tau) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        __syncthreads();
+        uint32_t off = s_cnt;
+        if (f) keys[off + pos] = k;
+        __syncthreads();
+        if (threadIdx.x == 0) s_cnt = off + agg;
+        __syncthreads();
+    }
+    const int cnt = (int)s_cnt;
+    // top want0 (= target) by d; ties at the cut broken by ascending slot (index.rs:1689-1691)
+    uint64_t K = ~0ull;
+    if (cnt > target) K = block_select_kth(keys, cnt, nullptr, 0, target, 5, 0, hist256);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    uint32_t* out = b.cand + (size_t)q * b.cand_cap;
+    for (int base = 0; base < cnt; base += kBS) {
+        int i = base + threadIdx.x;
+        uint64_t k = i < cnt ? keys[i] : ~0ull;
+        uint32_t f = (i < cnt && k <= K) ? 1u : 0u;
+        uint32_t pos, agg;
+        BS(scan).ExclusiveSum(f, pos, agg);
+        uint32_t off = s_cnt;
+        if (f && off + pos < (uint32_t)b.cand_cap) out[off + pos] = (uint32_t)k;
+        __syncthreads();
+        if (threadIdx.x == 0) s_cnt = off + agg;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) b.cand_n[q] = min(s_cnt, (uint32_t)b.cand_cap);
+}
+
+}  // namespace
+
+// ---- launchers ----------------------------------------------------------------------------------------
+
+void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint32_t* chosen, const float* cscore,
+                     const uint32_t* nch, int nprobe, int want0, bool adaptive, float at_margin, bool filtering,
+                     uint32_t flo, uint32_t fhi, const PerQueryBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    { Tick tk(kKPqPrep, st);
+    k_pq_prep<<<nq, kBS, 0, st>>>(ix, chosen, nch, nprobe, b); }
+    { Tick tk(kKPqScan, st);
+    k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b); }
+    int nb = (int)(ix.maxk >> 6) + 1;
+    size_t smem = (size_t)nb * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
+    set_smem((const void*)k_pq_fold, smem);
+    int target = std::max(want0, 1);
+    { Tick tk(kKPqFold, st);
+    k_pq_fold<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b); }
+}
+
+}  // namespace dev
+}  // namespace maivs
