@@ -374,6 +374,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
         b.overflow = d_flags_;
         b.gtau = bp.take<uint32_t>(nq);
         b.lad = bp.take<uint32_t>((size_t)nq * dev::kLadStride);
+        b.work = bp.take<uint32_t>(1);
         rsc = bp.take<float>((size_t)nq * cand_cap);
         ritem = bp.take<uint32_t>((size_t)nq + 1);
     };

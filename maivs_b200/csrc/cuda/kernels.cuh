@@ -147,6 +147,7 @@ struct CellMajorBufs {
     uint32_t* overflow;   // 1: queries whose buffers overflowed
     uint32_t* gtau;       // nq: the rest scan's falling cut-off (starts at tau)
     uint32_t* lad;        // nq x kLadStride: rungs below tau, seed shortfalls, rest counts
+    uint32_t* work;       // 1: the persistent tensor-core scan's cell counter
 };
 // Rungs of the falling cut-off per query (see k_seed): 8 rungs at about (3/4)^(l+1) of the seed
 // survivors' rank, then as many "needed" counts and as many running counters.

@@ -249,6 +249,7 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
         b.overflow = d_flags_;
         b.gtau = bp.take<uint32_t>(nq);
         b.lad = bp.take<uint32_t>((size_t)nq * dev::kLadStride);
+        b.work = bp.take<uint32_t>(1);
         r.rsc = bp.take<float>((size_t)nq * cand_cap);
         r.ritem = bp.take<uint32_t>((size_t)nq + 1);
         r.xsend = bp.take<uint8_t>(r.lb);
