@@ -73,6 +73,13 @@ int maivs_set_filter(maivs_index* ix, int has_filter, uint32_t lo, uint32_t hi);
  * index.rs:3348); default 32. */
 int maivs_set_cell_major_min_batch(maivs_index* ix, size_t n);
 
+/* Build device (no counterpart in the reference, which builds on its CPU threads): with
+ * device >= 0, train_centroids, add_batch and the centroid tree run their k-means and their
+ * vector placement on that GPU (exact-order dot products, so the index is the one the host build
+ * makes, array for array); -1 (the default) builds on the host cores. A build step the GPU could
+ * not run is computed on the host and counted in stats "build_gpu_failures". */
+int maivs_set_build_device(maivs_index* ix, int device);
+
 /* __len__ (index.rs:3474) */
 int maivs_len(const maivs_index* ix, size_t* n);
 /* One value of stats() (index.rs:3393-3472) by name, e.g. "n_cells", "tree_depth". */

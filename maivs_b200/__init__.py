@@ -165,6 +165,11 @@ class FlatCellIndex:
         """Smallest batch that takes the cell-major join (reference: 2 x its thread count)."""
         self._check(_lib.lib().maivs_set_cell_major_min_batch(self._h, int(n)))
 
+    def set_build_device(self, device: int | None) -> None:
+        """Run the build's k-means and vector placement on CUDA device `device` (None: the host
+        cores). The index built is the same either way, array for array."""
+        self._check(_lib.lib().maivs_set_build_device(self._h, -1 if device is None else int(device)))
+
     def to_device(self, device: int = 0) -> None:
         """Build the device image now on CUDA device `device` (search does it on first use)."""
         self._check(_lib.lib().maivs_to_device(self._h, int(device)))
@@ -342,7 +347,7 @@ class FlatCellIndex:
     _STATS = ("n_live", "n_cells", "free_slots", "quant_scale", "scan_bytes_per_vec", "cell_size_mean",
               "cell_size_max", "cell_size_min", "max_assign", "centroid_graph_nodes", "tree_depth",
               "tree_top_width", "tree_fanout", "tree_beam_frac", "replication_factor", "member_entries",
-              "total_bytes", "live_cells", "device_bytes")
+              "total_bytes", "live_cells", "device_bytes", "build_device", "build_gpu_failures")
 
     def stats(self) -> dict:
         out = {}

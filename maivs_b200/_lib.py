@@ -35,6 +35,7 @@ _SIGS = {
     "maivs_set_tags": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
     "maivs_set_filter": (C.c_int, [C.c_void_p, C.c_int, C.c_uint32, C.c_uint32]),
     "maivs_set_cell_major_min_batch": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "maivs_set_build_device": (C.c_int, [C.c_void_p, C.c_int]),
     "maivs_len": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
     "maivs_stat": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double)]),
     "maivs_to_device": (C.c_int, [C.c_void_p, C.c_int]),

@@ -41,6 +41,7 @@ SOURCES = [
     ("cuda/engine.cu", "nvcc"),
     ("cuda/static_search.cu", "nvcc"),
     ("cuda/shard.cu", "nvcc"),
+    ("cuda/build.cu", "nvcc"),
 ]
 HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/dev_common.cuh",
            "cuda/umma.cuh", "cuda/engine.h"]

@@ -341,6 +341,17 @@ int maivs_set_cell_major_min_batch(maivs_index* ix, size_t n) {
     return MAIVS_OK;
 }
 
+int maivs_set_build_device(maivs_index* ix, int device) {
+    LOCK(ix);
+    if (device >= 0) {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n)
+            return fail(ix, MAIVS_NO_DEVICE, "no CUDA device " + std::to_string(device) + " for the index build");
+    }
+    ix->h.build_device = device < 0 ? -1 : device;
+    return MAIVS_OK;
+}
+
 int maivs_len(const maivs_index* ix, size_t* n) {
     if (!ix || !n) return MAIVS_BAD_ARG;
     *n = ix->h.n_live;
@@ -378,6 +389,8 @@ int maivs_stat(maivs_index* ix, const char* name, double* value) {
     else if (s == "member_entries") *value = (double)entries;
     else if (s == "centroid_graph_nodes") *value = 0.0;
     else if (s == "device_bytes") *value = ix->d ? (double)ix->d->device_bytes() : 0.0;
+    else if (s == "build_device") *value = (double)h.build_device;
+    else if (s == "build_gpu_failures") *value = (double)h.build_gpu_failures;
     else if (s == "total_bytes") {
         size_t b = h.vecs_f32.size() * 4 + h.scan_i8.size() + h.bits.size() * 8 + h.ext_ids.size() * 8 +
                    h.slot_cell.size() * 4 + h.slot_cells.size() * 4 + h.tags.size() * 4 + entries * 4 +

@@ -66,7 +66,8 @@ std::string HostIndex::train_centroids(const float* data, size_t n_all, size_t n
         train.assign(data, data + n_all * dim);
         n_train = n_all;
     }
-    std::vector<float> cents = hierarchical_kmeans(train.data(), n_train, dim, n_cells, sd);
+    std::vector<float> cents = hierarchical_kmeans(train.data(), n_train, dim, n_cells, sd, build_device,
+                                                   &build_gpu_failures);
     size_t m = cents.size() / dim;
     for (size_t c = 0; c < m; ++c) normalize(cents.data() + c * dim, dim);
     cells.clear();
@@ -274,7 +275,7 @@ void HostIndex::rebuild_centroid_tree() {
     for (size_t i = 0; i < live.size(); ++i)
         std::copy(cells[live[i]].centroid.begin(), cells[live[i]].centroid.end(), flat.begin() + i * dim);
     tree = build_centroid_tree(flat.data(), live.data(), live.size(), dim, signs.data(), dim_pad, nw, tree_fanout,
-                               tree_beam_frac);
+                               tree_beam_frac, build_device, &build_gpu_failures);
 }
 
 void HostIndex::maybe_rebuild_centroid_tree() {
@@ -390,19 +391,22 @@ void HostIndex::encode_i8(const float* v, int8_t* out) const {
 }
 
 void HostIndex::append_parallel(const uint64_t* ids, const float* data, size_t n,
-                                const std::vector<std::vector<uint32_t>>& asg) {
+                                const std::vector<std::vector<uint32_t>>& asg, const uint64_t* codes) {
     // index.rs:2566-2667
     size_t base = ext_ids.size();
     bool store_i8 = i8_rerank;
     if (keep_f32) vecs_f32.insert(vecs_f32.end(), data, data + n * dim);
     bits.resize((base + n) * nw, 0);
+    if (codes) std::copy(codes, codes + n * nw, bits.begin() + base * nw);  // computed on the build GPU
+    if (!codes) {
 #pragma omp parallel
-    {
-        std::vector<float> rot(dim_pad);
+        {
+            std::vector<float> rot(dim_pad);
 #pragma omp for schedule(static)
-        for (long long i = 0; i < (long long)n; ++i) {
-            rotate(data + (size_t)i * dim, dim, signs.data(), dim_pad, rot.data());
-            pack_signs_trunc(rot.data(), dim_pad, &bits[(base + i) * nw], nw);
+            for (long long i = 0; i < (long long)n; ++i) {
+                rotate(data + (size_t)i * dim, dim, signs.data(), dim_pad, rot.data());
+                pack_signs_trunc(rot.data(), dim_pad, &bits[(base + i) * nw], nw);
+            }
         }
     }
     if (store_i8) {
@@ -465,13 +469,29 @@ std::string HostIndex::add_batch(const uint64_t* ids, const float* data, size_t 
         sq_min = lo;
     }
     std::vector<std::vector<uint32_t>> asg(n);
+    // on the build GPU: homes and codes of every vector (the codes are then not recomputed here)
+    std::vector<uint64_t> gpu_codes;
+    bool gpu_placed = false;
+    if (build_device >= 0 && tree && n > 0) {
+        gpu_codes.resize(n * nw);
+        std::string e = gpu_place(build_device, *this, data, n, asg, gpu_codes.data());
+        if (e.empty()) {
+            gpu_placed = true;
+        } else {
+            ++build_gpu_failures;
+            build_gpu_error = e;
+            gpu_codes.clear();
+            asg.assign(n, {});
+        }
+    }
 #pragma omp parallel
     {
         std::vector<float> rot(dim_pad);
         std::vector<uint64_t> qb(nw);
         std::vector<uint32_t> out;
 #pragma omp for schedule(dynamic, 64)
-        for (long long i = 0; i < (long long)n; ++i) asg[i] = assign_cells_routed(data + (size_t)i * dim, rot, qb, out);
+        for (long long i = 0; i < (long long)n; ++i)
+            if (!gpu_placed || asg[i].empty()) asg[i] = assign_cells_routed(data + (size_t)i * dim, rot, qb, out);
     }
     // Freed slots are refilled first, serially (index.rs:3090-3200).
     size_t n_reuse = std::min(free_slots.size(), n);
@@ -499,7 +519,8 @@ std::string HostIndex::add_batch(const uint64_t* ids, const float* data, size_t 
     }
     if (n_reuse < n) {
         std::vector<std::vector<uint32_t>> rest(asg.begin() + n_reuse, asg.end());
-        append_parallel(ids + n_reuse, data + n_reuse * dim, n - n_reuse, rest);
+        append_parallel(ids + n_reuse, data + n_reuse * dim, n - n_reuse, rest,
+                        gpu_codes.empty() ? nullptr : gpu_codes.data() + n_reuse * nw);
     }
     for (auto& c : cells) {
         // Cell::recompute_centroid (index.rs:380-393)

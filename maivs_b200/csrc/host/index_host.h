@@ -56,13 +56,18 @@ constexpr size_t kGraphMinCells = 65536;   // graph.rs:33
 
 std::unique_ptr<CentroidTree> build_centroid_tree(const float* cell_cents, const uint32_t* cell_ids, size_t m,
                                                   size_t dim, const float* signs, size_t dim_pad, size_t nw,
-                                                  size_t fanout, float beam_frac);
+                                                  size_t fanout, float beam_frac, int device = -1,
+                                                  size_t* gpu_failures = nullptr);
 
-// Spherical Lloyd k-means (tree.rs:179-248); returns (assign, centroids).
+// Spherical Lloyd k-means (tree.rs:179-248); returns (assign, centroids). With device >= 0 the
+// assignment and the sums run on that GPU (csrc/cuda/build.cu, same results); a GPU failure is
+// counted in *gpu_failures (when given) and the host computes the step instead.
 void kmeans_spherical(const float* x, size_t n, size_t dim, size_t k, size_t iters, uint64_t seed,
-                      std::vector<uint32_t>& assign, std::vector<float>& cents);
+                      std::vector<uint32_t>& assign, std::vector<float>& cents, int device = -1,
+                      size_t* gpu_failures = nullptr);
 // Two-level k-means (tree.rs:257-348).
-std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, size_t k, uint64_t seed);
+std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, size_t k, uint64_t seed,
+                                       int device = -1, size_t* gpu_failures = nullptr);
 
 // Keep the `keep` smallest (h, id) pairs, ties at the cut-off in encounter order (tree.rs:120-159).
 void keep_smallest(std::vector<std::pair<uint32_t, uint32_t>>& v, size_t keep, size_t bits);
@@ -129,6 +134,13 @@ struct HostIndex {
     // Bumped on every mutation; the device image remembers the version it was built from.
     uint64_t version = 0;
 
+    // GPU that runs the heavy parts of the build (k-means, placement), or -1 for the host cores.
+    // The results are the same either way; build steps the GPU could not run are counted here and
+    // were computed on the host.
+    int build_device = -1;
+    size_t build_gpu_failures = 0;
+    std::string build_gpu_error;
+
     // ---- API mirrored from the reference's #[pymethods] ----
     // Returns an empty string on success, otherwise the error message.
     std::string init(size_t dim, const std::string& scan_mode, size_t rerank_factor, uint64_t seed, size_t code_bits);
@@ -160,9 +172,18 @@ struct HostIndex {
     std::vector<uint32_t> assign_cells_routed(const float* v, std::vector<float>& rot, std::vector<uint64_t>& qb,
                                               std::vector<uint32_t>& out) const;
     std::vector<uint32_t> pick_orthogonal(std::vector<std::pair<uint32_t, float>>& scored) const;
-    void append_parallel(const uint64_t* ids, const float* data, size_t n, const std::vector<std::vector<uint32_t>>& asg);
+    void append_parallel(const uint64_t* ids, const float* data, size_t n, const std::vector<std::vector<uint32_t>>& asg,
+                         const uint64_t* codes = nullptr);
     void encode_i8(const float* v, int8_t* out) const;
 };
+
+// GPU build steps (csrc/cuda/build.cu); each returns an empty string on success.
+std::string gpu_kmeans_spherical(int device, const float* x, size_t n, size_t dim, size_t k, size_t iters,
+                                 uint64_t seed, std::vector<uint32_t>& assign, std::vector<float>& cents);
+// Homes of n vectors through the centroid tree (assign_cells_routed), and their codes (n x nw).
+// Vectors left without homes (none with the reference's shortlist) are for the caller to place.
+std::string gpu_place(int device, const HostIndex& h, const float* data, size_t n,
+                      std::vector<std::vector<uint32_t>>& asg, uint64_t* codes_out);
 
 // Reference on-disk format "MAIVS2\0\1" (src/persist.rs); empty string on success.
 std::string save_index(const HostIndex& h, const std::string& path);

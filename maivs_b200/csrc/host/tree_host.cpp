@@ -13,8 +13,15 @@
 namespace maivs {
 
 void kmeans_spherical(const float* x, size_t n, size_t dim, size_t k, size_t iters, uint64_t seed,
-                      std::vector<uint32_t>& assign, std::vector<float>& cents) {
+                      std::vector<uint32_t>& assign, std::vector<float>& cents, int device, size_t* gpu_failures) {
     // tree.rs:179-248
+    if (device >= 0 && n > 0) {
+        if (gpu_kmeans_spherical(device, x, n, dim, k, iters, seed, assign, cents).empty()) return;
+        if (gpu_failures) {
+#pragma omp atomic
+            ++*gpu_failures;
+        }
+    }
     k = std::min(std::max<size_t>(k, 1), n);
     cents.assign(k * dim, 0.0f);
     size_t stride = std::max<size_t>(n / k, 1);
@@ -69,17 +76,18 @@ void kmeans_spherical(const float* x, size_t n, size_t dim, size_t k, size_t ite
     }
 }
 
-std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, size_t k, uint64_t seed) {
+std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, size_t k, uint64_t seed, int device,
+                                       size_t* gpu_failures) {
     // tree.rs:257-348
     k = std::min(std::max<size_t>(k, 1), n);
     std::vector<uint32_t> assign;
     std::vector<float> cents;
     if (k <= 64 || n <= k * 4) {
-        kmeans_spherical(x, n, dim, k, 12, seed, assign, cents);
+        kmeans_spherical(x, n, dim, k, 12, seed, assign, cents, device, gpu_failures);
         return cents;
     }
     size_t k1 = (size_t)std::ceil(std::sqrt((double)k));
-    kmeans_spherical(x, n, dim, k1, 8, seed, assign, cents);
+    kmeans_spherical(x, n, dim, k1, 8, seed, assign, cents, device, gpu_failures);
     std::vector<std::vector<uint32_t>> groups(k1);
     for (size_t i = 0; i < n; ++i) groups[assign[i]].push_back((uint32_t)i);
 
@@ -116,7 +124,7 @@ std::vector<float> hierarchical_kmeans(const float* x, size_t n, size_t dim, siz
         std::vector<uint32_t> a;
         std::vector<float> cs;
         uint64_t gseed = seed ^ ((uint64_t)(g + 1) * 0x9E3779B9ull);
-        kmeans_spherical(buf.data(), idx.size(), dim, subs[g], 12, gseed, a, cs);
+        kmeans_spherical(buf.data(), idx.size(), dim, subs[g], 12, gseed, a, cs, device, gpu_failures);
         std::copy(cs.begin(), cs.begin() + subs[g] * dim, out.begin() + offs[g] * dim);
     }
     size_t fill = 0;
@@ -162,7 +170,7 @@ static void code_of_centroid(const float* c, size_t dim, const float* signs, siz
 
 std::unique_ptr<CentroidTree> build_centroid_tree(const float* cell_cents, const uint32_t* cell_ids, size_t m,
                                                   size_t dim, const float* signs, size_t dim_pad, size_t nw,
-                                                  size_t fanout, float beam_frac) {
+                                                  size_t fanout, float beam_frac, int device, size_t* gpu_failures) {
     // tree.rs:354-453
     if (m < 2 || nw == 0) return nullptr;
     fanout = std::max<size_t>(fanout, 2);
@@ -185,7 +193,7 @@ std::unique_ptr<CentroidTree> build_centroid_tree(const float* cell_cents, const
         if (k >= cur_n) break;
         std::vector<uint32_t> assign;
         std::vector<float> parents;
-        kmeans_spherical(cur.data(), cur_n, dim, k, 10, 0x9E3779B97F4A7C15ull, assign, parents);
+        kmeans_spherical(cur.data(), cur_n, dim, k, 10, 0x9E3779B97F4A7C15ull, assign, parents, device, gpu_failures);
         TreeLevel lv;
         lv.n = k;
         lv.child_len.assign(k, 0);
