@@ -77,13 +77,16 @@ def recall(ids: np.ndarray, truth: np.ndarray) -> float:
     return float(np.mean([len(set(a.tolist()) & set(b.tolist())) / K for a, b in zip(ids, truth)]))
 
 
-def build_quality(X: np.ndarray, threads: int):
+def build_quality(X: np.ndarray, threads: int, build_device: int | None = None):
+    """The `quality` preset (bench/fair/fairbench.py:98-119); build_device runs the build's k-means
+    and placement on that GPU (the same index as the host build)."""
     import maivs_b200 as M
 
     M.set_num_threads(threads)  # torchrun exports OMP_NUM_THREADS=1
 
     n, d = X.shape
     ix = M.FlatCellIndex(d, "binary", 16, 0x5EED, 0)
+    ix.set_build_device(build_device)
     ix.set_orthogonal_polysemy(2, 1.0)
     ix.set_fastscan(True)
     ix.set_two_stage(True, 2)
@@ -96,7 +99,7 @@ def build_quality(X: np.ndarray, threads: int):
     return ix
 
 
-def build_memory(X: np.ndarray, threads: int):
+def build_memory(X: np.ndarray, threads: int, build_device: int | None = None):
     """The reference's `memory` preset (bench/fair/fairbench.py:98-106): quality + per-dimension SQ8 rerank."""
     import maivs_b200 as M
 
@@ -104,6 +107,7 @@ def build_memory(X: np.ndarray, threads: int):
 
     n, d = X.shape
     ix = M.FlatCellIndex(d, "binary", 16, 0x5EED, 0)
+    ix.set_build_device(build_device)
     ix.set_per_dim_sq(True)
     ix.set_orthogonal_polysemy(2, 1.0)
     ix.set_fastscan(True)
@@ -343,7 +347,7 @@ def run_maivs(args):
     X, Q, Qs = mixture(args.seed, args.n, args.nq, 384, 1000, 0.35)
     threads = max(1, (os.cpu_count() or 1) // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", ws))))
     t0 = time.perf_counter()
-    ix = build_quality(X, threads)
+    ix = build_quality(X, threads, build_device=local)
     build_s = time.perf_counter() - t0
     ix.to_device(local)
     truth = brute_force_topk(X, Q, K, str(dev))
@@ -531,6 +535,7 @@ def run_maivs(args):
             "recall_at_10": round(rec, 4), "recall_at_10_shifted": round(rec_ood, 4),
             "cells": int(ix.stats()["n_cells"]), "l2_flush": "256 MiB write before each step, outside its timing",
             "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU", "build_s": round(build_s, 1),
+            "build": "k-means and placement on the GPU (maivs_set_build_device)",
             "step_ms_min_max": [round(min(step_ms), 4), round(max(step_ms), 4)], "overflow_flags": overflow,
         },
         "e2e": {"value": round(e2e_qps, 1), "unit": "queries/s", "h2d_bytes_per_step": args.nq * 384 * 4,
@@ -668,7 +673,7 @@ def run_sharded(args):
     if rank == 0 and not os.path.exists(path):
         X, Q = mixture_torch(args.seed, n, nq, 384, 10_000, 0.35, dev)
         t0 = time.perf_counter()
-        ix0 = build_quality(X, os.cpu_count() or 1)
+        ix0 = build_quality(X, os.cpu_count() or 1, build_device=local)
         build_s = time.perf_counter() - t0
         ix0.save(path + ".part")
         del ix0
@@ -821,7 +826,7 @@ def run_lowbatch(args):
     X, Q, _ = mixture(args.seed, args.n, args.nq, 384, 1000, 0.35)
     threads = os.cpu_count() or 1
     t0 = time.perf_counter()
-    ix = build_memory(X, threads)
+    ix = build_memory(X, threads, build_device=0)
     build_s = time.perf_counter() - t0
     ix.to_device(0)
     truth = brute_force_topk(X, Q, K, str(dev))
