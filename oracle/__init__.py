@@ -50,7 +50,7 @@ class _Arrays(C.Structure):
         ("tree_depth", C.c_uint64), ("tree_level_n", C.c_void_p), ("tree_codes", C.c_void_p),
         ("tree_code_off", C.c_void_p), ("tree_child_start", C.c_void_p), ("tree_child_len", C.c_void_p),
         ("tree_child_off", C.c_void_p), ("tree_leaf_codes", C.c_void_p), ("tree_leaf_ids", C.c_void_p),
-        ("config", C.c_void_p), ("n_config", C.c_uint64),
+        ("config", C.c_void_p), ("n_config", C.c_uint64), ("bits", C.c_void_p), ("n_bits", C.c_uint64),
     ]
 
 
@@ -98,6 +98,16 @@ def lib() -> C.CDLL:
         L.oracle_build_compact.argtypes = [vp]
         L.oracle_build_take_index.restype = vp
         L.oracle_build_take_index.argtypes = [vp]
+        L.oracle_build_snapshot.restype = vp
+        L.oracle_build_snapshot.argtypes = [vp]
+        L.oracle_build_remove.restype = C.c_int
+        L.oracle_build_remove.argtypes = [vp, u64]
+        L.oracle_build_has_id.restype = C.c_int
+        L.oracle_build_has_id.argtypes = [vp, u64]
+        L.oracle_build_n_live.restype = u64
+        L.oracle_build_n_live.argtypes = [vp]
+        L.oracle_build_fork.restype = vp
+        L.oracle_build_fork.argtypes = [vp]
         L.oracle_build_export.argtypes = [vp]
         L.oracle_build_array.restype = C.c_int
         L.oracle_build_array.argtypes = [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64), C.POINTER(u64)]
@@ -117,7 +127,7 @@ class OracleIndex:
     NAMES = ("signs", "centroids", "r_bound", "cell_members", "cell_member_off", "fs_codes", "fs_off", "slot_cells",
              "ext_ids", "cent_bits", "cent_sq8", "csq_min", "csq_step", "vecs_f32", "scan_i8", "sq_min", "sq_step",
              "tags", "tree_level_n", "tree_codes", "tree_code_off", "tree_child_start", "tree_child_len",
-             "tree_child_off", "tree_leaf_codes", "tree_leaf_ids", "config")
+             "tree_child_off", "tree_leaf_codes", "tree_leaf_ids", "config", "bits")
 
     def __init__(self, arrays: dict):
         self.a = {k: np.ascontiguousarray(v) for k, v in arrays.items()}
@@ -133,8 +143,9 @@ class OracleIndex:
                      "slot_cells", "ext_ids", "cent_bits", "cent_sq8", "csq_min", "csq_step", "vecs_f32",
                      "scan_i8", "sq_min", "sq_step", "tags", "tree_level_n", "tree_codes", "tree_code_off",
                      "tree_child_start", "tree_child_len", "tree_child_off", "tree_leaf_codes", "tree_leaf_ids",
-                     "config"):
+                     "config", "bits"):
             setattr(s, name, _p(a.get(name)))
+        s.n_bits = a["bits"].size if "bits" in a else 0
         s.n_fs_codes = a["fs_codes"].size
         s.n_cent_bits = a["cent_bits"].size
         s.n_cent_sq8 = a["cent_sq8"].size
@@ -287,7 +298,7 @@ _ARRAY_DTYPES = {
     "sq_min": np.float32, "sq_step": np.float32, "signs": np.float32, "tags": np.uint32,
     "tree_level_n": np.uint64, "tree_codes": np.uint64, "tree_code_off": np.uint64, "tree_child_start": np.uint64,
     "tree_child_len": np.uint64, "tree_child_off": np.uint64, "tree_leaf_codes": np.uint64,
-    "tree_leaf_ids": np.uint32, "config": np.float64,
+    "tree_leaf_ids": np.uint32, "config": np.float64, "bits": np.uint64,
 }
 
 
@@ -388,6 +399,33 @@ class OracleBuild:
 
     def index(self) -> "OracleIndex":
         return OracleIndex.from_build(self)
+
+    def remove(self, id: int) -> bool:
+        """remove (index.rs:3223-3276)."""
+        self._exported = False
+        return bool(lib().oracle_build_remove(self.h, int(id)))
+
+    def has_id(self, id: int) -> bool:
+        return bool(lib().oracle_build_has_id(self.h, int(id)))
+
+    def n_live(self) -> int:
+        return int(lib().oracle_build_n_live(self.h))
+
+    def fork_empty(self) -> "OracleBuild":
+        """fork_empty (index.rs:2330-2400): same configuration and centroids, no vectors,
+        FastScan off."""
+        f = OracleBuild.__new__(OracleBuild)
+        f.dim = self.dim
+        f.h = lib().oracle_build_fork(self.h)
+        f._exported = False
+        return f
+
+    def snapshot(self) -> "OracleIndex":
+        """A searchable copy of the index as it stands (the build stays usable)."""
+        o = OracleIndex.__new__(OracleIndex)
+        o.a = {}
+        o.h = lib().oracle_build_snapshot(self.h)
+        return o
 
     def take_index(self) -> "OracleIndex":
         """The searchable index, moving the build's large arrays into it (no copies; the build

@@ -3,9 +3,10 @@
 // A CPU restatement, in C++17 + AVX2 + OpenMP, of the reference's query hot path
 // (V47VANSH/MAIVS, Rust): src/quantize.rs (rotation, codes, FastScan tables and block sums),
 // src/tree.rs:120-159 and :559-628 (tree beam search), src/index.rs:41-343 (SIMD dots),
-// :1168-1305 (route_query), :1309-1378 (rerank_exact), :1381-1864 (search_one, FastScan
-// branch), :1873-1980 (route_batch), :1999-2311 (search_batch_cellmajor), :3316-3391
-// (search_batch). Each function below cites the lines it follows.
+// :1168-1305 (route_query), :1309-1378 (rerank_exact), :1381-1864 (search_one, FastScan and
+// Hamming branches), :1873-1980 (route_batch), :1999-2311 (search_batch_cellmajor, FastScan),
+// :3316-3391 (search_batch), and the build's mutations (add_batch with freed-slot refill, remove,
+// compact_arena, fork_empty). Each function below cites the lines it follows.
 //
 // Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline arm load this library; the
 // product never links or calls it. It consumes an index's arrays (as exported by the product's
@@ -28,6 +29,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <unordered_map>
 #include <string>
 #include <vector>
 
@@ -312,6 +314,7 @@ struct OIndex {
     std::vector<uint32_t> fs_off;
     std::vector<uint32_t> slot_cells;
     std::vector<uint64_t> ext_ids;
+    std::vector<uint64_t> bits;  // nw words per slot (the Hamming scan of a non-FastScan index)
     std::vector<uint64_t> cent_bits;
     std::vector<uint8_t> cent_sq8;
     std::vector<float> csq_min, csq_step;
@@ -550,13 +553,65 @@ std::vector<std::pair<float, uint64_t>> search_one(const OIndex& ix, const float
         }
         for (size_t i = n; i-- > 0;) suffix[i] = std::fmax(bounds[i], suffix[i + 1]);
     }
-    // FastScan bucket queue on d >> 6 with a falling tau (index.rs:1630-1692)
     rotate(q, ix.dim, ix.signs.data(), ix.dim_pad, b.rot.data());
+    const size_t target = std::max<size_t>(want0, 1);
+    if (!(ix.fastscan && ix.compacted && !ix.fs_off.empty())) {
+        // Hamming bucket queue over the flat codes (index.rs:1693-1808, no cascade): tau starts
+        // at the code length and falls while the candidates strictly below it fill target; every
+        // candidate at or below the final tau goes to the rerank, ties included (:1843-1848).
+        const uint32_t dp = (uint32_t)(nw * 64);
+        std::vector<uint64_t> qb(nw);
+        pack_signs_trunc(b.rot.data(), ix.dim_pad, qb.data(), nw);
+        std::vector<uint32_t> hist(dp + 1, 0);
+        std::vector<std::pair<uint32_t, uint32_t>> hc;  // (h, slot)
+        uint32_t tau = dp;
+        size_t kept = 0;
+        for (size_t ci_i = 0; ci_i < chosen.size(); ++ci_i) {
+            uint32_t ci = chosen[ci_i];
+            const uint32_t* mem = ix.member_ptr(ci);
+            size_t nmem = ix.members(ci);
+            for (size_t i = 0; i < nmem; ++i) {
+                uint32_t slot = mem[i];
+                if (!keep(slot) || (dedup && seen(slot, ci))) continue;
+                uint32_t h = hamming(qb.data(), &ix.bits[(size_t)slot * nw], nw);
+                if (h <= tau) {  // offer! (:1704-1717)
+                    hc.push_back({h, slot});
+                    hist[h] += 1;
+                    kept += 1;
+                    while (tau > 0 && kept - hist[tau] >= target) {
+                        kept -= hist[tau];
+                        tau -= 1;
+                    }
+                }
+            }
+            if (hc.size() > 4 * target + 1024) {
+                uint32_t t = tau;
+                hc.erase(std::remove_if(hc.begin(), hc.end(), [t](const std::pair<uint32_t, uint32_t>& x) {
+                             return x.first > t;
+                         }),
+                         hc.end());
+            }
+            if (ix.adaptive && kept >= target) {
+                // score_to_cos(hamming_score(tau, dp)) (index.rs:1139-1164, quantize.rs:206-208)
+                float dpf = (float)dp;
+                float s = dpf - 2.0f * (float)tau;
+                float hh = (dpf - s) * 0.5f;
+                float thr = std::cos(3.14159265358979323846f * hh / dpf);
+                if (suffix[ci_i + 1] < thr - ix.at_margin) break;
+            }
+        }
+        std::vector<uint32_t> slots;
+        for (auto& x : hc)
+            if (x.first <= tau) slots.push_back(x.second);
+        if (cands_out) *cands_out = slots;
+        if (slots.empty()) return {};
+        return rerank_exact(ix, q, slots, k);
+    }
+    // FastScan bucket queue on d >> 6 with a falling tau (index.rs:1630-1692)
     FsQuery fq = fs_query(b.rot.data(), ix.dim_pad, nw);
     const size_t bb = nw * 64 * 32 / 8;
     const uint32_t maxk = fq.maxk;
     const float norm = std::sqrt(2.0f * (float)ix.dim_pad / 3.14159265358979323846f);
-    const size_t target = std::max<size_t>(want0, 1);
     std::vector<uint32_t> hist(nw * 64 + 1, 0);
     struct HC {
         uint32_t h, slot;
@@ -1072,6 +1127,8 @@ struct OBuild {
     std::vector<int8_t> scan_i8;
     std::vector<float> vecs_f32, sq_min, sq_step;
     std::vector<uint32_t> slot_cell, slot_cells;
+    std::vector<uint32_t> free_slots;                 // freed by remove, refilled LIFO by add
+    std::unordered_map<uint64_t, uint32_t> id_to_slot;
     // cells and derived state
     std::vector<BCell> cells;
     std::vector<uint64_t> cent_bits;
@@ -1423,8 +1480,62 @@ int build_train(OBuild& b, const float* data, size_t n_all, size_t n_cells, size
     return 0;
 }
 
-// add_batch (index.rs:2987-3212) for a build with no reused slots: scale and SQ8 fit from the
-// first batch, parallel placement, append_parallel (:2566-2667), centroid update, derived state.
+// Cell::recompute_centroid (index.rs:379-392)
+void recompute_centroid(BCell& c, size_t dim) {
+    if (c.members.empty()) return;
+    float nrm = 0.0f;
+    for (float v : c.sum) nrm += v * v;
+    nrm = std::sqrt(nrm);
+    if (nrm > 1e-12f)
+        for (size_t j = 0; j < dim; ++j) c.centroid[j] = c.sum[j] / nrm;
+}
+
+// fork_empty (index.rs:2330-2400): a new empty index with this one's configuration, rotation,
+// quantisation parameters and centroids (sums zero, no members); FastScan off, not compacted;
+// derived state refreshed (so its tree covers every cell until the first insert).
+void build_fork(const OBuild& src, OBuild& f) {
+    f.dim = src.dim;
+    f.dim_pad = src.dim_pad;
+    f.nw = src.nw;
+    f.rerank_factor = src.rerank_factor;
+    f.seed = src.seed;
+    f.signs = src.signs;
+    f.graph_route = src.graph_route;
+    f.graph_min_cells = src.graph_min_cells;
+    f.tree_route = src.tree_route;
+    f.tree_min_cells = src.tree_min_cells;
+    f.tree_fanout = src.tree_fanout;
+    f.tree_beam_frac = src.tree_beam_frac;
+    f.tree_cells = 0;
+    f.two_stage = src.two_stage;
+    f.centroid_sq8 = src.centroid_sq8;
+    f.shortlist_mult = src.shortlist_mult;
+    f.quant_scale = src.quant_scale;
+    f.n_live = 0;
+    f.max_assign = src.max_assign;
+    f.spill_margin = src.spill_margin;
+    f.spill_lambda = src.spill_lambda;
+    f.compacted = false;
+    f.fastscan = false;
+    f.i8_rerank = src.i8_rerank;
+    f.per_dim_sq = src.per_dim_sq;
+    f.sq_min = src.sq_min;
+    f.sq_step = src.sq_step;
+    f.keep_f32 = src.keep_f32;
+    f.adaptive = src.adaptive;
+    f.at_margin = src.at_margin;
+    f.cm_min_batch = src.cm_min_batch;
+    f.cells.resize(src.cells.size());
+    for (size_t c = 0; c < src.cells.size(); ++c) {
+        f.cells[c].centroid = src.cells[c].centroid;
+        f.cells[c].sum.assign(src.dim, 0.0f);
+    }
+    refresh_derived(f);
+}
+
+// add_batch (index.rs:2987-3212): scale and SQ8 fit from the first batch, parallel placement, the
+// serial refill of freed slots (LIFO, :3076-3198), append_parallel for the rest (:2566-2667),
+// centroid update, derived state.
 int build_add(OBuild& b, const uint64_t* ids, const float* data, size_t n) {
     if (b.cells.empty()) return 1;
     size_t dim = b.dim, nw = b.nw, ma = b.max_assign;
@@ -1455,68 +1566,128 @@ int build_add(OBuild& b, const uint64_t* ids, const float* data, size_t n) {
 #pragma omp for schedule(dynamic, 256)
         for (size_t i = 0; i < n; ++i) asg[i] = assign_cells(b, data + i * dim, rot, qb, tout);
     }
+    const bool store_i8 = b.i8_rerank;
+    auto encode_i8 = [&](const float* v, int8_t* o) {
+        for (size_t j = 0; j < dim; ++j) {
+            if (b.per_dim_sq) {
+                float q = std::round((v[j] - b.sq_min[j]) / b.sq_step[j]);
+                o[j] = (int8_t)(uint8_t)std::min(std::max(q, 0.0f), 255.0f);
+            } else {
+                float q = std::round(v[j] * b.quant_scale);
+                o[j] = (int8_t)std::min(std::max(q, -127.0f), 127.0f);
+            }
+        }
+    };
+    // freed slots first, one vector at a time
+    const size_t n_reuse = std::min(b.free_slots.size(), n);
+    {
+        std::vector<float> rot(b.dim_pad);
+        for (size_t i = 0; i < n_reuse; ++i) {
+            const float* v = data + i * dim;
+            uint32_t slot = b.free_slots.back();
+            b.free_slots.pop_back();
+            size_t off = (size_t)slot * dim;
+            if (b.keep_f32) std::copy(v, v + dim, b.vecs_f32.begin() + off);
+            b.code_of(v, rot, &b.bits[(size_t)slot * nw]);
+            if (store_i8) encode_i8(v, &b.scan_i8[off]);
+            b.ext_ids[slot] = ids[i];
+            b.slot_cell[slot] = asg[i][0];
+            for (size_t j = 0; j < ma; ++j) b.slot_cells[(size_t)slot * ma + j] = j < asg[i].size() ? asg[i][j] : UINT32_MAX;
+            for (size_t j = 0; j < asg[i].size(); ++j) {
+                BCell& c = b.cells[asg[i][j]];
+                c.members.push_back(slot);
+                if (j == 0)
+                    for (size_t t = 0; t < dim; ++t) c.sum[t] += v[t];
+            }
+            b.id_to_slot[ids[i]] = slot;
+            b.n_live += 1;
+        }
+    }
+    // the rest appended to the arena
+    const size_t na = n - n_reuse;
+    const float* adata = data + n_reuse * dim;
+    const uint64_t* aids = ids + n_reuse;
+    const std::vector<uint32_t>* aasg = asg.data() + n_reuse;
     size_t base = b.ext_ids.size();
-    bool store_i8 = b.i8_rerank;
-    if (b.keep_f32) b.vecs_f32.insert(b.vecs_f32.end(), data, data + n * dim);
-    b.bits.resize((base + n) * nw);
-    if (store_i8) b.scan_i8.resize((base + n) * dim);
+    if (b.keep_f32) b.vecs_f32.insert(b.vecs_f32.end(), adata, adata + na * dim);
+    b.bits.resize((base + na) * nw);
+    if (store_i8) b.scan_i8.resize((base + na) * dim);
 #pragma omp parallel
     {
         std::vector<float> rot(b.dim_pad);
 #pragma omp for schedule(static)
-        for (size_t i = 0; i < n; ++i) {
-            const float* v = data + i * dim;
+        for (size_t i = 0; i < na; ++i) {
+            const float* v = adata + i * dim;
             b.code_of(v, rot, &b.bits[(base + i) * nw]);
-            if (store_i8) {
-                int8_t* o = &b.scan_i8[(base + i) * dim];
-                for (size_t j = 0; j < dim; ++j) {
-                    if (b.per_dim_sq) {
-                        float q = std::round((v[j] - b.sq_min[j]) / b.sq_step[j]);
-                        o[j] = (int8_t)(uint8_t)std::min(std::max(q, 0.0f), 255.0f);
-                    } else {
-                        float q = std::round(v[j] * b.quant_scale);
-                        o[j] = (int8_t)std::min(std::max(q, -127.0f), 127.0f);
-                    }
-                }
-            }
+            if (store_i8) encode_i8(v, &b.scan_i8[(base + i) * dim]);
         }
     }
-    for (size_t i = 0; i < n; ++i) {
+    for (size_t i = 0; i < na; ++i) {
         uint32_t slot = (uint32_t)(base + i);
-        b.ext_ids.push_back(ids[i]);
-        b.slot_cell.push_back(asg[i][0]);
-        for (size_t j = 0; j < ma; ++j) b.slot_cells.push_back(j < asg[i].size() ? asg[i][j] : UINT32_MAX);
-        for (uint32_t ci : asg[i]) b.cells[ci].members.push_back(slot);
+        b.ext_ids.push_back(aids[i]);
+        b.slot_cell.push_back(aasg[i][0]);
+        for (size_t j = 0; j < ma; ++j) b.slot_cells.push_back(j < aasg[i].size() ? aasg[i][j] : UINT32_MAX);
+        for (uint32_t ci : aasg[i]) b.cells[ci].members.push_back(slot);
+        b.id_to_slot[aids[i]] = slot;
     }
-    b.n_live += n;
-    // primary sums: each cell adds its own vectors in input order
+    b.n_live += na;
+    // primary sums: each cell adds its own appended vectors in input order
     size_t m = b.cells.size();
-    std::vector<size_t> st(m + 1, 0), ord(n);
-    for (size_t i = 0; i < n; ++i) ++st[asg[i][0] + 1];
+    std::vector<size_t> st(m + 1, 0), ord(na);
+    for (size_t i = 0; i < na; ++i) ++st[aasg[i][0] + 1];
     for (size_t c = 0; c < m; ++c) st[c + 1] += st[c];
     {
         std::vector<size_t> pos(st.begin(), st.end() - 1);
-        for (size_t i = 0; i < n; ++i) ord[pos[asg[i][0]]++] = i;
+        for (size_t i = 0; i < na; ++i) ord[pos[aasg[i][0]]++] = i;
     }
 #pragma omp parallel for schedule(dynamic, 16)
     for (size_t c = 0; c < m; ++c) {
         float* s = b.cells[c].sum.data();
         for (size_t r = st[c]; r < st[c + 1]; ++r) {
-            const float* v = data + ord[r] * dim;
+            const float* v = adata + ord[r] * dim;
             for (size_t j = 0; j < dim; ++j) s[j] += v[j];
         }
     }
-    // Cell::recompute_centroid (index.rs:379-392)
-    for (auto& c : b.cells) {
-        if (c.members.empty()) continue;
-        float nrm = 0.0f;
-        for (float v : c.sum) nrm += v * v;
-        nrm = std::sqrt(nrm);
-        if (nrm > 1e-12f)
-            for (size_t j = 0; j < dim; ++j) c.centroid[j] = c.sum[j] / nrm;
-    }
+    for (auto& c : b.cells) recompute_centroid(c, dim);
     refresh_derived(b);
     return 0;
+}
+
+// remove (index.rs:3223-3276): the vector leaves its primary cell's sum (read back from whichever
+// store exists), is swap-removed from every home's member list, and its slot is freed. The derived
+// routing state is not refreshed.
+bool build_remove(OBuild& b, uint64_t id) {
+    auto it = b.id_to_slot.find(id);
+    if (it == b.id_to_slot.end()) return false;
+    uint32_t slot = it->second;
+    b.id_to_slot.erase(it);
+    b.compacted = false;
+    size_t dim = b.dim, ma = b.max_assign, primary = b.slot_cell[slot], vs = (size_t)slot * dim;
+    BCell& pc = b.cells[primary];
+    if (b.keep_f32) {
+        for (size_t j = 0; j < dim; ++j) pc.sum[j] -= b.vecs_f32[vs + j];
+    } else if (b.per_dim_sq) {
+        for (size_t j = 0; j < dim; ++j) pc.sum[j] -= (float)(uint8_t)b.scan_i8[vs + j] * b.sq_step[j] + b.sq_min[j];
+    } else {
+        float inv = 1.0f / b.quant_scale;
+        for (size_t j = 0; j < dim; ++j) pc.sum[j] -= (float)b.scan_i8[vs + j] * inv;
+    }
+    for (size_t j = 0; j < ma; ++j) {
+        uint32_t ci = b.slot_cells[(size_t)slot * ma + j];
+        if (ci == UINT32_MAX) continue;
+        auto& mem = b.cells[ci].members;
+        for (size_t p = 0; p < mem.size(); ++p)
+            if (mem[p] == slot) {
+                mem[p] = mem.back();
+                mem.pop_back();
+                break;
+            }
+        b.slot_cells[(size_t)slot * ma + j] = UINT32_MAX;
+    }
+    recompute_centroid(pc, dim);
+    b.free_slots.push_back(slot);
+    b.n_live -= 1;
+    return true;
 }
 
 // compact_arena (index.rs:929-1112): cluster-major renumbering by primary cell, member lists
@@ -1534,11 +1705,17 @@ void build_compact(OBuild& b) {
             new_of_old[s] = (uint32_t)old_of_new.size();
             old_of_new.push_back(s);
         }
-    for (size_t s = 0; s < old_n; ++s)  // every slot is live in a first-batch build
-        if (new_of_old[s] == UINT32_MAX) {
-            new_of_old[s] = (uint32_t)old_of_new.size();
-            old_of_new.push_back((uint32_t)s);
-        }
+    {
+        // live slots the loop above missed (none in a consistent index), in slot order; freed
+        // slots are dropped
+        std::vector<uint8_t> live(old_n, 0);
+        for (auto& kv : b.id_to_slot) live[kv.second] = 1;
+        for (size_t s = 0; s < old_n; ++s)
+            if (live[s] && new_of_old[s] == UINT32_MAX) {
+                new_of_old[s] = (uint32_t)old_of_new.size();
+                old_of_new.push_back((uint32_t)s);
+            }
+    }
     size_t nn = old_of_new.size();
     auto permute = [&](auto& arr, size_t w) {
         if (arr.empty()) return;
@@ -1555,9 +1732,15 @@ void build_compact(OBuild& b) {
     permute(b.slot_cell, 1);
     permute(b.slot_cells, ma);
     for (auto& c : b.cells) {
+        c.members.erase(std::remove_if(c.members.begin(), c.members.end(),
+                                       [&](uint32_t mbr) { return new_of_old[mbr] == UINT32_MAX; }),
+                        c.members.end());
         for (auto& mbr : c.members) mbr = new_of_old[mbr];
         std::sort(c.members.begin(), c.members.end());
     }
+    b.id_to_slot.clear();
+    for (size_t ns = 0; ns < b.ext_ids.size(); ++ns) b.id_to_slot[b.ext_ids[ns]] = (uint32_t)ns;
+    b.free_slots.clear();
     b.prim_len.clear();
     b.rep_off.clear();
     if (ma > 1 && nw > 0) {
@@ -1629,6 +1812,7 @@ void bexport(OBuildHandle* h) {
     bput(h, "vecs_f32", b.vecs_f32.data(), b.vecs_f32.size());
     bput(h, "scan_i8", b.scan_i8.data(), b.scan_i8.size());
     bput(h, "ext_ids", b.ext_ids.data(), b.ext_ids.size());
+    bput(h, "bits", b.bits.data(), b.bits.size());
     bput(h, "slot_cell", b.slot_cell.data(), b.slot_cell.size());
     bput(h, "slot_cells", b.slot_cells.data(), b.slot_cells.size());
     std::vector<uint32_t> mem, moff{0};
@@ -1678,6 +1862,71 @@ void bexport(OBuildHandle* h) {
     bput(h, "tree_leaf_ids", li.data(), li.size());
 }
 
+// The searchable index of a build: its arrays moved out (take) or copied.
+OIndex* make_index(OBuild& b, bool take) {
+    auto* ix = new OIndex();
+    ix->dim = b.dim;
+    ix->dim_pad = b.dim_pad;
+    ix->nw = b.nw;
+    ix->M = b.cells.size();
+    ix->ma = b.max_assign;
+    ix->n_slots = b.ext_ids.size();
+    ix->signs = b.signs;
+    ix->mem_off.push_back(0);
+    for (auto& c : b.cells) {
+        ix->centroids.insert(ix->centroids.end(), c.centroid.begin(), c.centroid.end());
+        ix->r_bound.push_back(c.r_bound);
+        ix->mem.insert(ix->mem.end(), c.members.begin(), c.members.end());
+        ix->mem_off.push_back((uint32_t)ix->mem.size());
+    }
+    if (take) ix->fs_codes = std::move(b.fs_codes); else ix->fs_codes = b.fs_codes;
+    if (take) ix->fs_off = std::move(b.fs_off); else ix->fs_off = b.fs_off;
+    if (take) ix->slot_cells = std::move(b.slot_cells); else ix->slot_cells = b.slot_cells;
+    if (take) ix->ext_ids = std::move(b.ext_ids); else ix->ext_ids = b.ext_ids;
+    ix->cent_bits = b.cent_bits;
+    ix->cent_sq8 = b.cent_sq8;
+    if (!b.cent_sq8.empty()) {
+        ix->csq_min = b.csq_min;
+        ix->csq_step = b.csq_step;
+    }
+    if (take) ix->vecs_f32 = std::move(b.vecs_f32); else ix->vecs_f32 = b.vecs_f32;
+    if (take) ix->scan_i8 = std::move(b.scan_i8); else ix->scan_i8 = b.scan_i8;
+    ix->sq_min = b.sq_min;
+    ix->sq_step = b.sq_step;
+    ix->rerank_factor = b.rerank_factor;
+    ix->two_stage = b.two_stage;
+    ix->shortlist_mult = b.shortlist_mult;
+    ix->centroid_sq8 = b.centroid_sq8;
+    ix->has_tree = b.has_tree;
+    ix->fastscan = b.fastscan;
+    ix->per_dim_sq = b.per_dim_sq;
+    ix->i8_rerank = b.i8_rerank;
+    ix->adaptive = b.adaptive;
+    ix->at_margin = b.at_margin;
+    ix->compacted = b.compacted;
+    ix->n_live = b.n_live;
+    ix->cm_min_batch = b.cm_min_batch;
+    ix->has_filter = false;
+    ix->flo = 0;
+    ix->fhi = 0xFFFFFFFFu;
+    ix->beam_frac = b.has_tree ? b.tree_bf : 0.0f;
+    ix->n_leaf = b.has_tree ? b.leaf_ids.size() : 0;
+    ix->graph_route = b.graph_route;
+    ix->graph_min_cells = b.graph_min_cells;
+    if (b.has_tree) {
+        ix->levels = b.tview.levels;
+        ix->leaf_codes = b.leaf_codes;
+        ix->leaf_ids = b.leaf_ids;
+    }
+    if (take) {
+        ix->bits = std::move(b.bits);
+        b.bits.shrink_to_fit();
+    } else {
+        ix->bits = b.bits;
+    }
+    return ix;
+}
+
 }  // namespace
 
 // ---- C API used by the tests and the CPU-baseline arm of bench.py ------------------------------
@@ -1725,6 +1974,9 @@ struct oracle_arrays {
     // configuration, in the product's "config" array order
     const double* config;
     uint64_t n_config;
+    // flat codes, nw words per slot (may be null for a FastScan index)
+    const uint64_t* bits;
+    uint64_t n_bits;
 };
 
 void* oracle_index_new(const oracle_arrays* a) {
@@ -1756,6 +2008,7 @@ void* oracle_index_new(const oracle_arrays* a) {
     cp(ix->sq_min, a->sq_min, a->sq_min ? a->dim : 0);
     cp(ix->sq_step, a->sq_step, a->sq_step ? a->dim : 0);
     cp(ix->tags, a->tags, a->n_tags);
+    cp(ix->bits, a->bits, a->n_bits);
     const double* c = a->config;
     ix->rerank_factor = (size_t)c[3];
     ix->two_stage = c[4] != 0;
@@ -1805,7 +2058,8 @@ void oracle_index_set_rerank_factor(void* p, uint64_t rf) {
 
 // search_batch (index.rs:3316-3391): ids/scores nq*k padded; cand_out (optional) receives per
 // query the candidate slots sent to the rerank, sorted, as nq rows of cand_cap (UINT32_MAX pad)
-// with counts in cand_n. Returns 0, or 7 for an unsupported routing mode.
+// with counts in cand_n. Returns 0, 7 for an unsupported routing mode, or 8 for a cell-major
+// batch over an index without FastScan blocks.
 int oracle_search_batch(void* p, const float* Q, uint64_t nq, uint64_t k, uint64_t nprobe, float tc, float beta,
                         int cell_major, uint64_t* ids, float* scores, uint32_t* cand_out, uint64_t cand_cap,
                         uint32_t* cand_n, int* used_cell_major) {
@@ -1818,6 +2072,8 @@ int oracle_search_batch(void* p, const float* Q, uint64_t nq, uint64_t k, uint64
     // cm_ok (index.rs:3343-3348); a compacted multi-home index always has its polysemic runs
     bool cm = cell_major && ix.compacted && !ix.has_filter && nq >= ix.cm_min_batch;
     if (used_cell_major) *used_cell_major = cm ? 1 : 0;
+    // the cell-major join is restated for FastScan codes only
+    if (cm && !(ix.fastscan && !ix.fs_off.empty())) return 8;
     std::vector<std::vector<uint32_t>> cands(nq);
     std::vector<std::vector<std::pair<float, uint64_t>>> res(nq);
     if (cm) {
@@ -2034,69 +2290,26 @@ int oracle_build_add(void* p, const uint64_t* ids, const float* data, uint64_t n
 
 void oracle_build_compact(void* p) { build_compact(static_cast<OBuildHandle*>(p)->b); }
 
+int oracle_build_remove(void* p, uint64_t id) { return build_remove(static_cast<OBuildHandle*>(p)->b, id) ? 1 : 0; }
+
+int oracle_build_has_id(void* p, uint64_t id) { return static_cast<OBuildHandle*>(p)->b.id_to_slot.count(id) ? 1 : 0; }
+
+uint64_t oracle_build_n_live(void* p) { return static_cast<OBuildHandle*>(p)->b.n_live; }
+
+// A new build handle: fork_empty of this one.
+void* oracle_build_fork(void* p) {
+    auto* h = new OBuildHandle();
+    build_fork(static_cast<OBuildHandle*>(p)->b, h->b);
+    return h;
+}
+
 // The searchable index straight from a finished build, moving the large arrays instead of copying
 // them (the build handle keeps its configuration but no longer its arena). Same contents as
 // oracle_index_new over the exported arrays.
-void* oracle_build_take_index(void* p) {
-    OBuild& b = static_cast<OBuildHandle*>(p)->b;
-    auto* ix = new OIndex();
-    ix->dim = b.dim;
-    ix->dim_pad = b.dim_pad;
-    ix->nw = b.nw;
-    ix->M = b.cells.size();
-    ix->ma = b.max_assign;
-    ix->n_slots = b.ext_ids.size();
-    ix->signs = b.signs;
-    ix->mem_off.push_back(0);
-    for (auto& c : b.cells) {
-        ix->centroids.insert(ix->centroids.end(), c.centroid.begin(), c.centroid.end());
-        ix->r_bound.push_back(c.r_bound);
-        ix->mem.insert(ix->mem.end(), c.members.begin(), c.members.end());
-        ix->mem_off.push_back((uint32_t)ix->mem.size());
-    }
-    ix->fs_codes = std::move(b.fs_codes);
-    ix->fs_off = std::move(b.fs_off);
-    ix->slot_cells = std::move(b.slot_cells);
-    ix->ext_ids = std::move(b.ext_ids);
-    ix->cent_bits = b.cent_bits;
-    ix->cent_sq8 = b.cent_sq8;
-    if (!b.cent_sq8.empty()) {
-        ix->csq_min = b.csq_min;
-        ix->csq_step = b.csq_step;
-    }
-    ix->vecs_f32 = std::move(b.vecs_f32);
-    ix->scan_i8 = std::move(b.scan_i8);
-    ix->sq_min = b.sq_min;
-    ix->sq_step = b.sq_step;
-    ix->rerank_factor = b.rerank_factor;
-    ix->two_stage = b.two_stage;
-    ix->shortlist_mult = b.shortlist_mult;
-    ix->centroid_sq8 = b.centroid_sq8;
-    ix->has_tree = b.has_tree;
-    ix->fastscan = b.fastscan;
-    ix->per_dim_sq = b.per_dim_sq;
-    ix->i8_rerank = b.i8_rerank;
-    ix->adaptive = b.adaptive;
-    ix->at_margin = b.at_margin;
-    ix->compacted = b.compacted;
-    ix->n_live = b.n_live;
-    ix->cm_min_batch = b.cm_min_batch;
-    ix->has_filter = false;
-    ix->flo = 0;
-    ix->fhi = 0xFFFFFFFFu;
-    ix->beam_frac = b.has_tree ? b.tree_bf : 0.0f;
-    ix->n_leaf = b.has_tree ? b.leaf_ids.size() : 0;
-    ix->graph_route = b.graph_route;
-    ix->graph_min_cells = b.graph_min_cells;
-    if (b.has_tree) {
-        ix->levels = b.tview.levels;
-        ix->leaf_codes = b.leaf_codes;
-        ix->leaf_ids = b.leaf_ids;
-    }
-    b.bits.clear();
-    b.bits.shrink_to_fit();
-    return ix;
-}
+void* oracle_build_take_index(void* p) { return make_index(static_cast<OBuildHandle*>(p)->b, true); }
+
+// A searchable copy of the build as it stands; the build stays usable (a mutable segment).
+void* oracle_build_snapshot(void* p) { return make_index(static_cast<OBuildHandle*>(p)->b, false); }
 
 // Snapshot of every array (call after the build steps), then one array by name.
 void oracle_build_export(void* p) { bexport(static_cast<OBuildHandle*>(p)); }
