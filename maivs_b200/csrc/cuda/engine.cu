@@ -66,9 +66,12 @@ T* DeviceIndex::upload_vec(const std::vector<T>& v) {
 }
 
 std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, uint32_t c_hi) {
-    if (!h.compacted || !h.fastscan || h.fs_off.empty())
-        return "the GPU search needs a compacted FastScan index: call set_fastscan(True) and compact() first";
+    // A compacted FastScan index is scanned by table sums (per-query path and cell-major join);
+    // any other index by Hamming distance over its flat codes, per query (index.rs:1624-1626: the
+    // FastScan branch needs fastscan && compacted).
+    const bool fs = h.compacted && h.fastscan && !h.fs_off.empty();
     if (h.nw > 16) return "codes longer than 1024 bits are not supported";
+    if (!fs && h.bits.size() < h.ext_ids.size() * h.nw) return "the index has no flat codes to scan";
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return "no CUDA device is visible";
     if (device < 0 || device >= ndev) return "device ordinal out of range";
@@ -90,15 +93,17 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
     v.M = (int)M;
     v.ma = (int)ma;
     v.maxk = 255u * (uint32_t)npos;
+    v.ham = fs ? 0 : 1;
 
     // ---- scan layout: per cell, its members' codes as position-major 8-member nibble words ----
+    // (Hamming scan: the member lists only, beside the flat codes)
     std::vector<uint32_t> moff(M + 1, 0), woff(M + 1, 0);
     max_members_ = 0;
     for (size_t c = 0; c < M; ++c) {
         size_t n = (c >= c_lo && c < c_hi) ? h.cells[c].members.size() : 0;
         max_members_ = std::max(max_members_, n);
         moff[c + 1] = moff[c] + (uint32_t)n;
-        woff[c + 1] = woff[c] + (uint32_t)(npos * ((n + 7) / 8));
+        woff[c + 1] = woff[c] + (fs ? (uint32_t)(npos * ((n + 7) / 8)) : 0u);
     }
     {
         // seed scan blocks per query: the seed cells' groups of an average live cell, 128 a block,
@@ -115,6 +120,7 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
         size_t n = moff[c + 1] - moff[c], ng = (n + 7) / 8;
         std::copy(mem.begin(), mem.begin() + n, slots.begin() + moff[c]);
         uint32_t* cw = codes.data() + woff[c];
+        if (!fs) continue;
         for (size_t g = 0; g < ng; ++g)
             for (size_t b = 0; b < 8 && 8 * g + b < n; ++b) {
                 const uint64_t* code = &h.bits[(size_t)mem[8 * g + b] * nw];
@@ -136,7 +142,8 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
     moff_ = moff;
     v.cell_woff = upload_vec(woff);
     v.cell_slots = upload_vec(slots);
-    v.cell_codes = upload_vec(codes);
+    v.cell_codes = fs ? upload_vec(codes) : nullptr;
+    v.bits = fs ? nullptr : upload_vec(h.bits);
     v.slot_cells = upload_vec(h.slot_cells);
     v.ext_ids = upload_vec(h.ext_ids);
     v.tags = h.tags.empty() ? nullptr : upload_vec(h.tags);
@@ -438,8 +445,12 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     const int M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
     const int nprobe = std::max(1, std::min(a.nprobe, M));
     const int want0 = (int)((size_t)a.k * h.rerank_factor);
-    const int cand_cap = std::max(want0, 1);
     const int ent_cap = (int)std::min<size_t>((size_t)nprobe * max_members_ + 1, (size_t)1 << 30);
+    // FastScan keeps exactly want0 candidates; the Hamming scan keeps every tie at its cut-off, so
+    // its buffer has room to spare and grows after an overflow
+    const int cand_cap = view_.ham ? (int)std::min<size_t>((size_t)(2 * std::max(want0, 1) + 256) * grow_factor,
+                                                           (size_t)ent_cap)
+                                   : std::max(want0, 1);
     const bool filtering = h.has_filter && !h.tags.empty();
     const bool tree_router = h.tree != nullptr;
     const int chunk = std::min(a.nq, kPerQueryChunk);
@@ -545,6 +556,12 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
     if (a.nq <= 0) return kOk;
     cudaSetDevice(device_);
     if (!st) st = stream_;
+    if (view_.ham && (exch_ || use_cell_major(h, a))) {
+        err = exch_ ? "a sharded search needs FastScan blocks: call set_fastscan(True) and compact() first"
+                    : "the GPU cell-major join needs FastScan blocks: call set_fastscan(True) (then compact()), "
+                      "or search with cell_major=False";
+        return kUnsupported;
+    }
     dev::take_launch_error(nullptr);
     cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
     int rc = exch_                  ? search_sharded(h, dQ, a, d_ids, d_scores, d_nout, st, err)

@@ -84,7 +84,8 @@ class DeviceIndex {
     DebugOut* dbg = nullptr;
 
     ~DeviceIndex();
-    // Builds the device image from a compacted FastScan host index; returns an error message.
+    // Builds the device image of a host index; returns an error message. A compacted FastScan index
+    // gets the FastScan layout (both search paths); any other index its flat codes (per-query).
     // With a cell range, only cells [c_lo, c_hi) keep their members (a cell-range shard); the
     // routing tables and the rerank rows are always whole.
     std::string upload(const HostIndex& h, int device, uint32_t c_lo = 0, uint32_t c_hi = 0xFFFFFFFFu);
@@ -95,6 +96,8 @@ class DeviceIndex {
         shard_world_ = x ? world : 1;
     }
     bool sharded() const { return exch_ != nullptr; }
+    // scanned by Hamming distance over flat codes (no compacted FastScan blocks): per-query only
+    bool hamming() const { return view_.ham != 0; }
     uint64_t version() const { return version_; }
     int device() const { return device_; }
     cudaStream_t stream() const { return stream_; }

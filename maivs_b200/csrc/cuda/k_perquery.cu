@@ -1,5 +1,6 @@
-// The per-query path (index.rs search_one :1381-1864, FastScan branch): probe ranks, the scan of
-// every probed cell, and the sequential bucket queue with the adaptive stop.
+// The per-query path (index.rs search_one :1381-1864): probe ranks, the scan of every probed cell
+// (FastScan table sums, or Hamming distances over the flat codes of an index without FastScan
+// blocks), and the sequential bucket queue with the adaptive stop.
 #include "dev_common.cuh"
 
 namespace maivs {
@@ -39,6 +40,27 @@ __global__ void __launch_bounds__(kBS) k_pq_prep(IndexView ix, const uint32_t* _
         __syncthreads();
     }
     if (threadIdx.x == 0) so[n] = s_run;
+}
+
+// Tag filter (index.rs:1430-1439) and the per-query exactly-once rule (:1443-1460): false when
+// `slot` is filtered out or has another home ranked before probe r of cell c.
+__device__ __forceinline__ bool pq_member_ok(const IndexView& ix, uint32_t slot, uint32_t c, int r,
+                                             const uint32_t* crank, int filtering, uint32_t flo, uint32_t fhi) {
+    if (filtering) {
+        const uint32_t tg = __ldg(ix.tags + slot);
+        if (tg < flo || tg > fhi) return false;
+    }
+    if (ix.ma > 1) {
+        const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
+        for (int j = 0; j < ix.ma; ++j) {
+            const uint32_t h = __ldg(hs + j);
+            if (h != kNoCell && h != c) {
+                const uint32_t rh = __ldg(crank + h);
+                if (rh != kNoCell && rh < (uint32_t)r) return false;
+            }
+        }
+    }
+    return true;
 }
 
 // Every member of every chosen cell: (d << 32 | slot) when canonical under the first-ranked-home
@@ -92,24 +114,7 @@ __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const
                 const uint32_t sum = (tot >> (16 * (bb & 1))) & 0xFFFFu;
                 const uint32_t d = ix.maxk - sum;
                 const uint32_t slot = __ldg(ix.cell_slots + moff + pos);
-                bool ok = true;
-                if (filtering) {
-                    const uint32_t tg = __ldg(ix.tags + slot);
-                    ok = tg >= flo && tg <= fhi;
-                }
-                if (ok && ix.ma > 1) {
-                    const uint32_t* hs = ix.slot_cells + (size_t)slot * ix.ma;
-                    for (int j = 0; j < ix.ma; ++j) {
-                        const uint32_t h = __ldg(hs + j);
-                        if (h != kNoCell && h != c) {
-                            const uint32_t rh = __ldg(crank + h);
-                            if (rh != kNoCell && rh < (uint32_t)r) {
-                                ok = false;
-                                break;
-                            }
-                        }
-                    }
-                }
+                const bool ok = pq_member_ok(ix, slot, c, r, crank, filtering, flo, fhi);
                 out[pos] = ok ? (((uint64_t)d << 32) | slot) : kInvalidEntry;
             }
         }
@@ -117,16 +122,65 @@ __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const
     }
 }
 
-// The sequential part of the per-query scan: cells in probe order feed a bucket queue on d >> 6
-// with a falling cut-off tau, and the scan stops once no later cell can reach the current
-// want0-th best (index.rs:1630-1679). tau after any prefix of cells is the target-th smallest
-// bucket among that prefix's surviving entries, so whole cells are folded at once.
+// The Hamming scan of an index without compacted FastScan blocks (index.rs:1693-1790): every
+// member of every chosen cell as (h << 32 | slot), h = popcount(query code ^ member code) over the
+// flat codes (quantize.rs:183-201), under the same filter and exactly-once rules. One CTA per
+// (probe, query); a thread scores one member at a time, the query's code in shared memory. The
+// members of a compacted cell are consecutive slots, so a warp's code reads are one contiguous run.
+__global__ void __launch_bounds__(kBS) k_pq_scan_ham(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
+                                                     const uint32_t* __restrict__ nch, int nprobe, int filtering,
+                                                     uint32_t flo, uint32_t fhi, PerQueryBufs b) {
+    __shared__ uint64_t s_q[16];  // nw <= 16 words
+    const int r = blockIdx.x, q = blockIdx.y;
+    if (r >= (int)nch[q]) return;
+    const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
+    if (so[r + 1] > (uint32_t)b.ent_cap) return;  // reported by the fold
+    const uint32_t c = chosen[(size_t)q * nprobe + r];
+    const uint32_t moff = ix.cell_moff[c];
+    const int nc = (int)(ix.cell_moff[c + 1] - moff);
+    const int nw = ix.nw;
+    if (threadIdx.x < nw) s_q[threadIdx.x] = e.qbits[(size_t)q * nw + threadIdx.x];
+    __syncthreads();
+    const uint32_t* crank = b.crank + (size_t)q * ix.M;
+    uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
+    for (int pos = threadIdx.x; pos < nc; pos += kBS) {
+        const uint32_t slot = __ldg(ix.cell_slots + moff + pos);
+        const uint64_t* code = ix.bits + (size_t)slot * nw;
+        uint32_t h = 0;
+        for (int w = 0; w < nw; ++w) h += (uint32_t)__popcll(s_q[w] ^ __ldg(code + w));
+        const bool ok = pq_member_ok(ix, slot, c, r, crank, filtering, flo, fhi);
+        out[pos] = ok ? (((uint64_t)h << 32) | slot) : kInvalidEntry;
+    }
+}
+
+// score_to_cos(hamming_score(tau, dp)) of the binary scan (index.rs:1139-1164, quantize.rs:206-208):
+// s = dp - 2 tau, h = (dp - s) / 2, cos(pi h / dp), each step rounded to f32 as the reference does;
+// the cosine is rounded once from double precision (as cell_bound's).
+__device__ __forceinline__ float ham_tau_cos(uint32_t tau, uint32_t dp) {
+    const float dpf = (float)dp;
+    const float s = __fsub_rn(dpf, __fmul_rn(2.0f, (float)tau));
+    const float h = __fmul_rn(__fsub_rn(dpf, s), 0.5f);
+    const float x = __fdiv_rn(__fmul_rn(3.14159274101257324f, h), dpf);
+    return (float)cos((double)x);
+}
+
+// The sequential part of the per-query scan: cells in probe order feed a bucket queue with a
+// falling cut-off tau, and the scan stops once no later cell can reach the current want0-th best.
+// FastScan (kHam = false, index.rs:1630-1692): buckets d >> 6, the stop threshold from the table
+// estimate of the bucket's worst distance, then the top want0 by exact d. Hamming (kHam = true,
+// :1693-1848): buckets are the distances themselves, the threshold is score_to_cos of tau, and
+// every entry at or below the final tau is a candidate (ties kept). tau after any prefix of cells
+// is the target-th smallest bucket among that prefix's surviving entries, so whole cells are
+// folded at once.
+template <bool kHam>
 __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                                  const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
                                                  int nprobe, int target, int adaptive, float at_margin,
                                                  PerQueryBufs b) {
     extern __shared__ uint32_t sh[];
-    const int nb = (int)(ix.maxk >> 6) + 1;
+    constexpr int kShift = kHam ? 0 : 6;
+    const uint32_t top = kHam ? (uint32_t)ix.nw * 64u : ix.maxk >> 6;  // the largest bucket
+    const int nb = (int)top + 1;
     uint32_t* hist = sh;              // nb buckets
     float* suffix = reinterpret_cast<float*>(sh + nb);  // nprobe + 1
     __shared__ uint32_t s_add, s_tau, s_stop, s_cnt;
@@ -154,20 +208,20 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
             for (int i = n - 1; i >= 0; --i) suffix[i] = fmaxf(suffix[i], suffix[i + 1]);
     }
     if (threadIdx.x == 0) {
-        s_tau = ix.maxk >> 6;
+        s_tau = top;
         s_kept = 0;
         s_add = 0;
         s_stop = (uint32_t)n;
     }
     __syncthreads();
-    const float norm = fs_norm(ix.dim_pad);
-    const float delta = e.fs_delta[q], bias = e.fs_bias[q];
+    const float norm = kHam ? 0.0f : fs_norm(ix.dim_pad);
+    const float delta = kHam ? 0.0f : e.fs_delta[q], bias = kHam ? 0.0f : e.fs_bias[q];
     for (int r = 0; r < n; ++r) {
         const uint32_t tau = s_tau;
         for (uint32_t i = so[r] + threadIdx.x; i < so[r + 1]; i += kBS) {
             uint64_t k = ent[i];
             if (k == kInvalidEntry) continue;
-            uint32_t hc = (uint32_t)(k >> 32) >> 6;
+            uint32_t hc = (uint32_t)(k >> 32) >> kShift;
             if (hc <= tau) {
                 atomicAdd(&hist[hc], 1u);
                 atomicAdd(&s_add, 1u);
@@ -201,20 +255,49 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
             const unsigned long long kept = s_kept;
             const uint32_t t = s_tau;
             if (adaptive && kept >= (unsigned long long)target) {
-                uint32_t wsub = ((t + 1) << 6) - 1;
-                uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
-                float thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+                float thr;
+                if (kHam) {
+                    thr = ham_tau_cos(t, top);
+                } else {
+                    uint32_t wsub = ((t + 1) << 6) - 1;
+                    uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
+                    thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+                }
                 if (suffix[r + 1] < __fsub_rn(thr, at_margin)) s_stop = (uint32_t)(r + 1);
             }
         }
         __syncthreads();
         if (s_stop != (uint32_t)n) break;
     }
-    // candidates: entries of the scanned cells with bucket <= tau (index.rs:1680-1685)
+    // candidates: entries of the scanned cells with bucket <= tau (index.rs:1680-1685, :1809-1814)
     const uint32_t tau = s_tau, end = so[s_stop];
-    uint64_t* keys = b.ent + (size_t)q * b.ent_cap;  // compacted in place (order-free)
     using BS = cub::BlockScan<uint32_t, kBS>;
     __shared__ typename BS::TempStorage scan;
+    if (kHam) {
+        // every one of them goes to the rerank; more than cand_cap is an overflow (the host
+        // enlarges the buffers and searches again)
+        uint32_t* out = b.cand + (size_t)q * b.cand_cap;
+        if (threadIdx.x == 0) s_cnt = 0;
+        __syncthreads();
+        for (uint32_t base = 0; base < end; base += kBS) {
+            uint32_t i = base + threadIdx.x;
+            uint64_t k = i < end ? ent[i] : kInvalidEntry;
+            uint32_t f = (k != kInvalidEntry && (uint32_t)(k >> 32) <= tau) ? 1u : 0u;
+            uint32_t pos, agg;
+            BS(scan).ExclusiveSum(f, pos, agg);
+            uint32_t off = s_cnt;
+            if (f && off + pos < (uint32_t)b.cand_cap) out[off + pos] = (uint32_t)k;
+            __syncthreads();
+            if (threadIdx.x == 0) s_cnt = off + agg;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            if (s_cnt > (uint32_t)b.cand_cap) atomicAdd(b.overflow, 1u);
+            b.cand_n[q] = min(s_cnt, (uint32_t)b.cand_cap);
+        }
+        return;
+    }
+    uint64_t* keys = b.ent + (size_t)q * b.ent_cap;  // compacted in place (order-free)
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     for (uint32_t base = 0; base < end; base += kBS) {
@@ -263,13 +346,22 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
     { Tick tk(kKPqPrep, st);
     k_pq_prep<<<nq, kBS, 0, st>>>(ix, chosen, nch, nprobe, b); }
     { Tick tk(kKPqScan, st);
-    k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b); }
-    int nb = (int)(ix.maxk >> 6) + 1;
+    if (ix.ham)
+        k_pq_scan_ham<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b);
+    else
+        k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b); }
+    int nb = ix.ham ? ix.nw * 64 + 1 : (int)(ix.maxk >> 6) + 1;
     size_t smem = (size_t)nb * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
-    set_smem((const void*)k_pq_fold, smem);
+    const void* fold = ix.ham ? (const void*)k_pq_fold<true> : (const void*)k_pq_fold<false>;
+    set_smem(fold, smem);
     int target = std::max(want0, 1);
     { Tick tk(kKPqFold, st);
-    k_pq_fold<<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0, at_margin, b); }
+    if (ix.ham)
+        k_pq_fold<true><<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0,
+                                               at_margin, b);
+    else
+        k_pq_fold<false><<<nq, kBS, smem, st>>>(ix, e, chosen, cscore, nch, nprobe, target, adaptive ? 1 : 0,
+                                                at_margin, b); }
 }
 
 }  // namespace dev

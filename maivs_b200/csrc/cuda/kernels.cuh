@@ -34,6 +34,10 @@ struct IndexView {
     // (two homes at most; null otherwise). The exactly-once rule then needs one probed-bit test.
     const uint32_t* cell_lower;
     const uint32_t* tags;        // n_slots or null
+    // Hamming scan (an index without compacted FastScan blocks): the members' flat sign codes,
+    // nw words per slot, scanned by Hamming distance (index.rs:1693-1808); cell_codes is null
+    int ham;
+    const uint64_t* bits;
     // rerank store
     int rerank_mode;  // 0 f32, 1 per-dimension SQ8, 2 global int8
     const float* vecs_f32;

@@ -369,6 +369,11 @@ int search_emulated_shards(const HostIndex& h, std::vector<std::unique_ptr<Devic
                            const SearchArgs& a, uint64_t* d_ids, float* d_scores, uint32_t* d_nout, cudaStream_t st,
                            std::string& err) {
     const int W = (int)shards.size();
+    for (auto& sh : shards)
+        if (sh->hamming()) {
+            err = "a sharded search needs FastScan blocks: call set_fastscan(True) and compact() first";
+            return kUnsupported;
+        }
     std::vector<DeviceIndex::ShardRun> runs(W);
     auto gather = [&](bool topk) -> int {
         for (int s = 0; s < W; ++s)

@@ -85,13 +85,14 @@ int DeviceIndex::search_static(const HostIndex& h, const float* dQ, const Search
     const int nq = a.nq, M = view_.M, dim = view_.dim, nw = view_.nw, npos = view_.npos;
     const int nprobe = std::max(1, std::min(a.nprobe, M));
     const int want0 = (int)((size_t)a.k * h.rerank_factor);
-    const int cand_cap = std::max(want0, 1);
     const size_t ent_need = (size_t)nprobe * max_members_ + 1;
     if (ent_need > (size_t)1 << 30) {
         err = "nprobe x largest cell is too large for the allocation-free search";
         return kBadArg;
     }
     const int ent_cap = (int)ent_need;
+    // the Hamming scan keeps every tie at its cut-off: room for every scanned member
+    const int cand_cap = view_.ham ? ent_cap : std::max(want0, 1);
     const bool filtering = h.has_filter && !h.tags.empty();
     const bool tree_router = h.tree != nullptr;
 

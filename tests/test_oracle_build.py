@@ -69,3 +69,28 @@ def test_oracle_build_is_thread_count_independent():
     b8 = oracle_build_index(X, tree_min_cells=64)
     for name in ARRAYS:
         assert np.array_equal(b1.array(name).view(np.uint8), b8.array(name).view(np.uint8)), name
+
+
+@pytest.mark.parametrize("homes", [1, 2])
+def test_mutations_equal_oracle(homes):
+    """remove (index.rs:3223-3276), the refill of freed slots by add_batch (:3076-3198) and a
+    compaction that drops them (:929-1112), in the same order on both sides: the uncompacted and
+    the compacted index must match array for array (the uncompacted one is what the GPU's Hamming
+    scan reads)."""
+    X, _ = mixture(np.random.default_rng(77 + homes), 14_000, 384, 120)
+    base, extra = X[:12_000], X[12_000:]
+    kw = dict(homes=homes, tree_min_cells=32)
+    ix = build_index(base, rf=8, **kw)
+    b = oracle_build_index(base, rf=8, **kw)
+    gone = list(range(3, 12_000, 11))
+    for i in gone:
+        assert ix.remove(i) and b.remove(i)
+    assert not ix.remove(3) and not b.remove(3)
+    assert_same_index(ix, b)
+    new_ids = np.arange(50_000, 50_000 + extra.shape[0], dtype=np.uint64)
+    ix.add_batch(new_ids, extra)
+    b.add_batch(new_ids, extra)
+    assert_same_index(ix, b)
+    ix.compact()
+    b.compact()
+    assert_same_index(ix, b)
