@@ -179,6 +179,68 @@ int maivs_search_batch_sharded_emulated(maivs_index* ix, int world, const float*
  * "tree_leaf_ids", "config". */
 int maivs_array(maivs_index* ix, const char* name, const void** data, size_t* count, size_t* elem_bytes);
 
+/* ConcurrentIndex (src/concurrent.rs): immutable sealed segments plus one mutable head, deletes
+ * as tombstones by external id; reads never wait for a whole insert batch. One opaque handle is
+ * one ConcurrentIndex. Inserts, deletes, sealing and the configuration run on the host cores under
+ * the reference's locks (head -> sealed -> dead); search runs every segment and the head on the
+ * GPU by the per-query path (Hamming scan: segments never have FastScan blocks, as fork_empty
+ * turns FastScan off) and merges them in one kernel: tombstones dropped, one entry per id (its
+ * best score), best k, exact score ties by ascending id. Calls on one handle may come from any
+ * number of threads; its GPU searches run one at a time. Status codes as above;
+ * maivs_concurrent_last_error describes the last failure. */
+typedef struct maivs_concurrent maivs_concurrent;
+
+/* ConcurrentIndex(dim, scan_mode="binary", rerank_factor=8, seed=0x5EED, code_bits=0,
+ * seal_at=1000000) (concurrent.rs:159-172). On failure *out still holds a handle carrying the
+ * message; free it with maivs_concurrent_free. */
+int maivs_concurrent_new(size_t dim, const char* scan_mode, size_t rerank_factor, uint64_t seed, size_t code_bits,
+                         size_t seal_at, maivs_concurrent** out);
+void maivs_concurrent_free(maivs_concurrent* cx);
+const char* maivs_concurrent_last_error(maivs_concurrent* cx);
+/* train_centroids(vectors, n_cells, sample=262144, seed=0x5EED) on the head (concurrent.rs:322-326) */
+int maivs_concurrent_train_centroids(maivs_concurrent* cx, const float* vectors, size_t n, size_t n_cells,
+                                     size_t sample, uint64_t seed);
+/* add_batch(ids, vectors) (concurrent.rs:247-261): into the head, which is compacted and sealed
+ * into a segment once it holds seal_at vectors (the new head keeps its centroids, fork_empty). */
+int maivs_concurrent_add_batch(maivs_concurrent* cx, const uint64_t* ids, const float* vectors, size_t n);
+/* remove(id) -> bool (concurrent.rs:265-277): a tombstone; *removed = 0 for an unknown id or one
+ * already removed. remove_many(ids) -> count (:280-293). */
+int maivs_concurrent_remove(maivs_concurrent* cx, uint64_t id, int* removed);
+int maivs_concurrent_remove_many(maivs_concurrent* cx, const uint64_t* ids, size_t n, size_t* n_removed);
+/* seal() (:296-299); purge_head() -> count (:304-314): tombstoned head vectors are removed (in
+ * ascending id; the reference walks a hash set) and the head compacted; compact() (:343). */
+int maivs_concurrent_seal(maivs_concurrent* cx);
+int maivs_concurrent_purge_head(maivs_concurrent* cx, size_t* n_purged);
+int maivs_concurrent_compact(maivs_concurrent* cx);
+/* head configuration (concurrent.rs:328-341); a sealed segment keeps the settings it was built
+ * with. set_parallel_scan only records the flag: it picks the reference's CPU threading, and the
+ * GPU scan is parallel either way (keeping every tie at the cut-off, as the sequential path). */
+int maivs_concurrent_set_per_dim_sq(maivs_concurrent* cx, int on);
+int maivs_concurrent_set_two_stage(maivs_concurrent* cx, int on, size_t mult);
+int maivs_concurrent_set_adaptive(maivs_concurrent* cx, int on, float margin);
+int maivs_concurrent_set_parallel_scan(maivs_concurrent* cx, int on);
+int maivs_concurrent_set_graph_route(maivs_concurrent* cx, int on, size_t min_cells);
+int maivs_concurrent_set_tree_route(maivs_concurrent* cx, int on, size_t min_cells, size_t fanout,
+                                    float beam_frac);
+/* __len__ (:219-224) and one value of stats() (:226-242): "segments", "head_live",
+ * "sealed_live", "tombstones", "n_live", or any maivs_stat name of the head. */
+int maivs_concurrent_len(maivs_concurrent* cx, size_t* n);
+int maivs_concurrent_stat(maivs_concurrent* cx, const char* name, double* value);
+/* CUDA device of the searches (default 0). */
+int maivs_concurrent_to_device(maivs_concurrent* cx, int device);
+/* search(query, k, nprobe=16, target_confidence=0.95, beta=8.0) (:176-185): up to k results,
+ * *n_out of them. search_batch(queries, ...) (:187-217): nq*k, padded with UINT64_MAX / -inf. */
+int maivs_concurrent_search(maivs_concurrent* cx, const float* query, size_t k, size_t nprobe,
+                            float target_confidence, float beta, uint64_t* ids, float* scores, size_t* n_out);
+int maivs_concurrent_search_batch(maivs_concurrent* cx, const float* queries, size_t nq, size_t k, size_t nprobe,
+                                  float target_confidence, float beta, uint64_t* ids, float* scores);
+/* Inspection (no counterpart in the reference): the number of sealed segments, and one array of
+ * segment `segment` (-1 = the head) under maivs_array's names; the pointer stays valid until that
+ * segment next changes. */
+int maivs_concurrent_segments(maivs_concurrent* cx, size_t* n);
+int maivs_concurrent_array(maivs_concurrent* cx, long long segment, const char* name, const void** data,
+                           size_t* count, size_t* elem_bytes);
+
 /* profile(on) / profile_read(reset=True) (src/prof.rs:76-98): device time per query phase. The
  * reader fills up to `cap` (name, milliseconds) pairs; names are static strings. */
 int maivs_profile(int on);

@@ -72,6 +72,34 @@ _SIGS = {
     "maivs_debug_cellmajor": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_float,
                                         C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
                                         C.c_size_t]),
+    "maivs_concurrent_new": (C.c_int, [C.c_size_t, C.c_char_p, C.c_size_t, C.c_uint64, C.c_size_t, C.c_size_t,
+                                       C.POINTER(C.c_void_p)]),
+    "maivs_concurrent_free": (None, [C.c_void_p]),
+    "maivs_concurrent_last_error": (C.c_char_p, [C.c_void_p]),
+    "maivs_concurrent_train_centroids": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                                   C.c_uint64]),
+    "maivs_concurrent_add_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    "maivs_concurrent_remove": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_int)]),
+    "maivs_concurrent_remove_many": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_seal": (C.c_int, [C.c_void_p]),
+    "maivs_concurrent_purge_head": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_compact": (C.c_int, [C.c_void_p]),
+    "maivs_concurrent_set_per_dim_sq": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_concurrent_set_two_stage": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t]),
+    "maivs_concurrent_set_adaptive": (C.c_int, [C.c_void_p, C.c_int, C.c_float]),
+    "maivs_concurrent_set_parallel_scan": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_concurrent_set_graph_route": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t]),
+    "maivs_concurrent_set_tree_route": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t, C.c_size_t, C.c_float]),
+    "maivs_concurrent_len": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_stat": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double)]),
+    "maivs_concurrent_to_device": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_concurrent_search": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_float, C.c_float,
+                                          C.c_void_p, C.c_void_p, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_search_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                                C.c_float, C.c_float, C.c_void_p, C.c_void_p]),
+    "maivs_concurrent_segments": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_array": (C.c_int, [C.c_void_p, C.c_longlong, C.c_char_p, C.POINTER(C.c_void_p),
+                                         C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "maivs_profile": (C.c_int, [C.c_int]),
     "maivs_profile_read": (C.c_int, [C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.c_size_t,
                                      C.POINTER(C.c_size_t)]),

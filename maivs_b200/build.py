@@ -32,6 +32,7 @@ SOURCES = [
     ("host/index_build.cpp", "cxx"),
     ("host/persist.cpp", "cxx"),
     ("capi.cpp", "cxx"),
+    ("concurrent.cpp", "cxx"),
     ("cuda/clock.cu", "nvcc"),
     ("cuda/k_route.cu", "nvcc"),
     ("cuda/k_cellmajor.cu", "nvcc"),
@@ -42,8 +43,9 @@ SOURCES = [
     ("cuda/static_search.cu", "nvcc"),
     ("cuda/shard.cu", "nvcc"),
     ("cuda/build.cu", "nvcc"),
+    ("cuda/k_merge.cu", "nvcc"),
 ]
-HEADERS = ["host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/dev_common.cuh",
+HEADERS = ["handle.h", "host/hostmath.h", "host/index_host.h", "cuda/common.cuh", "cuda/kernels.cuh", "cuda/dev_common.cuh",
            "cuda/umma.cuh", "cuda/engine.h"]
 
 

@@ -19,23 +19,7 @@
 using maivs::DeviceIndex;
 using maivs::HostIndex;
 
-struct maivs_index {
-    HostIndex h;
-    // cell-range sharding (declared before `d`, which points at it, so it is destroyed after)
-    std::unique_ptr<maivs::Exchange> exch;
-    int shard_rank = 0, shard_world = 1;
-    std::unique_ptr<DeviceIndex> d;
-    // shards of the in-process emulation of the sharded protocol
-    std::vector<std::unique_ptr<DeviceIndex>> emu;
-    uint64_t emu_version = ~0ull;
-    int emu_world = 0, emu_device = -1;
-    int device = 0;
-    std::string err;
-    std::mutex mu;
-    // host copies served by maivs_array, rebuilt on demand
-    std::map<std::string, std::vector<uint8_t>> arrays;
-    uint64_t arrays_version = ~0ull;
-};
+#include "handle.h"
 
 namespace {
 
@@ -67,6 +51,7 @@ int ensure_device(maivs_index* ix) {
         return fail(ix, MAIVS_NO_DEVICE, "no CUDA device is visible; the MAIVS GPU search has no CPU fallback");
     if (ix->d && ix->d->version() == ix->h.version && ix->d->device() == ix->device) return MAIVS_OK;
     auto d = std::make_unique<DeviceIndex>();
+    if (ix->d) d->grow_factor = ix->d->grow_factor;  // candidate buffers stay as large as they grew
     uint32_t lo = 0, hi = 0xFFFFFFFFu;
     if (ix->exch) maivs::shard_range(ix->h, ix->shard_rank, ix->shard_world, &lo, &hi);
     std::string e = d->upload(ix->h, ix->device, lo, hi);
@@ -173,6 +158,11 @@ void build_arrays(maivs_index* ix) {
 }
 
 }  // namespace
+
+namespace maivs_capi {
+int device_image(maivs_index* ix) { return ensure_device(ix); }
+void host_arrays(maivs_index* ix) { build_arrays(ix); }
+}  // namespace maivs_capi
 
 extern "C" {
 

@@ -62,7 +62,7 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kKScanMma, kKSeedScan, kKAllGather, kNumKernels
+    kKScanMma, kKSeedScan, kKAllGather, kKSegMerge, kNumKernels
 };
 const char* kernel_name(int id);
 // Brackets a step that is not one of this library's kernels (an NCCL collective) on the thread's
@@ -206,6 +206,15 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
 void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int nq, const uint32_t* cand,
                    const uint32_t* cand_n, int cand_cap, int k, uint64_t* ids, float* scores, uint32_t* out_n,
                    float* score_scratch, uint32_t* item_scratch, uint32_t* err, cudaStream_t st);
+
+// ConcurrentIndex::finish (concurrent.rs:83-110) of every query over L per-segment result lists:
+// list l of query q is ids/scores[(l * nq + q) * want ..] with nout[l * nq + q] entries. Drops the
+// ids found in `tomb` (ascending, ntomb entries), keeps one entry per id (its best score), and
+// writes the best k by score (exact ties by ascending id) to out_ids/out_scores (nq x k, padded
+// with UINT64_MAX / -inf). `scratch` holds L * want * 16 bytes per query.
+void launch_segment_merge(const uint64_t* ids, const float* scores, const uint32_t* nout, int L, int nq, int want,
+                          const uint64_t* tomb, int ntomb, int k, void* scratch, uint64_t* out_ids, float* out_scores,
+                          cudaStream_t st);
 
 }  // namespace dev
 }  // namespace maivs

@@ -535,6 +535,66 @@ std::string HostIndex::add_batch(const uint64_t* ids, const float* data, size_t 
     return "";
 }
 
+void HostIndex::fork_empty(HostIndex& f) const {
+    // index.rs:2330-2400
+    f.dim = dim;
+    f.dim_pad = dim_pad;
+    f.nw = nw;
+    f.seed = seed;
+    f.rerank_factor = rerank_factor;
+    f.signs = signs;
+    f.two_stage = two_stage;
+    f.shortlist_mult = shortlist_mult;
+    f.centroid_sq8 = centroid_sq8;
+    f.tree_route = tree_route;
+    f.tree_min_cells = tree_min_cells;
+    f.tree_fanout = tree_fanout;
+    f.tree_beam_frac = tree_beam_frac;
+    f.graph_route = graph_route;
+    f.graph_min_cells = graph_min_cells;
+    f.max_assign = max_assign;
+    f.spill_margin = spill_margin;
+    f.spill_lambda = spill_lambda;
+    f.fastscan = false;
+    f.per_dim_sq = per_dim_sq;
+    f.i8_rerank = i8_rerank;
+    f.keep_f32 = keep_f32;
+    f.adaptive = adaptive;
+    f.at_margin = at_margin;
+    f.quant_scale = quant_scale;
+    f.cm_min_batch = cm_min_batch;
+    f.sq_min = sq_min;
+    f.sq_step = sq_step;
+    f.build_device = build_device;
+    f.bits.clear();
+    f.scan_i8.clear();
+    f.vecs_f32.clear();
+    f.ext_ids.clear();
+    f.slot_cell.clear();
+    f.slot_cells.clear();
+    f.free_slots.clear();
+    f.id_to_slot.clear();
+    f.tags.clear();
+    f.has_filter = false;
+    f.filter_lo = 0;
+    f.filter_hi = 0xFFFFFFFFu;
+    f.n_live = 0;
+    f.compacted = false;
+    f.prim_len.clear();
+    f.rep_off.clear();
+    f.fs_codes.clear();
+    f.fs_off.clear();
+    f.tree.reset();
+    f.tree_cells = 0;
+    f.cells.assign(cells.size(), Cell{});
+    for (size_t c = 0; c < cells.size(); ++c) {
+        f.cells[c].centroid = cells[c].centroid;
+        f.cells[c].sum.assign(dim, 0.0f);
+    }
+    f.refresh_derived();
+    ++f.version;
+}
+
 bool HostIndex::remove(uint64_t id) {
     // index.rs:3223-3276
     auto it = id_to_slot.find(id);

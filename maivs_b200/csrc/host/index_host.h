@@ -158,6 +158,9 @@ struct HostIndex {
     void set_replication(size_t max_assign, float spill_margin);
     void set_fastscan(bool on);
     std::string set_tags(const uint64_t* ids, const uint32_t* tags, size_t n);
+    // fork_empty (index.rs:2330-2400): `f` becomes an empty index with this one's configuration,
+    // rotation, quantisation parameters and centroids; FastScan off, not compacted, no tags.
+    void fork_empty(HostIndex& f) const;
 
     size_t live_cell_count() const;
     void refresh_derived();
