@@ -1,7 +1,7 @@
 """B200-native MAIVS query engine: a drop-in for the reference's `maivs` Python module.
 
-`FlatCellIndex` keeps the reference's constructor, method names, defaults, return types and
-errors (src/index.rs #[pymethods], src/lib.rs:32-39). The index is built on the host cores;
+`FlatCellIndex` and `ConcurrentIndex` keep the reference's constructors, method names, defaults,
+return types and errors (src/index.rs and src/concurrent.rs #[pymethods], src/lib.rs:32-39). The index is built on the host cores;
 `search` / `search_batch` run on the GPU through hand-written sm_100a kernels behind the C ABI of
 include/maivs_b200.h. There is no CPU search path: without a CUDA device, search raises.
 """
@@ -14,7 +14,8 @@ import numpy as np
 
 from . import _lib
 
-__all__ = ["FlatCellIndex", "profile", "profile_read", "MaivsError", "nccl_unique_id", "shard_over_torch"]
+__all__ = ["FlatCellIndex", "ConcurrentIndex", "profile", "profile_read", "MaivsError", "nccl_unique_id",
+           "shard_over_torch"]
 
 
 class MaivsError(RuntimeError):
@@ -42,7 +43,10 @@ class FlatCellIndex:
     cell-major batch search and exact rerank; queries run on the GPU.
 
     Only scan_mode="binary" is served (the reference's "f32"/"i8" modes are ablations that no
-    preset uses); a compacted FastScan index is required before searching."""
+    preset uses). A compacted FastScan index is searched by FastScan table sums (per query or by
+    the cell-major join); any other index (before compact(), after a remove(), FastScan off) by
+    Hamming distance per query, as the reference does (the cell-major join then needs
+    set_fastscan(True) and compact())."""
 
     def __init__(self, dim: int, scan_mode: str = "f32", rerank_factor: int = 4, seed: int = 0x5EED,
                  code_bits: int = 0):
@@ -221,8 +225,9 @@ class FlatCellIndex:
     @staticmethod
     def load(path: str) -> "FlatCellIndex":
         """Load an index written by save() here or by the reference. Like the reference, the loaded
-        index is not compacted and has FastScan off: call set_fastscan(True) and compact() before
-        searching it on the GPU."""
+        index is not compacted and has FastScan off, so it is searched per query by Hamming
+        distance; set_fastscan(True) and compact() give it the FastScan scan and the cell-major
+        join."""
         L = _lib.lib()
         h = C.c_void_p()
         rc = L.maivs_load(str(path).encode(), C.byref(h))
@@ -387,6 +392,177 @@ CONFIG_FIELDS = ("dim", "dim_pad", "nw", "rerank_factor", "two_stage", "shortlis
                  "max_assign", "fastscan", "per_dim_sq", "i8_rerank", "keep_f32", "adaptive", "at_margin",
                  "quant_scale", "compacted", "n_live", "cm_min_batch", "has_filter", "filter_lo", "filter_hi",
                  "tree_beam_frac", "tree_n_leaf", "graph_route", "graph_min_cells")
+
+
+class ConcurrentIndex:
+    """Reads over immutable segments plus one mutable head (src/concurrent.rs): inserts go to the
+    head, which is compacted and sealed into a segment at `seal_at` vectors; deletes are tombstones
+    by id. Every search runs all segments and the head on the GPU (per query, Hamming scan) and
+    merges them there (tombstones dropped, one entry per id, best k). Safe to call from several
+    threads; a write blocks readers for one insert batch at most."""
+
+    def __init__(self, dim: int, scan_mode: str = "binary", rerank_factor: int = 8, seed: int = 0x5EED,
+                 code_bits: int = 0, seal_at: int = 1_000_000):
+        L = _lib.lib()
+        h = C.c_void_p()
+        rc = L.maivs_concurrent_new(int(dim), scan_mode.encode(), int(rerank_factor), int(seed) & (2**64 - 1),
+                                    int(code_bits), int(seal_at), C.byref(h))
+        self._h = h
+        self._dim = int(dim)
+        if rc != _lib.OK:
+            msg = L.maivs_concurrent_last_error(h).decode() if h else "allocation failed"
+            if h:
+                L.maivs_concurrent_free(h)
+            self._h = None
+            raise ValueError(msg)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            _lib.lib().maivs_concurrent_free(h)
+            self._h = None
+
+    def _check(self, rc: int) -> None:
+        if rc == _lib.OK:
+            return
+        L = _lib.lib()
+        msg = L.maivs_concurrent_last_error(self._h).decode()
+        if rc in (_lib.BAD_SHAPE, _lib.BAD_ARG, _lib.BAD_STATE):
+            raise ValueError(msg)
+        raise MaivsError(f"{L.maivs_status_string(rc).decode()}: {msg}")
+
+    @property
+    def dim(self) -> int:
+        return self._dim
+
+    # ---- reads (GPU) ----
+    def search(self, query: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+               beta: float = 8.0):
+        q = np.ascontiguousarray(np.asarray(query, dtype=np.float32).reshape(-1))
+        if q.shape[0] != self._dim:
+            raise ValueError("query dim mismatch")
+        ids = np.empty(max(int(k), 1), dtype=np.uint64)
+        sc = np.empty(max(int(k), 1), dtype=np.float32)
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_search(self._h, _ptr(q), int(k), int(nprobe),
+                                                       float(target_confidence), float(beta), _ptr(ids), _ptr(sc),
+                                                       C.byref(n)))
+        m = n.value
+        return [int(x) for x in ids[:m]], [float(x) for x in sc[:m]]
+
+    def search_batch_arrays(self, queries: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+                            beta: float = 8.0):
+        """search_batch returning numpy arrays (ids uint64 [nq*k], scores float32 [nq*k])."""
+        Q = _as_f32_matrix(queries, "queries", self._dim)
+        nq = Q.shape[0]
+        ids = np.empty(nq * int(k), dtype=np.uint64)
+        sc = np.empty(nq * int(k), dtype=np.float32)
+        self._check(_lib.lib().maivs_concurrent_search_batch(self._h, _ptr(Q), nq, int(k), int(nprobe),
+                                                             float(target_confidence), float(beta), _ptr(ids),
+                                                             _ptr(sc)))
+        return ids, sc
+
+    def search_batch(self, queries: np.ndarray, k: int, nprobe: int = 16, target_confidence: float = 0.95,
+                     beta: float = 8.0):
+        ids, sc = self.search_batch_arrays(queries, k, nprobe, target_confidence, beta)
+        return ids.tolist(), sc.tolist()
+
+    def __len__(self) -> int:
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_len(self._h, C.byref(n)))
+        return n.value
+
+    def stats(self) -> dict:
+        out = {}
+        v = C.c_double(0.0)
+        for name in FlatCellIndex._STATS + ("segments", "head_live", "sealed_live", "tombstones"):
+            self._check(_lib.lib().maivs_concurrent_stat(self._h, name.encode(), C.byref(v)))
+            out[name] = float(v.value)
+        return out
+
+    # ---- writes (host cores) ----
+    def add_batch(self, ids, vectors: np.ndarray) -> None:
+        ids_a = np.ascontiguousarray(np.asarray(list(ids) if not isinstance(ids, np.ndarray) else ids,
+                                                dtype=np.uint64))
+        v = np.asarray(vectors)
+        if v.ndim != 2 or v.shape[0] != ids_a.shape[0] or v.shape[1] != self._dim:
+            raise ValueError("shape mismatch")
+        if v.dtype != np.float32:
+            raise TypeError("vectors must be a float32 numpy array")
+        if not v.flags["C_CONTIGUOUS"]:
+            raise ValueError("vectors must be C-contiguous (use np.ascontiguousarray)")
+        self._check(_lib.lib().maivs_concurrent_add_batch(self._h, _ptr(ids_a), _ptr(v), ids_a.shape[0]))
+
+    def remove(self, id: int) -> bool:
+        r = C.c_int(0)
+        self._check(_lib.lib().maivs_concurrent_remove(self._h, int(id), C.byref(r)))
+        return bool(r.value)
+
+    def remove_many(self, ids) -> int:
+        a = np.ascontiguousarray(np.asarray(list(ids) if not isinstance(ids, np.ndarray) else ids, dtype=np.uint64))
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_remove_many(self._h, _ptr(a) if a.size else None, a.shape[0],
+                                                            C.byref(n)))
+        return n.value
+
+    def seal(self) -> None:
+        self._check(_lib.lib().maivs_concurrent_seal(self._h))
+
+    def purge_head(self) -> int:
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_purge_head(self._h, C.byref(n)))
+        return n.value
+
+    # ---- configuration (the head; concurrent.rs:316-343) ----
+    def train_centroids(self, vectors: np.ndarray, n_cells: int, sample: int = 262_144, seed: int = 0x5EED) -> None:
+        v = _as_f32_matrix(vectors, "vectors", self._dim)
+        self._check(_lib.lib().maivs_concurrent_train_centroids(self._h, _ptr(v), v.shape[0], int(n_cells),
+                                                                int(sample), int(seed) & (2**64 - 1)))
+
+    def set_per_dim_sq(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_per_dim_sq(self._h, int(bool(on))))
+
+    def set_two_stage(self, on: bool, mult: int) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_two_stage(self._h, int(bool(on)), int(mult)))
+
+    def set_adaptive(self, on: bool, margin: float) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_adaptive(self._h, int(bool(on)), float(margin)))
+
+    def set_parallel_scan(self, on: bool) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_parallel_scan(self._h, int(bool(on))))
+
+    def set_graph_route(self, on: bool, min_cells: int = 0) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_graph_route(self._h, int(bool(on)), int(min_cells)))
+
+    def set_tree_route(self, on: bool, min_cells: int = 0, fanout: int = 0, beam_frac: float = 0.0) -> None:
+        self._check(_lib.lib().maivs_concurrent_set_tree_route(self._h, int(bool(on)), int(min_cells), int(fanout),
+                                                               float(beam_frac)))
+
+    def compact(self) -> None:
+        self._check(_lib.lib().maivs_concurrent_compact(self._h))
+
+    def to_device(self, device: int = 0) -> None:
+        """CUDA device of the searches (default 0)."""
+        self._check(_lib.lib().maivs_concurrent_to_device(self._h, int(device)))
+
+    # ---- inspection (no counterpart in the reference) ----
+    def n_segments(self) -> int:
+        n = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_segments(self._h, C.byref(n)))
+        return n.value
+
+    def segment_array(self, segment: int, name: str) -> np.ndarray:
+        """Copy of one array of sealed segment `segment` (-1: the head), as FlatCellIndex.array."""
+        p = C.c_void_p()
+        n = C.c_size_t(0)
+        eb = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_array(self._h, int(segment), name.encode(), C.byref(p), C.byref(n),
+                                                      C.byref(eb)))
+        dt = np.dtype(_ARRAY_DTYPES.get(name))
+        if n.value == 0 or not p.value:
+            return np.zeros(0, dtype=dt)
+        raw = np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(n.value * eb.value,))
+        return raw.view(dt).copy()
 
 
 def nccl_unique_id() -> bytes:

@@ -461,3 +461,114 @@ def build_preset(X: np.ndarray, preset: str = "quality", rerank_factor: int = 16
     b.add_batch(np.arange(n, dtype=np.uint64) if ids is None else ids, X)
     b.compact()
     return b
+
+
+class OracleConcurrentIndex:
+    """ConcurrentIndex (src/concurrent.rs) restated over oracle builds: sealed segments, one mutable
+    head, tombstones. Every search runs search_one on each segment and on the head (the per-query
+    path, :113-131) with k over-fetched twice once tombstones exist (:50-52, :116-117), then
+    finish (:83-110): tombstones dropped, the best score per id, the best k (exact ties by ascending
+    id, the product's rule for the reference's unstable sort). Single-threaded: the locks of the
+    reference order concurrent calls but do not change what one sequence of calls computes."""
+
+    OVERFETCH = 2
+
+    def __init__(self, dim: int, scan_mode: str = "binary", rerank_factor: int = 8, seed: int = 0x5EED,
+                 code_bits: int = 0, seal_at: int = 1_000_000):
+        self.dim = int(dim)
+        self.head = OracleBuild(dim, scan_mode, rerank_factor, seed, code_bits)
+        self.sealed: list[tuple[OracleBuild, OracleIndex]] = []
+        self.dead: set[int] = set()
+        self.sealed_live = 0
+        self.seal_at = max(int(seal_at), 1)
+        self.par_scan = False
+
+    # seal_locked (:134-152)
+    def _seal(self) -> None:
+        if self.head.n_live() == 0:
+            return
+        self.head.compact()
+        fresh = self.head.fork_empty()
+        frozen, self.head = self.head, fresh
+        self.sealed.append((frozen, frozen.snapshot()))
+        self.sealed_live += frozen.n_live()
+
+    def add_batch(self, ids, vectors) -> None:  # :247-261
+        self.head.add_batch(ids, vectors)
+        if self.head.n_live() >= self.seal_at:
+            self._seal()
+
+    def _known(self, id: int) -> bool:
+        return self.head.has_id(id) or any(b.has_id(id) for b, _ in self.sealed)
+
+    def remove(self, id: int) -> bool:  # :265-277
+        id = int(id)
+        if not self._known(id) or id in self.dead:
+            return False
+        self.dead.add(id)
+        return True
+
+    def remove_many(self, ids) -> int:  # :280-293
+        return sum(self.remove(int(i)) for i in ids)
+
+    def seal(self) -> None:
+        self._seal()
+
+    def purge_head(self) -> int:  # :304-314, victims in ascending id
+        victims = sorted(i for i in self.dead if self.head.has_id(i))
+        for i in victims:
+            self.head.remove(i)
+            self.dead.discard(i)
+        self.head.compact()
+        return len(victims)
+
+    def compact(self) -> None:
+        self.head.compact()
+
+    def train_centroids(self, vectors, n_cells: int, sample: int = 262_144, seed: int = 0x5EED) -> None:
+        self.head.train_centroids(vectors, n_cells, sample, seed)
+
+    def set_per_dim_sq(self, on: bool) -> None:
+        self.head.set_per_dim_sq(on)
+
+    def set_two_stage(self, on: bool, mult: int) -> None:
+        self.head.set_two_stage(on, mult)
+
+    def set_adaptive(self, on: bool, margin: float) -> None:
+        self.head.set_adaptive(on, margin)
+
+    def set_parallel_scan(self, on: bool) -> None:
+        self.par_scan = bool(on)
+
+    def set_graph_route(self, on: bool, min_cells: int = 0) -> None:
+        self.head.set_graph_route(on, min_cells)
+
+    def set_tree_route(self, on: bool, min_cells: int = 0, fanout: int = 0, beam_frac: float = 0.0) -> None:
+        self.head.set_tree_route(on, min_cells, fanout, beam_frac)
+
+    def __len__(self) -> int:
+        return max(self.sealed_live + self.head.n_live() - len(self.dead), 0)
+
+    def search_batch(self, Q: np.ndarray, k: int, nprobe: int = 16, tc: float = 0.95, beta: float = 8.0):
+        """ids (uint64, nq*k) and scores (float32, nq*k), padded with UINT64_MAX / -inf."""
+        Q = np.ascontiguousarray(Q, dtype=np.float32)
+        nq = Q.shape[0]
+        want = k if not self.dead else k * self.OVERFETCH
+        lists = [o.search_batch(Q, want, nprobe, tc, beta, cell_major=False)[:2] for _, o in self.sealed]
+        lists.append(self.head.snapshot().search_batch(Q, want, nprobe, tc, beta, cell_major=False)[:2])
+        ids = np.full(nq * k, np.iinfo(np.uint64).max, np.uint64)
+        sc = np.full(nq * k, -np.inf, np.float32)
+        pad = np.iinfo(np.uint64).max
+        for qi in range(nq):
+            best: dict[int, np.float32] = {}
+            for li, ls in lists:
+                for i, s in zip(li[qi * want:(qi + 1) * want].tolist(), ls[qi * want:(qi + 1) * want]):
+                    if i == pad or i in self.dead:
+                        continue
+                    if i not in best or s > best[i]:
+                        best[i] = s
+            top = sorted(best.items(), key=lambda t: (-float(t[1]), t[0]))[:k]
+            for r, (i, s) in enumerate(top):
+                ids[qi * k + r] = i
+                sc[qi * k + r] = s
+        return ids, sc
