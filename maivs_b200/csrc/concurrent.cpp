@@ -234,7 +234,10 @@ int search_pass(maivs_concurrent* cx, const SegList& segs, const float* Q, size_
         if (le != cudaSuccess)
             return cfail(cx, MAIVS_CUDA_ERROR,
                          std::string("launch of ") + maivs::dev::kernel_name(kid) + " failed: " + cudaGetErrorString(le));
-        if (cudaMemcpyAsync(hp + qb, oid, ob, cudaMemcpyDeviceToHost, cx->st) != cudaSuccess ||
+        // ids, then scores (separate device carves)
+        if (cudaMemcpyAsync(hp + qb, oid, nq * k * sizeof(uint64_t), cudaMemcpyDeviceToHost, cx->st) != cudaSuccess ||
+            cudaMemcpyAsync(hp + qb + nq * k * sizeof(uint64_t), osc, nq * k * sizeof(float), cudaMemcpyDeviceToHost,
+                            cx->st) != cudaSuccess ||
             cudaStreamSynchronize(cx->st) != cudaSuccess)
             return cfail(cx, MAIVS_CUDA_ERROR, std::string("search failed: ") + cudaGetErrorString(cudaGetLastError()));
         // candidate-buffer overflows of any segment: enlarge that segment's buffers, search again
