@@ -905,6 +905,114 @@ def run_lowbatch(args):
     print(json.dumps(out), flush=True)
 
 
+def run_concurrent(args):
+    """ConcurrentIndex (src/concurrent.rs) on the config-2 vectors: 500k x 384 inserted in batches of
+    50k with seal_at 100k (five sealed segments), 1% of them deleted (tombstones), then 20k more
+    into the head. One step = one search_batch of 1,000 queries through the public API with host
+    buffers (every segment and the head searched on the GPU, merged there): end-to-end QPS, at the
+    smallest nprobe on the grid whose R@10 against brute force over the live vectors is >= 0.99."""
+    import torch
+
+    import maivs_b200 as M
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_new = 20_000
+    X, Q, _ = mixture(args.seed, args.n + n_new, args.nq, 384, 1000, 0.35)
+    base, extra = X[:args.n], X[args.n:]
+    rf = args.rf or 32
+    seal_at = 100_000
+    batch = 50_000
+    dead = np.arange(0, args.n, 100, dtype=np.uint64)
+    ncells = max(16, args.n // 128)
+
+    def drive(cx):
+        cx.train_centroids(base, ncells)
+        for lo in range(0, args.n, batch):
+            cx.add_batch(np.arange(lo, min(lo + batch, args.n), dtype=np.uint64),
+                         np.ascontiguousarray(base[lo:lo + batch]))
+        cx.remove_many(dead)
+        cx.add_batch(np.arange(args.n, args.n + n_new, dtype=np.uint64), np.ascontiguousarray(extra))
+
+    t0 = time.perf_counter()
+    cx = M.ConcurrentIndex(384, "binary", rf, 0x5EED, 0, seal_at)
+    cx.set_build_device(0)
+    drive(cx)
+    build_s = time.perf_counter() - t0
+    cx.to_device(0)
+    live = np.ones(X.shape[0], bool)
+    live[dead.astype(np.int64)] = False
+    live_ids = np.nonzero(live)[0]
+    truth = live_ids[brute_force_topk(X[live_ids], Q, K, str(dev))]
+
+    def search(np_):
+        ids, _ = cx.search_batch_arrays(Q, K, np_, 1.0, 8.0)
+        return ids
+
+    np_, rec = NP_GRID[-1], 0.0
+    for p in NP_GRID:
+        r = recall(search(p), truth)
+        np_, rec = p, r
+        if r >= TARGET_RECALL:
+            break
+    for _ in range(max(args.warmup, 3)):
+        search(np_)
+    steps = max(args.steps, 10)
+    ts = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        search(np_)
+        ts.append(time.perf_counter() - t)
+    mean_s = float(np.mean(ts))
+    cx.kernel_clock(True)
+    cx.kernel_times(reset=True)
+    for _ in range(5):
+        search(np_)
+    kt = cx.kernel_times(reset=True)
+    cx.kernel_clock(False)
+    tot = max(sum(v[0] for v in kt.values()), 1e-9)
+    shares = {k: round(v[0] / tot, 4) for k, v in kt.items() if v[1]}
+    # the reference's path restated (the oracle's ConcurrentIndex over its own builds of the same
+    # calls), on every host core, over a bounded sample; and parity of that sample
+    threads = os.cpu_count() or 1
+    oracle.lib().oracle_set_threads(threads)
+    ox = oracle.OracleConcurrentIndex(384, "binary", rf, 0x5EED, 0, seal_at)
+    drive(ox)
+    sample = np.ascontiguousarray(Q[:args.parity_sample or 200])
+    ref_ids, ref_sc = ox.search_batch(sample, K, np_, 1.0, 8.0)
+    got_ids, got_sc = cx.search_batch_arrays(sample, K, np_, 1.0, 8.0)
+    parity = bool(np.array_equal(got_ids, ref_ids) and np.array_equal(got_sc.view(np.uint32), ref_sc.view(np.uint32)))
+    ct = []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 12.0 or not ct:
+        t = time.perf_counter()
+        ox.search_batch(sample, K, np_, 1.0, 8.0)
+        ct.append(time.perf_counter() - t)
+    qps = args.nq / mean_s
+    out = {"metric": "ConcurrentIndex batch QPS at R@10=0.99 (d=384), 5 sealed segments + head, 1% tombstones",
+           "value": round(qps, 1), "unit": "queries/s", "n_gpus": 1, "steps": steps, "warmup": max(args.warmup, 3),
+           "ms_per_step": round(mean_s * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "u64", "data": "synthetic",
+           "e2e": {"value": round(qps, 1), "unit": "queries/s", "h2d_bytes_per_step": int(Q.nbytes),
+                   "d2h_bytes_per_step": int(args.nq * K * 12)},
+           "config": {"workload": "ConcurrentIndex over BASELINE configs[1]'s vectors (500k x 384 Gaussian mixture, "
+                                  "1000 comps, sigma 0.35) + 20k inserted after 1% deletes; reference defaults "
+                                  "(tree routing, no adaptive), Hamming scan per query per segment",
+                      "n": args.n + n_new, "segments": cx.n_segments(), "head_live": int(cx.stats()["head_live"]),
+                      "tombstones": int(dead.size), "rerank_factor": rf, "nprobe": np_,
+                      "recall_at_10": round(rec, 4), "build_s": round(build_s, 1), "timing": "host clock around "
+                      "each search_batch call (host buffers in and out; the call synchronises)"},
+           "kernel_shares": shares, "gpu_launches": int(sum(v[1] for v in kt.values()) / 5),
+           "parity": {"sample": int(sample.shape[0]), "ids_and_scores_equal": parity},
+           "cpu_baseline": {"value": round(sample.shape[0] / float(np.mean(ct)), 1), "unit": "queries/s",
+                            "cores": threads, "kind": "port",
+                            "sample": f"{sample.shape[0]} queries per call through the oracle's ConcurrentIndex "
+                                      f"(search_one per segment on {threads} threads, then finish); "
+                                      f"mean of {len(ct)} calls"}}
+    print(json.dumps(out), flush=True)
+
+
 def run_reference(args):
     """The reference's CPU path (the oracle: a C++ restatement of the reference's Rust build and
     query path; the reference itself cannot be built here) on every host core. The index is the
@@ -1019,11 +1127,12 @@ def main():
     ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
     ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
     ap.add_argument("--no-sweep", action="store_true", help="config2: skip the (rf, nprobe) recall sweep")
-    ap.add_argument("--workload", choices=("auto", "config2", "sharded", "lowbatch"), default="auto",
+    ap.add_argument("--workload", choices=("auto", "config2", "sharded", "lowbatch", "concurrent"), default="auto",
                     help="auto: sharded under torchrun (WORLD_SIZE set), else config2. config2: the headline 500k "
                          "batch on one GPU (replicas when forced under torchrun); sharded: configs[3], 5.2M vectors "
                          "with cells sharded by range over the N GPUs; lowbatch: configs[2], memory preset at "
-                         "batch 1 and 16")
+                         "batch 1 and 16; concurrent: a ConcurrentIndex (sealed segments + head + tombstones) over "
+                         "the config2 vectors")
     ap.add_argument("--parity-sample", type=int, default=1000,
                     help="sharded: queries of the timed batch checked against the oracle (0: none)")
     args = ap.parse_args()
@@ -1040,6 +1149,8 @@ def main():
         run_sharded(args)
     elif args.workload == "lowbatch":
         run_lowbatch(args)
+    elif args.workload == "concurrent":
+        run_concurrent(args)
     else:
         run_maivs(args)
 

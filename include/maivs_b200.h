@@ -95,7 +95,11 @@ int maivs_search(maivs_index* ix, const float* query, size_t k, size_t nprobe, f
                  uint64_t* ids, float* scores, size_t* n_out);
 
 /* search_batch(queries, k, nprobe=16, target_confidence=0.95, beta=8.0, cell_major=True)
- * (index.rs:3316-3391). ids/scores are nq*k, row-major, padded with UINT64_MAX / -inf. */
+ * (index.rs:3316-3391). ids/scores are nq*k, row-major, padded with UINT64_MAX / -inf. A compacted
+ * FastScan index is scanned by FastScan table sums (cell-major join or per query); any other index
+ * (before compact(), after a remove(), FastScan off) by Hamming distance per query, as the reference
+ * does (index.rs:1624-1626); the cell-major join of a compacted index without FastScan blocks is
+ * MAIVS_UNSUPPORTED on the GPU (search it with cell_major = 0, or set FastScan and compact). */
 int maivs_search_batch(maivs_index* ix, const float* queries, size_t nq, size_t k, size_t nprobe,
                        float target_confidence, float beta, int cell_major, uint64_t* ids, float* scores);
 
@@ -142,8 +146,9 @@ int maivs_search_batch_device_noalloc(maivs_index* ix, const float* d_queries, s
 
 /* save(path) / load(path) (index.rs:3594-3603, src/persist.rs): the reference's on-disk format
  * "MAIVS2\0\1", so files move between the two implementations. A loaded index is not compacted
- * and has FastScan off, as in the reference; call maivs_set_fastscan(1) and maivs_compact() before
- * searching it on the GPU. maivs_load always returns a handle in *out (on failure it holds the
+ * and has FastScan off, as in the reference, so it is searched per query by Hamming distance;
+ * maivs_set_fastscan(1) and maivs_compact() give it the FastScan scan and the cell-major join.
+ * maivs_load always returns a handle in *out (on failure it holds the
  * message for maivs_last_error; free it with maivs_index_free). Only scan_mode "binary" files
  * without f16 rerank rows load. */
 int maivs_save(maivs_index* ix, const char* path);
@@ -222,6 +227,9 @@ int maivs_concurrent_set_parallel_scan(maivs_concurrent* cx, int on);
 int maivs_concurrent_set_graph_route(maivs_concurrent* cx, int on, size_t min_cells);
 int maivs_concurrent_set_tree_route(maivs_concurrent* cx, int on, size_t min_cells, size_t fanout,
                                     float beam_frac);
+/* Build device of the head and of every later head (no counterpart in the reference), as
+ * maivs_set_build_device. */
+int maivs_concurrent_set_build_device(maivs_concurrent* cx, int device);
 /* __len__ (:219-224) and one value of stats() (:226-242): "segments", "head_live",
  * "sealed_live", "tombstones", "n_live", or any maivs_stat name of the head. */
 int maivs_concurrent_len(maivs_concurrent* cx, size_t* n);
@@ -238,6 +246,11 @@ int maivs_concurrent_search_batch(maivs_concurrent* cx, const float* queries, si
  * segment `segment` (-1 = the head) under maivs_array's names; the pointer stays valid until that
  * segment next changes. */
 int maivs_concurrent_segments(maivs_concurrent* cx, size_t* n);
+/* Instrumentation (no counterpart in the reference): per-kernel device times of this handle's
+ * searches (every segment, the head and the merge), as maivs_kernel_clock / maivs_kernel_times. */
+int maivs_concurrent_kernel_clock(maivs_concurrent* cx, int on);
+int maivs_concurrent_kernel_times(maivs_concurrent* cx, int reset, const char** names, double* ms,
+                                  uint64_t* launches, size_t cap, size_t* n_out);
 int maivs_concurrent_array(maivs_concurrent* cx, long long segment, const char* name, const void** data,
                            size_t* count, size_t* elem_bytes);
 

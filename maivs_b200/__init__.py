@@ -541,11 +541,31 @@ class ConcurrentIndex:
     def compact(self) -> None:
         self._check(_lib.lib().maivs_concurrent_compact(self._h))
 
+    def set_build_device(self, device: int | None) -> None:
+        """Run the head's k-means and placement on CUDA device `device` (None: the host cores);
+        later heads inherit it. The index built is the same either way."""
+        self._check(_lib.lib().maivs_concurrent_set_build_device(self._h, -1 if device is None else int(device)))
+
     def to_device(self, device: int = 0) -> None:
         """CUDA device of the searches (default 0)."""
         self._check(_lib.lib().maivs_concurrent_to_device(self._h, int(device)))
 
-    # ---- inspection (no counterpart in the reference) ----
+    # ---- inspection and instrumentation (no counterpart in the reference) ----
+    def kernel_clock(self, on: bool) -> None:
+        """Time every kernel of subsequent searches (all segments, the head, the merge)."""
+        self._check(_lib.lib().maivs_concurrent_kernel_clock(self._h, int(bool(on))))
+
+    def kernel_times(self, reset: bool = False) -> dict:
+        """{kernel name: (total ms, launches)} accumulated while the clock was on."""
+        n = 32
+        names = (C.c_char_p * n)()
+        ms = (C.c_double * n)()
+        la = (C.c_uint64 * n)()
+        got = C.c_size_t(0)
+        self._check(_lib.lib().maivs_concurrent_kernel_times(self._h, int(bool(reset)), names, ms, la, n,
+                                                             C.byref(got)))
+        return {names[i].decode(): (float(ms[i]), int(la[i])) for i in range(got.value)}
+
     def n_segments(self) -> int:
         n = C.c_size_t(0)
         self._check(_lib.lib().maivs_concurrent_segments(self._h, C.byref(n)))

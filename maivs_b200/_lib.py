@@ -90,6 +90,7 @@ _SIGS = {
     "maivs_concurrent_set_parallel_scan": (C.c_int, [C.c_void_p, C.c_int]),
     "maivs_concurrent_set_graph_route": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t]),
     "maivs_concurrent_set_tree_route": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t, C.c_size_t, C.c_float]),
+    "maivs_concurrent_set_build_device": (C.c_int, [C.c_void_p, C.c_int]),
     "maivs_concurrent_len": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
     "maivs_concurrent_stat": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double)]),
     "maivs_concurrent_to_device": (C.c_int, [C.c_void_p, C.c_int]),
@@ -98,6 +99,9 @@ _SIGS = {
     "maivs_concurrent_search_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
                                                 C.c_float, C.c_float, C.c_void_p, C.c_void_p]),
     "maivs_concurrent_segments": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t)]),
+    "maivs_concurrent_kernel_clock": (C.c_int, [C.c_void_p, C.c_int]),
+    "maivs_concurrent_kernel_times": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
+                                                C.POINTER(C.c_uint64), C.c_size_t, C.POINTER(C.c_size_t)]),
     "maivs_concurrent_array": (C.c_int, [C.c_void_p, C.c_longlong, C.c_char_p, C.POINTER(C.c_void_p),
                                          C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "maivs_profile": (C.c_int, [C.c_int]),

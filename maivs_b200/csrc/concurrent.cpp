@@ -49,6 +49,9 @@ struct maivs_concurrent {
     size_t dtomb_cap = 0;
     uint64_t tomb_version = ~0ull;
     int ntomb = 0;
+    // per-kernel device times (instrumentation): the merge's here, the searches' in each image
+    bool clock_on = false;
+    std::unique_ptr<maivs::dev::KernelClock> clock;
 
     std::mutex err_mu;
     std::string err;
@@ -188,6 +191,7 @@ int search_pass(maivs_concurrent* cx, const SegList& segs, const float* Q, size_
             seg->device = cx->device;
             int rc = maivs_capi::device_image(seg);
             if (rc != MAIVS_OK) return cfail(cx, rc, seg->err);
+            if (cx->clock_on) seg->d->enable_kernel_clock(true);
             std::string e;
             rc = seg->d->search_device(seg->h, dQ, a, li, ls, ln, cx->st, e);
             if (rc != MAIVS_OK) return cfail(cx, rc, e);
@@ -227,8 +231,10 @@ int search_pass(maivs_concurrent* cx, const SegList& segs, const float* Q, size_
             }
         }
         maivs::dev::take_launch_error(nullptr);
+        maivs::dev::set_thread_clock(cx->clock_on ? cx->clock.get() : nullptr);
         maivs::dev::launch_segment_merge(lid, lsc, lnout, (int)L, (int)nq, (int)want, cx->dtomb, cx->ntomb, (int)k,
                                          scratch, oid, osc, cx->st);
+        maivs::dev::set_thread_clock(nullptr);
         int kid = -1;
         cudaError_t le = maivs::dev::take_launch_error(&kid);
         if (le != cudaSuccess)
@@ -409,6 +415,10 @@ int maivs_concurrent_set_parallel_scan(maivs_concurrent* cx, int on) {
     cx->par_scan = on != 0;
     return MAIVS_OK;
 }
+int maivs_concurrent_set_build_device(maivs_concurrent* cx, int device) {
+    // kept by fork_empty, so every later head builds there too
+    return with_head_write(cx, [&](maivs::HostIndex& h) { h.build_device = device < 0 ? -1 : device; });
+}
 int maivs_concurrent_set_graph_route(maivs_concurrent* cx, int on, size_t min_cells) {
     return with_head_write(cx, [&](maivs::HostIndex& h) {
         h.graph_route = on != 0;
@@ -539,6 +549,59 @@ int maivs_concurrent_search(maivs_concurrent* cx, const float* query, size_t k, 
     size_t n = 0;
     while (n < k && ids[n] != UINT64_MAX) ++n;
     if (n_out) *n_out = n;
+    return MAIVS_OK;
+}
+
+int maivs_concurrent_kernel_clock(maivs_concurrent* cx, int on) {
+    if (!cx) return MAIVS_BAD_ARG;
+    std::lock_guard<std::mutex> gl(cx->gpu_mu);
+    cx->clock_on = on != 0;
+    if (cx->clock_on && !cx->clock) cx->clock = std::make_unique<maivs::dev::KernelClock>();
+    if (!cx->clock_on) {
+        cx->clock.reset();
+        auto segs = snapshot(cx);
+        for (auto& sg : *segs)
+            if (sg->d) sg->d->enable_kernel_clock(false);
+        std::shared_lock<std::shared_mutex> hl(cx->head_mu);
+        if (cx->head->d) cx->head->d->enable_kernel_clock(false);
+    }
+    return MAIVS_OK;
+}
+
+int maivs_concurrent_kernel_times(maivs_concurrent* cx, int reset, const char** names, double* ms,
+                                  uint64_t* launches, size_t cap, size_t* n_out) {
+    if (!cx) return MAIVS_BAD_ARG;
+    std::lock_guard<std::mutex> gl(cx->gpu_mu);
+    std::vector<maivs::dev::KernelClock*> clocks;
+    if (cx->clock) clocks.push_back(cx->clock.get());
+    auto segs = snapshot(cx);
+    for (auto& sg : *segs)
+        if (sg->d && sg->d->kernel_clock()) clocks.push_back(sg->d->kernel_clock());
+    {
+        std::shared_lock<std::shared_mutex> hl(cx->head_mu);
+        if (cx->head->d && cx->head->d->kernel_clock()) clocks.push_back(cx->head->d->kernel_clock());
+    }
+    if (cx->st) cudaStreamSynchronize(cx->st);
+    for (auto* c : clocks) c->collect();
+    const size_t n = std::min<size_t>(cap, maivs::dev::kNumKernels);
+    if (n_out) *n_out = n;
+    for (size_t i = 0; i < n; ++i) {
+        double t = 0.0;
+        uint64_t l = 0;
+        for (auto* c : clocks) {
+            t += c->ms[i];
+            l += c->launches[i];
+        }
+        if (names) names[i] = maivs::dev::kernel_name((int)i);
+        if (ms) ms[i] = t;
+        if (launches) launches[i] = l;
+    }
+    if (reset)
+        for (auto* c : clocks)
+            for (size_t i = 0; i < maivs::dev::kNumKernels; ++i) {
+                c->ms[i] = 0.0;
+                c->launches[i] = 0;
+            }
     return MAIVS_OK;
 }
 
