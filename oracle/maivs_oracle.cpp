@@ -335,6 +335,14 @@ struct OIndex {
     uint32_t flo, fhi;
 
     size_t members(size_t c) const { return mem_off[c + 1] - mem_off[c]; }
+    // non-empty cells: the centroid graph exists when there are graph_min_cells of them
+    // (rebuild_centroid_graph, index.rs:625-636)
+    size_t live_cells() const {
+        size_t n = 0;
+        for (size_t c = 0; c + 1 < mem_off.size(); ++c) n += mem_off[c + 1] > mem_off[c];
+        return n;
+    }
+    size_t n_live_cells = 0;
     const uint32_t* member_ptr(size_t c) const { return mem.data() + mem_off[c]; }
     bool live(size_t c) const { return members(c) > 0; }
 };
@@ -444,7 +452,7 @@ int route_query(const OIndex& ix, const float* q, size_t nprobe, float tc, float
         tree_search(ix, b.q_bits.data(), want_c, tout);
         for (uint32_t ci : tout)
             if (ix.live(ci)) b.cscores.push_back({ci, cent_score(ix, ci, q, b.cqs.data(), cqbase)});
-    } else if (ix.graph_route && ix.n_live >= ix.graph_min_cells) {
+    } else if (ix.graph_route && ix.n_live_cells >= ix.graph_min_cells) {
         return -1;
     } else if (ix.two_stage && !ix.cent_bits.empty()) {
         rotate(q, dim, ix.signs.data(), ix.dim_pad, b.rot.data());
@@ -1924,6 +1932,7 @@ OIndex* make_index(OBuild& b, bool take) {
     } else {
         ix->bits = b.bits;
     }
+    ix->n_live_cells = ix->live_cells();
     return ix;
 }
 
@@ -2044,6 +2053,7 @@ void* oracle_index_new(const oracle_arrays* a) {
         cp(ix->leaf_codes, a->tree_leaf_codes, ix->n_leaf * a->nw);
         cp(ix->leaf_ids, a->tree_leaf_ids, ix->n_leaf);
     }
+    ix->n_live_cells = ix->live_cells();
     return ix;
 }
 
