@@ -266,17 +266,15 @@ __device__ __forceinline__ uint32_t ham_row(const uint64_t* qb, const uint64_t* 
     return h;
 }
 
-// route_batch (index.rs:1873-1927) in two kernels. k_route_ham: the Hamming distance of every
-// (query, centroid) pair into hs (nq x M, 0xFFFF for empty cells); a CTA takes kRouteQB queries x
-// kRouteCh centroids, each thread kRouteCh / kBS centroids (read once, scored against the CTA's
-// queries held in shared memory), so the grid covers the GPU whatever the batch. k_route_cut: one
-// warp per query counts its row into a warp-private histogram, finds the counting cut-off (the
-// smallest t with at least want_c live cells at or below it, index.rs:86-104; ties kept) and
-// compacts the shortlist in cell order with ballots.
-constexpr int kRouteQB = 8;      // queries per CTA of k_route_ham
-constexpr int kRouteCh = 1024;   // centroids per CTA of k_route_ham
-constexpr int kCutWarps = 8;     // queries (warps) per CTA of k_route_cut
+// Smallest t with prefix(t) >= want over hist[0..bits] (the counting cut-off of index.rs:86-104);
+// bits when never reached. Warp 0 computes it.
+constexpr int kRouteQB = 4;  // queries per CTA of the flat router (one warp each in pass 2)
+constexpr int kRouteSmemH = 160 * 1024;  // Hamming rows kept in shared memory up to this size
 
+// Pass 1: every centroid code is loaded once per CTA and scored against kRouteQB queries; the
+// Hamming values (0xFFFF for empty cells) go to shared memory, or to the `hs` scratch (nq x M)
+// when M is too large, plus a per-query histogram. Pass 2: warp j finds query j's counting
+// cut-off and compacts its shortlist in cell order with ballots.
 // Hamming distances of one centroid code to the CTA's queries; NW > 0: that many words, unrolled
 // and read 16 bytes at a time (rows of NW words are 16-byte aligned for even NW); NW = 0: any nw.
 template <int NW>
@@ -306,54 +304,50 @@ __device__ __forceinline__ void ham_rows(const uint64_t (*qb)[16], const uint64_
 }
 
 template <int NW>
-__global__ void __launch_bounds__(kBS) k_route_ham(IndexView ix, QueryEnc e, int nq, uint16_t* __restrict__ hs) {
+__global__ void __launch_bounds__(kBS) k_route_flat(IndexView ix, QueryEnc e, int nq, int want_c, int all,
+                                                    int h_in_smem, uint16_t* hs, uint32_t* sl, uint32_t* sl_n,
+                                                    int sl_cap) {
+    extern __shared__ uint32_t rsh[];
     __shared__ uint64_t qb[kRouteQB][16];
-    const int q0 = blockIdx.x * kRouteQB, nw = ix.nw, M = ix.M;
+    const int q0 = blockIdx.x * kRouteQB, nw = ix.nw, bits = nw * 64, M = ix.M;
     const int nqb = min(kRouteQB, nq - q0);
-    for (int i = threadIdx.x; i < kRouteQB * 16; i += kBS) {
-        int j = i / 16, w = i % 16;
-        qb[j][w] = (j < nqb && w < nw) ? e.qbits[(size_t)(q0 + j) * nw + w] : 0ull;
-    }
-    __syncthreads();
-    const int c0 = blockIdx.y * kRouteCh;
-#pragma unroll
-    for (int u = 0; u < kRouteCh / kBS; ++u) {
-        const int c = c0 + u * kBS + threadIdx.x;
-        if (c >= M) break;
-        uint32_t h[kRouteQB];
-        const bool lv = ix.live[c] != 0;
-        if (lv) ham_rows<NW>(qb, ix.cent_bits + (size_t)c * nw, nw, h);
-#pragma unroll
-        for (int j = 0; j < kRouteQB; ++j)
-            if (j < nqb) hs[(size_t)(q0 + j) * M + c] = lv ? (uint16_t)h[j] : (uint16_t)0xFFFF;
-    }
-}
-
-__global__ void __launch_bounds__(kCutWarps * 32) k_route_cut(IndexView ix, int nq, int want_c,
-                                                              const uint16_t* __restrict__ hs, uint32_t* sl,
-                                                              uint32_t* sl_n, int sl_cap) {
-    extern __shared__ uint32_t csh[];  // kCutWarps x (bits + 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.x * kCutWarps + warp;
-    const int bits = ix.nw * 64, M = ix.M;
-    if (q >= nq) return;
-    uint32_t* hist = csh + (size_t)warp * (bits + 1);
-    for (int i = lane; i <= bits; i += 32) hist[i] = 0;
-    __syncwarp();
-    const uint16_t* hq = hs + (size_t)q * M;
-    for (int c = lane; c < M; c += 32) {
-        const uint32_t h = hq[c];
-        if (h != 0xFFFFu) atomicAdd(&hist[h], 1u);
+    uint32_t* hist = rsh;                                                     // kRouteQB x (bits + 1)
+    uint16_t* hrow = h_in_smem ? reinterpret_cast<uint16_t*>(rsh + kRouteQB * (bits + 1))
+                               : hs + (size_t)q0 * M;                         // kRouteQB x M
+    if (!all) {
+        for (int i = threadIdx.x; i < kRouteQB * 16; i += kBS) {
+            int j = i / 16, w = i % 16;
+            qb[j][w] = (j < nqb && w < nw) ? e.qbits[(size_t)(q0 + j) * nw + w] : 0ull;
+        }
+        for (int i = threadIdx.x; i < kRouteQB * (bits + 1); i += kBS) hist[i] = 0;
+        __syncthreads();
+        for (int c = threadIdx.x; c < M; c += kBS) {
+            uint32_t h[kRouteQB];
+            const bool lv = ix.live[c] != 0;
+            if (lv) ham_rows<NW>(qb, ix.cent_bits + (size_t)c * nw, nw, h);
+#pragma unroll
+            for (int j = 0; j < kRouteQB; ++j) {
+                if (j < nqb) {
+                    hrow[(size_t)j * M + c] = lv ? (uint16_t)h[j] : (uint16_t)0xFFFF;
+                    if (lv) atomicAdd(&hist[j * (bits + 1) + h[j]], 1u);
+                }
+            }
+        }
+        __syncthreads();
     }
-    __syncwarp();
-    const int cut = want_c == 0 ? 0 : warp_hist_cut(hist, bits, want_c);
+    if (warp >= nqb) return;
+    const int q = q0 + warp;
+    int cut = bits;
+    if (!all) cut = want_c == 0 ? 0 : warp_hist_cut(hist + warp * (bits + 1), bits, want_c);
+    const uint16_t* hq = hrow + (size_t)warp * M;
     uint32_t count = 0;
     for (int base = 0; base < M; base += 128) {
         bool f[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int c = base + u * 32 + lane;
-            f[u] = c < M && hq[c] <= (uint16_t)cut;
+            f[u] = c < M && (all ? ix.live[c] != 0 : hq[c] <= (uint16_t)cut);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -363,25 +357,6 @@ __global__ void __launch_bounds__(kCutWarps * 32) k_route_cut(IndexView ix, int 
             if (f[u] && pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + pos] = (uint32_t)c;
             count += (uint32_t)__popc(m);
         }
-    }
-    if (lane == 0) sl_n[q] = count;
-}
-
-// Every live cell, in cell order (route_batch's shortlist when want_c covers all live cells).
-__global__ void __launch_bounds__(kCutWarps * 32) k_route_all(IndexView ix, int nq, uint32_t* sl, uint32_t* sl_n,
-                                                              int sl_cap) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q = blockIdx.x * kCutWarps + warp;
-    const int M = ix.M;
-    if (q >= nq) return;
-    uint32_t count = 0;
-    for (int base = 0; base < M; base += 32) {
-        const int c = base + lane;
-        const bool f = c < M && ix.live[c] != 0;
-        unsigned m = __ballot_sync(0xFFFFFFFFu, f);
-        uint32_t pos = count + (uint32_t)__popc(m & ((1u << lane) - 1u));
-        if (f && pos < (uint32_t)sl_cap) sl[(size_t)q * sl_cap + pos] = (uint32_t)c;
-        count += (uint32_t)__popc(m);
     }
     if (lane == 0) sl_n[q] = count;
 }
@@ -866,28 +841,34 @@ void launch_encode(const IndexView& ix, const float* Q, int nq, const QueryEnc& 
 void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_c, uint16_t* hs, uint32_t* sl,
                        uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
-    const dim3 grid((nq + kRouteQB - 1) / kRouteQB, (ix.M + kRouteCh - 1) / kRouteCh);
-    {
-        Tick tk(kKRouteFlat, st);
-        switch (ix.nw) {
-            case 8: k_route_ham<8><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-            case 4: k_route_ham<4><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-            case 2: k_route_ham<2><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-            case 12: k_route_ham<12><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-            case 16: k_route_ham<16><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-            default: k_route_ham<0><<<grid, kBS, 0, st>>>(ix, e, nq, hs); break;
-        }
+    const size_t hist_b = (size_t)kRouteQB * (ix.nw * 64 + 1) * sizeof(uint32_t);
+    const size_t h_b = (size_t)kRouteQB * ix.M * sizeof(uint16_t);
+    const int in_smem = h_b <= (size_t)kRouteSmemH ? 1 : 0;
+    const size_t smem = hist_b + (in_smem ? h_b : 0);
+    const int grid = (nq + kRouteQB - 1) / kRouteQB;
+    const void* fn = ix.nw == 8    ? (const void*)k_route_flat<8>
+                     : ix.nw == 4  ? (const void*)k_route_flat<4>
+                     : ix.nw == 2  ? (const void*)k_route_flat<2>
+                     : ix.nw == 12 ? (const void*)k_route_flat<12>
+                     : ix.nw == 16 ? (const void*)k_route_flat<16>
+                                   : (const void*)k_route_flat<0>;
+    set_smem(fn, smem);
+    Tick tk(kKRouteFlat, st);
+    switch (ix.nw) {
+        case 8: k_route_flat<8><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 4: k_route_flat<4><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 2: k_route_flat<2><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 12: k_route_flat<12><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        case 16: k_route_flat<16><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
+        default: k_route_flat<0><<<grid, kBS, smem, st>>>(ix, e, nq, want_c, 0, in_smem, hs, sl, sl_n, sl_cap); break;
     }
-    const size_t smem = (size_t)kCutWarps * (ix.nw * 64 + 1) * sizeof(uint32_t);
-    set_smem((const void*)k_route_cut, smem);
-    Tick tk(kKRouteCut, st);
-    k_route_cut<<<(nq + kCutWarps - 1) / kCutWarps, kCutWarps * 32, smem, st>>>(ix, nq, want_c, hs, sl, sl_n, sl_cap);
 }
 
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
+    QueryEnc e{};
     Tick tk(kKRouteFlat, st);
-    k_route_all<<<(nq + kCutWarps - 1) / kCutWarps, kCutWarps * 32, 0, st>>>(ix, nq, sl, sl_n, sl_cap);
+    k_route_flat<0><<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, 0, nullptr, sl, sl_n, sl_cap);
 }
 
 void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,

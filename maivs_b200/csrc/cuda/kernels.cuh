@@ -62,7 +62,7 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kKScanMma, kKSeedScan, kKAllGather, kKSegMerge, kKRouteCut, kNumKernels
+    kKScanMma, kKSeedScan, kKAllGather, kKSegMerge, kNumKernels
 };
 const char* kernel_name(int id);
 // Brackets a step that is not one of this library's kernels (an NCCL collective) on the thread's
