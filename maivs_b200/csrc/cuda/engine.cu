@@ -12,7 +12,11 @@ namespace maivs {
 
 namespace {
 
-constexpr int kPerQueryChunk = 64;  // queries per per-query pipeline pass (bounds its scratch)
+// Queries per pass of the per-query pipeline: the whole batch when its scratch (probe ranks,
+// shortlists, entries and candidates of every query) fits in kPerQueryScratch, else the largest
+// power-of-two share of it that does, but never fewer than kPerQueryMinChunk.
+constexpr size_t kPerQueryScratch = size_t(1) << 30;
+constexpr int kPerQueryMinChunk = 64;
 constexpr uint32_t kNoCellHost = 0xFFFFFFFFu;  // an unused home in slot_cells
 
 struct Bump {
@@ -179,6 +183,13 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
         std::copy(h.cells[c].centroid.begin(), h.cells[c].centroid.end(), cf.begin() + c * dim);
     }
     v.live = upload_vec(live);
+    {
+        std::vector<uint32_t> ll;
+        for (size_t c = 0; c < M; ++c)
+            if (live[c]) ll.push_back((uint32_t)c);
+        v.live_list = upload_vec(ll);
+        v.n_live_cells = (int)ll.size();
+    }
     v.r_bound = upload_vec(rb);
     v.cent_f32 = upload_vec(cf);
     v.signs = upload_vec(h.signs);
@@ -453,7 +464,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
                                    : std::max(want0, 1);
     const bool filtering = h.has_filter && !h.tags.empty();
     const bool tree_router = h.tree != nullptr;
-    const int chunk = std::min(a.nq, kPerQueryChunk);
+    int chunk = a.nq;
 
     float* rsc = nullptr;       // rerank scores (chunk x cand_cap) of the flattened gather
     float* rss = nullptr;       // centroid re-order scores of the shortlists (chunk x M)
@@ -497,6 +508,11 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     dev::PerQueryBufs b{};
     Bump sizing{nullptr, 0, 0};
     carve(sizing, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
+    while (sizing.off > kPerQueryScratch && chunk > kPerQueryMinChunk) {
+        chunk = std::max(kPerQueryMinChunk, (chunk + 1) / 2);
+        sizing = Bump{nullptr, 0, 0};
+        carve(sizing, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
+    }
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
     Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};

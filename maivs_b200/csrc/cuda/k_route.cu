@@ -864,11 +864,24 @@ void launch_route_flat(const IndexView& ix, const QueryEnc& e, int nq, int want_
     }
 }
 
+// Every live cell, in cell order, as every query's shortlist (route_query with neither tree nor
+// two-stage codes scores all live cells, index.rs:1260-1270): a copy of the list built at upload.
+__global__ void k_route_all(IndexView ix, int nq, uint32_t* __restrict__ sl, uint32_t* __restrict__ sl_n, int sl_cap) {
+    const int n = ix.n_live_cells;
+    const size_t total = (size_t)nq * n;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t q = i / n, j = i - q * n;
+        if (j < (size_t)sl_cap) sl[q * sl_cap + j] = __ldg(ix.live_list + j);
+        if (j == 0) sl_n[q] = (uint32_t)n;
+    }
+}
+
 void launch_route_all(const IndexView& ix, int nq, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st) {
     if (nq <= 0) return;
-    QueryEnc e{};
+    const size_t total = (size_t)nq * std::max(ix.n_live_cells, 1);
+    const int grid = (int)std::min<size_t>((total + kBS - 1) / kBS, 148 * 16);
     Tick tk(kKRouteFlat, st);
-    k_route_flat<0><<<(nq + kRouteQB - 1) / kRouteQB, kBS, 0, st>>>(ix, e, nq, 0, 1, 0, nullptr, sl, sl_n, sl_cap);
+    k_route_all<<<grid, kBS, 0, st>>>(ix, nq, sl, sl_n, sl_cap);
 }
 
 void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int* beams, int want, uint32_t* scratch,

@@ -21,6 +21,8 @@ struct IndexView {
     const float* csq_min;       // dim
     const float* csq_step;      // dim
     const uint8_t* live;        // M: cell has members
+    const uint32_t* live_list;  // the live cells, ascending
+    int n_live_cells;
     const float* r_bound;       // M
     const float* signs;         // 2 x dim_pad
     // scan layout: cell c's members are cell_slots[cell_moff[c] ..], its codes are the words
