@@ -562,6 +562,51 @@ __device__ int warp_hist_cut(const uint32_t* hist, int bits, long long want) {
     return res;
 }
 
+
+// warp_hist_cut over the composite histogram run[i] + layers[0][i] + ... + layers[nl - 1][i]
+// (layer l at layers + l * stride): the smallest t with prefix(t) >= want, bits when never
+// reached; *total receives the composite sum over every bucket. Every lane returns the same.
+__device__ int warp_cut_layers(const uint32_t* run, const uint32_t* layers, int stride, int nl, int bits,
+                               long long want, long long* total) {
+    const int lane = threadIdx.x & 31;
+    const int nb = bits + 1;
+    const int per = (nb + 31) / 32;
+    const int b0 = lane * per, b1 = min(b0 + per, nb);
+    auto val = [&](int i) -> uint32_t {
+        uint32_t v = run[i];
+        for (int l = 0; l < nl; ++l) v += layers[l * stride + i];
+        return v;
+    };
+    long long s = 0;
+    for (int i = b0; i < b1; ++i) s += val(i);
+    long long inc = s;
+    for (int o = 1; o < 32; o <<= 1) {
+        long long v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    *total = __shfl_sync(0xFFFFFFFFu, inc, 31);
+    const long long excl = inc - s;
+    const int found = (excl < want && inc >= want) ? 1 : 0;
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, found);
+    int res = bits;
+    if (bal) {
+        const int src = __ffs(bal) - 1;
+        int t = bits;
+        if (lane == src) {
+            long long c = excl;
+            for (int i = b0; i < b1; ++i) {
+                c += val(i);
+                if (c >= want) {
+                    t = i;
+                    break;
+                }
+            }
+        }
+        res = __shfl_sync(0xFFFFFFFFu, t, src);
+    }
+    return res;
+}
+
 }  // namespace
 
 }  // namespace dev

@@ -169,9 +169,42 @@ __device__ __forceinline__ float ham_tau_cos(uint32_t tau, uint32_t dp) {
 // FastScan (kHam = false, index.rs:1630-1692): buckets d >> 6, the stop threshold from the table
 // estimate of the bucket's worst distance, then the top want0 by exact d. Hamming (kHam = true,
 // :1693-1848): buckets are the distances themselves, the threshold is score_to_cos of tau, and
-// every entry at or below the final tau is a candidate (ties kept). tau after any prefix of cells
-// is the target-th smallest bucket among that prefix's surviving entries, so whole cells are
-// folded at once.
+// every entry at or below the final tau is a candidate (ties kept).
+// tau after cells 0..r is the target-th smallest bucket over those cells' surviving entries (the
+// sequential walk's falling cut-off depends only on that multiset), and "kept >= target" is "at
+// least target entries so far", so the stop rule is decided for kFoldG cells at once: each cell of
+// the round gets its own histogram layer, the layers are made cumulative in place (layer w = the
+// running histogram plus cells 0..w of the round), warp w takes the cut-off of layer w, and the
+// first cell whose stop rule holds ends the scan. Without adaptive probing every probe is scanned
+// and the cut-off is computed once. Entries are read kFoldU per thread with independent loads.
+constexpr int kFoldG = kBS / 32;
+constexpr int kFoldU = 8;
+constexpr int kFoldEqMax = 1024;  // entries of the cut-off bucket ranked directly
+
+// Histogram of the entries [i0, i1) by bucket: into hist[b], or, with s_so (the round's cell
+// offsets, ng cells), into the layer of the entry's cell, hist + layer * hs.
+template <int kShift>
+__device__ __forceinline__ void fold_count(const uint64_t* __restrict__ ent, uint32_t i0, uint32_t i1, uint32_t* hist,
+                                           const uint32_t* s_so, int hs) {
+    for (uint32_t base = i0 + threadIdx.x; base < i1; base += kBS * kFoldU) {
+        uint64_t kk[kFoldU];
+#pragma unroll
+        for (int u = 0; u < kFoldU; ++u) {
+            const uint32_t i = base + (uint32_t)u * kBS;
+            kk[u] = i < i1 ? ent[i] : kInvalidEntry;
+        }
+#pragma unroll
+        for (int u = 0; u < kFoldU; ++u) {
+            if (kk[u] == kInvalidEntry) continue;
+            const uint32_t i = base + (uint32_t)u * kBS;
+            int l = 0;
+            if (s_so)
+                while (i >= s_so[l + 1]) ++l;
+            atomicAdd(&hist[l * hs + ((uint32_t)(kk[u] >> 32) >> kShift)], 1u);
+        }
+    }
+}
+
 template <bool kHam>
 __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                                  const float* __restrict__ cscore, const uint32_t* __restrict__ nch,
@@ -181,12 +214,15 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
     constexpr int kShift = kHam ? 0 : 6;
     const uint32_t top = kHam ? (uint32_t)ix.nw * 64u : ix.maxk >> 6;  // the largest bucket
     const int nb = (int)top + 1;
-    uint32_t* hist = sh;              // nb buckets
-    float* suffix = reinterpret_cast<float*>(sh + nb);  // nprobe + 1
-    __shared__ uint32_t s_add, s_tau, s_stop, s_cnt;
-    __shared__ unsigned long long s_kept;
+    const int hs = (nb + 3) & ~3;
+    uint32_t* run = sh;                                                      // nb buckets: cells before the round
+    uint32_t* layers = sh + hs;                                              // kFoldG x hs: the round's cells
+    float* suffix = reinterpret_cast<float*>(sh + (size_t)(kFoldG + 1) * hs);  // nprobe + 1
+    __shared__ uint32_t s_tau, s_stop, s_cnt;
+    __shared__ uint32_t s_cut[kFoldG], s_flag[kFoldG], s_so[kFoldG + 1];
     __shared__ uint32_t hist256[256];
     const int q = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = (int)nch[q];
     const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
     const uint64_t* ent = b.ent + (size_t)q * b.ent_cap;
@@ -197,7 +233,7 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
         }
         return;
     }
-    for (int i = threadIdx.x; i < nb; i += kBS) hist[i] = 0;
+    for (int i = threadIdx.x; i < nb; i += kBS) run[i] = 0;
     if (adaptive) {
         // suffix[i] = max bound over cells i..n-1 (index.rs:1467-1490)
         for (int i = threadIdx.x; i < n; i += kBS)
@@ -209,65 +245,75 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
     }
     if (threadIdx.x == 0) {
         s_tau = top;
-        s_kept = 0;
-        s_add = 0;
         s_stop = (uint32_t)n;
     }
     __syncthreads();
-    const float norm = kHam ? 0.0f : fs_norm(ix.dim_pad);
-    const float delta = kHam ? 0.0f : e.fs_delta[q], bias = kHam ? 0.0f : e.fs_bias[q];
-    for (int r = 0; r < n; ++r) {
-        const uint32_t tau = s_tau;
-        for (uint32_t i = so[r] + threadIdx.x; i < so[r + 1]; i += kBS) {
-            uint64_t k = ent[i];
-            if (k == kInvalidEntry) continue;
-            uint32_t hc = (uint32_t)(k >> 32) >> kShift;
-            if (hc <= tau) {
-                atomicAdd(&hist[hc], 1u);
-                atomicAdd(&s_add, 1u);
-            }
+    if (!adaptive) {
+        fold_count<kShift>(ent, 0, so[n], run, nullptr, 0);
+        __syncthreads();
+        if (warp == 0) {
+            long long tot;
+            const int cut = warp_cut_layers(run, nullptr, 0, 0, (int)top, (long long)target, &tot);
+            if (lane == 0) s_tau = (uint32_t)cut;
         }
         __syncthreads();
-        // the falling cut-off: the smallest bucket t (not above the current one) whose prefix count
-        // still reaches target, i.e. the sequential walk down from tau done as one warp scan
-        if (threadIdx.x < 32) {
-            const unsigned long long kept0 = s_kept + s_add;
-            const uint32_t t0 = s_tau;
-            uint32_t t = t0;
-            unsigned long long kept = kept0;
-            if (kept0 >= (unsigned long long)target && t0 > 0) {
-                const int cut = warp_hist_cut(hist, (int)t0, (long long)target);
-                unsigned long long below = 0;  // prefix(cut), summed by the warp
-                for (int i = threadIdx.x; i <= cut; i += 32) below += hist[i];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) below += __shfl_xor_sync(0xFFFFFFFFu, below, o);
-                t = (uint32_t)cut;
-                kept = below;
-            }
-            if (threadIdx.x == 0) {
-                s_add = 0;
-                s_kept = kept;
-                s_tau = t;
-            }
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const unsigned long long kept = s_kept;
-            const uint32_t t = s_tau;
-            if (adaptive && kept >= (unsigned long long)target) {
-                float thr;
-                if (kHam) {
-                    thr = ham_tau_cos(t, top);
-                } else {
-                    uint32_t wsub = ((t + 1) << 6) - 1;
-                    uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
-                    thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+    } else {
+        const float norm = kHam ? 0.0f : fs_norm(ix.dim_pad);
+        const float delta = kHam ? 0.0f : e.fs_delta[q], bias = kHam ? 0.0f : e.fs_bias[q];
+        for (int g0 = 0; g0 < n; g0 += kFoldG) {
+            const int ng = min(kFoldG, n - g0);
+            for (int i = threadIdx.x; i < ng * hs; i += kBS) layers[i] = 0;
+            if (threadIdx.x <= ng) s_so[threadIdx.x] = so[g0 + threadIdx.x];
+            __syncthreads();
+            fold_count<kShift>(ent, s_so[0], s_so[ng], layers, s_so, hs);
+            __syncthreads();
+            // cumulative in place: layer l = run + cells 0..l of the round
+            for (int i = threadIdx.x; i < nb; i += kBS) {
+                uint32_t v = run[i];
+                for (int l = 0; l < ng; ++l) {
+                    v += layers[l * hs + i];
+                    layers[l * hs + i] = v;
                 }
-                if (suffix[r + 1] < __fsub_rn(thr, at_margin)) s_stop = (uint32_t)(r + 1);
             }
+            __syncthreads();
+            if (warp < ng) {
+                long long tot;
+                const int cut =
+                    warp_cut_layers(layers + warp * hs, nullptr, 0, 0, (int)top, (long long)target, &tot);
+                if (lane == 0) {
+                    uint32_t stop = 0;
+                    if (tot >= (long long)target) {
+                        const uint32_t t = (uint32_t)cut;
+                        float thr;
+                        if (kHam) {
+                            thr = ham_tau_cos(t, top);
+                        } else {
+                            const uint32_t wsub = ((t + 1) << 6) - 1;
+                            const uint32_t worst = ix.maxk > wsub ? ix.maxk - wsub : 0u;
+                            thr = clampf(__fdiv_rn(fs_estimate(delta, bias, worst), norm), -1.0f, 1.0f);
+                        }
+                        stop = suffix[g0 + warp + 1] < __fsub_rn(thr, at_margin) ? 1u : 0u;
+                    }
+                    s_cut[warp] = (uint32_t)cut;
+                    s_flag[warp] = stop;
+                }
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int w = 0;
+                while (w < ng && !s_flag[w]) ++w;
+                if (w < ng) {
+                    s_stop = (uint32_t)(g0 + w + 1);
+                    s_tau = s_cut[w];
+                } else {
+                    s_tau = s_cut[ng - 1];
+                }
+            }
+            __syncthreads();
+            if (s_stop != (uint32_t)n) break;
+            for (int i = threadIdx.x; i < nb; i += kBS) run[i] = layers[(ng - 1) * hs + i];
+            __syncthreads();
         }
-        __syncthreads();
-        if (s_stop != (uint32_t)n) break;
     }
     // candidates: entries of the scanned cells with bucket <= tau (index.rs:1680-1685, :1809-1814)
     const uint32_t tau = s_tau, end = so[s_stop];
@@ -314,9 +360,42 @@ __global__ void __launch_bounds__(kBS) k_pq_fold(IndexView ix, QueryEnc e, const
         __syncthreads();
     }
     const int cnt = (int)s_cnt;
-    // top want0 (= target) by d; ties at the cut broken by ascending slot (index.rs:1689-1691)
+    // top want0 (= target) by d; ties at the cut broken by ascending slot (index.rs:1689-1691).
+    // Every entry of a bucket below tau is in (fewer than target of them); the rest are the
+    // smallest keys of bucket tau, ranked directly when that bucket is small.
     uint64_t K = ~0ull;
-    if (cnt > target) K = block_select_kth(keys, cnt, nullptr, 0, target, 5, 0, hist256);
+    if (cnt > target) {
+        __shared__ uint64_t s_eq[kFoldEqMax];
+        __shared__ uint32_t s_neq;
+        __shared__ uint64_t s_k;
+        if (threadIdx.x == 0) {
+            s_neq = 0;
+            s_k = ~0ull;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < cnt; i += kBS) {
+            const uint64_t k = keys[i];
+            if (((uint32_t)(k >> 32) >> 6) == tau) {
+                const uint32_t at = atomicAdd(&s_neq, 1u);
+                if (at < (uint32_t)kFoldEqMax) s_eq[at] = k;
+            }
+        }
+        __syncthreads();
+        const int neq = (int)s_neq;
+        if (neq <= kFoldEqMax) {
+            const int need = target - (cnt - neq);  // >= 1: the entries below bucket tau are fewer than target
+            for (int i = threadIdx.x; i < neq; i += kBS) {
+                const uint64_t k = s_eq[i];
+                int r = 0;
+                for (int j = 0; j < neq; ++j) r += s_eq[j] < k ? 1 : 0;
+                if (r == need - 1) s_k = k;
+            }
+            __syncthreads();
+            K = s_k;
+        } else {
+            K = block_select_kth(keys, cnt, nullptr, 0, target, 5, 0, hist256);
+        }
+    }
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     uint32_t* out = b.cand + (size_t)q * b.cand_cap;
@@ -350,8 +429,8 @@ void launch_perquery(const IndexView& ix, const QueryEnc& e, int nq, const uint3
         k_pq_scan_ham<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b);
     else
         k_pq_scan<<<dim3(nprobe, nq), kBS, 0, st>>>(ix, e, chosen, nch, nprobe, filtering ? 1 : 0, flo, fhi, b); }
-    int nb = ix.ham ? ix.nw * 64 + 1 : (int)(ix.maxk >> 6) + 1;
-    size_t smem = (size_t)nb * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
+    const int nb = ix.ham ? ix.nw * 64 + 1 : (int)(ix.maxk >> 6) + 1;
+    const size_t smem = (size_t)(kFoldG + 1) * ((nb + 3) & ~3) * sizeof(uint32_t) + (size_t)(nprobe + 1) * sizeof(float);
     const void* fold = ix.ham ? (const void*)k_pq_fold<true> : (const void*)k_pq_fold<false>;
     set_smem(fold, smem);
     int target = std::max(want0, 1);
