@@ -44,7 +44,7 @@ const char* kernel_name(int id) {
                                              "k_scan_cm", "k_final_cm",  "k_pq_prep",    "k_pq_scan",
                                              "k_pq_fold", "k_rerank",    "k_topk",       "k_rerank_items",
                                              "k_seed_finish", "k_local_list", "k_merge_topk", "k_scan_mma",
-                                             "k_seed_scan", "nccl_all_gather", "k_segment_merge"};
+                                             "k_seed_scan", "nccl_all_gather", "k_segment_merge", "k_rescore_dots", "k_probe_select"};
     return id >= 0 && id < kNumKernels ? names[id] : "?";
 }
 

@@ -38,6 +38,10 @@ void set_smem(const void* f, size_t bytes);
 void launch_scan_mma(const IndexView& ix, const QueryEnc& e, const CellMajorBufs& b, cudaStream_t st);
 // Centroid re-order scores of every (query, shortlist cell) pair by the flattened register gather
 // (k_rerank.cu): item numbering, then k_rescore_dots.
+// Centroid re-order scores of every (query, live cell) pair when every shortlist is the live-cell
+// list (k_rerank.cu, tiled); false when the rows do not suit it (then nothing was launched).
+bool launch_rescore_all(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, bool use_sq8, int cap,
+                        float* rs_scores, cudaStream_t st);
 void launch_rescore_dots(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
                          const uint32_t* sl_n, int sl_cap, bool use_sq8, float* rs_scores, uint32_t* rs_items,
                          cudaStream_t st);

@@ -299,6 +299,7 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
     const size_t mult2 = std::max<size_t>(h.shortlist_mult, 2);
     int expect = (int)std::min<size_t>(n_live_, 1u << 30);  // typical shortlist length
     bool have_codes = h.two_stage && !h.cent_bits.empty();
+    bool all_live = false;
     if (batch_router && have_codes) {
         // route_batch (index.rs:1873-1980): exact flat Hamming shortlist for every query
         int want_c = (int)std::min<size_t>((size_t)nprobe * mult2, n_live_);
@@ -322,9 +323,10 @@ int DeviceIndex::route(const HostIndex& h, const dev::QueryEnc& e, const float* 
         expect = want_c;
     } else {
         dev::launch_route_all(view_, nq, sl, sl_n, M, st);
+        all_live = true;
     }
     dev::launch_rescore_select(view_, e, dQ, nq, sl, sl_n, M, nprobe, tc, beta, use_sq8_, chosen, cscore, nch,
-                               d_flags_ + 1, rs_scores, rs_items, expect, st);
+                               d_flags_ + 1, rs_scores, rs_items, expect, all_live, st);
     return kOk;
 }
 

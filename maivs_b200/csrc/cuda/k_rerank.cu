@@ -764,13 +764,144 @@ void launch_rescore_dots(const IndexView& ix, const QueryEnc& e, const float* Q,
         per_sm = 1;
     const RowSrc src{ix.dim, use_sq8 ? e.cqs : Q, e.cqbase, ix.cent_f32, ix.cent_sq8};
     {
-        Tick tk(kKRescore, st);
+        Tick tk(kKRerankItems, st);
         k_rerank_items<<<1, 1024, 0, st>>>(sl_n, nq, gather_rows(mode), rs_items);
+    }
+    {
+        Tick tk(kKRescoreDots, st);
         if (mode == 1)
             k_rescore_dots<1><<<sms * per_sm, 256, smem, st>>>(src, sl, sl_n, rs_items, nq, sl_cap, rs_scores);
         else
             k_rescore_dots<0><<<sms * per_sm, 256, smem, st>>>(src, sl, sl_n, rs_items, nq, sl_cap, rs_scores);
     }
+}
+
+// ---- centroid re-order over every live cell, as a tiled product ---------------------------------
+// With neither a tree nor two-stage codes, route_query scores every live cell (index.rs:1260-1270),
+// so every query of the batch has the same shortlist. A CTA takes kRaQ queries x kRaC cells with
+// both operands staged in shared memory; each thread owns 2 queries x 4 cells and, for every pair,
+// the eight FMA chains of the exact dot (element i on chain i % 8, elements in order), closed as
+// ((c0 + c4) + (c2 + c6)) + ((c1 + c5) + (c3 + c7)), the tail added in order, then the SQ8 base:
+// the value row_dots computes for the pair. Row strides are padded so the 16 rows a warp reads at
+// once fall on distinct banks.
+constexpr int kRaQ = 32, kRaC = 64;
+
+template <int kMode>  // 0: f32 centroids with the raw query, 1: SQ8 centroids with the pre-scaled query + base
+__global__ void __launch_bounds__(256) k_rescore_all(RowSrc src, const uint32_t* __restrict__ live_list, int nl,
+                                                     int nq, int cap, float* __restrict__ score_out) {
+    extern __shared__ __align__(16) uint8_t ra_sh[];
+    const int dim = src.dim, full8 = dim & ~7, n8 = full8 >> 3;
+    const int qs = ((dim + 3) & ~3) + 8;                                   // floats per staged query
+    const int rs = kMode == 0 ? (((dim + 3) & ~3) + 8) * 4 : dim + 8;      // bytes per staged row
+    float* sq = reinterpret_cast<float*>(ra_sh);
+    uint8_t* sr = ra_sh + (size_t)kRaQ * qs * 4;
+    const int q0 = blockIdx.x * kRaQ, c0 = blockIdx.y * kRaC;
+    const int nqb = min(kRaQ, nq - q0), ncb = min(kRaC, nl - c0);
+    for (int i = threadIdx.x; i < kRaQ * dim; i += 256) {
+        const int j = i / dim, t = i - j * dim;
+        sq[j * qs + t] = j < nqb ? __ldg(src.qsrc + (size_t)(q0 + j) * dim + t) : 0.0f;
+    }
+    if (kMode == 0) {
+        const int w4 = dim >> 2;  // float4 per row
+        for (int i = threadIdx.x; i < kRaC * w4; i += 256) {
+            const int r = i / w4, t = i - r * w4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < ncb) v = __ldg(reinterpret_cast<const float4*>(src.rows_f32 + (size_t)__ldg(live_list + c0 + r) * dim) + t);
+            *reinterpret_cast<float4*>(sr + (size_t)r * rs + 16 * t) = v;
+        }
+    } else {
+        const int w16 = dim >> 4;  // 16-byte words per row
+        for (int i = threadIdx.x; i < kRaC * w16; i += 256) {
+            const int r = i / w16, t = i - r * w16;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (r < ncb) v = __ldg(reinterpret_cast<const uint4*>(src.rows_u8 + (size_t)__ldg(live_list + c0 + r) * dim) + t);
+            uint2* d = reinterpret_cast<uint2*>(sr + (size_t)r * rs + 16 * t);
+            d[0] = make_uint2(v.x, v.y);
+            d[1] = make_uint2(v.z, v.w);
+        }
+    }
+    __syncthreads();
+    const int qa = 2 * (threadIdx.x >> 4), cb = threadIdx.x & 15;  // queries qa, qa + 1; cells cb + 16 u
+    float acc[2][4][8];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int l = 0; l < 8; ++l) acc[a][u][l] = 0.0f;
+    for (int m = 0; m < n8; ++m) {
+        float qv[2][8];
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+            const float4 x = *reinterpret_cast<const float4*>(sq + (qa + a) * qs + 8 * m);
+            const float4 y = *reinterpret_cast<const float4*>(sq + (qa + a) * qs + 8 * m + 4);
+            qv[a][0] = x.x; qv[a][1] = x.y; qv[a][2] = x.z; qv[a][3] = x.w;
+            qv[a][4] = y.x; qv[a][5] = y.y; qv[a][6] = y.z; qv[a][7] = y.w;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float rv[8];
+            const uint8_t* rp = sr + (size_t)(cb + 16 * u) * rs;
+            if (kMode == 0) {
+                const float4 x = *reinterpret_cast<const float4*>(rp + 32 * m);
+                const float4 y = *reinterpret_cast<const float4*>(rp + 32 * m + 16);
+                rv[0] = x.x; rv[1] = x.y; rv[2] = x.z; rv[3] = x.w;
+                rv[4] = y.x; rv[5] = y.y; rv[6] = y.z; rv[7] = y.w;
+            } else {
+                const uint2 w = *reinterpret_cast<const uint2*>(rp + 8 * m);
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    rv[l] = byte_val(w.x, l, false);
+                    rv[4 + l] = byte_val(w.y, l, false);
+                }
+            }
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+#pragma unroll
+                for (int l = 0; l < 8; ++l) acc[a][u][l] = __fmaf_rn(qv[a][l], rv[l], acc[a][u][l]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        const int q = qa + a;
+        if (q >= nqb) continue;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int c = cb + 16 * u;
+            if (c >= ncb) continue;
+            const float* v = acc[a][u];
+            float sc = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[4]), __fadd_rn(v[2], v[6])),
+                                 __fadd_rn(__fadd_rn(v[1], v[5]), __fadd_rn(v[3], v[7])));
+            const uint8_t* rp = sr + (size_t)c * rs;
+            for (int i = full8; i < dim; ++i) {
+                const float x = kMode == 0 ? reinterpret_cast<const float*>(rp)[i] : (float)rp[i];
+                sc = __fadd_rn(sc, __fmul_rn(sq[q * qs + i], x));
+            }
+            if (kMode == 1) sc = __fadd_rn(__ldg(src.qbase + q0 + q), sc);
+            score_out[(size_t)(q0 + q) * cap + c0 + c] = sc;
+        }
+    }
+}
+
+bool launch_rescore_all(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, bool use_sq8, int cap,
+                        float* rs_scores, cudaStream_t st) {
+    const int dim = ix.dim, nl = ix.n_live_cells;
+    if (nq <= 0 || nl <= 0) return false;
+    if (use_sq8 ? dim % 16 != 0 : dim % 4 != 0) return false;
+    const size_t qb = (size_t)kRaQ * (((dim + 3) & ~3) + 8) * 4;
+    const size_t rb = (size_t)kRaC * (use_sq8 ? dim + 8 : (((dim + 3) & ~3) + 8) * 4);
+    const size_t smem = qb + rb;
+    if (smem > 220 * 1024) return false;
+    const void* fn = use_sq8 ? (const void*)k_rescore_all<1> : (const void*)k_rescore_all<0>;
+    set_smem(fn, smem);
+    const RowSrc src{dim, use_sq8 ? e.cqs : Q, e.cqbase, ix.cent_f32, ix.cent_sq8};
+    const dim3 grid((nq + kRaQ - 1) / kRaQ, (nl + kRaC - 1) / kRaC);
+    Tick tk(kKRescoreDots, st);
+    if (use_sq8)
+        k_rescore_all<1><<<grid, 256, smem, st>>>(src, ix.live_list, nl, nq, cap, rs_scores);
+    else
+        k_rescore_all<0><<<grid, 256, smem, st>>>(src, ix.live_list, nl, nq, cap, rs_scores);
+    return true;
 }
 
 void launch_merge_topk(const uint8_t* tall, size_t rank_bytes, int W, int nq, int k, uint64_t* ids, float* scores,

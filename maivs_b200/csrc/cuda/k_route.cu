@@ -897,7 +897,7 @@ void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int
 void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
                            const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
                            uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, float* rs_scores,
-                           uint32_t* rs_items, int expect_n, cudaStream_t st) {
+                           uint32_t* rs_items, int expect_n, bool all_live, cudaStream_t st) {
     if (nq <= 0) return;
     const int row_bytes = use_sq8 ? ix.dim : ix.dim * 4;
     if (expect_n <= 128 && row_bytes % 16 == 0 && nprobe <= kSmallShortlist) {
@@ -916,15 +916,25 @@ void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* 
         }
         return;
     }
+    const int small = std::max(next_pow2(std::max(nprobe, 1)), 1024);
+    if (rs_scores && rs_items && small <= kSortCap && all_live &&
+        launch_rescore_all(ix, e, Q, nq, use_sq8, sl_cap, rs_scores, st)) {
+        // every shortlist is the live-cell list: the tiled product scored it, then the selection
+        const size_t psm = (size_t)small * sizeof(uint64_t);
+        set_smem((const void*)k_probe_select, psm);
+        Tick tk(kKProbeSelect, st);
+        k_probe_select<<<nq, kBS, psm, st>>>(sl, sl_n, rs_scores, sl_cap, nprobe, small, tc, beta, chosen, cscore, nch,
+                                             err);
+        return;
+    }
     if (rs_scores && rs_items && row_bytes % 16 == 0) {
         // scores of every (query, shortlist cell) pair by the flattened register gather, then a
         // per-query selection
         launch_rescore_dots(ix, e, Q, nq, sl, sl_n, sl_cap, use_sq8, rs_scores, rs_items, st);
-        const int small = std::max(next_pow2(std::max(nprobe, 1)), 1024);
         if (small <= kSortCap) {
             const size_t psm = (size_t)small * sizeof(uint64_t);
             set_smem((const void*)k_probe_select, psm);
-            Tick tk(kKRescore, st);
+            Tick tk(kKProbeSelect, st);
             k_probe_select<<<nq, kBS, psm, st>>>(sl, sl_n, rs_scores, sl_cap, nprobe, small, tc, beta, chosen,
                                                  cscore, nch, err);
             return;

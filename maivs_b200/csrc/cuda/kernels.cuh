@@ -64,7 +64,7 @@ struct IndexView {
 enum KernelId : int {
     kKEncode = 0, kKRouteFlat, kKRouteTree, kKRescore, kKSeed, kKInvCount, kKInvScan, kKInvScatter,
     kKScanCm, kKFinalCm, kKPqPrep, kKPqScan, kKPqFold, kKRerank, kKTopk, kKRerankItems, kKSeedFinish, kKLocalList, kKMergeTopk,
-    kKScanMma, kKSeedScan, kKAllGather, kKSegMerge, kNumKernels
+    kKScanMma, kKSeedScan, kKAllGather, kKSegMerge, kKRescoreDots, kKProbeSelect, kNumKernels
 };
 const char* kernel_name(int id);
 // Brackets a step that is not one of this library's kernels (an NCCL collective) on the thread's
@@ -125,10 +125,11 @@ void launch_route_tree(const IndexView& ix, const QueryEnc& e, int nq, const int
                        int scratch_cap, uint32_t* sl, uint32_t* sl_n, int sl_cap, cudaStream_t st);
 // SQ8 (or f32) re-order of the shortlist, top-nprobe by score desc (ties: lower cell id first),
 // nucleus cut (index.rs:1931-1977, :1283-1301).
+// all_live: every query's shortlist is the live-cell list (scored by a tiled product).
 void launch_rescore_select(const IndexView& ix, const QueryEnc& e, const float* Q, int nq, const uint32_t* sl,
                            const uint32_t* sl_n, int sl_cap, int nprobe, float tc, float beta, bool use_sq8,
                            uint32_t* chosen, float* cscore, uint32_t* nch, uint32_t* err, float* rs_scores,
-                           uint32_t* rs_items, int expect_n, cudaStream_t st);
+                           uint32_t* rs_items, int expect_n, bool all_live, cudaStream_t st);
 
 // Cell-major batch (index.rs:1999-2311).
 struct CellMajorBufs {
