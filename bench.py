@@ -1018,6 +1018,134 @@ def run_concurrent(args):
     print(json.dumps(out), flush=True)
 
 
+def run_filtered(args):
+    """BASELINE configs[4] scaled to one GPU: d = 768 unit vectors from a seeded mixture (one
+    component per 1,000 vectors, sigma 0.3), the `memory` preset with 768-bit codes (96 B) and
+    per-dimension SQ8 rows, 10,000-query batches, k = 100, uniform tags in [0, 1000) and a filter
+    tag < t at 1% and 10% selectivity (bench/fair/filtered.py of the reference draws them the same
+    way). A filter turns the cell-major join off (index.rs:3343-3348), so every search is the
+    per-query path with the tag checked in the scan. Per selectivity: the smallest nprobe on the
+    grid whose R@100 against the exact top 100 of the vectors that pass is >= 0.9, its
+    device-resident and end-to-end batch QPS, and the ids and scores of a sample against the oracle
+    over the same index."""
+    import torch
+
+    import maivs_b200 as M
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, nq, k, rf = args.n, args.nq, 100, args.rf or 4
+    X, Q, _ = mixture(args.seed, n, nq, 768, max(n // 1000, 16), 0.3)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    ix = M.FlatCellIndex(768, "binary", rf, 0x5EED, 768)
+    ix.set_per_dim_sq(True)
+    ix.set_orthogonal_polysemy(2, 1.0)
+    ix.set_fastscan(True)
+    ix.set_two_stage(True, 2)
+    ix.set_graph_route(False, 10**9)
+    ix.set_tree_route(True, 2048, 16)
+    ix.set_adaptive(True, 0.02)
+    ix.set_build_device(0)
+    ix.train_centroids(X, n // 128)
+    ix.add_batch(np.arange(n, dtype=np.uint64), X)
+    ix.compact()
+    build_s = time.perf_counter() - t0
+    tags = np.random.default_rng(2).integers(0, 1000, n).astype(np.uint32)
+    ix.set_tags(np.arange(n, dtype=np.uint64), tags)
+    ix.to_device(0)
+    cells = int(ix.stats()["n_cells"])
+    stream = torch.cuda.Stream(dev)
+    dq = torch.from_numpy(Q).to(dev)
+    d_ids = torch.empty(nq * k, dtype=torch.int64, device=dev)
+    d_sc = torch.empty(nq * k, dtype=torch.float32, device=dev)
+    xt = torch.from_numpy(X).to(dev)
+    qt = torch.from_numpy(Q).to(dev)
+    out = {"metric": "filtered batch QPS at R@100>=0.9, d=768 memory preset, k=100, 1% and 10% selectivity",
+           "unit": "queries/s", "higher_is_better": True, "n_gpus": 1, "steps": args.steps,
+           "warmup": max(args.warmup, 3), "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+           "data": "synthetic",
+           "config": {"workload": f"BASELINE configs[4] scaled to {n:,} x 768 on one GPU (mixture of {max(n // 1000, 16)} "
+                                  "components, sigma 0.3), memory preset with 768-bit codes, 10,000-query batches, "
+                                  "k=100, uniform tags in [0,1000), filter tag < t; per-query path", "n": n,
+                      "nq_per_step": nq, "k": k, "rerank_factor": rf, "cells": cells, "build_s": round(build_s, 1)}}
+    per = {}
+    for sel, t in (("1%", 10), ("10%", 100)):
+        ix.set_filter(0, t - 1)
+        sub = np.nonzero(tags < t)[0]
+        st = torch.from_numpy(sub.astype(np.int64)).to(dev)
+        xs = xt[st]
+        truth = []
+        for i in range(0, nq, 1024):
+            truth.append(st[torch.topk(qt[i:i + 1024] @ xs.T, k, dim=1).indices].cpu().numpy())
+        del xs
+        truth = np.concatenate(truth)
+
+        def run(np_):
+            ix.search_batch_device(dq.data_ptr(), nq, k, d_ids.data_ptr(), d_sc.data_ptr(), np_, 1.0, 8.0, True,
+                                   stream.cuda_stream)
+            torch.cuda.synchronize(dev)
+
+        def rec100():
+            got = d_ids.cpu().numpy().view(np.uint64).reshape(nq, k).astype(np.int64)
+            return float(np.mean([len(set(a) & set(b)) / k for a, b in zip(got.tolist(), truth.tolist())]))
+
+        np_sel, r_sel, sweep = None, 0.0, []
+        for np_ in (64, 128, 256, 512, 1024, 2048):
+            if np_ > cells:
+                break
+            run(np_)
+            r = rec100()
+            sweep.append({"nprobe": np_, "recall_at_100": round(r, 4)})
+            np_sel, r_sel = np_, r
+            if r >= 0.9:
+                break
+        for _ in range(max(args.warmup, 3)):
+            run(np_sel)
+        ms = []
+        torch.cuda.profiler.start()
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ix.search_batch_device(dq.data_ptr(), nq, k, d_ids.data_ptr(), d_sc.data_ptr(), np_sel, 1.0, 8.0, True,
+                                   stream.cuda_stream)
+            e1.record(stream)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        torch.cuda.profiler.stop()
+        flags = ix.device_flags(stream.cuda_stream)
+        e2e = []
+        for _ in range(max(args.steps // 2, 2)):
+            t1 = time.perf_counter()
+            ids_h, sc_h = ix.search_batch_arrays(Q, k, np_sel, 1.0, 8.0, True)
+            e2e.append(time.perf_counter() - t1)
+        sample = np.ascontiguousarray(Q[:200])
+        o = oracle.OracleIndex.from_index(ix)
+        oracle.lib().oracle_set_threads(threads)
+        t1 = time.perf_counter()
+        ref_ids, ref_sc, *_ = o.search_batch(sample, k, np_sel, 1.0, 8.0, True, threads=threads)
+        cpu_s = time.perf_counter() - t1
+        del o
+        parity = bool(np.array_equal(ids_h[:200 * k], ref_ids)
+                      and np.array_equal(sc_h[:200 * k].view(np.uint32), ref_sc.view(np.uint32)))
+        per[sel] = {"nprobe": np_sel, "recall_at_100": round(r_sel, 4), "sweep": sweep,
+                    "value": round(nq / (float(np.mean(ms)) / 1e3), 1), "ms_per_step": round(float(np.mean(ms)), 3),
+                    "e2e_qps": round(nq / float(np.mean(e2e)), 1), "overflow_flags": int(flags),
+                    "parity": {"sample": 200, "ids_and_scores_equal": parity},
+                    "cpu_baseline": {"value": round(200 / cpu_s, 1), "unit": "queries/s", "cores": threads,
+                                     "kind": "port", "sample": f"200 queries, one call, nprobe {np_sel}, the oracle "
+                                                               "over the same index's arrays"}}
+        ix.set_filter()
+    out["selectivity"] = per
+    out["value"] = per["10%"]["value"]
+    out["ms_per_step"] = per["10%"]["ms_per_step"]
+    out["e2e"] = {"value": per["10%"]["e2e_qps"], "unit": "queries/s", "h2d_bytes_per_step": int(Q.nbytes),
+                  "d2h_bytes_per_step": int(nq * k * 12)}
+    out["cpu_baseline"] = per["10%"]["cpu_baseline"]
+    print(json.dumps(out), flush=True)
+
+
 def run_reference(args):
     """The reference's CPU path (the oracle: a C++ restatement of the reference's Rust build and
     query path; the reference itself cannot be built here) on every host core. The index is the
@@ -1132,12 +1260,14 @@ def main():
     ap.add_argument("--rf", type=int, default=0, help="sharded workload: fixed rerank factor (with --nprobe)")
     ap.add_argument("--nprobe", type=int, default=0, help="sharded workload: fixed nprobe instead of the sweep")
     ap.add_argument("--no-sweep", action="store_true", help="config2: skip the (rf, nprobe) recall sweep")
-    ap.add_argument("--workload", choices=("auto", "config2", "sharded", "lowbatch", "concurrent"), default="auto",
+    ap.add_argument("--workload", choices=("auto", "config2", "sharded", "lowbatch", "concurrent", "filtered"),
+                    default="auto",
                     help="auto: sharded under torchrun (WORLD_SIZE set), else config2. config2: the headline 500k "
                          "batch on one GPU (replicas when forced under torchrun); sharded: configs[3], 5.2M vectors "
                          "with cells sharded by range over the N GPUs; lowbatch: configs[2], memory preset at "
                          "batch 1 and 16; concurrent: a ConcurrentIndex (sealed segments + head + tombstones) over "
-                         "the config2 vectors")
+                         "the config2 vectors; filtered: configs[4] scaled to one GPU (d=768 memory preset, k=100, "
+                         "1% and 10% tag filters)")
     ap.add_argument("--parity-sample", type=int, default=1000,
                     help="sharded: queries of the timed batch checked against the oracle (0: none)")
     args = ap.parse_args()
@@ -1145,9 +1275,9 @@ def main():
         args.workload = "sharded" if "WORLD_SIZE" in os.environ else "config2"
     sharded = args.workload == "sharded"
     if args.n is None:
-        args.n = 5_200_000 if sharded else 500_000
+        args.n = 5_200_000 if sharded else 1_000_000 if args.workload == "filtered" else 500_000
     if args.nq is None:
-        args.nq = 10_000 if sharded else 1000
+        args.nq = 10_000 if sharded or args.workload == "filtered" else 1000
     if args.impl == "reference":
         run_reference_sharded(args) if sharded else run_reference(args)
     elif sharded:
@@ -1156,6 +1286,8 @@ def main():
         run_lowbatch(args)
     elif args.workload == "concurrent":
         run_concurrent(args)
+    elif args.workload == "filtered":
+        run_filtered(args)
     else:
         run_maivs(args)
 
