@@ -15,7 +15,7 @@ namespace {
 // Queries per pass of the per-query pipeline: the whole batch when its scratch (probe ranks,
 // shortlists, entries and candidates of every query) fits in kPerQueryScratch, else the largest
 // power-of-two share of it that does, but never fewer than kPerQueryMinChunk.
-constexpr size_t kPerQueryScratch = size_t(1) << 30;
+constexpr size_t kPerQueryScratch = size_t(4) << 30;
 constexpr int kPerQueryMinChunk = 64;
 constexpr uint32_t kNoCellHost = 0xFFFFFFFFu;  // an unused home in slot_cells
 

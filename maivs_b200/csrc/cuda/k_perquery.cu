@@ -69,12 +69,19 @@ __device__ __forceinline__ bool pq_member_ok(const IndexView& ix, uint32_t slot,
 // 32 member groups (256 members) the 8 warps sum disjoint slices of the nibble positions and
 // combine their packed 16-bit partials in shared memory (exact: a member's total is at most
 // 255 x npos), then every thread resolves one member (slot, tag filter, the per-query exactly-once
-// rule against the probe ranks), so the members' dependent loads run side by side.
+// rule against the probe ranks), so the members' dependent loads run side by side. Under a filter
+// the groups whose eight members all fail it are written out as invalid entries up front and only
+// the others are summed (the reference sums every block and drops the members afterwards; the
+// entries are the same).
+constexpr int kPqMaxG = 512;  // member groups of a cell that the filtered scan compacts (4,096 members)
+
 __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const uint32_t* __restrict__ chosen,
                                                  const uint32_t* __restrict__ nch, int nprobe, int filtering,
                                                  uint32_t flo, uint32_t fhi, PerQueryBufs b) {
     __shared__ __align__(16) uint8_t s_lut[16 * 16 * 16];  // npos <= 256 positions x 16 entries
     __shared__ uint32_t s_part[kBS / 32][32][4];
+    __shared__ uint16_t s_gl[kPqMaxG];
+    __shared__ int s_nact;
     const int r = blockIdx.x, q = blockIdx.y;
     if (r >= (int)nch[q]) return;
     const uint32_t* so = b.seg_off + (size_t)q * (nprobe + 1);
@@ -88,25 +95,48 @@ __global__ void __launch_bounds__(kBS) k_pq_scan(IndexView ix, QueryEnc e, const
     uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kBS / 32;
     const int npos = ix.npos;
+    const bool compact = filtering && ng <= kPqMaxG;
+    if (threadIdx.x == 0) s_nact = 0;
     {
         const uint4* src = reinterpret_cast<const uint4*>(e.lut + (size_t)q * npos * 16);
         for (int i = threadIdx.x; i < npos; i += kBS) reinterpret_cast<uint4*>(s_lut)[i] = src[i];
     }
     __syncthreads();
+    if (compact) {
+        for (int g = threadIdx.x; g < ng; g += kBS) {
+            bool any = false;
+            for (int bb = 0; bb < 8; ++bb) {
+                const int pos = 8 * g + bb;
+                if (pos < nc) {
+                    const uint32_t tg = __ldg(ix.tags + __ldg(ix.cell_slots + moff + pos));
+                    any |= tg >= flo && tg <= fhi;
+                }
+            }
+            if (any) {
+                s_gl[atomicAdd(&s_nact, 1)] = (uint16_t)g;
+            } else {
+                for (int bb = 0; bb < 8 && 8 * g + bb < nc; ++bb) out[8 * g + bb] = kInvalidEntry;
+            }
+        }
+        __syncthreads();
+    }
+    const int nact = compact ? s_nact : ng;
     // this warp's slice of the positions
     const int p0 = (int)((long long)npos * warp / nwarps), p1 = (int)((long long)npos * (warp + 1) / nwarps);
-    for (int g0 = 0; g0 < ng; g0 += 32) {
-        const int g = g0 + lane;
-        const bool act = g < ng;
+    for (int a0 = 0; a0 < nact; a0 += 32) {
+        const int ai = a0 + lane;
+        const bool act = ai < nact;
+        const int g = act ? (compact ? (int)s_gl[ai] : ai) : 0;
         uint32_t acc[4];
         group_sums_range(codes, ng, g, act, s_lut, p0, p1, acc);
 #pragma unroll
         for (int i = 0; i < 4; ++i) s_part[warp][lane][i] = acc[i];
         __syncthreads();
-        // thread t: member 8 * (g0 + t / 8) + t % 8 of this chunk
+        // thread t: member 8 * group(a0 + t / 8) + t % 8 of this chunk
         {
             const int gl = threadIdx.x >> 3, bb = threadIdx.x & 7;
-            const int pos = 8 * (g0 + gl) + bb;
+            const int a = a0 + gl;
+            const int pos = a < nact ? 8 * (compact ? (int)s_gl[a] : a) + bb : nc;
             if (pos < nc) {
                 uint32_t tot = 0;
 #pragma unroll
@@ -145,11 +175,14 @@ __global__ void __launch_bounds__(kBS) k_pq_scan_ham(IndexView ix, QueryEnc e, c
     uint64_t* out = b.ent + (size_t)q * b.ent_cap + so[r];
     for (int pos = threadIdx.x; pos < nc; pos += kBS) {
         const uint32_t slot = __ldg(ix.cell_slots + moff + pos);
-        const uint64_t* code = ix.bits + (size_t)slot * nw;
-        uint32_t h = 0;
-        for (int w = 0; w < nw; ++w) h += (uint32_t)__popcll(s_q[w] ^ __ldg(code + w));
-        const bool ok = pq_member_ok(ix, slot, c, r, crank, filtering, flo, fhi);
-        out[pos] = ok ? (((uint64_t)h << 32) | slot) : kInvalidEntry;
+        uint64_t entry = kInvalidEntry;
+        if (pq_member_ok(ix, slot, c, r, crank, filtering, flo, fhi)) {  // the code is read only when kept
+            const uint64_t* code = ix.bits + (size_t)slot * nw;
+            uint32_t h = 0;
+            for (int w = 0; w < nw; ++w) h += (uint32_t)__popcll(s_q[w] ^ __ldg(code + w));
+            entry = ((uint64_t)h << 32) | slot;
+        }
+        out[pos] = entry;
     }
 }
 
