@@ -107,7 +107,9 @@ int maivs_search_batch(maivs_index* ix, const float* queries, size_t nq, size_t 
  * NULL = the handle's stream). Returns once the work is enqueued; after synchronising the stream,
  * maivs_device_flags() reports whether any query's candidate buffer overflowed (then the results
  * of that call must be discarded and the call repeated; the handle has already enlarged its
- * buffers). Same semantics as maivs_search_batch otherwise. */
+ * buffers). Same semantics as maivs_search_batch otherwise. Searches on one handle share its
+ * workspace: a search enqueued on another stream than the handle's previous one waits for it on
+ * the device (an event), so the two never overlap. */
 int maivs_search_batch_device(maivs_index* ix, const float* d_queries, size_t nq, size_t k, size_t nprobe,
                               float target_confidence, float beta, int cell_major, uint64_t* d_ids, float* d_scores,
                               void* stream);

@@ -1,5 +1,8 @@
 // Per-kernel device clock, launch counter and first-launch-error record of the query kernels.
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "dev_common.cuh"
 
@@ -98,8 +101,55 @@ void clock_end(int id, cudaStream_t st) {
 }
 unsigned long long total_launches() { return g_launches.load(); }
 
+// The attribute and occupancy queries cost host time on every launch of a search; their answers
+// only change with the device, so they are remembered per (device, kernel).
+namespace {
+std::mutex g_attr_mu;
+std::map<std::pair<int, const void*>, size_t> g_smem_set;
+std::map<std::tuple<int, const void*, int, size_t>, int> g_occ;
+int cur_device() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return dev;
+}
+}  // namespace
+
 void set_smem(const void* f, size_t bytes) {
-    if (bytes > 0) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (bytes == 0) return;
+    const auto key = std::make_pair(cur_device(), f);
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    auto it = g_smem_set.find(key);
+    if (it != g_smem_set.end() && it->second >= bytes) return;
+    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess)
+        g_smem_set[key] = bytes;
+}
+
+int blocks_per_sm(const void* f, int threads, size_t smem) {
+    const auto key = std::make_tuple(cur_device(), f, threads, smem);
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        auto it = g_occ.find(key);
+        if (it != g_occ.end()) return it->second;
+    }
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, threads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    g_occ[key] = per_sm;
+    return per_sm;
+}
+
+int sm_count() {
+    const int dev = cur_device();
+    static std::mutex mu;
+    static std::map<int, int> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = sms;
+    return sms;
 }
 
 }  // namespace dev

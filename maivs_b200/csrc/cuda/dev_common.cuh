@@ -32,6 +32,10 @@ struct Tick {
 // The 48 KiB default covers static plus dynamic shared memory, so any dynamic request opts in to
 // its exact size; a refused opt-in surfaces as the launch error recorded by Tick.
 void set_smem(const void* f, size_t bytes);
+// Resident CTAs per SM of kernel f (cudaOccupancyMaxActiveBlocksPerMultiprocessor, at least 1) and
+// the current device's SM count, both remembered per device.
+int blocks_per_sm(const void* f, int threads, size_t smem);
+int sm_count();
 
 // ---- launchers of kernels that another stage's launcher starts -----------------------------------
 // k_scan_mma (k_scan_mma.cu) over every cell the batch's rest probes hit kMmaMinQueries times or more.

@@ -16,6 +16,8 @@ namespace {
 // shortlists, entries and candidates of every query) fits in kPerQueryScratch, else the largest
 // power-of-two share of it that does, but never fewer than kPerQueryMinChunk.
 constexpr size_t kPerQueryScratch = size_t(4) << 30;
+// Host-buffer batches of this many queries or more are searched as two halves on two streams.
+constexpr int kSplitQueries = 512;
 constexpr int kPerQueryMinChunk = 64;
 constexpr uint32_t kNoCellHost = 0xFFFFFFFFu;  // an unused home in slot_cells
 
@@ -45,11 +47,18 @@ DeviceIndex::~DeviceIndex() {
     if (device_ >= 0) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
     for (void* p : allocs_) cudaFree(p);
-    if (ws_) cudaFree(ws_);
+    if (stream2_) cudaStreamSynchronize(stream2_);
+    for (void* w : ws_)
+        if (w) cudaFree(w);
     if (io_) cudaFree(io_);
     if (pin_) cudaFreeHost(pin_);
     for (auto& e : ev_)
         if (e) cudaEventDestroy(e);
+    for (auto& e : split_ev_)
+        if (e) cudaEventDestroy(e);
+    for (auto& e : ws_ev_)
+        if (e) cudaEventDestroy(e);
+    if (stream2_) cudaStreamDestroy(stream2_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -245,17 +254,18 @@ std::string DeviceIndex::upload(const HostIndex& h, int device, uint32_t c_lo, u
 }
 
 int DeviceIndex::ensure_ws(size_t bytes, std::string& err) {
-    if (bytes <= ws_bytes_) return kOk;
-    if (ws_) {
-        cudaStreamSynchronize(stream_);
-        cudaDeviceSynchronize();
-        cudaFree(ws_);
-        ws_ = nullptr;
-        ws_bytes_ = 0;
+    void*& w = ws_[ws_sel_];
+    size_t& wb = ws_bytes_[ws_sel_];
+    if (bytes <= wb) return kOk;
+    if (w) {
+        cudaDeviceSynchronize();  // searches in flight on any stream may still use it
+        cudaFree(w);
+        w = nullptr;
+        wb = 0;
     }
     size_t want = bytes + bytes / 4;
-    CUDA_TRY(cudaMalloc(&ws_, want));
-    ws_bytes_ = want;
+    CUDA_TRY(cudaMalloc(&w, want));
+    wb = want;
     return kOk;
 }
 
@@ -286,7 +296,8 @@ int DeviceIndex::global_flags(cudaStream_t st, uint32_t out[4]) {
 }
 
 bool DeviceIndex::use_cell_major(const HostIndex& h, const SearchArgs& a) const {
-    // cm_ok (index.rs:3343-3348)
+    // cm_ok (index.rs:3343-3348); a part of a split batch keeps the whole batch's choice
+    if (a.path >= 0) return a.path == 1;
     return a.cell_major && h.compacted && (h.max_assign == 1 || !h.rep_off.empty()) && !h.has_filter &&
            (size_t)a.nq >= h.cm_min_batch;
 }
@@ -407,7 +418,7 @@ int DeviceIndex::run_cellmajor(const HostIndex& h, const float* dQ, const Search
     carve(sizing, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
-    Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
+    Bump bp{static_cast<char*>(ws()), 0, ws_bytes()};
     carve(bp, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
 
     last_ = LastCall{};
@@ -517,7 +528,7 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
     }
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
-    Bump bp{static_cast<char*>(ws_), 0, ws_bytes_};
+    Bump bp{static_cast<char*>(ws()), 0, ws_bytes()};
     carve(bp, e, sl, sl_n, hs, tsc, chosen, cscore, nch, b);
 
     last_ = LastCall{};
@@ -558,7 +569,8 @@ int DeviceIndex::run_perquery(const HostIndex& h, const float* dQ, const SearchA
 }
 
 int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids,
-                               float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err) {
+                               float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err,
+                               bool clear_flags) {
     if (h.version != version_) {
         err = "the index changed since it was uploaded";
         return kBadState;
@@ -581,10 +593,15 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
         return kUnsupported;
     }
     dev::take_launch_error(nullptr);
-    cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
+    // the previous search with this workspace may have been enqueued on another stream
+    const int w = ws_sel_;
+    if (ws_ev_live_[w]) cudaStreamWaitEvent(st, ws_ev_[w], 0);
+    if (clear_flags) cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st);
     int rc = exch_                  ? search_sharded(h, dQ, a, d_ids, d_scores, d_nout, st, err)
              : use_cell_major(h, a) ? run_cellmajor(h, dQ, a, d_ids, d_scores, d_nout, st, err)
                                     : run_perquery(h, dQ, a, d_ids, d_scores, d_nout, st, err);
+    if (!ws_ev_[w]) cudaEventCreateWithFlags(&ws_ev_[w], cudaEventDisableTiming);
+    ws_ev_live_[w] = ws_ev_[w] && cudaEventRecord(ws_ev_[w], st) == cudaSuccess;
     int kid = -1;
     cudaError_t le = dev::take_launch_error(&kid);
     if (le != cudaSuccess) {
@@ -652,11 +669,48 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
     }
     // ids, scores and counts are laid out alike in the device and pinned buffers: one copy back
     const size_t out_off = al(qb), out_len = al(ib) + al(sb) + nb;
+    // two halves on two streams (not for a sharded image, whose ranks must take the same collective
+    // steps, nor under a debug stop or phase timing, which describe one search)
+    const bool split = !exch_ && !dbg && !timing_ && !clock_ && a.nq >= kSplitQueries;
+    if (split && !stream2_) {
+        CUDA_TRY(cudaStreamCreateWithFlags(&stream2_, cudaStreamNonBlocking));
+        for (auto& e : split_ev_) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const size_t half = (nq / 2) & ~size_t(63);  // keeps the second half 256-byte aligned
+    const size_t pq0[2] = {0, half}, pn[2] = {half, nq - half};
+    SearchArgs part = a;
+    if (split) part.path = use_cell_major(h, a) ? 1 : 0;
     int rc = kOk;
     for (int attempt = 0; attempt < 4; ++attempt) {
-        CUDA_TRY(cudaMemcpyAsync(dQ, hQ, qb, cudaMemcpyHostToDevice, stream_));
-        rc = search_device(h, dQ, a, dI, dS, dN, stream_, err);
-        if (rc != kOk) return rc;
+        if (!split) {
+            CUDA_TRY(cudaMemcpyAsync(dQ, hQ, qb, cudaMemcpyHostToDevice, stream_));
+            rc = search_device(h, dQ, a, dI, dS, dN, stream_, err);
+            if (rc != kOk) return rc;
+        } else {
+            // the counters are cleared once, before either half can raise one
+            CUDA_TRY(cudaMemsetAsync(d_flags_, 0, fb, stream_));
+            CUDA_TRY(cudaEventRecord(split_ev_[0], stream_));
+            CUDA_TRY(cudaStreamWaitEvent(stream2_, split_ev_[0], 0));
+            // both halves' copies first, then the searches: the second copy crosses PCIe while the
+            // first half is searched (staging per half, or a copy enqueued after the first search's
+            // launches, measured slower)
+            for (int p = 0; p < 2; ++p)
+                CUDA_TRY(cudaMemcpyAsync(dQ + pq0[p] * dim, hQ + pq0[p] * dim, pn[p] * dim * sizeof(float),
+                                         cudaMemcpyHostToDevice, p ? stream2_ : stream_));
+            for (int p = 0; p < 2; ++p) {
+                part.nq = (int)pn[p];
+                ws_sel_ = p;
+                rc = search_device(h, dQ + pq0[p] * dim, part, dI + pq0[p] * k, dS + pq0[p] * k, dN + pq0[p],
+                                   p ? stream2_ : stream_, err, false);
+                ws_sel_ = 0;
+                if (rc != kOk) {
+                    cudaStreamSynchronize(stream2_);
+                    return rc;
+                }
+            }
+            CUDA_TRY(cudaEventRecord(split_ev_[1], stream2_));
+            CUDA_TRY(cudaStreamWaitEvent(stream_, split_ev_[1], 0));
+        }
         CUDA_TRY(cudaMemcpyAsync(hp + out_off, dp + out_off, out_len, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaMemcpyAsync(hF, d_flags_, fb, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaStreamSynchronize(stream_));

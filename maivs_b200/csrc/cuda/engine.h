@@ -35,6 +35,9 @@ struct SearchArgs {
     float tc = 0.95f;
     float beta = 8.0f;
     bool cell_major = true;
+    // -1: the batch chooses the cell-major join or the per-query path (index.rs:3343-3348); 0 / 1:
+    // a part of a larger batch keeps that batch's choice (per-query / cell-major)
+    int path = -1;
 };
 
 // Per-phase device times of the last search, in milliseconds (the reference's profile phases
@@ -105,15 +108,20 @@ class DeviceIndex {
     // Search with device-resident queries and outputs, enqueued on `st`. Chooses the cell-major
     // join or the per-query path like the reference's search_batch (index.rs:3343-3348).
     // Returns a Status; `err` receives a message on failure.
+    // With clear_flags false the overflow/error counters are left as they are (the caller cleared
+    // them for several searches in flight together).
     int search_device(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
-                      uint32_t* d_nout, cudaStream_t st, std::string& err);
+                      uint32_t* d_nout, cudaStream_t st, std::string& err, bool clear_flags = true);
     // Per-query search of at most 64 device-resident queries whose scratch is a fixed 32 MiB
     // device array defined in static_search.cu (allocates nothing; calls share the array, so
     // overlapping calls race). Returns kBadArg when the search needs more scratch than that.
     int search_static(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                       cudaStream_t st, std::string& err);
     // Host buffers: copies in, searches, copies out, synchronises, and retries with larger
-    // candidate buffers if any query overflowed them.
+    // candidate buffers if any query overflowed them. A batch of kSplitQueries or more goes as two
+    // halves on two streams with a workspace each, so that the second half's queries cross PCIe
+    // while the first half is searched (every query's result depends only on that query and the
+    // path the whole batch chose).
     int search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
                     uint32_t* nout, std::string& err);
 
@@ -190,8 +198,18 @@ class DeviceIndex {
     size_t n_live_ = 0, n_leaf_ = 0, max_members_ = 0, tree_cap_ = 0;
     bool use_sq8_ = false;
     uint32_t* d_flags_ = nullptr;  // [0] overflow, [1] routing errors
-    void* ws_ = nullptr;
-    size_t ws_bytes_ = 0;
+    // search workspaces: ws_[ws_sel_] serves the search being enqueued (two for a split batch)
+    void* ws_[2] = {nullptr, nullptr};
+    size_t ws_bytes_[2] = {0, 0};
+    int ws_sel_ = 0;
+    void* ws() const { return ws_[ws_sel_]; }
+    size_t ws_bytes() const { return ws_bytes_[ws_sel_]; }
+    // recorded after each search that used ws_[i]; a later search on another stream waits on it,
+    // so searches sharing a workspace never overlap on the device
+    cudaEvent_t ws_ev_[2] = {nullptr, nullptr};
+    bool ws_ev_live_[2] = {false, false};
+    cudaStream_t stream2_ = nullptr;  // the second half of a split host-buffer batch
+    cudaEvent_t split_ev_[2] = {nullptr, nullptr};
     // pinned staging for the host-buffer API
     void* pin_ = nullptr;
     size_t pin_bytes_ = 0;

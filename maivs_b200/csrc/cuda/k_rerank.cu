@@ -757,11 +757,7 @@ void launch_rescore_dots(const IndexView& ix, const QueryEnc& e, const float* Q,
     const void* fn = mode == 1 ? (const void*)k_rescore_dots<1> : (const void*)k_rescore_dots<0>;
     const size_t smem = (size_t)8 * ((ix.dim + 3) & ~3) * sizeof(float);
     set_smem(fn, smem);
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess || per_sm < 1)
-        per_sm = 1;
+    const int sms = sm_count(), per_sm = blocks_per_sm(fn, 256, smem);
     const RowSrc src{ix.dim, use_sq8 ? e.cqs : Q, e.cqbase, ix.cent_f32, ix.cent_sq8};
     {
         Tick tk(kKRerankItems, st);
@@ -927,12 +923,8 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
                                                : (const void*)k_rerank_gather<2>;
         const size_t smem = (size_t)8 * ((ix.dim + 3) & ~3) * sizeof(float);
         set_smem(fn, smem);
-        int dev = 0, sms = 148, per_sm = 1;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem) != cudaSuccess || per_sm < 1)
-            per_sm = 1;
-        const int grid = sms * per_sm;
+        const int sms = sm_count();
+        const int grid = sms * blocks_per_sm(fn, 256, smem);
         const RowSrc src{ix.dim, ix.rerank_mode == 1 ? e.rqs : Q, e.rbase, ix.vecs_f32, ix.rr_u8};
         // f32 rows of 384 or 768 dimensions: the streamed kernel (the query chain in registers)
         const int rstride = ix.dim + ((8 - ix.dim % 32) + 32) % 32;  // rows of a warp on distinct banks

@@ -309,9 +309,7 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
 
 void launch_scan_mma(const IndexView& ix, const QueryEnc& e, const CellMajorBufs& b, cudaStream_t st) {
     using P = PScan<8, 2>;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
     cudaMemsetAsync(b.work, 0, sizeof(uint32_t), st);
     set_smem((const void*)k_scan_mma<8, 2>, P::kSmem);
     Tick tk(kKScanMma, st);

@@ -261,7 +261,7 @@ int DeviceIndex::shard_begin(const HostIndex& h, const float* dQ, const SearchAr
     carve(sizing);
     int rc = ensure_ws(sizing.off + 256, err);
     if (rc != kOk) return rc;
-    Bump bp{static_cast<char*>(ws_)};
+    Bump bp{static_cast<char*>(ws())};
     carve(bp);
 
     last_ = LastCall{};
