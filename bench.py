@@ -419,6 +419,7 @@ def run_maivs(args):
     step_ms = [a.elapsed_time(b) for a, b in evs]
     total_ms = float(sum(step_ms))
     overflow = ix.device_flags(stream.cuda_stream)
+    kbusy = ix.kernel_busy()
     ktimes = ix.kernel_times(reset=True)
     ix.kernel_clock(False)
     stats = ix.last_search_stats()
@@ -480,6 +481,8 @@ def run_maivs(args):
     name = dom_kernel
     kms, kl = ktimes.get(name, (0.0, 0))
     per_launch_ms = kms / max(kl, 1)
+    # launches of the kernel per step: 2 when the library searches the batch as two halves
+    lps = kl / max(args.steps, 1)
     row_bytes = stats.get("rerank_row_bytes", 1536.0)
     if name == "k_rerank":
         alg = union_rows * row_bytes
@@ -498,8 +501,14 @@ def run_maivs(args):
     else:
         alg = stats.get("scan_code_bytes", 0.0) + stats.get("rerank_bytes", 0.0)
         what = "scan codes + rerank rows"
-    achieved = alg / (per_launch_ms / 1e3) / 1e9 if per_launch_ms > 0 else 0.0
+    # the batch's algorithmic bytes over the time per step during which the kernel ran: the two
+    # halves' launches of a split batch overlap, so their summed durations would count that twice
+    busy_ms = kbusy.get(name, 0.0) / max(args.steps, 1)
+    alg_launch = alg / max(lps, 1.0)
+    achieved = alg / (busy_ms / 1e3) / 1e9 if busy_ms > 0 else 0.0
     traffic = ncu_traffic(name, stats)
+    if traffic:
+        traffic = round(traffic / max(lps, 1.0))
 
     # the scan: algorithmic code bytes (union of scanned cells, each once per batch) over the scan
     # kernels' device time from the all-kernel pass
@@ -543,8 +552,11 @@ def run_maivs(args):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                     "algorithmic_bytes_per_launch": round(alg), "avg_launch_ms": round(per_launch_ms, 5),
-                     "what": what, "peak_src": peaks["src"]},
+                     "algorithmic_bytes_per_launch": round(alg_launch), "avg_launch_ms": round(per_launch_ms, 5),
+                     "launches_per_step": round(lps, 2), "algorithmic_bytes_per_step": round(alg),
+                     "busy_ms_per_step": round(busy_ms, 5),
+                     "what": what + "; achieved = bytes per step / busy_ms_per_step (the time per step during "
+                                    "which at least one launch of the kernel ran)", "peak_src": peaks["src"]},
         "scan": {"kernels": scan_k, "bytes_per_step": round(scan_bytes), "ms_per_step": round(scan_ms, 5),
                  "achieved": round(scan_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                  "frac": round(scan_gbs / peaks["hbm_gbs"], 4),

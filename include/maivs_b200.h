@@ -272,6 +272,10 @@ int maivs_kernel_clock(maivs_index* ix, int on);
 int maivs_kernel_clock_only(maivs_index* ix, const char* kernel);
 int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* ms, uint64_t* launches, size_t cap,
                        size_t* n_out);
+/* Per kernel, the device time during which at least one of its launches ran, since the clock's
+ * last reset (maivs_kernel_times with reset): launches on several streams that overlap in time
+ * (the two halves of a split batch) count once here and once each in maivs_kernel_times. */
+int maivs_kernel_busy(maivs_index* ix, const char** names, double* busy_ms, size_t cap, size_t* n_out);
 uint64_t maivs_launch_count(void);
 /* Host threads of the index build and host-side search staging for the calling thread
  * (omp_set_num_threads; no counterpart in the reference). Under launchers that export

@@ -291,6 +291,16 @@ class FlatCellIndex:
         self._check(_lib.lib().maivs_kernel_times(self._h, int(bool(reset)), names, ms, la, n, C.byref(got)))
         return {names[i].decode(): (float(ms[i]), int(la[i])) for i in range(got.value)}
 
+    def kernel_busy(self) -> dict:
+        """{kernel name: ms during which at least one of its launches ran} since the clock's last
+        reset (read it before kernel_times(reset=True)); overlapping launches count once."""
+        n = 32
+        names = (C.c_char_p * n)()
+        ms = (C.c_double * n)()
+        got = C.c_size_t(0)
+        self._check(_lib.lib().maivs_kernel_busy(self._h, names, ms, n, C.byref(got)))
+        return {names[i].decode(): float(ms[i]) for i in range(got.value)}
+
     def last_search_stats(self) -> dict:
         """Work counters of the last search (probes, candidates, bytes scanned and reranked)."""
         cap = 64

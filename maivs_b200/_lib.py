@@ -62,6 +62,8 @@ _SIGS = {
     "maivs_kernel_clock_only": (C.c_int, [C.c_void_p, C.c_char_p]),
     "maivs_kernel_times": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
                                      C.POINTER(C.c_uint64), C.c_size_t, C.POINTER(C.c_size_t)]),
+    "maivs_kernel_busy": (C.c_int, [C.c_void_p, C.POINTER(C.c_char_p), C.POINTER(C.c_double), C.c_size_t,
+                                    C.POINTER(C.c_size_t)]),
     "maivs_launch_count": (C.c_uint64, []),
     "maivs_set_num_threads": (C.c_int, [C.c_int]),
     "maivs_last_search_stats": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_double), C.c_size_t,

@@ -664,8 +664,22 @@ int maivs_kernel_times(maivs_index* ix, int reset, const char** names, double* m
     if (reset && c)
         for (size_t i = 0; i < maivs::dev::kNumKernels; ++i) {
             c->ms[i] = 0.0;
+            c->busy[i] = 0.0;
             c->launches[i] = 0;
         }
+    return MAIVS_OK;
+}
+
+int maivs_kernel_busy(maivs_index* ix, const char** names, double* busy_ms, size_t cap, size_t* n_out) {
+    LOCK(ix);
+    size_t n = std::min<size_t>(cap, maivs::dev::kNumKernels);
+    if (n_out) *n_out = n;
+    maivs::dev::KernelClock* c = ix->d ? ix->d->kernel_clock() : nullptr;
+    if (c) c->collect();
+    for (size_t i = 0; i < n; ++i) {
+        if (names) names[i] = maivs::dev::kernel_name((int)i);
+        if (busy_ms) busy_ms[i] = c ? c->busy[i] : 0.0;
+    }
     return MAIVS_OK;
 }
 

@@ -1,8 +1,10 @@
 // Per-kernel device clock, launch counter and first-launch-error record of the query kernels.
+#include <algorithm>
 #include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
 
 #include "dev_common.cuh"
 
@@ -82,10 +84,41 @@ void KernelClock::end(cudaStream_t st) {
 }
 
 void KernelClock::collect() {
+    // every mark's interval against one origin event (the first pending mark's start; others may
+    // start before it on another stream, giving negative offsets), merged per kernel into busy time
+    std::vector<std::vector<std::pair<float, float>>> iv(kNumKernels);
+    cudaEvent_t origin = nullptr;
     for (auto& m : pending) {
         float t = 0.0f;
-        if (cudaEventSynchronize(m.b) == cudaSuccess && cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess)
+        if (cudaEventSynchronize(m.b) == cudaSuccess && cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess) {
             ms[m.id] += t;
+            if (!origin) origin = m.a;
+            float s0 = 0.0f, s1 = 0.0f;
+            if (cudaEventElapsedTime(&s0, origin, m.a) == cudaSuccess &&
+                cudaEventElapsedTime(&s1, origin, m.b) == cudaSuccess)
+                iv[m.id].push_back({s0, s1});
+            else
+                busy[m.id] += t;
+        }
+    }
+    for (int id = 0; id < kNumKernels; ++id) {
+        auto& v = iv[id];
+        std::sort(v.begin(), v.end());
+        float lo = 0.0f, hi = 0.0f;
+        bool open = false;
+        for (const auto& x : v) {
+            if (open && x.first <= hi) {
+                hi = std::max(hi, x.second);
+                continue;
+            }
+            if (open) busy[id] += hi - lo;
+            lo = x.first;
+            hi = x.second;
+            open = true;
+        }
+        if (open) busy[id] += hi - lo;
+    }
+    for (auto& m : pending) {
         pool.push_back(m.a);
         pool.push_back(m.b);
     }

@@ -16,7 +16,7 @@ namespace {
 // shortlists, entries and candidates of every query) fits in kPerQueryScratch, else the largest
 // power-of-two share of it that does, but never fewer than kPerQueryMinChunk.
 constexpr size_t kPerQueryScratch = size_t(4) << 30;
-// Host-buffer batches of this many queries or more are searched as two halves on two streams.
+// Batches of this many queries or more may be searched as two halves on two streams.
 constexpr int kSplitQueries = 512;
 constexpr int kPerQueryMinChunk = 64;
 constexpr uint32_t kNoCellHost = 0xFFFFFFFFu;  // an unused home in slot_cells
@@ -592,6 +592,8 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
                       "or search with cell_major=False";
         return kUnsupported;
     }
+    if (clear_flags && split_halves(h, a)) return search_halves(h, dQ, nullptr, a, d_ids, d_scores, d_nout, st, err);
+    if (a.path < 0) last_split_ = false;
     dev::take_launch_error(nullptr);
     // the previous search with this workspace may have been enqueued on another stream
     const int w = ws_sel_;
@@ -608,6 +610,52 @@ int DeviceIndex::search_device(const HostIndex& h, const float* dQ, const Search
         err = std::string("launch of ") + dev::kernel_name(kid) + " failed: " + cudaGetErrorString(le);
         return le == cudaErrorMemoryAllocation ? kOom : kCudaError;
     }
+    return rc;
+}
+
+bool DeviceIndex::split_halves(const HostIndex& h, const SearchArgs& a) const {
+    // beyond the seed cells the join scans each probed cell once for all the queries that probe
+    // it, and halves would scan it twice (measured: 4.58 -> 6.16 ms for 5,000 queries at nprobe 256)
+    if (exch_ || dbg || timing_ || a.path >= 0 || a.nq < kSplitQueries) return false;
+    return use_cell_major(h, a) && std::min(a.nprobe, view_.M) <= dev::kSeedCells;
+}
+
+int DeviceIndex::search_halves(const HostIndex& h, const float* dQ, const float* hQ, const SearchArgs& a,
+                               uint64_t* d_ids, float* d_scores, uint32_t* d_nout, cudaStream_t st,
+                               std::string& err) {
+    if (!stream2_) {
+        CUDA_TRY(cudaStreamCreateWithFlags(&stream2_, cudaStreamNonBlocking));
+        for (auto& e : split_ev_) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const size_t nq = a.nq, dim = view_.dim, k = a.k;
+    const size_t half = (nq / 2) & ~size_t(63);  // keeps the second half 256-byte aligned
+    const size_t q0[2] = {0, half}, n[2] = {half, nq - half};
+    cudaStream_t ps[2] = {st, stream2_};
+    SearchArgs part = a;
+    part.path = use_cell_major(h, a) ? 1 : 0;
+    // the counters are cleared once, before either half can raise one
+    CUDA_TRY(cudaMemsetAsync(d_flags_, 0, 4 * sizeof(uint32_t), st));
+    CUDA_TRY(cudaEventRecord(split_ev_[0], st));
+    CUDA_TRY(cudaStreamWaitEvent(stream2_, split_ev_[0], 0));
+    // both halves' copies before either search, so that the second crosses PCIe during the first
+    // search (a copy enqueued after the first half's launches measured slower)
+    if (hQ)
+        for (int p = 0; p < 2; ++p)
+            CUDA_TRY(cudaMemcpyAsync(const_cast<float*>(dQ) + q0[p] * dim, hQ + q0[p] * dim,
+                                     n[p] * dim * sizeof(float), cudaMemcpyHostToDevice, ps[p]));
+    int rc = kOk;
+    for (int p = 0; p < 2 && rc == kOk; ++p) {
+        part.nq = (int)n[p];
+        ws_sel_ = p;
+        rc = search_device(h, dQ + q0[p] * dim, part, d_ids + q0[p] * k, d_scores + q0[p] * k,
+                           d_nout ? d_nout + q0[p] : nullptr, ps[p], err, false);
+        ws_sel_ = 0;
+        last_half_[p] = last_;
+    }
+    last_split_ = rc == kOk;
+    // the caller's stream goes on after both halves
+    CUDA_TRY(cudaEventRecord(split_ev_[1], stream2_));
+    CUDA_TRY(cudaStreamWaitEvent(st, split_ev_[1], 0));
     return rc;
 }
 
@@ -669,48 +717,16 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
     }
     // ids, scores and counts are laid out alike in the device and pinned buffers: one copy back
     const size_t out_off = al(qb), out_len = al(ib) + al(sb) + nb;
-    // two halves on two streams (not for a sharded image, whose ranks must take the same collective
-    // steps, nor under a debug stop or phase timing, which describe one search)
-    const bool split = !exch_ && !dbg && !timing_ && !clock_ && a.nq >= kSplitQueries;
-    if (split && !stream2_) {
-        CUDA_TRY(cudaStreamCreateWithFlags(&stream2_, cudaStreamNonBlocking));
-        for (auto& e : split_ev_) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    }
-    const size_t half = (nq / 2) & ~size_t(63);  // keeps the second half 256-byte aligned
-    const size_t pq0[2] = {0, half}, pn[2] = {half, nq - half};
-    SearchArgs part = a;
-    if (split) part.path = use_cell_major(h, a) ? 1 : 0;
+    const bool split = split_halves(h, a);
     int rc = kOk;
     for (int attempt = 0; attempt < 4; ++attempt) {
         if (!split) {
             CUDA_TRY(cudaMemcpyAsync(dQ, hQ, qb, cudaMemcpyHostToDevice, stream_));
             rc = search_device(h, dQ, a, dI, dS, dN, stream_, err);
-            if (rc != kOk) return rc;
         } else {
-            // the counters are cleared once, before either half can raise one
-            CUDA_TRY(cudaMemsetAsync(d_flags_, 0, fb, stream_));
-            CUDA_TRY(cudaEventRecord(split_ev_[0], stream_));
-            CUDA_TRY(cudaStreamWaitEvent(stream2_, split_ev_[0], 0));
-            // both halves' copies first, then the searches: the second copy crosses PCIe while the
-            // first half is searched (staging per half, or a copy enqueued after the first search's
-            // launches, measured slower)
-            for (int p = 0; p < 2; ++p)
-                CUDA_TRY(cudaMemcpyAsync(dQ + pq0[p] * dim, hQ + pq0[p] * dim, pn[p] * dim * sizeof(float),
-                                         cudaMemcpyHostToDevice, p ? stream2_ : stream_));
-            for (int p = 0; p < 2; ++p) {
-                part.nq = (int)pn[p];
-                ws_sel_ = p;
-                rc = search_device(h, dQ + pq0[p] * dim, part, dI + pq0[p] * k, dS + pq0[p] * k, dN + pq0[p],
-                                   p ? stream2_ : stream_, err, false);
-                ws_sel_ = 0;
-                if (rc != kOk) {
-                    cudaStreamSynchronize(stream2_);
-                    return rc;
-                }
-            }
-            CUDA_TRY(cudaEventRecord(split_ev_[1], stream2_));
-            CUDA_TRY(cudaStreamWaitEvent(stream_, split_ev_[1], 0));
+            rc = search_halves(h, dQ, hQ, a, dI, dS, dN, stream_, err);
         }
+        if (rc != kOk) return rc;
         CUDA_TRY(cudaMemcpyAsync(hp + out_off, dp + out_off, out_len, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaMemcpyAsync(hF, d_flags_, fb, cudaMemcpyDeviceToHost, stream_));
         CUDA_TRY(cudaStreamSynchronize(stream_));
@@ -749,17 +765,38 @@ void DeviceIndex::enable_kernel_clock(bool on) {
 
 std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
     std::vector<std::pair<std::string, double>> out;
-    if (!last_.valid) return out;
+    // a split batch: its two halves' per-query arrays, one after the other (only the seed-only join
+    // splits, so there is no per-cell query count to combine)
+    std::vector<const LastCall*> parts;
+    if (last_split_)
+        parts = {&last_half_[0], &last_half_[1]};
+    else
+        parts = {&last_};
+    for (const LastCall* p : parts)
+        if (!p->valid) return out;
     cudaSetDevice(device_);
-    cudaStreamSynchronize(last_.st);
-    const int nq = last_.nq, np = last_.nprobe, M = view_.M;
+    int nq = 0;
+    for (const LastCall* p : parts) {
+        cudaStreamSynchronize(p->st);
+        nq += p->nq;
+    }
+    const int np = last_.nprobe, M = view_.M;
     auto get = [&](const uint32_t* d, size_t n) {
         std::vector<uint32_t> v(n, 0);
         if (d && n) cudaMemcpy(v.data(), d, n * sizeof(uint32_t), cudaMemcpyDeviceToHost);
         return v;
     };
-    std::vector<uint32_t> nch = get(last_.nch, nq), chosen = get(last_.chosen, (size_t)nq * np),
-                          sl_n = get(last_.sl_n, nq), cand_n = get(last_.cand_n, nq);
+    // the per-query array `field` of every part, concatenated (`per` entries a query)
+    auto gather = [&](const uint32_t* LastCall::*field, size_t per) {
+        std::vector<uint32_t> v;
+        for (const LastCall* p : parts) {
+            std::vector<uint32_t> x = get(p->*field, (size_t)p->nq * per);
+            v.insert(v.end(), x.begin(), x.end());
+        }
+        return v;
+    };
+    std::vector<uint32_t> nch = gather(&LastCall::nch, 1), chosen = gather(&LastCall::chosen, np),
+                          sl_n = gather(&LastCall::sl_n, 1), cand_n = gather(&LastCall::cand_n, 1);
     const double code_bytes = (double)view_.nw * 8.0;
     double probes = 0, shortlist = 0, cands = 0;
     for (int q = 0; q < nq; ++q) {
@@ -776,10 +813,10 @@ std::vector<std::pair<std::string, double>> DeviceIndex::last_stats() {
     out.push_back({"rerank_bytes", cands * row_bytes});
     out.push_back({"route_code_bytes", (double)M * code_bytes});
     if (last_.cell_major) {
-        std::vector<uint32_t> start = np > dev::kSeedCells ? get(last_.cell_cnt, (size_t)M + 1)
-                                                           : std::vector<uint32_t>((size_t)M + 1, 0),
-                              seed_n = get(last_.seed_n, nq),
-                              rest_n = get(last_.rest_n, nq), rest_hi = get(last_.rest_hi, nq);
+        std::vector<uint32_t> start = np > dev::kSeedCells && !last_split_ ? get(last_.cell_cnt, (size_t)M + 1)
+                                                                           : std::vector<uint32_t>((size_t)M + 1, 0),
+                              seed_n = gather(&LastCall::seed_n, 1),
+                              rest_n = gather(&LastCall::rest_n, 1), rest_hi = gather(&LastCall::rest_hi, 1);
         double cells = 0, bytes = 0, pairs = 0, seed_pairs = 0, seed_kept = 0, rest_kept = 0, rest_probes = 0;
         std::vector<uint8_t> seen(M, 0);
         double seed_bytes = 0, seed_union_bytes = 0;

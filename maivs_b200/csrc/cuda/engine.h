@@ -118,10 +118,7 @@ class DeviceIndex {
     int search_static(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                       cudaStream_t st, std::string& err);
     // Host buffers: copies in, searches, copies out, synchronises, and retries with larger
-    // candidate buffers if any query overflowed them. A batch of kSplitQueries or more goes as two
-    // halves on two streams with a workspace each, so that the second half's queries cross PCIe
-    // while the first half is searched (every query's result depends only on that query and the
-    // path the whole batch chose).
+    // candidate buffers if any query overflowed them.
     int search_host(const HostIndex& h, const float* Q, const SearchArgs& a, uint64_t* ids, float* scores,
                     uint32_t* nout, std::string& err);
 
@@ -169,6 +166,18 @@ class DeviceIndex {
    private:
     int search_sharded(const HostIndex& h, const float* dQ, const SearchArgs& a, uint64_t* d_ids, float* d_scores,
                        uint32_t* d_nout, cudaStream_t st, std::string& err);
+    // A batch of kSplitQueries or more whose queries' work is independent of one another (the
+    // cell-major join probing only the seed cells) is searched as two halves, one on `st` and one
+    // on stream2_, with a workspace each: the halves' short dependent kernels overlap each other.
+    // Not for a sharded image (its ranks take the same collective steps), a debug stop or phase
+    // timing (both describe one search); the kernel clock times each half's launches.
+    // Every query's result depends only on that query and on the path the whole batch chose, which
+    // both halves keep, so the results are those of one search over the batch.
+    bool split_halves(const HostIndex& h, const SearchArgs& a) const;
+    // With hQ (pinned host queries), each half is first copied into dQ on its own stream, so the
+    // second half's copy overlaps the first half's search.
+    int search_halves(const HostIndex& h, const float* dQ, const float* hQ, const SearchArgs& a, uint64_t* d_ids,
+                      float* d_scores, uint32_t* d_nout, cudaStream_t st, std::string& err);
     Exchange* exch_ = nullptr;
     uint32_t* d_flags_all_ = nullptr;  // world x 4 counters gathered by global_flags
     int shard_rank_ = 0, shard_world_ = 1;
@@ -208,7 +217,7 @@ class DeviceIndex {
     // so searches sharing a workspace never overlap on the device
     cudaEvent_t ws_ev_[2] = {nullptr, nullptr};
     bool ws_ev_live_[2] = {false, false};
-    cudaStream_t stream2_ = nullptr;  // the second half of a split host-buffer batch
+    cudaStream_t stream2_ = nullptr;  // the second half of a split batch
     cudaEvent_t split_ev_[2] = {nullptr, nullptr};
     // pinned staging for the host-buffer API
     void* pin_ = nullptr;
@@ -225,6 +234,9 @@ class DeviceIndex {
                        *cand_n = nullptr, *seed_n = nullptr, *rest_n = nullptr, *rest_hi = nullptr;
         cudaStream_t st = nullptr;
     } last_;
+    // a split batch's halves (last_split_): last_stats describes both together
+    LastCall last_half_[2];
+    bool last_split_ = false;
     PhaseTimes phases_;
     cudaEvent_t ev_[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
 };

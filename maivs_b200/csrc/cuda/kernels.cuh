@@ -79,6 +79,9 @@ struct KernelClock {
     std::vector<Mark> pending;
     std::vector<cudaEvent_t> pool;
     double ms[kNumKernels] = {0};
+    // time during which at least one launch of the kernel ran (launches on several streams may
+    // overlap; ms counts overlapping time once per launch, busy once)
+    double busy[kNumKernels] = {0};
     unsigned long long launches[kNumKernels] = {0};
     int only = -1;  // >= 0: time only this kernel
     bool wants(int id) const { return only < 0 || only == id; }
