@@ -12,9 +12,11 @@ namespace {
 // The FastScan sum of a (query, member) pair is sum_j LUT_q[16 j + nib_j(member)], i.e. the dot
 // product of the query's u8 table row (K = 16 x npos bytes) with the one-hot expansion of the
 // member's nibbles. For a cell that many queries probe this is a dense u8 x u8 -> s32 GEMM:
-// M = 128 queries x N = 256 members per tile, K in chunks of 128 bytes (8 nibble positions), A
-// (tables) and B (one-hot nibbles) written into shared memory in the K-major 128-byte swizzled
-// layout, four kind::i8 tcgen05.mma per chunk into a TMEM accumulator (128 lanes x 256 columns).
+// M = 128 queries x N = up to 256 members per tile (the tile's members rounded up to 16, so a
+// 100-member cell costs 112 columns of MMA, not 256), K in chunks of 128 bytes (8 nibble
+// positions), A (tables) and B (one-hot nibbles) written into shared memory in the K-major
+// 128-byte swizzled layout, four kind::i8 tcgen05.mma per chunk into a TMEM accumulator (128 lanes
+// x 256 columns allocated).
 // The epilogue reads the sums with tcgen05.ld and applies k_scan_cm's rule (d = maxk - sum <= the
 // query's falling cut-off, canonical home) to append survivors, counting them under the query's
 // rungs. Sums are exact integers, so the survivors equal k_scan_cm's.
@@ -39,7 +41,8 @@ __device__ __forceinline__ void bar_arrive(uint64_t* bar) {
 }
 
 // NPW producer warps build the operands; warp NPW issues the MMAs; S stages. The epilogue splits the
-// accumulator over the producer warps: TMEM lane quarter (warp % 4) x kCols-column slice (warp / 4).
+// accumulator over the producer warps: TMEM lane quarter (warp % 4) x an equal slice of the tile's
+// columns (warp / 4).
 template <int NPW, int S>
 struct PScan {
     static constexpr int kProd = NPW * 32;
@@ -47,7 +50,6 @@ struct PScan {
     static constexpr int kBlocks = NPW == 8 ? 2 : 1;  // CTAs per SM
     static constexpr int kAPer = kMmaQ * 8 / kProd;   // 16-byte A pieces per producer and chunk
     static constexpr int kBMem = kMmaN * 8 / kProd;   // one-hot members per producer and chunk
-    static constexpr int kCols = kMmaN / (NPW / 4);   // accumulator columns per epilogue warp
     static constexpr size_t kSmem = (size_t)S * kMmaStageBytes + 1024;
 };
 
@@ -85,7 +87,6 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = s_tmem;
-    const uint32_t idesc = umma::idesc_u8_s32(kMmaQ, kMmaN);
     // operand roles: A rows ra + (kProd / 8) u at 16-byte chunk ch; B members 8 g + kBMem hh + u at
     // position ch
     const int ch = tid & 7, ra = tid >> 3, g = (tid >> 3) / (8 / P::kBMem), hh = (tid >> 3) % (8 / P::kBMem);
@@ -109,6 +110,9 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
         for (uint32_t qt = 0; qt < nqc && !bad; qt += kMmaQ) {
             const int nq_t = (int)min((uint32_t)kMmaQ, nqc - qt);
             for (int mt = 0; mt < nc && !bad; mt += kMmaN) {
+                // the MMAs cover only this tile's members, rounded up to the M = 128 step of N (16)
+                const int n_tile = (min(kMmaN, nc - mt) + 15) & ~15;
+                const uint32_t idesc = umma::idesc_u8_s32(kMmaQ, n_tile);
                 __syncthreads();  // the previous tile's epilogue is done with s_q, s_r0 and the accumulator
                 if (tid < nq_t) {
                     const uint32_t q = qof[s0 + qt + tid];
@@ -219,7 +223,9 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
                 umma::fence_after_sync();
                 if (!issuer_warp) {
                 const int lq = warp & 3, cq = warp >> 2;
-                constexpr int kCols = P::kCols;
+                // the tile's n_tile columns split evenly over the column groups, 16 columns a load
+                constexpr int kGroups = NPW / 4;
+                const int cw = ((n_tile + 16 * kGroups - 1) / (16 * kGroups)) * 16, c0 = cw * cq;
                 const int r = 32 * lq + lane;
                 const bool vq = !bad && r < nq_t;
                 const uint32_t t = vq ? *reinterpret_cast<volatile const uint32_t*>(b.gtau + s_q[r]) : 0u;
@@ -249,11 +255,11 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
                     }
                     __syncwarp();
                 };
-                for (int cb = 0; cb < kCols; cb += 16) {
+                for (int cb = 0; cb < cw && c0 + cb < n_tile; cb += 16) {
                     uint32_t v[16];
-                    umma::tmem_ld16(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(kCols * cq + cb), v);
+                    umma::tmem_ld16(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(c0 + cb), v);
                     umma::tmem_wait_ld();
-                    const int m0 = mt + kCols * cq + cb;
+                    const int m0 = mt + c0 + cb;
 #pragma unroll
                     for (int h2 = 0; h2 < 2; ++h2) {
                         uint32_t hit = 0;
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(PScan<NPW, S>::kT, PScan<NPW, S>::kBlocks) k_s
                             if (lane >= o) pre += y;
                         }
                         uint32_t pos = cur + pre - nh;
-                        const uint32_t mbase = (uint32_t)(kCols * cq + cb + 8 * h2);
+                        const uint32_t mbase = (uint32_t)(c0 + cb + 8 * h2);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             if (!((hit >> j) & 1u)) continue;
