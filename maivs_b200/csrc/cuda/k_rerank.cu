@@ -450,6 +450,7 @@ __global__ void __launch_bounds__(256) k_rerank_gather(RowSrc src, const uint32_
 // the CTA sets *err, waits (bounded) for the copies it has in flight and returns.
 constexpr int kStreamRows = 32;
 constexpr size_t kStreamSmemMax = 222 * 1024;
+constexpr size_t kStreamSmemSM = 228 * 1024;  // shared memory of one SM (per CTA: 1 KB reserved, 1.25 KB static)
 
 __device__ __forceinline__ void bulk_row_copy(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
     asm volatile(
@@ -931,16 +932,21 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
         const size_t stage_bytes = (size_t)kStreamRows * rstride * sizeof(float);
         const void* sf = nullptr;
         int stages = 0;
+        int per_sm = 1;  // CTAs of the streamed kernel per SM
         if (ix.rerank_mode == 0 && ix.dim == 384) {
-            sf = (const void*)k_rerank_stream<4, 48>;
-            stages = 4;
+            // two CTAs per SM of two stages each: one CTA's sums overlap the other's copies
+            sf = (const void*)k_rerank_stream<2, 48>;
+            stages = 2;
+            per_sm = 2;
         } else if (ix.rerank_mode == 0 && ix.dim == 768) {
             sf = (const void*)k_rerank_stream<2, 96>;
             stages = 2;
         }
         // the item numbering goes into the stream kernel's shared memory when it fits beside the stages
+        // (of per_sm CTAs on one SM)
         const size_t items_bytes = ((size_t)nq + 1) * sizeof(uint32_t);
-        const bool local_items = sf && (size_t)stages * stage_bytes + items_bytes <= kStreamSmemMax;
+        const bool local_items =
+            sf && (size_t)per_sm * ((size_t)stages * stage_bytes + items_bytes + 2560) <= kStreamSmemSM;
         if (!local_items) {
             Tick tk(kKRerankItems, st);
             k_rerank_items<<<1, 1024, 0, st>>>(cand_n, nq, gather_rows(ix.rerank_mode), item_scratch);
@@ -951,7 +957,7 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
             set_smem(sf, ssm);
             Tick tk(kKRerank, st);
             if (ix.dim == 384)
-                k_rerank_stream<4, 48><<<sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
+                k_rerank_stream<2, 48><<<per_sm * sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
                                                               score_scratch, err);
             else
                 k_rerank_stream<2, 96><<<sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
