@@ -689,7 +689,7 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
     }
     char* hp = static_cast<char*>(pin_);
     char* dp = static_cast<char*>(io_);
-    float* hQ = reinterpret_cast<float*>(hp);
+    float* hQ_stage = reinterpret_cast<float*>(hp);
     uint64_t* hI = reinterpret_cast<uint64_t*>(hp + al(qb));
     float* hS = reinterpret_cast<float*>(hp + al(qb) + al(ib));
     uint32_t* hN = reinterpret_cast<uint32_t*>(hp + al(qb) + al(ib) + al(sb));
@@ -698,9 +698,17 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
     uint64_t* dI = reinterpret_cast<uint64_t*>(dp + al(qb));
     float* dS = reinterpret_cast<float*>(dp + al(qb) + al(ib));
     uint32_t* dN = reinterpret_cast<uint32_t*>(dp + al(qb) + al(ib) + al(sb));
+    // queries already in page-locked memory (cudaMallocHost / cudaHostRegister, e.g. a pinned torch
+    // tensor) are copied to the device from where they are; any other buffer goes through the
+    // pinned staging copy first
+    cudaPointerAttributes pa{};
+    const cudaError_t pe = cudaPointerGetAttributes(&pa, Q);
+    if (pe != cudaSuccess) cudaGetLastError();  // clears the (non-sticky) error of an unknown pointer
+    const bool q_pinned = pe == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    const float* hQ = q_pinned ? Q : hQ_stage;
     // staging copy into pinned memory: large batches are copied by several host threads (one
     // thread's memcpy is slower than the PCIe transfer that follows)
-    {
+    if (!q_pinned) {
         constexpr size_t kPart = size_t(256) << 10;
         const long long parts = (long long)((qb + kPart - 1) / kPart);
         const int thr = (int)std::min<long long>(std::min(parts, 8LL), (long long)omp_get_max_threads());
@@ -708,11 +716,11 @@ int DeviceIndex::search_host(const HostIndex& h, const float* Q, const SearchArg
 #pragma omp parallel for num_threads(thr) schedule(static)
             for (long long i = 0; i < parts; ++i) {
                 const size_t o = (size_t)i * kPart;
-                std::memcpy(reinterpret_cast<char*>(hQ) + o, reinterpret_cast<const char*>(Q) + o,
+                std::memcpy(reinterpret_cast<char*>(hQ_stage) + o, reinterpret_cast<const char*>(Q) + o,
                             std::min(kPart, qb - o));
             }
         } else {
-            std::memcpy(hQ, Q, qb);
+            std::memcpy(hQ_stage, Q, qb);
         }
     }
     // ids, scores and counts are laid out alike in the device and pinned buffers: one copy back

@@ -100,3 +100,20 @@ def test_split_keeps_the_whole_batch_path(built):
         _same(_device_search(ix, small, K, 8, True), ref_s)
     finally:
         ix.set_cell_major_min_batch(old)
+
+
+@pytest.mark.parametrize("nq", [300, 1_100])
+def test_pinned_queries_copied_without_staging(built, nq):
+    """Queries in page-locked host memory (here a pinned torch tensor) are copied to the device from
+    where they are, without the host API's staging copy: the results are the oracle's, for a batch
+    that splits into two halves and for one that does not."""
+    import torch
+
+    ix, Q = built
+    ref, _ = _oracle(ix, Q[:nq], 8, True)
+    pinned = torch.from_numpy(np.ascontiguousarray(Q[:nq])).pin_memory()
+    assert pinned.is_pinned()
+    _same(ix.search_batch_arrays(pinned.numpy(), K, 8, 1.0, 8.0, True), ref)
+    # the same buffer again, then a pageable copy: nothing of the previous call is reused
+    _same(ix.search_batch_arrays(pinned.numpy(), K, 8, 1.0, 8.0, True), ref)
+    _same(ix.search_batch_arrays(np.array(Q[:nq]), K, 8, 1.0, 8.0, True), ref)
