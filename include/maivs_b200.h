@@ -99,7 +99,9 @@ int maivs_search(maivs_index* ix, const float* query, size_t k, size_t nprobe, f
  * FastScan index is scanned by FastScan table sums (cell-major join or per query); any other index
  * (before compact(), after a remove(), FastScan off) by Hamming distance per query, as the reference
  * does (index.rs:1624-1626); the cell-major join of a compacted index without FastScan blocks is
- * MAIVS_UNSUPPORTED on the GPU (search it with cell_major = 0, or set FastScan and compact). */
+ * MAIVS_UNSUPPORTED on the GPU (search it with cell_major = 0, or set FastScan and compact).
+ * `queries` may be any host memory; queries in page-locked memory (cudaMallocHost, cudaHostRegister)
+ * are copied to the device from where they are, others through the library's pinned staging buffer. */
 int maivs_search_batch(maivs_index* ix, const float* queries, size_t nq, size_t k, size_t nprobe,
                        float target_confidence, float beta, int cell_major, uint64_t* ids, float* scores);
 
