@@ -957,8 +957,8 @@ void launch_rerank(const IndexView& ix, const float* Q, const QueryEnc& e, int n
             set_smem(sf, ssm);
             Tick tk(kKRerank, st);
             if (ix.dim == 384)
-                k_rerank_stream<2, 48><<<per_sm * sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
-                                                              score_scratch, err);
+                k_rerank_stream<2, 48><<<per_sm * sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap,
+                                                                       rstride, score_scratch, err);
             else
                 k_rerank_stream<2, 96><<<sms, 256, ssm, st>>>(src, cand, cand_n, io, nq, cand_cap, rstride,
                                                               score_scratch, err);
