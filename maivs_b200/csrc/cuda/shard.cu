@@ -79,6 +79,9 @@ const NcclApi& nccl() {
 constexpr double kNcclWaitSeconds = 120.0;  // communicator set-up and each collective's enqueue
 
 // Waits for a non-blocking communicator to leave ncclInProgress; aborts it on error or timeout.
+// A collective's enqueue normally settles within microseconds, and the search stream gets no
+// further launches until it has, so the first 2 ms poll with yields; longer waits (communicator
+// set-up) sleep 50 us between polls.
 ncclResult_t nccl_settle(ncclComm_t comm) {
     const NcclApi& n = nccl();
     auto t0 = std::chrono::steady_clock::now();
@@ -88,7 +91,10 @@ ncclResult_t nccl_settle(ncclComm_t comm) {
         if (st != ncclInProgress) return st;
         double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (s > kNcclWaitSeconds) return ncclInProgress;
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (s < 2e-3)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
