@@ -176,3 +176,41 @@ def test_shuffle_tree_is_the_reference_hsum_order():
             v = np.array([f32(v[i]) + f32(v[i ^ off]) for i in range(8)], dtype=f32)
         want = f32(f32(f32(c[0] + c[4]) + f32(c[2] + c[6])) + f32(f32(c[1] + c[5]) + f32(c[3] + c[7])))
         assert v[0].tobytes() == want.tobytes()
+
+
+@pytest.mark.parametrize("ngroups", [1, 2, 4])
+def test_scan_mma_epilogue_columns_cover_the_tile_once(ngroups):
+    """k_scan_mma's epilogue: the tile's N = members rounded up to 16 columns are split over the
+    column groups (warp / 4) in slices of cw = 16 * ceil(N / (16 * groups)) columns, loaded 16 at a
+    time while the load starts below N. Every column below N is read by exactly one group, no load
+    reaches past N (so never past the 256 allocated TMEM columns), and N is a legal kind::i8 width
+    for M = 128 (a multiple of 16 from 16 to 256)."""
+    for members in range(1, 600):
+        for mt in range(0, members, 256):
+            n_tile = (min(256, members - mt) + 15) & ~15
+            assert n_tile % 16 == 0 and 16 <= n_tile <= 256
+            cw = ((n_tile + 16 * ngroups - 1) // (16 * ngroups)) * 16
+            seen = np.zeros(n_tile, dtype=int)
+            for cq in range(ngroups):
+                c0 = cw * cq
+                cb = 0
+                while cb < cw and c0 + cb < n_tile:
+                    assert c0 + cb + 16 <= n_tile
+                    seen[c0 + cb:c0 + cb + 16] += 1
+                    cb += 16
+            assert (seen == 1).all(), (members, mt, ngroups)
+
+
+def test_rerank_stream_two_ctas_fit_one_sm():
+    """The streamed rerank at d = 384 runs two CTAs of two 32-row stages per SM; its item table
+    goes into shared memory only when both CTAs (stages, table, 1 KB reserved, 1.25 KB static) still
+    fit the SM's 228 KB, otherwise into global memory (k_rerank_items)."""
+    rstride = 384 + ((8 - 384 % 32) + 32) % 32
+    stage = 32 * rstride * 4
+    sm = 228 * 1024
+    for nq in (1, 448, 552, 1000, 3000, 3455, 3456, 5000, 10000):
+        items = (nq + 1) * 4
+        local = 2 * (2 * stage + items + 2560) <= sm
+        need = 2 * (2 * stage + (items if local else 0) + 1024 + 1280)
+        assert need <= sm, nq  # two CTAs are resident whichever way the table goes
+        assert local == (nq <= 3455), nq
