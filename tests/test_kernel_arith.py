@@ -1,11 +1,12 @@
 """The integer arithmetic of the FastScan sums and of the distance select, restated on the CPU.
 
-The device code (maivs_b200/csrc/cuda/kernels.cu) looks up 8 members' table bytes with byte
-permutes (`lut16x8`), adds the looked-up bytes as whole 32-bit words and widens only the odd
-bytes (`GroupAcc`), and selects the kth smallest distance with two histograms over the keys' own
-range (`block_select_d`). These tests check each identity the kernels rely on against the
-definition, on random inputs and on the edge values (all 255s, npos = 256, ties); the GPU tests
-then check the kernels themselves against the oracle.
+The device code (maivs_b200/csrc/cuda/dev_common.cuh, k_cellmajor.cu) looks up 8 members' table
+bytes with byte permutes (`lut16x8`), adds the looked-up bytes as whole 32-bit words and widens
+only the odd bytes (`GroupAcc`), and selects the kth smallest distance with two histograms over
+the keys' own range (`block_select_d`). These tests check each identity the kernels rely on
+against the definition, on random inputs and on the edge values (all 255s, npos = 256, ties), and
+the index arithmetic of the rerank's work split, the tensor-core scan's epilogue and the rerank's
+shared-memory fit; the GPU tests then check the kernels themselves against the oracle.
 """
 from __future__ import annotations
 
